@@ -1,0 +1,160 @@
+/*
+ * polarflash_b200.h -- C ABI of the B200 (sm_100a) compressed-linear library.
+ *
+ * The library computes y = W x directly from packed low-bit weights
+ * (INT4/INT3/INT2 codes, E8 root residual-VQ indices, recursive polar
+ * blocks), with the inverse block randomized Walsh-Hadamard transform of the
+ * weight folded in as a forward transform of x.  Every pointer argument
+ * named "device" must point into memory of the current CUDA device; every
+ * launch goes to the caller's stream and returns without synchronising.
+ * No entry point allocates device memory: scratch space is the caller's
+ * `workspace` buffer (size from pf_qlinear_workspace_size).
+ *
+ * Errors: every entry point returns a pf_status.  Argument errors are found on
+ * the host before anything is launched; PF_ERR_CUDA reports a launch failure
+ * (cudaGetLastError) and pf_last_cuda_error() returns the CUDA error code.
+ */
+#ifndef POLARFLASH_B200_H
+#define POLARFLASH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PF_API __attribute__((visibility("default")))
+#else
+#define PF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (the Python layer maps them to ValueError / RuntimeError as
+ * the reference does, polarflash_quant/unified_quantizer.py:100-101,
+ * polarflash_rt/cuda/native_kernels.py:396-410). */
+typedef enum pf_status {
+  PF_OK = 0,
+  PF_ERR_INVALID_ARGUMENT = 1, /* null pointer, unknown enum value          */
+  PF_ERR_SHAPE = 2,            /* M, K or N outside what the format allows  */
+  PF_ERR_ALIGNMENT = 3,        /* a device pointer is not aligned enough    */
+  PF_ERR_UNSUPPORTED = 4,      /* format/parameter combination not built    */
+  PF_ERR_WORKSPACE = 5,        /* workspace missing or too small            */
+  PF_ERR_CUDA = 6,             /* CUDA launch / runtime failure             */
+  PF_ERR_TIMEOUT = 7           /* a bounded device wait gave up             */
+} pf_status;
+
+/* Packed weight formats.  Codes of the reference formats are bit-identical
+ * to the reference packers (polarflash_quant/bitpacking.py); the *_G128 and
+ * E8 formats are extensions defined in the same conventions.
+ *
+ *  PF_FMT_INT4_G128  codes: u32 words, 8 codes per word (code i at bits 4i),
+ *                    16 words per (row, 128-column group); scales, mins:
+ *                    fp16 [M][K/128]; w = q*s + m (the asymmetric convention of
+ *                    polarflash_rt/kv_cache/compressed_kv.py:115-146).
+ *  PF_FMT_INT3_G128  10 codes per word (code i at bits 3i, bits 30-31 zero),
+ *                    13 words per (row, group); scales/mins as INT4_G128.
+ *  PF_FMT_INT2_G128  16 codes per word (code i at bits 2i), 8 words per group.
+ *  PF_FMT_INT4       reference pack_int4 stream (bitpacking.py:16-31), rows of
+ *                    K/2 bytes; w = (code - 8) * scale.
+ *  PF_FMT_INT3       reference pack_int3 stream (bitpacking.py:88-123), rows of
+ *                    3K/8 bytes; w = (code - 4) * scale.
+ *  PF_FMT_INT2       reference pack_int2 stream (bitpacking.py:49-65), rows of
+ *                    K/4 bytes; w = (code - 2) * scale.
+ *                    For the three reference INT formats `scale` is
+ *                    tensor_scale (UnifiedQuantizer, unified_quantizer.py:154-178)
+ *                    or, when `scales` is non-NULL, fp32 [M] per-row scales
+ *                    (NativeLowBitCUDAEngine, native_kernels.py:415-576).
+ *  PF_FMT_E8_RVQ2_G128  idx: u8 [M][K/8][2] (stage-interleaved root indices in
+ *                    generate_e8_roots order, e8_lattice.py:21-50); scales: fp16
+ *                    [M][K/128][2]; w8 = s1*r[i1] + s2*r[i2].
+ *  PF_FMT_POLAR_RECURSIVE  encode_packed stream (polar_quant.py:381-487):
+ *                    MSB-first blocks of params[1..d] bits, rows of K/d blocks;
+ *                    params[0] = d (block size), params[1..d] = allocation;
+ *                    tensor_scale = r_scale.
+ *  PF_FMT_POLAR2D    2-D polar pairs (polar_quant.py:18-73): MSB-first
+ *                    (r << theta_bits | theta); params[0] = r_bits,
+ *                    params[1] = theta_bits; tensor_scale = r_scale.
+ */
+typedef enum pf_format {
+  PF_FMT_INT4_G128 = 1,
+  PF_FMT_INT3_G128 = 2,
+  PF_FMT_INT2_G128 = 3,
+  PF_FMT_INT4 = 4,
+  PF_FMT_INT3 = 5,
+  PF_FMT_INT2 = 6,
+  PF_FMT_E8_RVQ2_G128 = 7,
+  PF_FMT_POLAR_RECURSIVE = 8,
+  PF_FMT_POLAR2D = 9
+} pf_format;
+
+typedef enum pf_dtype { PF_DTYPE_F32 = 0, PF_DTYPE_F16 = 1, PF_DTYPE_BF16 = 2 } pf_dtype;
+
+/* A packed weight resident on the device.  Replaces the (raw_bytes,
+ * quant_meta) pair that PolarLinearLayer keeps (polarflash_rt/cpu/engine.py:36-56). */
+typedef struct pf_qweight {
+  int32_t format;            /* pf_format                                      */
+  int32_t M;                 /* out_features (rows of W)                       */
+  int32_t K;                 /* in_features (columns of W)                     */
+  int32_t had_block;         /* RWHT block the weight was rotated with; 0 = none
+                                (hadamard_block_size after _init_dims,
+                                polarflash_quant/transforms/hadamard.py:93-99) */
+  const void* codes;         /* device: packed payload                         */
+  const void* scales;        /* device: per format (see above), may be NULL    */
+  const void* mins;          /* device: fp16 group mins for *_G128, else NULL  */
+  const int8_t* had_signs;   /* device: K per-column signs (+1/-1), or NULL    */
+  double tensor_scale;       /* per-tensor scale / polar r_scale               */
+  int32_t params[20];        /* format parameters (polar block size, alloc)    */
+} pf_qweight;
+
+/* Library identity. */
+PF_API const char* pf_version(void);
+PF_API const char* pf_status_string(int status);
+PF_API int pf_last_cuda_error(void);
+
+/* Checks a descriptor (shapes, pointers, alignment) without launching. */
+PF_API int pf_qweight_check(const pf_qweight* w);
+
+/* Bytes of device scratch pf_qlinear needs for N input rows. */
+PF_API int pf_qlinear_workspace_size(const pf_qweight* w, int N, size_t* bytes);
+
+/* y[N][M] (fp32) = x[N][K] * W^T (+ bias[M]).  Replaces PolarLinearLayer.forward
+ * (polarflash_rt/cpu/engine.py:90-96) and, through it, PFlashCUDAEngine.forward_layer
+ * (polarflash_rt/cuda/engine.py:129-145): the dequantize -> inverse RWHT ->
+ * torch.matmul chain becomes one fused launch sequence on `stream`.
+ * x: device, dtype pf_dtype, row-major [N][K]; bias: device fp32 [M] or NULL;
+ * y: device fp32 [N][M]; workspace: device, 256-byte aligned. */
+PF_API int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias,
+               float* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* W_hat[M][K] (fp32) = decoded weight, followed by the inverse block RWHT
+ * when `inverse_rwht` is non-zero and the weight is rotated.  Replaces
+ * UnifiedQuantizer.dequantize (polarflash_quant/unified_quantizer.py:242-324). */
+PF_API int pf_dequant(const pf_qweight* w, float* W_out, int inverse_rwht, void* stream);
+
+/* Unpacked codes u8 [M][K] (bit-exact with the reference unpackers,
+ * bitpacking.py:34-156) for the INT formats; E8: indices u8 [M][K/8][2]. */
+PF_API int pf_unpack_codes(const pf_qweight* w, uint8_t* codes_out, void* stream);
+
+/* Block randomized Walsh-Hadamard on rows of a [rows][K] fp32 matrix
+ * (BlockHadamardTransform.forward / .inverse, hadamard.py:119-169).
+ * signs: device, K per-column +-1 as int8; block: effective block size. */
+PF_API int pf_rwht(const float* in, float* out, int rows, int K, int block, const int8_t* signs,
+            int inverse, void* stream);
+
+/* NativeLowBitCUDAEngine mirrors (polarflash_rt/cuda/native_kernels.py:415-576):
+ * packed uint8 [M][K/2] (int4, nibble - 8) or [M][K/4] (int2, code - 2),
+ * per-row fp32 scales [M], fp32 x / y, no rotation. */
+PF_API int pf_native_gemv_int4(const float* x, const uint8_t* packed, const float* scales, int M,
+                        int K, float* y, void* workspace, size_t workspace_bytes, void* stream);
+PF_API int pf_native_gemv_int2(const float* x, const uint8_t* packed, const float* scales, int M,
+                        int K, float* y, void* workspace, size_t workspace_bytes, void* stream);
+PF_API int pf_native_gemm_int4(const float* X, const uint8_t* packed, const float* scales, int N,
+                        int M, int K, float* Y, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POLARFLASH_B200_H */

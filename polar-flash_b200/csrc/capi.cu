@@ -1,0 +1,396 @@
+// C ABI entry points: argument validation on the host, then the launch
+// sequence (x-prep, GEMV) on the caller's stream.  Nothing here allocates.
+#include <string.h>
+
+#include "gemv.cuh"
+
+using namespace pfb;
+
+namespace {
+
+thread_local int g_last_cuda_error = 0;
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return PF_OK;
+  g_last_cuda_error = (int)e;
+  return PF_ERR_CUDA;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Block plan of BlockHadamardTransform._init_dims (hadamard.py:93-116).
+int make_plan(int K, int block, HadPlan* p) {
+  memset(p, 0, sizeof(*p));
+  if (block == 0) return PF_OK;
+  if (!pow2(block) || block < 2 || block > kMaxHadBlock || block > K) return PF_ERR_UNSUPPORTED;
+  p->block = block;
+  p->nfull = K / block;
+  int off = p->nfull * block, rem = K - off;
+  while (rem > 1) {
+    int p2 = 1;
+    while (p2 * 2 <= rem) p2 *= 2;
+    if (p->ncasc >= kMaxCascade) return PF_ERR_UNSUPPORTED;
+    p->casc_off[p->ncasc] = off;
+    p->casc_size[p->ncasc] = p2;
+    p->ncasc++;
+    off += p2;
+    rem -= p2;
+  }
+  p->rot_end = off;
+  return PF_OK;
+}
+
+int row_words_of(int fmt, int K) {
+  switch (fmt) {
+    case PF_FMT_INT4_G128: return (K / 128) * 16;
+    case PF_FMT_INT3_G128: return (K / 128) * 13;
+    case PF_FMT_INT2_G128: return (K / 128) * 8;
+    case PF_FMT_INT4: return K / 8;
+    case PF_FMT_INT3: return 3 * K / 32;
+    case PF_FMT_INT2: return K / 16;
+    default: return 0;
+  }
+}
+
+struct PolarShape {
+  int d, tb, row_bytes;
+  int alloc[17];
+};
+
+int polar_shape(const pf_qweight* w, PolarShape* ps) {
+  memset(ps, 0, sizeof(*ps));
+  if (w->format == PF_FMT_POLAR_RECURSIVE) {
+    int d = w->params[0];
+    if (d != 2 && d != 4 && d != 8 && d != 16) return PF_ERR_UNSUPPORTED;
+    ps->d = d;
+    for (int i = 0; i < d; ++i) {
+      int b = w->params[1 + i];
+      if (b < 1 || (i > 0 && b > 6) || (i == 0 && b > 16)) return PF_ERR_UNSUPPORTED;
+      ps->alloc[i] = b;
+      ps->tb += b;
+    }
+  } else {
+    int rb = w->params[0], thb = w->params[1];
+    if (rb < 1 || rb > 16 || thb < 1 || thb > 6) return PF_ERR_UNSUPPORTED;
+    ps->d = 2;
+    ps->alloc[0] = rb;
+    ps->alloc[1] = thb;
+    ps->tb = rb + thb;
+  }
+  if (ps->tb > 32) return PF_ERR_UNSUPPORTED;
+  if (w->K % ps->d) return PF_ERR_SHAPE;
+  long long bits = (long long)(w->K / ps->d) * ps->tb;
+  if (bits % 8) return PF_ERR_SHAPE;
+  ps->row_bytes = (int)(bits / 8);
+  return PF_OK;
+}
+
+int check(const pf_qweight* w) {
+  if (!w) return PF_ERR_INVALID_ARGUMENT;
+  if (w->M <= 0 || w->K <= 0) return PF_ERR_SHAPE;
+  if (!w->codes) return PF_ERR_INVALID_ARGUMENT;
+  if (w->had_block != 0) {
+    if (!w->had_signs) return PF_ERR_INVALID_ARGUMENT;
+    HadPlan p;
+    int st = make_plan(w->K, w->had_block, &p);
+    if (st) return st;
+  }
+  switch (w->format) {
+    case PF_FMT_INT4_G128:
+    case PF_FMT_INT3_G128:
+    case PF_FMT_INT2_G128: {
+      if (w->K % 128) return PF_ERR_SHAPE;
+      if (!w->scales || !w->mins) return PF_ERR_INVALID_ARGUMENT;
+      size_t al = w->format == PF_FMT_INT4_G128 ? 16 : w->format == PF_FMT_INT2_G128 ? 8 : 4;
+      if (!aligned(w->codes, al) || !aligned(w->scales, 2) || !aligned(w->mins, 2)) return PF_ERR_ALIGNMENT;
+      return PF_OK;
+    }
+    case PF_FMT_INT4:
+    case PF_FMT_INT3:
+    case PF_FMT_INT2: {
+      if (w->K % 32) return PF_ERR_SHAPE;
+      size_t al = w->format == PF_FMT_INT4 ? 16 : w->format == PF_FMT_INT2 ? 8 : 4;
+      if (!aligned(w->codes, al)) return PF_ERR_ALIGNMENT;
+      if (w->scales && !aligned(w->scales, 4)) return PF_ERR_ALIGNMENT;
+      return PF_OK;
+    }
+    case PF_FMT_E8_RVQ2_G128: {
+      if (w->K % 128) return PF_ERR_SHAPE;
+      if (!w->scales) return PF_ERR_INVALID_ARGUMENT;
+      if (!aligned(w->codes, 2) || !aligned(w->scales, 4)) return PF_ERR_ALIGNMENT;
+      return PF_OK;
+    }
+    case PF_FMT_POLAR_RECURSIVE:
+    case PF_FMT_POLAR2D: {
+      PolarShape ps;
+      return polar_shape(w, &ps);
+    }
+    default: return PF_ERR_INVALID_ARGUMENT;
+  }
+}
+
+int tokens_per_pass(int N) { return N < kMaxGemvTokens ? N : kMaxGemvTokens; }
+int nt_of(int np) { return np <= 4 ? 1 : np <= 8 ? 2 : 4; }
+
+size_t workspace_bytes(const pf_qweight* w, int N) {
+  int np = tokens_per_pass(N < 1 ? 1 : N);
+  size_t Gp = (size_t)(w->K + 127) / 128;
+  if (is_int_format(w->format)) {
+    int NT = nt_of(np);
+    return round_up((size_t)NT * Gp * 2048, 256) + round_up(Gp * 8 * NT * sizeof(float), 256);
+  }
+  return round_up((size_t)np * Gp * 128 * sizeof(float), 256);
+}
+
+size_t dtype_size(int dt) { return dt == PF_DTYPE_F32 ? 4 : 2; }
+
+int qlinear_pass(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, int N,
+                 const float* bias, float* y, void* ws, cudaStream_t s) {
+  const int K = w->K, M = w->M;
+  const int Gp = (K + 127) / 128;
+  PrepArgs pa;
+  memset(&pa, 0, sizeof(pa));
+  pa.x = x;
+  pa.x_dtype = x_dtype;
+  pa.N = N;
+  pa.K = K;
+  pa.Kp = Gp * 128;
+  pa.plan = plan;
+  pa.signs = w->had_signs;
+  pa.fmt = w->format;
+  pa.y = y;
+  pa.bias = bias;
+  pa.M = M;
+  if (is_int_format(w->format)) {
+    const int NT = nt_of(N);
+    uint2* xfrag = static_cast<uint2*>(ws);
+    float* sx = reinterpret_cast<float*>(static_cast<char*>(ws) + round_up((size_t)NT * Gp * 2048, 256));
+    pa.mode = 0;
+    pa.NT = NT;
+    pa.slots = 4 * NT;
+    pa.xfrag = xfrag;
+    pa.sx = sx;
+    pa.init_y = 1;
+    int st = cuda_status(launch_prep(pa, s));
+    if (st) return st;
+    GemvIntArgs ga;
+    memset(&ga, 0, sizeof(ga));
+    ga.codes = w->codes;
+    ga.scales = w->scales;
+    ga.mins = static_cast<const __half*>(w->mins);
+    ga.tensor_scale = (float)w->tensor_scale;
+    ga.M = M;
+    ga.K = K;
+    ga.N = N;
+    ga.G = Gp;
+    ga.Gp = Gp;
+    ga.row_words = row_words_of(w->format, K);
+    ga.NT = NT;
+    const int rpi = gemv_int_rows_per_item(NT);
+    ga.n_row_items = (M + rpi - 1) / rpi;
+    const long long target = 148LL * 16;
+    long long cg = ((long long)Gp * ga.n_row_items + target - 1) / target;
+    if (cg < 1) cg = 1;
+    if (cg > Gp) cg = Gp;
+    ga.CG = (int)cg;
+    ga.n_items = ga.n_row_items * ((Gp + ga.CG - 1) / ga.CG);
+    ga.xfrag = xfrag;
+    ga.sx = sx;
+    ga.y = y;
+    int smode = is_group_int_format(w->format) ? kScaleGroup : (w->scales ? kScaleRow : kScaleTensor);
+    return cuda_status(launch_gemv_int(w->format, ga, smode, s));
+  }
+  // CUDA-core formats: plain x'
+  float* xplain = static_cast<float*>(ws);
+  pa.mode = 1;
+  pa.slots = N;
+  pa.xplain = xplain;
+  pa.init_y = 0;
+  int st = cuda_status(launch_prep(pa, s));
+  if (st) return st;
+  GemvCCArgs ca;
+  memset(&ca, 0, sizeof(ca));
+  ca.fmt = w->format;
+  ca.codes = w->codes;
+  ca.scales = w->scales;
+  ca.M = M;
+  ca.K = K;
+  ca.N = N;
+  ca.Kp = Gp * 128;
+  ca.xplain = xplain;
+  ca.bias = bias;
+  ca.y = y;
+  if (w->format != PF_FMT_E8_RVQ2_G128) {
+    PolarShape ps;
+    polar_shape(w, &ps);
+    ca.d = ps.d;
+    ca.tb = ps.tb;
+    ca.row_bytes = ps.row_bytes;
+    memcpy(ca.alloc, ps.alloc, sizeof(ca.alloc));
+    ca.r_scale = (float)w->tensor_scale;
+    ca.zero_rule = w->format == PF_FMT_POLAR2D;
+  }
+  return cuda_status(launch_gemv_cc(ca, s));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pf_version(void) { return "polarflash_b200 0.1.0 (sm_100a)"; }
+
+const char* pf_status_string(int status) {
+  switch (status) {
+    case PF_OK: return "ok";
+    case PF_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PF_ERR_SHAPE: return "unsupported shape";
+    case PF_ERR_ALIGNMENT: return "misaligned device pointer";
+    case PF_ERR_UNSUPPORTED: return "unsupported format parameters";
+    case PF_ERR_WORKSPACE: return "workspace missing or too small";
+    case PF_ERR_CUDA: return "CUDA error";
+    case PF_ERR_TIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int pf_last_cuda_error(void) { return g_last_cuda_error; }
+
+int pf_qweight_check(const pf_qweight* w) { return check(w); }
+
+int pf_qlinear_workspace_size(const pf_qweight* w, int N, size_t* bytes) {
+  int st = check(w);
+  if (st) return st;
+  if (!bytes || N < 0) return PF_ERR_INVALID_ARGUMENT;
+  *bytes = workspace_bytes(w, N);
+  return PF_OK;
+}
+
+int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias, float* y,
+               void* workspace, size_t ws_bytes, void* stream) {
+  int st = check(w);
+  if (st) return st;
+  if (N < 0 || x_dtype < PF_DTYPE_F32 || x_dtype > PF_DTYPE_BF16) return PF_ERR_INVALID_ARGUMENT;
+  if (N == 0) return PF_OK;
+  if (!x || !y) return PF_ERR_INVALID_ARGUMENT;
+  if (!workspace || ws_bytes < workspace_bytes(w, N)) return PF_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return PF_ERR_ALIGNMENT;
+  if (!aligned(x, dtype_size(x_dtype)) || !aligned(y, 4) || (bias && !aligned(bias, 4))) return PF_ERR_ALIGNMENT;
+  HadPlan plan;
+  st = make_plan(w->K, w->had_block, &plan);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t xs = dtype_size(x_dtype);
+  for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {
+    int np = N - t0 < kMaxGemvTokens ? N - t0 : kMaxGemvTokens;
+    st = qlinear_pass(w, plan, static_cast<const char*>(x) + (size_t)t0 * w->K * xs, x_dtype, np, bias,
+                      y + (size_t)t0 * w->M, workspace, s);
+    if (st) return st;
+  }
+  return PF_OK;
+}
+
+int pf_dequant(const pf_qweight* w, float* W_out, int inverse_rwht, void* stream) {
+  int st = check(w);
+  if (st) return st;
+  if (!W_out) return PF_ERR_INVALID_ARGUMENT;
+  DequantArgs a;
+  memset(&a, 0, sizeof(a));
+  a.fmt = w->format;
+  a.codes = w->codes;
+  a.scales = w->scales;
+  a.mins = static_cast<const __half*>(w->mins);
+  a.tensor_scale = (float)w->tensor_scale;
+  a.M = w->M;
+  a.K = w->K;
+  a.row_words = row_words_of(w->format, w->K);
+  a.W = W_out;
+  if (w->format == PF_FMT_POLAR_RECURSIVE || w->format == PF_FMT_POLAR2D) {
+    PolarShape ps;
+    polar_shape(w, &ps);
+    a.d = ps.d;
+    a.tb = ps.tb;
+    a.row_bytes = ps.row_bytes;
+    memcpy(a.alloc, ps.alloc, sizeof(a.alloc));
+    a.r_scale = (float)w->tensor_scale;
+    a.zero_rule = w->format == PF_FMT_POLAR2D;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = cuda_status(launch_dequant(a, s));
+  if (st) return st;
+  if (inverse_rwht && w->had_block) {
+    HadPlan plan;
+    make_plan(w->K, w->had_block, &plan);
+    for (int r0 = 0; r0 < w->M; r0 += 65535) {
+      int rows = w->M - r0 < 65535 ? w->M - r0 : 65535;
+      float* p = W_out + (size_t)r0 * w->K;
+      st = cuda_status(launch_rwht_rows(p, p, rows, w->K, plan, w->had_signs, 1, s));
+      if (st) return st;
+    }
+  }
+  return PF_OK;
+}
+
+int pf_unpack_codes(const pf_qweight* w, uint8_t* codes_out, void* stream) {
+  int st = check(w);
+  if (st) return st;
+  if (!codes_out) return PF_ERR_INVALID_ARGUMENT;
+  if (!is_int_format(w->format) && w->format != PF_FMT_E8_RVQ2_G128) return PF_ERR_UNSUPPORTED;
+  DequantArgs a;
+  memset(&a, 0, sizeof(a));
+  a.fmt = w->format;
+  a.codes = w->codes;
+  a.scales = w->scales;
+  a.M = w->M;
+  a.K = w->K;
+  a.row_words = row_words_of(w->format, w->K);
+  a.codes_out = codes_out;
+  return cuda_status(launch_unpack(a, static_cast<cudaStream_t>(stream)));
+}
+
+int pf_rwht(const float* in, float* out, int rows, int K, int block, const int8_t* signs, int inverse,
+            void* stream) {
+  if (!in || !out || !signs || rows < 0 || K <= 0) return PF_ERR_INVALID_ARGUMENT;
+  HadPlan plan;
+  int st = make_plan(K, block, &plan);
+  if (st) return st;
+  if (block == 0) return PF_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int r0 = 0; r0 < rows; r0 += 65535) {
+    int n = rows - r0 < 65535 ? rows - r0 : 65535;
+    st = cuda_status(launch_rwht_rows(in + (size_t)r0 * K, out + (size_t)r0 * K, n, K, plan, signs, inverse, s));
+    if (st) return st;
+  }
+  return PF_OK;
+}
+
+static int native_gemv(int fmt, const float* x, const uint8_t* packed, const float* scales, int N, int M,
+                       int K, float* y, void* ws, size_t ws_bytes, void* stream) {
+  if (!scales) return PF_ERR_INVALID_ARGUMENT;
+  pf_qweight w;
+  memset(&w, 0, sizeof(w));
+  w.format = fmt;
+  w.M = M;
+  w.K = K;
+  w.codes = packed;
+  w.scales = scales;
+  return pf_qlinear(&w, x, PF_DTYPE_F32, N, nullptr, y, ws, ws_bytes, stream);
+}
+
+int pf_native_gemv_int4(const float* x, const uint8_t* packed, const float* scales, int M, int K, float* y,
+                        void* ws, size_t ws_bytes, void* stream) {
+  return native_gemv(PF_FMT_INT4, x, packed, scales, 1, M, K, y, ws, ws_bytes, stream);
+}
+
+int pf_native_gemv_int2(const float* x, const uint8_t* packed, const float* scales, int M, int K, float* y,
+                        void* ws, size_t ws_bytes, void* stream) {
+  return native_gemv(PF_FMT_INT2, x, packed, scales, 1, M, K, y, ws, ws_bytes, stream);
+}
+
+int pf_native_gemm_int4(const float* X, const uint8_t* packed, const float* scales, int N, int M, int K,
+                        float* Y, void* ws, size_t ws_bytes, void* stream) {
+  return native_gemv(PF_FMT_INT4, X, packed, scales, N, M, K, Y, ws, ws_bytes, stream);
+}
+
+}  // extern "C"

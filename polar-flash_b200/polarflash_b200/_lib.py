@@ -1,0 +1,126 @@
+"""ctypes binding of libpolarflash_b200.so (the C ABI in include/polarflash_b200.h).
+
+The library is required: there is no CPU or PyTorch fallback for the compute
+path.  If the shared object is missing the import of the compute entry points
+raises immediately with the build command to run.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libpolarflash_b200.so")
+
+# pf_format
+FMT_INT4_G128 = 1
+FMT_INT3_G128 = 2
+FMT_INT2_G128 = 3
+FMT_INT4 = 4
+FMT_INT3 = 5
+FMT_INT2 = 6
+FMT_E8_RVQ2_G128 = 7
+FMT_POLAR_RECURSIVE = 8
+FMT_POLAR2D = 9
+
+# pf_dtype
+DTYPE_F32 = 0
+DTYPE_F16 = 1
+DTYPE_BF16 = 2
+
+# pf_status
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_SHAPE = 2
+ERR_ALIGNMENT = 3
+ERR_UNSUPPORTED = 4
+ERR_WORKSPACE = 5
+ERR_CUDA = 6
+ERR_TIMEOUT = 7
+
+# Every symbol include/polarflash_b200.h declares.
+EXPORTS = (
+    "pf_version", "pf_status_string", "pf_last_cuda_error", "pf_qweight_check",
+    "pf_qlinear_workspace_size", "pf_qlinear", "pf_dequant", "pf_unpack_codes", "pf_rwht",
+    "pf_native_gemv_int4", "pf_native_gemv_int2", "pf_native_gemm_int4",
+)
+
+
+class PFQWeight(ctypes.Structure):
+    """Mirror of ``struct pf_qweight``."""
+
+    _fields_ = [
+        ("format", ctypes.c_int32),
+        ("M", ctypes.c_int32),
+        ("K", ctypes.c_int32),
+        ("had_block", ctypes.c_int32),
+        ("codes", ctypes.c_void_p),
+        ("scales", ctypes.c_void_p),
+        ("mins", ctypes.c_void_p),
+        ("had_signs", ctypes.c_void_p),
+        ("tensor_scale", ctypes.c_double),
+        ("params", ctypes.c_int32 * 20),
+    ]
+
+
+class PolarFlashError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def load():
+    """Loads the CUDA library (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build the CUDA library with "
+            "`python polar-flash_b200/build.py` (there is no CPU fallback)")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+    QW = ctypes.POINTER(PFQWeight)
+    L.pf_version.restype = ctypes.c_char_p
+    L.pf_version.argtypes = []
+    L.pf_status_string.restype = ctypes.c_char_p
+    L.pf_status_string.argtypes = [I]
+    L.pf_last_cuda_error.restype = I
+    L.pf_last_cuda_error.argtypes = []
+    L.pf_qweight_check.restype = I
+    L.pf_qweight_check.argtypes = [QW]
+    L.pf_qlinear_workspace_size.restype = I
+    L.pf_qlinear_workspace_size.argtypes = [QW, I, ctypes.POINTER(SZ)]
+    L.pf_qlinear.restype = I
+    L.pf_qlinear.argtypes = [QW, P, I, I, P, P, P, SZ, P]
+    L.pf_dequant.restype = I
+    L.pf_dequant.argtypes = [QW, P, I, P]
+    L.pf_unpack_codes.restype = I
+    L.pf_unpack_codes.argtypes = [QW, P, P]
+    L.pf_rwht.restype = I
+    L.pf_rwht.argtypes = [P, P, I, I, I, P, I, P]
+    for name in ("pf_native_gemv_int4", "pf_native_gemv_int2"):
+        fn = getattr(L, name)
+        fn.restype = I
+        fn.argtypes = [P, P, P, I, I, P, P, SZ, P]
+    L.pf_native_gemm_int4.restype = I
+    L.pf_native_gemm_int4.argtypes = [P, P, P, I, I, I, P, P, SZ, P]
+    _lib = L
+    return L
+
+
+def check(status: int, what: str = "polarflash_b200") -> None:
+    """Raises the reference's exception classes for a non-zero pf_status:
+    ValueError for argument problems (unified_quantizer.py:100-101,
+    cuda/engine.py:91-92), RuntimeError for CUDA failures
+    (native_kernels.py:396-410, 465-466)."""
+    if status == OK:
+        return
+    L = load()
+    msg = L.pf_status_string(status).decode()
+    if status in (ERR_CUDA, ERR_TIMEOUT):
+        raise PolarFlashError(f"{what}: {msg} (cuda error {L.pf_last_cuda_error()})")
+    raise ValueError(f"{what}: {msg}")
+
+
+def version() -> str:
+    return load().pf_version().decode()

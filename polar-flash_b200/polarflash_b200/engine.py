@@ -1,0 +1,155 @@
+"""PFlashCUDAEngine mirror: .pflash archive -> device-resident packed layers.
+
+Same constructor and methods as the reference (polarflash_rt/cuda/engine.py:27-248).
+Differences by design: a layer uploads its packed payload once and its forward
+is the fused kernel (no decoded fp32 weight, no host dequantize, no per-call
+weight transfer); ``forward_layer`` keeps the reference's side stream and
+synchronize so callers see the same blocking behaviour.
+"""
+import gc
+from collections import OrderedDict
+from typing import Any, Dict, Optional
+
+import torch
+
+from .linear import PolarLinearLayer
+from .pflash import PFlashReader
+
+try:
+    import psutil
+except ImportError:  # pragma: no cover
+    psutil = None
+
+
+class PFlashCUDAEngine:
+    def __init__(self, pflash_path: str, device: str = "cuda:0", lazy: bool = True,
+                 max_cached_layers: Optional[int] = None, memory_budget_mb: Optional[float] = None,
+                 keep_cached: bool = True):
+        if not torch.cuda.is_available():
+            raise RuntimeError("PFlashCUDAEngine (polarflash_b200) needs a CUDA device")
+        self.pflash_path = pflash_path
+        self.device = torch.device(device)
+        self.reader = PFlashReader(pflash_path)
+        self.lazy = lazy
+        self.max_cached_layers = max_cached_layers
+        self.memory_budget_mb = memory_budget_mb
+        self.keep_cached = keep_cached
+        self.layers: "OrderedDict[str, PolarLinearLayer]" = OrderedDict()
+        self.stream = torch.cuda.Stream(device=self.device)
+        if not lazy:
+            for name in self.reader.tensor_catalog:
+                if len(self.reader.tensor_catalog[name]["shape"]) == 2:
+                    self.get_layer(name)
+
+    def get_layer(self, layer_name: str) -> PolarLinearLayer:
+        if layer_name in self.layers:
+            self.layers.move_to_end(layer_name)
+            return self.layers[layer_name]
+        if layer_name not in self.reader.tensor_catalog:
+            raise KeyError(f"Layer '{layer_name}' not registered in .pflash catalog.")
+        if self.max_cached_layers is not None and len(self.layers) >= self.max_cached_layers:
+            self.evict_oldest_layer()
+        if self.memory_budget_mb is not None:
+            while torch.cuda.memory_allocated(self.device) / 2 ** 20 > self.memory_budget_mb and self.layers:
+                self.evict_oldest_layer()
+        meta = self.reader.tensor_catalog[layer_name]
+        shape = meta["shape"]
+        if len(shape) != 2:
+            raise ValueError(f"Tensor '{layer_name}' is not 2D linear weight (shape: {shape})")
+        view = self.reader.get_tensor_view(layer_name, verify_checksum=False)
+        with torch.cuda.device(self.device):
+            layer = PolarLinearLayer(shape[1], shape[0], meta["dtype"], meta["quant_meta"], view,
+                                     keep_cached=self.keep_cached, device=self.device)
+        self.layers[layer_name] = layer
+        return layer
+
+    def evict_oldest_layer(self) -> Optional[str]:
+        if not self.layers:
+            return None
+        name, layer = self.layers.popitem(last=False)
+        layer.clear_cache()
+        del layer
+        torch.cuda.empty_cache()
+        return name
+
+    def evict_layer(self, layer_name: str) -> None:
+        if layer_name in self.layers:
+            layer = self.layers.pop(layer_name)
+            layer.clear_cache()
+            del layer
+            torch.cuda.empty_cache()
+
+    def forward_layer(self, layer_name: str, x: torch.Tensor) -> torch.Tensor:
+        layer = self.get_layer(layer_name)
+        x_dev = x.to(self.device)
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.stream):
+            out = layer(x_dev)
+        self.stream.synchronize()
+        if not self.keep_cached:
+            layer.clear_cache()
+        return out
+
+    def get_resident_memory_stats(self) -> Dict[str, Any]:
+        rss = 0.0
+        if psutil is not None:
+            try:
+                rss = psutil.Process().memory_info().rss / 2 ** 20
+            except Exception:  # noqa: BLE001
+                pass
+        return {
+            "device": str(self.device), "resident_host_ram_mb": round(rss, 2),
+            "cuda_vram_allocated_mb": round(torch.cuda.memory_allocated(self.device) / 2 ** 20, 2),
+            "cuda_vram_peak_mb": round(torch.cuda.max_memory_allocated(self.device) / 2 ** 20, 2),
+            "num_active_cached_layers": len(self.layers),
+            "total_catalog_layers": len(self.reader.tensor_catalog),
+            "cached_layer_names": list(self.layers.keys()),
+        }
+
+    def reclaim_memory(self) -> None:
+        for layer in self.layers.values():
+            layer.clear_cache()
+        self.layers.clear()
+        gc.collect()
+        torch.cuda.empty_cache()
+
+    def benchmark_gpu_throughput(self, batch_size: int = 1, seq_len: int = 256, iterations: int = 20) -> Dict[str, Any]:
+        names = [n for n, m in self.reader.tensor_catalog.items() if len(m["shape"]) == 2]
+        if not names:
+            return {"error": "No linear layers found."}
+        layer = self.get_layer(names[0])
+        x = torch.randn(batch_size, seq_len, layer.in_features, device=self.device)
+        for _ in range(5):
+            layer(x)
+        torch.cuda.synchronize(self.device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(iterations):
+            layer(x)
+        end.record()
+        end.synchronize()
+        lat = start.elapsed_time(end) / 1e3 / iterations
+        flops = 2 * batch_size * seq_len * layer.in_features * layer.out_features
+        packed = layer.qweight.nbytes() if layer.is_packed else len(layer._raw_bytes)
+        return {
+            "device": str(self.device),
+            "execution_architecture": "fused packed-weight GEMV/GEMM (polarflash_b200, sm_100a)"
+            if layer.is_packed else "dense cached weight + torch.matmul",
+            "is_fused_lowbit_kernel": layer.is_packed, "weights_packed_in_storage": True,
+            "layer_evaluated": names[0], "packed_storage_bytes": packed,
+            "unpacked_working_bytes": 0 if layer.is_packed else layer.in_features * layer.out_features * 4,
+            "average_latency_ms": lat * 1e3, "tokens_per_second": batch_size * seq_len / max(lat, 1e-9),
+            "achieved_tflops": flops / max(lat, 1e-9) / 1e12,
+            "vram_allocated_mb": torch.cuda.memory_allocated(self.device) / 2 ** 20,
+            "vram_peak_mb": torch.cuda.max_memory_allocated(self.device) / 2 ** 20,
+        }
+
+    def close(self) -> None:
+        self.reclaim_memory()
+        self.reader.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
