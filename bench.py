@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""Fused dequant-GEMV throughput on the Llama-3-8B linear set (INT3 and INT2,
+group-128 asymmetric, block-128 RWHT), batch-1 decode.
+
+One step = one pass over the 7-linear set (q/o 4096x4096, k/v 1024x4096,
+gate/up 14336x4096, down 4096x14336) at INT3 and again at INT2: 14 fused
+GEMVs over 156.7 MB of packed weights.  32 resident copies of the packed
+sets (one per layer of the 8B model, 5.0 GB) are cycled so every step reads
+weights untouched for the previous 31 steps (inputs >> the 126 MB L2).  The
+timed region replays CUDA graphs of the steps; inputs are resident in HBM.
+
+Metric: effective packed-weight GB/s (algorithmic bytes: packed codes +
+fp16 scales/mins + x + y).  At N GPUs (torchrun) each rank holds a column
+shard of an N-times-wider set (weak scaling: per-rank work is fixed) and the
+step ends with one NCCL all-gather of the step's outputs.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "polar-flash_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+LINEARS = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+           ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
+FORMATS = ("int3_g128", "int2_g128")
+# linears sharing one prepared input (q/k/v and gate/up read the same x in a layer)
+SHARED = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]
+METRIC = "fused dequant-GEMV packed-weight HBM GB/s (Llama-3-8B linear set, INT3+INT2 g128, batch 1)"
+WORKLOAD = "llama3-8b linear set (q,k,v,o,gate,up,down) INT3 g128 + INT2 g128, RWHT-128, fp16 x, batch 1"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--copies", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def synth_weight(M, K, seed, device):
+    """W ~ N(0, 0.02^2) with 0.1% of entries at +-20 sigma (seeded positions)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    W = torch.randn(M, K, generator=g, device=device) * 0.02
+    n = max(1, int(0.001 * M * K))
+    pos = torch.randint(0, M * K, (n,), generator=g, device=device)
+    sg = torch.randint(0, 2, (n,), generator=g, device=device).float() * 2 - 1
+    W.view(-1)[pos] = sg * 0.4
+    return W
+
+
+def alg_bytes(qw, N):
+    """Algorithmic bytes of one fused GEMV: packed payload + scales/mins + x
+    (fp16) + y (fp32)."""
+    return qw.nbytes() + N * qw.K * 2 + N * qw.M * 4
+
+
+class Clocks:
+    """nvidia-smi sampler (SM clock, max clock, throttle reasons) during a window."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_leg(fmt_sets, samples, threads=None):
+    """The reference's CPU path (decode -> inverse block RWHT -> fp32 matvec,
+    polarflash_rt/cpu/engine.py:58-96 via unified_quantizer.py:242-324) as the
+    oracle's C port, all host threads.  Returns (GB/s, seconds, cores, desc)."""
+    import oracle
+
+    if threads:
+        oracle.set_num_threads(threads)
+    cores = oracle.num_threads()
+    t_total, b_total = 0.0, 0
+    for (fmt, name, payload, M, K, x) in samples:
+        t0 = time.perf_counter()
+        W = oracle.dequantize(fmt, payload, M, K, {"hadamard_rotation": True, "hadamard_block_size": 128})
+        oracle.matvec_f32(W, x)
+        t_total += time.perf_counter() - t0
+        b_total += payload["words"].nbytes + payload["s"].nbytes + payload["m"].nbytes + x.size * 2 + M * 4
+    return b_total / t_total / 1e9, t_total, cores
+
+
+def host_payload(qw):
+    return {"words": qw.codes.cpu().numpy().view(np.uint32).reshape(qw.M, -1),
+            "s": qw.scales.cpu().numpy(), "m": qw.mins.cpu().numpy()}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference CPU path timed on the host cores; each
+    step is one linear of the set (cycled), a bounded sample."""
+    if rank != 0:
+        return
+    import oracle
+    from polarflash_b200.quantizer import rwht_cpu
+    from polarflash_b200 import encoders
+
+    samples = []
+    for fmt in FORMATS:
+        bits = int(fmt[3])
+        for i, (name, M, K) in enumerate(LINEARS):
+            W = synth_weight(M, K, 1000 + i, "cpu")
+            Wr = rwht_cpu(W, 128)
+            q, s, m = encoders.quant_g128_asym(Wr, bits)
+            words = encoders.pack_g128(q, bits).numpy().view(np.uint32)
+            x = torch.randn(args.batch, K, generator=torch.Generator().manual_seed(7)).half().float().numpy()
+            samples.append((fmt, name, {"words": words, "s": s.numpy(), "m": m.numpy()}, M, K, x))
+    cores = oracle.num_threads()
+    for w in range(args.warmup):
+        cpu_reference_leg(None, [samples[w % len(samples)]])
+    t, b = 0.0, 0
+    for k in range(args.steps):
+        gbs, tt, _ = cpu_reference_leg(None, [samples[k % len(samples)]])
+        t += tt
+        b += gbs * tt * 1e9
+    value = b / t / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": args.batch, "step": "one linear of the set, cycled"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} linears of the set (cycled), decode + inverse RWHT + fp32 matvec"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    from polarflash_b200 import encoders
+    from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
+    from polarflash_b200.qweight import QWeight, qlinear_multi, workspace
+
+    N = args.batch
+    # --- encode one set per format (this rank's column shard of the N-times-wider
+    # set), then replicate the packed buffers into `copies` resident copies
+    base = {}
+    for fmt in FORMATS:
+        bits = int(fmt[3])
+        for i, (name, M, K) in enumerate(LINEARS):
+            W = synth_weight(M, K, 1000 + 97 * rank + i, dev)
+            Wr = BlockHadamardTransform(K, 128, device=dev).forward(W)
+            q, s, m = encoders.quant_g128_asym(Wr, bits)
+            words = encoders.pack_g128(q, bits)
+            fmt_id = {3: 2, 2: 3}[bits]
+            base[(fmt, name)] = QWeight(fmt_id, M, K, words.view(torch.uint8).flatten(), s, m,
+                                        effective_block(128, K), column_signs(K, 128, dev))
+            del W, Wr, q
+    copies = []
+    for c in range(args.copies):
+        cp = {}
+        for key, qw in base.items():
+            if c == 0:
+                cp[key] = qw
+            else:
+                cp[key] = QWeight(qw.format, qw.M, qw.K, qw.codes.clone(), qw.scales.clone(), qw.mins.clone(),
+                                  qw.had_block, qw.had_signs)
+        copies.append(cp)
+    torch.cuda.synchronize()
+
+    g = torch.Generator().manual_seed(7)
+    xs = {K: torch.randn(N, K, generator=g).half().to(dev) for K in (4096, 14336)}
+    # every linear's y [N, M] is a contiguous block of one flat buffer, which is
+    # also the all-gather buffer at N GPUs and the D2H source of the e2e leg
+    y_total = sum(M for _, M, _ in LINEARS) * len(FORMATS)
+    y_all = torch.empty(N * y_total, dtype=torch.float32, device=dev)
+    outs = {}
+    off = 0
+    for fmt in FORMATS:
+        for name, M, _ in LINEARS:
+            outs[(fmt, name)] = y_all[off:off + N * M].view(N, M)
+            off += N * M
+    ws_need = max(qw.workspace_bytes(N) for qw in base.values())
+    ws = workspace(dev, ws_need)  # zero-filled once; every run leaves its counters zero
+    step_bytes = sum(alg_bytes(qw, N) for qw in base.values())
+    packed_bytes = sum(qw.nbytes() for qw in base.values())
+    launches_per_step = len(FORMATS) * (len(SHARED) + len(LINEARS))
+
+
+    def step(cp, run_only=False):
+        for fmt in FORMATS:
+            for grp in SHARED:
+                qws = [cp[(fmt, n)] for n in grp]
+                K = qws[0].K
+                if run_only:
+                    from polarflash_b200 import _lib
+                    import ctypes
+                    L = _lib.load()
+                    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+                    for n, q in zip(grp, qws):
+                        o = outs[(fmt, n)]
+                        _lib.check(L.pf_qlinear_run(ctypes.byref(q.descriptor()), N, None,
+                                                    ctypes.c_void_p(o.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                                    ws.numel(), sp))
+                else:
+                    qlinear_multi(qws, xs[K], workspace=ws, outs=[outs[(fmt, n)] for n in grp])
+
+    # warm-up (also compiles lazily-loaded modules)
+    for _ in range(3):
+        step(copies[0])
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(device=dev)
+    graphs, graphs_run = [], []
+    with torch.cuda.stream(stream):
+        for cp in copies:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                step(cp)
+            graphs.append(gr)
+        # run-only graphs (x' already prepared by the last replay): the GEMV kernel alone
+        for cp in copies:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                step(cp, run_only=True)
+            graphs_run.append(gr)
+    torch.cuda.synchronize()
+
+    def replay(k, gl):
+        gl[k % len(gl)].replay()
+        if world > 1:
+            dist.all_gather_into_tensor(gather_buf, y_all)
+
+    if world > 1:
+        gather_buf = torch.empty(world * y_all.numel(), dtype=torch.float32, device=dev)
+
+    with torch.cuda.stream(stream):
+        for k in range(args.warmup):
+            replay(k, graphs)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        clocks = Clocks(vis[local].strip() if local < len(vis) else str(local))
+        clocks.start()
+        t_wall0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for k in range(args.steps):
+            replay(k, graphs)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        # keep sampling clocks for at least ~1.5 s of the same replays when the
+        # timed region is shorter than the sampling interval allows
+        extra = 0
+        while time.perf_counter() - t_wall0 < 1.5 and extra < 200000:
+            for k in range(200):
+                replay(k, graphs)
+            extra += 200
+            torch.cuda.synchronize()
+        clk = clocks.stop()
+        if extra:
+            clk["window"] = "timed region + same-graph replays to 1.5 s"
+
+        # dominant kernel: the GEMV runs alone (x' prepared), CUDA events
+        steps_run = max(args.steps, 200)
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for k in range(10):
+            graphs_run[k % len(graphs_run)].replay()
+        r0.record(stream)
+        for k in range(steps_run):
+            graphs_run[k % len(graphs_run)].replay()
+        r1.record(stream)
+        torch.cuda.synchronize()
+        ms_run = r0.elapsed_time(r1) / steps_run
+
+        # e2e through the public API with host buffers: pinned x in, y out,
+        # copies inside the timed region (graph of H2D -> GEMVs -> D2H)
+        x_host = {K: torch.empty(N, K, dtype=torch.float16, pin_memory=True) for K in (4096, 14336)}
+        for K in x_host:
+            x_host[K].copy_(xs[K].cpu())
+        y_host = torch.empty(N * y_total, dtype=torch.float32, pin_memory=True)
+        e2e_graphs = []
+        for cp in copies[:4]:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for K in xs:
+                    xs[K].copy_(x_host[K], non_blocking=True)
+                step(cp)
+                y_host.copy_(y_all, non_blocking=True)
+            e2e_graphs.append(gr)
+        for k in range(5):
+            e2e_graphs[k % 4].replay()
+        torch.cuda.synchronize()
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(50, min(args.steps, 2000))
+        q0.record(stream)
+        for k in range(n_e2e):
+            e2e_graphs[k % 4].replay()
+        q1.record(stream)
+        torch.cuda.synchronize()
+        ms_e2e = q0.elapsed_time(q1) / n_e2e
+        h2d = sum(t.numel() * t.element_size() for t in x_host.values())
+        d2h = y_host.numel() * 4
+
+    # max over ranks
+    t = torch.tensor([ms, ms_run, ms_e2e], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_run, ms_e2e = (float(v) for v in t.tolist())
+    ms_step = ms / args.steps
+    value = world * step_bytes / (ms_step / 1e3) / 1e9
+
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:  # noqa: BLE001
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = step_bytes / (ms_run / 1e3) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemv_int_traffic.json")) as f:
+            traffic = json.load(f).get("bytes_per_step")
+    except Exception:  # noqa: BLE001
+        pass
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        samples = []
+        for fmt in FORMATS:
+            for name, M, K in LINEARS:
+                qw = base[(fmt, name)]
+                samples.append((fmt, name, host_payload(qw), M, K, xs[K].float().cpu().numpy()))
+        gbs, secs, cores = cpu_reference_leg(None, samples)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"one pass over the 14-linear set (decode + inverse RWHT + fp32 matvec), {secs:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch": N, "copies": args.copies,
+                       "packed_bytes_per_step": packed_bytes, "alg_bytes_per_step": step_bytes,
+                       "l2": f"{args.copies} resident copies ({args.copies * packed_bytes / 1e9:.2f} GB) cycled; "
+                             "inputs > 126 MB L2", "parallelism": f"column-shard x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                         "kernel": "gemv_int_kernel (14 GEMV launches per step, CUDA-event timed)",
+                         "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * step_bytes / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "how": "CUDA graph of public-API calls: pinned x H2D, 8 prepare + 14 GEMV launches, y D2H"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    for gr in graphs + graphs_run + e2e_graphs:
+        del gr
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

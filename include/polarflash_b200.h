@@ -115,7 +115,11 @@ PF_API int pf_last_cuda_error(void);
 /* Checks a descriptor (shapes, pointers, alignment) without launching. */
 PF_API int pf_qweight_check(const pf_qweight* w);
 
-/* Bytes of device scratch pf_qlinear needs for N input rows. */
+/* Bytes of device workspace pf_qlinear needs for N input rows.  The
+ * workspace holds the prepared activations x', split-K partial sums and a
+ * block of split-K arrival counters at its start.  Zero-fill a workspace once
+ * after allocating it; every call leaves the counters zero again.  Calls
+ * that share one workspace must be ordered (same stream). */
 PF_API int pf_qlinear_workspace_size(const pf_qweight* w, int N, size_t* bytes);
 
 /* y[N][M] (fp32) = x[N][K] * W^T (+ bias[M]).  Replaces PolarLinearLayer.forward
@@ -126,6 +130,15 @@ PF_API int pf_qlinear_workspace_size(const pf_qweight* w, int N, size_t* bytes);
  * y: device fp32 [N][M]; workspace: device, 256-byte aligned. */
 PF_API int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias,
                float* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The two halves of pf_qlinear for N <= 16: prepare writes x' (the forward
+ * block RWHT of x, in the layout the GEMV reads) into the workspace; run
+ * computes y from it.  One prepare serves several runs over weights with the
+ * same format, K and rotation (q/k/v or gate/up sharing one input). */
+PF_API int pf_qlinear_prepare(const pf_qweight* w, const void* x, int x_dtype, int N, void* workspace,
+                              size_t workspace_bytes, void* stream);
+PF_API int pf_qlinear_run(const pf_qweight* w, int N, const float* bias, float* y, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* W_hat[M][K] (fp32) = decoded weight, followed by the inverse block RWHT
  * when `inverse_rwht` is non-zero and the weight is rotated.  Replaces

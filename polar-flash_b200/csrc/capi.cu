@@ -134,8 +134,36 @@ int check(const pf_qweight* w) {
 int tokens_per_pass(int N) { return N < kMaxGemvTokens ? N : kMaxGemvTokens; }
 int nt_of(int np) { return np <= 4 ? 1 : np <= 8 ? 2 : 4; }
 
-size_t workspace_bytes(const pf_qweight* w, int N) {
-  int np = tokens_per_pass(N < 1 ? 1 : N);
+// Workspace layout (every part 256-byte aligned):
+//   [split-K counters: kCounterSlots u32, zero-filled once, left zero by every run]
+//   [x' region: fragments + group sums (INT) or plain fp32 x' (E8 / polar)]
+//   [split-K partials: n_chunks * N * M fp32 (INT, when n_chunks > 1)]
+// The x' region sits at a fixed offset for a given (format family, K, N), so
+// one prepare can serve several runs over weights of different M.
+constexpr size_t kCounterSlots = 4096;
+constexpr size_t kCounterBytes = kCounterSlots * sizeof(unsigned);
+
+struct IntPlan {
+  int NT, rpi, n_row_items, CG, n_chunks, Gp;
+};
+
+IntPlan plan_int(const pf_qweight* w, int np) {
+  IntPlan p;
+  p.NT = nt_of(np);
+  p.rpi = gemv_int_rows_per_item(p.NT);
+  p.Gp = (w->K + 127) / 128;
+  p.n_row_items = (w->M + p.rpi - 1) / p.rpi;
+  const long long target = 148LL * 16;  // warps resident across the 148 SMs
+  long long cg = ((long long)p.Gp * p.n_row_items + target - 1) / target;
+  if (cg < 1) cg = 1;
+  if (cg > p.Gp) cg = p.Gp;
+  if ((size_t)p.n_row_items > kCounterSlots) cg = p.Gp;  // enough rows: no split
+  p.CG = (int)cg;
+  p.n_chunks = (p.Gp + p.CG - 1) / p.CG;
+  return p;
+}
+
+size_t xprep_bytes(const pf_qweight* w, int np) {
   size_t Gp = (size_t)(w->K + 127) / 128;
   if (is_int_format(w->format)) {
     int NT = nt_of(np);
@@ -144,37 +172,65 @@ size_t workspace_bytes(const pf_qweight* w, int N) {
   return round_up((size_t)np * Gp * 128 * sizeof(float), 256);
 }
 
+size_t pass_bytes(const pf_qweight* w, int np) {
+  size_t b = kCounterBytes + xprep_bytes(w, np);
+  if (is_int_format(w->format)) {
+    IntPlan p = plan_int(w, np);
+    if (p.n_chunks > 1) b += round_up((size_t)p.n_chunks * np * w->M * sizeof(float), 256);
+  }
+  return b;
+}
+
+size_t workspace_bytes(const pf_qweight* w, int N) {
+  if (N < 1) N = 1;
+  size_t b = pass_bytes(w, tokens_per_pass(N));
+  int tail = N % kMaxGemvTokens;
+  if (N > kMaxGemvTokens && tail) {
+    size_t t = pass_bytes(w, tail);
+    if (t > b) b = t;
+  }
+  return b;
+}
+
 size_t dtype_size(int dt) { return dt == PF_DTYPE_F32 ? 4 : 2; }
 
-int qlinear_pass(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, int N,
-                 const float* bias, float* y, void* ws, cudaStream_t s) {
-  const int K = w->K, M = w->M;
-  const int Gp = (K + 127) / 128;
+int do_prepare(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, int N, void* ws,
+               cudaStream_t s) {
+  const int Gp = (w->K + 127) / 128;
+  char* base = static_cast<char*>(ws) + kCounterBytes;
   PrepArgs pa;
   memset(&pa, 0, sizeof(pa));
   pa.x = x;
   pa.x_dtype = x_dtype;
   pa.N = N;
-  pa.K = K;
+  pa.K = w->K;
   pa.Kp = Gp * 128;
   pa.plan = plan;
   pa.signs = w->had_signs;
   pa.fmt = w->format;
-  pa.y = y;
-  pa.bias = bias;
-  pa.M = M;
+  pa.M = w->M;
+  pa.init_y = 0;
   if (is_int_format(w->format)) {
     const int NT = nt_of(N);
-    uint2* xfrag = static_cast<uint2*>(ws);
-    float* sx = reinterpret_cast<float*>(static_cast<char*>(ws) + round_up((size_t)NT * Gp * 2048, 256));
     pa.mode = 0;
     pa.NT = NT;
     pa.slots = 4 * NT;
-    pa.xfrag = xfrag;
-    pa.sx = sx;
-    pa.init_y = 1;
-    int st = cuda_status(launch_prep(pa, s));
-    if (st) return st;
+    pa.xfrag = reinterpret_cast<uint2*>(base);
+    pa.sx = reinterpret_cast<float*>(base + round_up((size_t)NT * Gp * 2048, 256));
+  } else {
+    pa.mode = 1;
+    pa.slots = N;
+    pa.xplain = reinterpret_cast<float*>(base);
+  }
+  return cuda_status(launch_prep(pa, s));
+}
+
+int do_run(const pf_qweight* w, int N, const float* bias, float* y, void* ws, cudaStream_t s) {
+  const int K = w->K, M = w->M;
+  const int Gp = (K + 127) / 128;
+  char* base = static_cast<char*>(ws) + kCounterBytes;
+  if (is_int_format(w->format)) {
+    IntPlan p = plan_int(w, N);
     GemvIntArgs ga;
     memset(&ga, 0, sizeof(ga));
     ga.codes = w->codes;
@@ -187,29 +243,20 @@ int qlinear_pass(const pf_qweight* w, const HadPlan& plan, const void* x, int x_
     ga.G = Gp;
     ga.Gp = Gp;
     ga.row_words = row_words_of(w->format, K);
-    ga.NT = NT;
-    const int rpi = gemv_int_rows_per_item(NT);
-    ga.n_row_items = (M + rpi - 1) / rpi;
-    const long long target = 148LL * 16;
-    long long cg = ((long long)Gp * ga.n_row_items + target - 1) / target;
-    if (cg < 1) cg = 1;
-    if (cg > Gp) cg = Gp;
-    ga.CG = (int)cg;
-    ga.n_items = ga.n_row_items * ((Gp + ga.CG - 1) / ga.CG);
-    ga.xfrag = xfrag;
-    ga.sx = sx;
+    ga.NT = p.NT;
+    ga.CG = p.CG;
+    ga.n_row_items = p.n_row_items;
+    ga.n_chunks = p.n_chunks;
+    ga.n_items = p.n_row_items * p.n_chunks;
+    ga.xfrag = reinterpret_cast<const uint2*>(base);
+    ga.sx = reinterpret_cast<const float*>(base + round_up((size_t)p.NT * Gp * 2048, 256));
+    ga.bias = bias;
     ga.y = y;
+    ga.partials = reinterpret_cast<float*>(base + xprep_bytes(w, N));
+    ga.counters = static_cast<unsigned*>(ws);
     int smode = is_group_int_format(w->format) ? kScaleGroup : (w->scales ? kScaleRow : kScaleTensor);
     return cuda_status(launch_gemv_int(w->format, ga, smode, s));
   }
-  // CUDA-core formats: plain x'
-  float* xplain = static_cast<float*>(ws);
-  pa.mode = 1;
-  pa.slots = N;
-  pa.xplain = xplain;
-  pa.init_y = 0;
-  int st = cuda_status(launch_prep(pa, s));
-  if (st) return st;
   GemvCCArgs ca;
   memset(&ca, 0, sizeof(ca));
   ca.fmt = w->format;
@@ -219,7 +266,7 @@ int qlinear_pass(const pf_qweight* w, const HadPlan& plan, const void* x, int x_
   ca.K = K;
   ca.N = N;
   ca.Kp = Gp * 128;
-  ca.xplain = xplain;
+  ca.xplain = reinterpret_cast<const float*>(base);
   ca.bias = bias;
   ca.y = y;
   if (w->format != PF_FMT_E8_RVQ2_G128) {
@@ -267,15 +314,46 @@ int pf_qlinear_workspace_size(const pf_qweight* w, int N, size_t* bytes) {
   return PF_OK;
 }
 
-int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias, float* y,
-               void* workspace, size_t ws_bytes, void* stream) {
+static int common_args(const pf_qweight* w, int N, void* ws, size_t ws_bytes) {
   int st = check(w);
   if (st) return st;
-  if (N < 0 || x_dtype < PF_DTYPE_F32 || x_dtype > PF_DTYPE_BF16) return PF_ERR_INVALID_ARGUMENT;
+  if (N < 0) return PF_ERR_INVALID_ARGUMENT;
   if (N == 0) return PF_OK;
+  if (!ws || ws_bytes < workspace_bytes(w, N)) return PF_ERR_WORKSPACE;
+  if (!aligned(ws, 256)) return PF_ERR_ALIGNMENT;
+  return PF_OK;
+}
+
+int pf_qlinear_prepare(const pf_qweight* w, const void* x, int x_dtype, int N, void* workspace,
+                       size_t ws_bytes, void* stream) {
+  int st = common_args(w, N, workspace, ws_bytes);
+  if (st || N == 0) return st;
+  if (N > kMaxGemvTokens) return PF_ERR_SHAPE;
+  if (x_dtype < PF_DTYPE_F32 || x_dtype > PF_DTYPE_BF16) return PF_ERR_INVALID_ARGUMENT;
+  if (!x) return PF_ERR_INVALID_ARGUMENT;
+  if (!aligned(x, dtype_size(x_dtype))) return PF_ERR_ALIGNMENT;
+  HadPlan plan;
+  st = make_plan(w->K, w->had_block, &plan);
+  if (st) return st;
+  return do_prepare(w, plan, x, x_dtype, N, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int pf_qlinear_run(const pf_qweight* w, int N, const float* bias, float* y, void* workspace, size_t ws_bytes,
+                   void* stream) {
+  int st = common_args(w, N, workspace, ws_bytes);
+  if (st || N == 0) return st;
+  if (N > kMaxGemvTokens) return PF_ERR_SHAPE;
+  if (!y) return PF_ERR_INVALID_ARGUMENT;
+  if (!aligned(y, 4) || (bias && !aligned(bias, 4))) return PF_ERR_ALIGNMENT;
+  return do_run(w, N, bias, y, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias, float* y,
+               void* workspace, size_t ws_bytes, void* stream) {
+  int st = common_args(w, N, workspace, ws_bytes);
+  if (st || N == 0) return st;
+  if (x_dtype < PF_DTYPE_F32 || x_dtype > PF_DTYPE_BF16) return PF_ERR_INVALID_ARGUMENT;
   if (!x || !y) return PF_ERR_INVALID_ARGUMENT;
-  if (!workspace || ws_bytes < workspace_bytes(w, N)) return PF_ERR_WORKSPACE;
-  if (!aligned(workspace, 256)) return PF_ERR_ALIGNMENT;
   if (!aligned(x, dtype_size(x_dtype)) || !aligned(y, 4) || (bias && !aligned(bias, 4))) return PF_ERR_ALIGNMENT;
   HadPlan plan;
   st = make_plan(w->K, w->had_block, &plan);
@@ -284,8 +362,9 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
   const size_t xs = dtype_size(x_dtype);
   for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {
     int np = N - t0 < kMaxGemvTokens ? N - t0 : kMaxGemvTokens;
-    st = qlinear_pass(w, plan, static_cast<const char*>(x) + (size_t)t0 * w->K * xs, x_dtype, np, bias,
-                      y + (size_t)t0 * w->M, workspace, s);
+    st = do_prepare(w, plan, static_cast<const char*>(x) + (size_t)t0 * w->K * xs, x_dtype, np, workspace, s);
+    if (st) return st;
+    st = do_run(w, np, bias, y + (size_t)t0 * w->M, workspace, s);
     if (st) return st;
   }
   return PF_OK;

@@ -18,9 +18,13 @@ struct GemvIntArgs {
   int CG;         // groups per work item
   int n_row_items;
   int n_items;
+  int n_chunks;
   const uint2* xfrag;
   const float* sx;
+  const float* bias;
   float* y;
+  float* partials;     // [n_chunks][N][M] when n_chunks > 1
+  unsigned* counters;  // [n_row_items], zero on entry, left zero on exit
 };
 
 int gemv_int_rows_per_item(int NT);

@@ -308,6 +308,25 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_int_kernel(GemvIntArgs a) {
       }
   }
 
+  // Split-K combine.  One chunk: write y directly.  Several chunks: every
+  // item stores its partial, the last item of a row block (found with a
+  // counter) sums the partials in chunk order -- deterministic, no atomics
+  // on y -- adds the bias, writes y and re-arms the counter.
+  if (a.n_chunks == 1) {
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      const int t = 4 * i + c;
+      if (t < a.N) {
+#pragma unroll
+        for (int tr = 0; tr < TR; ++tr)
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr)
+            if (rp[tr][rr])
+              a.y[(size_t)t * a.M + rows[tr][rr]] = yacc[tr][i][rr] + (a.bias ? a.bias[rows[tr][rr]] : 0.f);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < NT; ++i) {
     const int t = 4 * i + c;
@@ -316,9 +335,34 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_int_kernel(GemvIntArgs a) {
       for (int tr = 0; tr < TR; ++tr)
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr)
-          if (rp[tr][rr]) atomicAdd(a.y + (size_t)t * a.M + rows[tr][rr], yacc[tr][i][rr]);
+          if (rp[tr][rr]) a.partials[((size_t)chunk * a.N + t) * a.M + rows[tr][rr]] = yacc[tr][i][rr];
     }
   }
+  __threadfence();
+  __syncwarp();
+  unsigned prev = 0;
+  if (lane == 0) prev = atomicAdd(a.counters + ritem, 1u);
+  prev = __shfl_sync(0xffffffffu, prev, 0);
+  if (prev != (unsigned)(a.n_chunks - 1)) return;
+  __threadfence();
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const int t = 4 * i + c;
+    if (t < a.N) {
+#pragma unroll
+      for (int tr = 0; tr < TR; ++tr)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          if (!rp[tr][rr]) continue;
+          const int row = rows[tr][rr];
+          float v = 0.f;
+          for (int ch = 0; ch < a.n_chunks; ++ch)
+            v += (ch == chunk) ? yacc[tr][i][rr] : __ldcg(a.partials + ((size_t)ch * a.N + t) * a.M + row);
+          a.y[(size_t)t * a.M + row] = v + (a.bias ? a.bias[row] : 0.f);
+        }
+    }
+  }
+  if (lane == 0) a.counters[ritem] = 0u;
 }
 
 template <int FMT, int NT, int TR>

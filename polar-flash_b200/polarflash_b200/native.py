@@ -13,6 +13,7 @@ from typing import Any, Dict, Optional
 import torch
 
 from . import _lib
+from .qweight import workspace as _workspace
 
 
 class NativeLowBitCUDAEngine:
@@ -54,7 +55,7 @@ class NativeLowBitCUDAEngine:
         qw.codes, qw.scales = packed.data_ptr(), scales.data_ptr()
         need = ctypes.c_size_t(0)
         _lib.check(_lib.load().pf_qlinear_workspace_size(ctypes.byref(qw), N or 1, ctypes.byref(need)), fn)
-        ws = torch.empty(int(need.value), dtype=torch.uint8, device=x.device)
+        ws = _workspace(x.device, int(need.value))
         stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
         P = ctypes.c_void_p
         L = _lib.load()

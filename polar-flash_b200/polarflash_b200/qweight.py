@@ -191,37 +191,94 @@ def extension_payload_bytes(qw: QWeight) -> bytes:
     return bytes(out)
 
 
-def qlinear(qw: QWeight, x: torch.Tensor, bias: Optional[torch.Tensor] = None,
-            workspace: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y = x @ W_hat.T (+ bias), fp32, W_hat never materialised.  x: [..., K]
-    CUDA tensor (fp32/fp16/bf16).  Launches on torch's current stream."""
+_ws_cache = {}
+
+
+def workspace(device, nbytes: int, stream=None) -> torch.Tensor:
+    """A zero-initialised workspace of at least `nbytes` for `device`, cached
+    per (device, stream): calls on one stream run in order, which is what
+    sharing a workspace needs."""
+    device = torch.device(device)
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    key = (device.index, s.cuda_stream)
+    ws = _ws_cache.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws_cache[key] = ws
+    return ws
+
+
+def _x2(qw: QWeight, x: torch.Tensor):
     if x.device.type != "cuda":
         raise ValueError("polarflash_b200.qlinear needs CUDA input tensors (no CPU path)")
     if x.shape[-1] != qw.K:
         raise ValueError(f"input feature dim {x.shape[-1]} != in_features {qw.K}")
     if x.dtype not in _X_DTYPES:
         x = x.float()
-    lead = x.shape[:-1]
     x2 = x.reshape(-1, qw.K)
     if not x2.is_contiguous():
         x2 = x2.contiguous()
+    return x2
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def qlinear(qw: QWeight, x: torch.Tensor, bias: Optional[torch.Tensor] = None,
+            workspace: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ W_hat.T (+ bias), fp32, W_hat never materialised.  x: [..., K]
+    CUDA tensor (fp32/fp16/bf16).  Launches on torch's current stream.  A
+    caller-provided `workspace` must have been zero-filled once."""
+    lead = x.shape[:-1]
+    x2 = _x2(qw, x)
     N = x2.shape[0]
     y = out if out is not None else torch.empty(N, qw.M, dtype=torch.float32, device=x.device)
     if N == 0:
         return y.reshape(*lead, qw.M)
     need = qw.workspace_bytes(N)
-    if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
-    b = None
-    if bias is not None:
-        b = bias.to(device=x.device, dtype=torch.float32).contiguous()
+    stream = torch.cuda.current_stream(x.device)
+    ws = workspace if workspace is not None else globals()["workspace"](x.device, need, stream)
+    if ws.numel() < need:
+        raise ValueError(f"workspace of {ws.numel()} bytes < {need} needed")
+    b = bias.to(device=x.device, dtype=torch.float32).contiguous() if bias is not None else None
     st = _lib.load().pf_qlinear(
-        ctypes.byref(qw.descriptor()), ctypes.c_void_p(x2.data_ptr()), _X_DTYPES[x2.dtype], N,
-        ctypes.c_void_p(b.data_ptr()) if b is not None else None, ctypes.c_void_p(y.data_ptr()),
-        ctypes.c_void_p(workspace.data_ptr()), need,
-        ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
+        ctypes.byref(qw.descriptor()), _ptr(x2), _X_DTYPES[x2.dtype], N, _ptr(b), _ptr(y), _ptr(ws),
+        ws.numel(), ctypes.c_void_p(stream.cuda_stream))
     _lib.check(st, "pf_qlinear")
     return y.reshape(*lead, qw.M)
+
+
+def qlinear_multi(qws, x: torch.Tensor, biases=None, workspace: Optional[torch.Tensor] = None, outs=None):
+    """[x @ W_i^T (+ b_i)] for weights sharing format, K and rotation (q/k/v,
+    gate/up): x is prepared once (pf_qlinear_prepare), then one pf_qlinear_run
+    per weight.  N <= 16 rows per call."""
+    qw0 = qws[0]
+    for q in qws[1:]:
+        if (q.format, q.K, q.had_block) != (qw0.format, qw0.K, qw0.had_block):
+            raise ValueError("qlinear_multi needs weights with the same format, K and rotation")
+    lead = x.shape[:-1]
+    x2 = _x2(qw0, x)
+    N = x2.shape[0]
+    if N > 16:
+        return [qlinear(q, x, None if biases is None else biases[i]) for i, q in enumerate(qws)]
+    need = max(q.workspace_bytes(N) for q in qws)
+    stream = torch.cuda.current_stream(x.device)
+    ws = workspace if workspace is not None else globals()["workspace"](x.device, need, stream)
+    L = _lib.load()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    _lib.check(L.pf_qlinear_prepare(ctypes.byref(qw0.descriptor()), _ptr(x2), _X_DTYPES[x2.dtype], N, _ptr(ws),
+                                    ws.numel(), sp), "pf_qlinear_prepare")
+    ys = []
+    for i, q in enumerate(qws):
+        y = outs[i] if outs is not None else torch.empty(N, q.M, dtype=torch.float32, device=x.device)
+        b = None
+        if biases is not None and biases[i] is not None:
+            b = biases[i].to(device=x.device, dtype=torch.float32).contiguous()
+        _lib.check(L.pf_qlinear_run(ctypes.byref(q.descriptor()), N, _ptr(b), _ptr(y), _ptr(ws), ws.numel(), sp),
+                   "pf_qlinear_run")
+        ys.append(y.reshape(*lead, q.M))
+    return ys
 
 
 def dequantize(qw: QWeight, inverse_rwht: bool = True) -> torch.Tensor:

@@ -1,0 +1,38 @@
+"""One fused linear on synthetic weights, launched a few times: the small case
+used for single-kernel ncu captures of the library's kernels.
+
+    python polar-flash_b200/profile_case.py --fmt int3_g128 --M 14336 --K 4096 --N 1 --iters 3
+"""
+import argparse
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+import torch  # noqa: E402
+
+from polarflash_b200 import UnifiedQuantizer, qlinear  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--fmt", default="int3_g128")
+    ap.add_argument("--M", type=int, default=14336)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--N", type=int, default=1)
+    ap.add_argument("--iters", type=int, default=3)
+    a = ap.parse_args()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    W = torch.randn(a.M, a.K, generator=g, device=dev) * 0.02
+    qw, _ = UnifiedQuantizer(backend=a.fmt, hadamard_block_size=128).quantize_to_qweight(W)
+    del W
+    x = torch.randn(a.N, a.K, generator=g, device=dev).half()
+    for _ in range(a.iters):
+        y = qlinear(qw, x)
+    torch.cuda.synchronize()
+    print(f"{a.fmt} {a.M}x{a.K} N={a.N}: packed {qw.nbytes()} B, y[0,:4] = {y[0, :4].tolist()}")
+
+
+if __name__ == "__main__":
+    main()
