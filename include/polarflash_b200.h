@@ -140,6 +140,19 @@ PF_API int pf_qlinear_prepare(const pf_qweight* w, const void* x, int x_dtype, i
 PF_API int pf_qlinear_run(const pf_qweight* w, int N, const float* bias, float* y, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* pf_qlinear for callers that cannot allocate device memory (no counterpart
+ * in the reference, which has no GPU linear of its own to mirror here).
+ * Same inputs, outputs and semantics as pf_qlinear, but the scratch space
+ * comes from a fixed 8 MiB array inside the library's device image, reserved
+ * on every GPU that loads the library until the process exits; no device
+ * memory is allocated.  Requests whose pf_qlinear_workspace_size exceeds
+ * 8 MiB return PF_ERR_WORKSPACE.  The first call on a device looks up the
+ * array's address and zeroes its counters (synchronous), so make it before
+ * any stream capture.  All calls on a device share the array: calls that
+ * overlap on the GPU (unordered streams) race on it. */
+PF_API int pf_qlinear_noalloc(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias,
+                              float* y, void* stream);
+
 /* W_hat[M][K] (fp32) = decoded weight, followed by the inverse block RWHT
  * when `inverse_rwht` is non-zero and the weight is rotated.  Replaces
  * UnifiedQuantizer.dequantize (polarflash_quant/unified_quantizer.py:242-324). */

@@ -40,7 +40,7 @@ ERR_TIMEOUT = 7
 EXPORTS = (
     "pf_version", "pf_status_string", "pf_last_cuda_error", "pf_qweight_check",
     "pf_qlinear_workspace_size", "pf_qlinear_prepare", "pf_qlinear_run", "pf_qlinear", "pf_dequant", "pf_unpack_codes", "pf_rwht",
-    "pf_native_gemv_int4", "pf_native_gemv_int2", "pf_native_gemm_int4",
+    "pf_native_gemv_int4", "pf_native_gemv_int2", "pf_native_gemm_int4", "pf_qlinear_noalloc",
 )
 
 
