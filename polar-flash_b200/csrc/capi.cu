@@ -1,5 +1,6 @@
 // C ABI entry points: argument validation on the host, then the launch
 // sequence (x-prep, GEMV) on the caller's stream.  Nothing here allocates.
+#include <stdlib.h>
 #include <string.h>
 
 #include "gemv.cuh"
@@ -135,13 +136,35 @@ int tokens_per_pass(int N) { return N < kMaxGemvTokens ? N : kMaxGemvTokens; }
 int nt_of(int np) { return np <= 4 ? 1 : np <= 8 ? 2 : 4; }
 
 // Workspace layout (every part 256-byte aligned):
-//   [split-K counters: kCounterSlots u32, zero-filled once, left zero by every run]
+//   [split-K counters + status word: kWsCounterBytes, zero-filled once, left zero]
 //   [x' region: fragments + group sums (INT) or plain fp32 x' (E8 / polar)]
-//   [split-K partials: n_chunks * N * M fp32 (INT, when n_chunks > 1)]
+//   [split-K partials]
 // The x' region sits at a fixed offset for a given (format family, K, N), so
 // one prepare can serve several runs over weights of different M.
-constexpr size_t kCounterSlots = 4096;
-constexpr size_t kCounterBytes = kCounterSlots * sizeof(unsigned);
+constexpr size_t kCounterBytes = kWsCounterBytes;
+
+// TMA-pipelined GEMV for INT4/INT3/INT2 group-128 and the INT4/INT2 reference
+// streams when K % 512 == 0; chosen from format and K only, so a prepare and
+// every run that shares it take the same path.  PF_GEMV_PATH=ldg forces the
+// register-prefetch GEMV, PF_GEMV_MAGIC=normal the 1 + q 2^(p-10) decode.
+bool use_tma(const pf_qweight* w) {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("PF_GEMV_PATH");
+    mode = (e && strcmp(e, "ldg") == 0) ? 0 : 1;
+  }
+  if (!mode) return false;
+  return tma_eligible(w->format, 1, w->K, reinterpret_cast<const void*>(16));
+}
+
+int tma_subnormal() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PF_GEMV_MAGIC");
+    v = (e && strcmp(e, "normal") == 0) ? 0 : 1;
+  }
+  return v;
+}
 
 struct IntPlan {
   int NT, rpi, n_row_items, CG, n_chunks, Gp;
@@ -157,14 +180,21 @@ IntPlan plan_int(const pf_qweight* w, int np) {
   long long cg = ((long long)p.Gp * p.n_row_items + target - 1) / target;
   if (cg < 1) cg = 1;
   if (cg > p.Gp) cg = p.Gp;
-  if ((size_t)p.n_row_items > kCounterSlots) cg = p.Gp;  // enough rows: no split
+  if ((size_t)p.n_row_items >= kWsStatusSlot) cg = p.Gp;  // enough rows: no split
   p.CG = (int)cg;
   p.n_chunks = (p.Gp + p.CG - 1) / p.CG;
   return p;
 }
 
+size_t tma_partials_bytes(const pf_qweight* w, int np) {
+  const int spb = (w->K / 128) / tma_stage_groups(w->format);
+  const int n_units = ((w->M + 63) / 64) * spb;
+  return round_up((size_t)2 * tma_grid(w->format, nt_of(np), n_units) * 64 * np * sizeof(float), 256);
+}
+
 size_t xprep_bytes(const pf_qweight* w, int np) {
   size_t Gp = (size_t)(w->K + 127) / 128;
+  if (use_tma(w)) return round_up(Gp * tma_record_bytes(np, nt_of(np)), 256);
   if (is_int_format(w->format)) {
     int NT = nt_of(np);
     return round_up((size_t)NT * Gp * 2048, 256) + round_up(Gp * 8 * NT * sizeof(float), 256);
@@ -174,6 +204,7 @@ size_t xprep_bytes(const pf_qweight* w, int np) {
 
 size_t pass_bytes(const pf_qweight* w, int np) {
   size_t b = kCounterBytes + xprep_bytes(w, np);
+  if (use_tma(w)) return b + tma_partials_bytes(w, np);
   if (is_int_format(w->format)) {
     IntPlan p = plan_int(w, np);
     if (p.n_chunks > 1) b += round_up((size_t)p.n_chunks * np * w->M * sizeof(float), 256);
@@ -210,6 +241,22 @@ int do_prepare(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dt
   pa.fmt = w->format;
   pa.M = w->M;
   pa.init_y = 0;
+  if (use_tma(w)) {
+    Prep2Args p2;
+    memset(&p2, 0, sizeof(p2));
+    p2.x = x;
+    p2.x_dtype = x_dtype;
+    p2.N = N;
+    p2.NT = nt_of(N);
+    p2.K = w->K;
+    p2.G = Gp;
+    p2.plan = plan;
+    p2.signs = w->had_signs;
+    p2.fmt = w->format;
+    p2.subnormal = tma_subnormal();
+    p2.rec = reinterpret_cast<unsigned char*>(base);
+    return cuda_status(launch_prep2(p2, s));
+  }
   if (is_int_format(w->format)) {
     const int NT = nt_of(N);
     pa.mode = 0;
@@ -229,6 +276,32 @@ int do_run(const pf_qweight* w, int N, const float* bias, float* y, void* ws, cu
   const int K = w->K, M = w->M;
   const int Gp = (K + 127) / 128;
   char* base = static_cast<char*>(ws) + kCounterBytes;
+  if (use_tma(w)) {
+    if (!tma_eligible(w->format, M, K, w->codes)) return PF_ERR_ALIGNMENT;
+    TmaArgs ta;
+    memset(&ta, 0, sizeof(ta));
+    ta.codes = w->codes;
+    ta.scales = w->scales;
+    ta.mins = static_cast<const __half*>(w->mins);
+    ta.tensor_scale = (float)w->tensor_scale;
+    ta.M = M;
+    ta.K = K;
+    ta.N = N;
+    ta.NT = nt_of(N);
+    ta.G = Gp;
+    ta.row_words = row_words_of(w->format, K);
+    ta.n_rb = (M + 63) / 64;
+    ta.spb = Gp / tma_stage_groups(w->format);
+    ta.n_units = ta.n_rb * ta.spb;
+    ta.rec = reinterpret_cast<const unsigned char*>(base);
+    ta.rec_bytes = (int)tma_record_bytes(N, ta.NT);
+    ta.bias = bias;
+    ta.y = y;
+    ta.partials = reinterpret_cast<float*>(base + xprep_bytes(w, N));
+    ta.counters = static_cast<unsigned*>(ws);
+    int smode = is_group_int_format(w->format) ? kScaleGroup : (w->scales ? kScaleRow : kScaleTensor);
+    return cuda_status(launch_gemv_tma(w->format, ta, smode, tma_subnormal(), s));
+  }
   if (is_int_format(w->format)) {
     IntPlan p = plan_int(w, N);
     GemvIntArgs ga;

@@ -117,6 +117,48 @@ __device__ __forceinline__ void frag_cols(int fmt, int c, int i, int& lo, int& h
   }
 }
 
+// In-place decode map of the TMA GEMV (gemv_tma.cu): the thread's i-th half2
+// holds the codes of columns (lo, hi) at mantissa bit position p, extracted
+// with one AND/OR and no shift where the code already sits below bit 10.
+//   INT4 (words 4c..4c+3, word t = i/4): (0,4)@0 (1,5)@4, then >>8: (2,6)@0 (3,7)@4
+//   INT2 (words 2c, 2c+1, word t = i/8): (k, k+8)@2k for k < 5, then >>10:
+//        (5+k, 13+k)@2k for k < 3
+//   INT3 g128 (words c, c+4, c+8 merged with <<1 halves): (0,5)@0 (1,6)@3 (2,7)@6,
+//        then >>9: (3,8)@0 (4,9)@3; half2 15 = word 12 codes (2c, 2c+1)@0
+__device__ __forceinline__ void frag_cols2(int fmt, int c, int i, int& lo, int& hi, int& p) {
+  switch (fmt) {
+    case PF_FMT_INT4_G128:
+    case PF_FMT_INT4: {
+      int w = 4 * c + (i >> 2), sub = i & 3;
+      lo = 8 * w + sub;
+      hi = lo + 4;
+      p = (sub & 1) ? 4 : 0;
+      break;
+    }
+    case PF_FMT_INT2_G128:
+    case PF_FMT_INT2: {
+      int w = 2 * c + (i >> 3), sub = i & 7;
+      lo = 16 * w + sub;
+      hi = lo + 8;
+      p = sub < 5 ? 2 * sub : 2 * (sub - 5);
+      break;
+    }
+    default: {  // PF_FMT_INT3_G128
+      if (i < 15) {
+        int t = i / 5, sub = i % 5, w = c + 4 * t;
+        lo = 10 * w + sub;
+        hi = lo + 5;
+        p = (sub == 1 || sub == 4) ? 3 : (sub == 2 ? 6 : 0);
+      } else {
+        lo = 120 + 2 * c;
+        hi = lo + 1;
+        p = 0;
+      }
+      break;
+    }
+  }
+}
+
 __device__ __forceinline__ float load_x(const void* x, int dtype, size_t idx) {
   if (dtype == PF_DTYPE_F16) return __half2float(static_cast<const __half*>(x)[idx]);
   if (dtype == PF_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(x)[idx]);

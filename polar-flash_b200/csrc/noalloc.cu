@@ -29,7 +29,7 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
-constexpr size_t kNoAllocCounterBytes = 4096 * sizeof(unsigned);  // split-K counters, must start at zero
+constexpr size_t kNoAllocCounterBytes = pfb::kWsCounterBytes;  // split-K counters, must start at zero
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];

@@ -300,3 +300,20 @@ def test_full_size_llama8b_ffn_linear(bits):
     lhs = qlinear(qw, 0.5 * x1 + 2.0 * x2)
     rhs = 0.5 * qlinear(qw, x1) + 2.0 * qlinear(qw, x2)
     assert_rel(lhs.cpu().numpy(), rhs.cpu().numpy(), rel=1e-5)
+
+
+def test_workspace_counters_return_to_zero():
+    """After a batch of calls (split-K combines on both GEMV paths), every
+    arrival counter is re-armed to zero and the device status word is clear."""
+    from polarflash_b200 import UnifiedQuantizer, qlinear
+    from polarflash_b200.qweight import workspace
+
+    dev = torch.device("cuda")
+    for fmt, K in (("int3_g128", 4096), ("int2_g128", 1024), ("int4_g128", 384)):
+        qw, _ = UnifiedQuantizer(backend=fmt, hadamard_block_size=128).quantize_to_qweight(_w(2048, K, 3).to(dev))
+        for N in (1, 6, 16):
+            qlinear(qw, _x(N, K, N).to(dev))
+    torch.cuda.synchronize()
+    ws = workspace(dev, 1)
+    head = ws[: 16384 * 4].view(torch.int32)
+    assert int(head.abs().sum()) == 0
