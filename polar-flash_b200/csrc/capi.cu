@@ -146,7 +146,7 @@ constexpr size_t kCounterBytes = kWsCounterBytes;
 // TMA-pipelined GEMV for INT4/INT3/INT2 group-128 and the INT4/INT2 reference
 // streams when K % 512 == 0; chosen from format and K only, so a prepare and
 // every run that shares it take the same path.  PF_GEMV_PATH=ldg forces the
-// register-prefetch GEMV, PF_GEMV_MAGIC=normal the 1 + q 2^(p-10) decode.
+// register-prefetch GEMV.
 bool use_tma(const pf_qweight* w) {
   static int mode = -1;
   if (mode < 0) {
@@ -157,14 +157,8 @@ bool use_tma(const pf_qweight* w) {
   return tma_eligible(w->format, 1, w->K, reinterpret_cast<const void*>(16));
 }
 
-int tma_subnormal() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("PF_GEMV_MAGIC");
-    v = (e && strcmp(e, "normal") == 0) ? 0 : 1;
-  }
-  return v;
-}
+// The TMA GEMV decodes codes to exact subnormal fp16 (q * 2^(p-24)).
+int tma_subnormal() { return 1; }
 
 struct IntPlan {
   int NT, rpi, n_row_items, CG, n_chunks, Gp;
@@ -187,9 +181,10 @@ IntPlan plan_int(const pf_qweight* w, int np) {
 }
 
 size_t tma_partials_bytes(const pf_qweight* w, int np) {
+  const int rows = tma_block_rows();
   const int spb = (w->K / 128) / tma_stage_groups(w->format);
-  const int n_units = ((w->M + 63) / 64) * spb;
-  return round_up((size_t)2 * tma_grid(w->format, nt_of(np), n_units) * 64 * np * sizeof(float), 256);
+  const int n_units = ((w->M + rows - 1) / rows) * spb;
+  return round_up((size_t)2 * tma_grid(w->format, nt_of(np), n_units) * rows * np * sizeof(float), 256);
 }
 
 size_t xprep_bytes(const pf_qweight* w, int np) {
@@ -290,7 +285,8 @@ int do_run(const pf_qweight* w, int N, const float* bias, float* y, void* ws, cu
     ta.NT = nt_of(N);
     ta.G = Gp;
     ta.row_words = row_words_of(w->format, K);
-    ta.n_rb = (M + 63) / 64;
+    ta.rows = tma_block_rows();
+    ta.n_rb = (M + ta.rows - 1) / ta.rows;
     ta.spb = Gp / tma_stage_groups(w->format);
     ta.n_units = ta.n_rb * ta.spb;
     ta.rec = reinterpret_cast<const unsigned char*>(base);

@@ -59,10 +59,10 @@ cudaError_t launch_gemv_cc(const GemvCCArgs& a, cudaStream_t s);
 
 // ---- TMA-pipelined integer GEMV (gemv_tma.cu) and its x-prep (prep.cu) ----
 // x' record per 128-column group: [NT tiles][8 k-steps][Lp lanes] uint2 B
-// fragments (Lp = 8N for N <= 4, else 32), then float4 {Sx, f, SB, 0} per
+// fragments (Lp = 8 for N = 1, else 32), then float4 {Sx, f, SB, 0} per
 // token slot (4 * NT).  Sx = sum of x' over the group, f = 2^E the group's
 // power-of-two normaliser, SB = sum of the B values (normal-magic decode).
-__host__ __device__ inline int tma_lanes(int N, int NT) { return NT == 1 ? 8 * N : 32; }
+__host__ __device__ inline int tma_lanes(int N, int NT) { return (NT == 1 && N == 1) ? 8 : 32; }
 __host__ __device__ inline size_t tma_record_bytes(int N, int NT) {
   return (size_t)NT * 8 * tma_lanes(N, NT) * 8 + (size_t)64 * NT;
 }
@@ -86,16 +86,18 @@ struct TmaArgs {
   float tensor_scale;
   int M, K, N, NT, G;
   int row_words;
-  int n_rb, spb, n_units;  // row blocks of 64 rows, stages per row block, units
+  int n_rb, spb, n_units;  // row blocks, stages per row block, units
+  int rows;                // rows per row block
   const unsigned char* rec;  // x' records
   int rec_bytes;
   const float* bias;
   float* y;
-  float* partials;         // [2 * grid][64][N]
+  float* partials;         // [2 * grid][rows][N]
   unsigned* counters;      // per (row block, consumer warp); status word at kWsStatusSlot
 };
 bool tma_eligible(int fmt, int M, int K, const void* codes);
 int tma_grid(int fmt, int NT, int n_units);
+int tma_block_rows();
 cudaError_t launch_gemv_tma(int fmt, const TmaArgs& a, int smode, int subnormal, cudaStream_t s);
 int tma_stage_groups(int fmt);
 
