@@ -35,8 +35,8 @@ namespace pfb {
 
 namespace {
 
-constexpr int kCWarps = 4;
-constexpr int kThreadsT = (kCWarps + 1) * 32;
+constexpr int kCWarps = 8;                     // consumer warps per CTA
+constexpr int kThreadsT = (kCWarps + 1) * 32;  // + 1 producer warp
 constexpr int kMaxCtasPerSm = 4;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
@@ -234,7 +234,7 @@ __device__ __forceinline__ long long cta_of(long long u, long long U, long long 
 template <int FMT, int NT, int LP, int TR, int SMODE>
 struct Stage {
   static constexpr int S = TmaFmt<FMT>::S;
-  static constexpr int kRowsBlk = 64 * TR;
+  static constexpr int kRowsBlk = 16 * kCWarps * TR;
   static constexpr uint32_t W = kRowsBlk * S * TmaFmt<FMT>::WPG * 4;
   static constexpr uint32_t R = NT * 8 * LP * 8 + 64 * NT;  // x' record per group
   static constexpr uint32_t X = S * R;
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kThreadsT, 2)
         woff12[tr][hh] = r & 7;
       }
     }
-  const uint32_t blane = (uint32_t)lane * 8;  // B fragment byte offset within a k-step row
+  const uint32_t blane = (uint32_t)(lane & (LP - 1)) * 8;  // B fragment byte offset within a k-step row
 
   float y[TR][NT][2];
   int seg_st0 = 0;
@@ -429,39 +429,42 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       const uint32_t rec = sb + L::XOFF + j * L::R;
 #pragma unroll
       for (int i = 0; i < NT; ++i) {
-        float acc[TR][4];
+        // two independent accumulator chains per tile (even / odd k-steps);
+        // lanes whose B columns carry no token read a valid finite value
+        // (columns of an MMA are independent, the extra outputs are unused)
+        float acc[TR][2][4];
 #pragma unroll
-        for (int tr = 0; tr < TR; ++tr) acc[tr][0] = acc[tr][1] = acc[tr][2] = acc[tr][3] = 0.f;
+        for (int tr = 0; tr < TR; ++tr)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) acc[tr][e][0] = acc[tr][e][1] = acc[tr][e][2] = acc[tr][e][3] = 0.f;
 #pragma unroll
         for (int j8 = 0; j8 < 8; ++j8) {
-          uint2 b = make_uint2(0u, 0u);
-          if (LP == 32 || lane < LP) b = lds64(rec + (uint32_t)((i * 8 + j8) * LP * 8) + blane);
+          const uint2 b = lds64(rec + (uint32_t)((i * 8 + j8) * LP * 8) + blane);
 #pragma unroll
           for (int tr = 0; tr < TR; ++tr)
-            mma16816(acc[tr], rc[tr][0].h(2 * j8), rc[tr][1].h(2 * j8), rc[tr][0].h(2 * j8 + 1),
+            mma16816(acc[tr][j8 & 1], rc[tr][0].h(2 * j8), rc[tr][1].h(2 * j8), rc[tr][0].h(2 * j8 + 1),
                      rc[tr][1].h(2 * j8 + 1), b.x, b.y);
         }
         const int t = 4 * i + c;
-        if (t < N) {
-          const float4 g4 = lds128f(rec + NT * 8 * LP * 8 + t * 16);
+        const float4 g4 = lds128f(rec + NT * 8 * LP * 8 + (t < N ? t : 0) * 16);
 #pragma unroll
-          for (int tr = 0; tr < TR; ++tr)
+        for (int tr = 0; tr < TR; ++tr)
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              float sv, mv;
-              if constexpr (SMODE == kScaleGroup) {
-                const float2 s2 = __half22float2(*reinterpret_cast<const __half2*>(&srow[tr][hh][j >> 1]));
-                const float2 m2 = __half22float2(*reinterpret_cast<const __half2*>(&mrow[tr][hh][j >> 1]));
-                sv = (j & 1) ? s2.y : s2.x;
-                mv = (j & 1) ? m2.y : m2.x;
-              } else {
-                sv = frow[tr][hh];
-                mv = -(float)kOffset * sv;
-              }
-              const float q = 1024.f * (acc[tr][2 * hh] + acc[tr][2 * hh + 1]);
-              y[tr][i][hh] += (sv * g4.y) * q + mv * g4.x;
+          for (int hh = 0; hh < 2; ++hh) {
+            float sv, mv;
+            if constexpr (SMODE == kScaleGroup) {
+              const float2 s2 = __half22float2(*reinterpret_cast<const __half2*>(&srow[tr][hh][j >> 1]));
+              const float2 m2 = __half22float2(*reinterpret_cast<const __half2*>(&mrow[tr][hh][j >> 1]));
+              sv = (j & 1) ? s2.y : s2.x;
+              mv = (j & 1) ? m2.y : m2.x;
+            } else {
+              sv = frow[tr][hh];
+              mv = -(float)kOffset * sv;
             }
-        }
+            const float q = 1024.f * ((acc[tr][0][2 * hh] + acc[tr][1][2 * hh]) +
+                                      (acc[tr][0][2 * hh + 1] + acc[tr][1][2 * hh + 1]));
+            y[tr][i][hh] += (sv * g4.y) * q + mv * g4.x;
+          }
       }
     }
     __syncwarp();
@@ -559,7 +562,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-constexpr int kTR = 2;  // 16-row MMA tiles per consumer warp (rows per block = 64 * kTR)
+constexpr int kTR = 1;  // 16-row MMA tiles per consumer warp (rows per block = 16 * kCWarps * kTR)
 
 template <int FMT, int NT, int LP, int SMODE>
 cudaError_t launch_one(const TmaArgs& a, cudaStream_t s) {
@@ -638,7 +641,7 @@ bool tma_eligible(int fmt, int M, int K, const void* codes) {
     return false;
   if (K % 512 != 0) return false;
   if (reinterpret_cast<uintptr_t>(codes) % 16) return false;
-  const long long n_rb = (M + 64 * kTR - 1) / (64 * kTR);
+  const long long n_rb = (M + 16 * kCWarps * kTR - 1) / (16 * kCWarps * kTR);
   if (n_rb * kCWarps >= (long long)kWsStatusSlot) return false;
   return encode_fn() != nullptr;
 }
@@ -646,7 +649,7 @@ bool tma_eligible(int fmt, int M, int K, const void* codes) {
 // CTAs of one launch: never more than the units, at most kMaxCtasPerSm per SM
 // (shared memory bounds the real residency; the partial-slot area is sized
 // for this count).
-int tma_block_rows() { return 64 * kTR; }
+int tma_block_rows() { return 16 * kCWarps * kTR; }
 
 int tma_grid(int fmt, int NT, int n_units) {
   (void)fmt;
