@@ -4,7 +4,8 @@ group-128 asymmetric, block-128 RWHT), batch-1 decode.
 
 One step = one pass over the 7-linear set (q/o 4096x4096, k/v 1024x4096,
 gate/up 14336x4096, down 4096x14336) at INT3 and again at INT2: 14 fused
-GEMVs over 156.7 MB of packed weights.  32 resident copies of the packed
+GEMVs over 156.7 MB of packed weights, issued as a layer issues them: one
+grouped launch per shared input (q|k|v, o, gate|up, down), 8 launches.  32 resident copies of the packed
 sets (one per layer of the 8B model, 5.0 GB) are cycled so every step reads
 weights untouched for the previous 31 steps (inputs >> the 126 MB L2).  The
 timed region replays CUDA graphs of the steps; inputs are resident in HBM.
@@ -34,7 +35,7 @@ import torch  # noqa: E402
 LINEARS = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
            ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
 FORMATS = ("int3_g128", "int2_g128")
-# linears sharing one prepared input (q/k/v and gate/up read the same x in a layer)
+# linears sharing one input (q/k/v and gate/up read the same x in a layer): one launch each
 SHARED = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]
 METRIC = "fused dequant-GEMV packed-weight HBM GB/s (Llama-3-8B linear set, INT3+INT2 g128, batch 1)"
 WORKLOAD = "llama3-8b linear set (q,k,v,o,gate,up,down) INT3 g128 + INT2 g128, RWHT-128, fp16 x, batch 1"
@@ -195,7 +196,7 @@ def main():
 
     from polarflash_b200 import encoders
     from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
-    from polarflash_b200.qweight import QWeight, qlinear_multi, workspace
+    from polarflash_b200.qweight import QWeight, group_workspace_bytes, qlinear_multi, workspace
 
     N = args.batch
     # --- encode one set per format (this rank's column shard of the N-times-wider
@@ -225,7 +226,8 @@ def main():
     torch.cuda.synchronize()
 
     g = torch.Generator().manual_seed(7)
-    xs = {K: torch.randn(N, K, generator=g).half().to(dev) for K in (4096, 14336)}
+    kdim = {name: K for name, _, K in LINEARS}
+    xs = {grp: torch.randn(N, kdim[grp[0]], generator=g).half().to(dev) for grp in SHARED}
     # every linear's y [N, M] is a contiguous block of one flat buffer, which is
     # also the all-gather buffer at N GPUs and the D2H source of the e2e leg
     y_total = sum(M for _, M, _ in LINEARS) * len(FORMATS)
@@ -236,30 +238,16 @@ def main():
         for name, M, _ in LINEARS:
             outs[(fmt, name)] = y_all[off:off + N * M].view(N, M)
             off += N * M
-    ws_need = max(qw.workspace_bytes(N) for qw in base.values())
-    ws = workspace(dev, ws_need)  # zero-filled once; every run leaves its counters zero
+    ws_need = max(group_workspace_bytes([base[(fmt, n)] for n in grp], N) for fmt in FORMATS for grp in SHARED)
+    ws = workspace(dev, ws_need)  # zero-filled once; every launch leaves its counters zero
     step_bytes = sum(alg_bytes(qw, N) for qw in base.values())
     packed_bytes = sum(qw.nbytes() for qw in base.values())
-    launches_per_step = len(FORMATS) * (len(SHARED) + len(LINEARS))
+    launches_per_step = len(FORMATS) * len(SHARED)
 
-
-    def step(cp, run_only=False):
+    def step(cp):
         for fmt in FORMATS:
             for grp in SHARED:
-                qws = [cp[(fmt, n)] for n in grp]
-                K = qws[0].K
-                if run_only:
-                    from polarflash_b200 import _lib
-                    import ctypes
-                    L = _lib.load()
-                    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-                    for n, q in zip(grp, qws):
-                        o = outs[(fmt, n)]
-                        _lib.check(L.pf_qlinear_run(ctypes.byref(q.descriptor()), N, None,
-                                                    ctypes.c_void_p(o.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
-                                                    ws.numel(), sp))
-                else:
-                    qlinear_multi(qws, xs[K], workspace=ws, outs=[outs[(fmt, n)] for n in grp])
+                qlinear_multi([cp[(fmt, n)] for n in grp], xs[grp], workspace=ws, outs=[outs[(fmt, n)] for n in grp])
 
     # warm-up (also compiles lazily-loaded modules)
     for _ in range(3):
@@ -267,19 +255,13 @@ def main():
     torch.cuda.synchronize()
 
     stream = torch.cuda.Stream(device=dev)
-    graphs, graphs_run = [], []
+    graphs = []
     with torch.cuda.stream(stream):
         for cp in copies:
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr, stream=stream):
                 step(cp)
             graphs.append(gr)
-        # run-only graphs (x' already prepared by the last replay): the GEMV kernel alone
-        for cp in copies:
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr, stream=stream):
-                step(cp, run_only=True)
-            graphs_run.append(gr)
     torch.cuda.synchronize()
 
     def replay(k, gl):
@@ -320,30 +302,22 @@ def main():
         if extra:
             clk["window"] = "timed region + same-graph replays to 1.5 s"
 
-        # dominant kernel: the GEMV runs alone (x' prepared), CUDA events
-        steps_run = max(args.steps, 200)
-        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        for k in range(10):
-            graphs_run[k % len(graphs_run)].replay()
-        r0.record(stream)
-        for k in range(steps_run):
-            graphs_run[k % len(graphs_run)].replay()
-        r1.record(stream)
-        torch.cuda.synchronize()
-        ms_run = r0.elapsed_time(r1) / steps_run
+        # the step holds nothing but the GEMV kernel's launches, so the dominant
+        # kernel's time per step is the timed region's (CUDA events, stream above)
+        ms_run = ms / args.steps
 
         # e2e through the public API with host buffers: pinned x in, y out,
         # copies inside the timed region (graph of H2D -> GEMVs -> D2H)
-        x_host = {K: torch.empty(N, K, dtype=torch.float16, pin_memory=True) for K in (4096, 14336)}
-        for K in x_host:
-            x_host[K].copy_(xs[K].cpu())
+        x_host = {grp: torch.empty(N, xs[grp].shape[1], dtype=torch.float16, pin_memory=True) for grp in xs}
+        for grp in x_host:
+            x_host[grp].copy_(xs[grp].cpu())
         y_host = torch.empty(N * y_total, dtype=torch.float32, pin_memory=True)
         e2e_graphs = []
         for cp in copies[:4]:
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr, stream=stream):
-                for K in xs:
-                    xs[K].copy_(x_host[K], non_blocking=True)
+                for grp in xs:
+                    xs[grp].copy_(x_host[grp], non_blocking=True)
                 step(cp)
                 y_host.copy_(y_all, non_blocking=True)
             e2e_graphs.append(gr)
@@ -390,7 +364,8 @@ def main():
         for fmt in FORMATS:
             for name, M, K in LINEARS:
                 qw = base[(fmt, name)]
-                samples.append((fmt, name, host_payload(qw), M, K, xs[K].float().cpu().numpy()))
+                grp = next(gp for gp in SHARED if name in gp)
+                samples.append((fmt, name, host_payload(qw), M, K, xs[grp].float().cpu().numpy()))
         gbs, secs, cores = cpu_reference_leg(None, samples)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                "sample": f"one pass over the 14-linear set (decode + inverse RWHT + fp32 matvec), {secs:.1f} s"}
@@ -406,17 +381,18 @@ def main():
                              "inputs > 126 MB L2", "parallelism": f"column-shard x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                         "kernel": "gemv_int_kernel (14 GEMV launches per step, CUDA-event timed)",
+                         "kernel": "gemv_tma_kernel (8 grouped launches per step: q|k|v, o, gate|up, down at "
+                                   "INT3 and INT2; CUDA events over the timed region)",
                          "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": round(world * step_bytes / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "how": "CUDA graph of public-API calls: pinned x H2D, 8 prepare + 14 GEMV launches, y D2H"},
+                    "how": "CUDA graph of public-API calls: pinned x H2D, 8 grouped GEMV launches, y D2H"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
-    for gr in graphs + graphs_run + e2e_graphs:
+    for gr in graphs + e2e_graphs:
         del gr
     if world > 1:
         dist.barrier()

@@ -116,8 +116,8 @@ PF_API int pf_last_cuda_error(void);
 PF_API int pf_qweight_check(const pf_qweight* w);
 
 /* Bytes of device workspace pf_qlinear needs for N input rows.  The
- * workspace holds the prepared activations x', split-K partial sums and a
- * block of split-K arrival counters at its start.  Zero-fill a workspace once
+ * workspace holds a block of split-K arrival counters at its start, split-K
+ * partial sums and, for the formats that need one, the prepared activations.  Zero-fill a workspace once
  * after allocating it; every call leaves the counters zero again.  Calls
  * that share one workspace must be ordered (same stream). */
 PF_API int pf_qlinear_workspace_size(const pf_qweight* w, int N, size_t* bytes);
@@ -131,14 +131,19 @@ PF_API int pf_qlinear_workspace_size(const pf_qweight* w, int N, size_t* bytes);
 PF_API int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias,
                float* y, void* workspace, size_t workspace_bytes, void* stream);
 
-/* The two halves of pf_qlinear for N <= 16: prepare writes x' (the forward
- * block RWHT of x, in the layout the GEMV reads) into the workspace; run
- * computes y from it.  One prepare serves several runs over weights with the
- * same format, K and rotation (q/k/v or gate/up sharing one input). */
-PF_API int pf_qlinear_prepare(const pf_qweight* w, const void* x, int x_dtype, int N, void* workspace,
-                              size_t workspace_bytes, void* stream);
-PF_API int pf_qlinear_run(const pf_qweight* w, int N, const float* bias, float* y, void* workspace,
-                          size_t workspace_bytes, void* stream);
+/* `count` linears in one call: y_i[N][M_i] = x_i[N][K_i] * W_i^T (+ bias_i),
+ * i < count (no counterpart in the reference, whose layers run one at a
+ * time; used where a model feeds one input to several weights: q/k/v,
+ * gate/up).  When every weight takes the streaming GEMV (INT formats with
+ * K % 512 == 0, one format and scale mode, rotation block <= 512, x 16-byte
+ * aligned for fp32 or 8-byte for fp16/bf16), each 16-token pass of up to four
+ * weights is ONE kernel launch; otherwise the weights run one after another
+ * as pf_qlinear.  ws, xs, biases (may be NULL, or hold NULLs) and ys are host
+ * arrays of `count` entries; the pointers they hold are device pointers. */
+PF_API int pf_qlinear_group_workspace_size(int count, const pf_qweight* const* ws, int N, size_t* bytes);
+PF_API int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* const* xs, int x_dtype, int N,
+                            const float* const* biases, float* const* ys, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /* pf_qlinear for callers that cannot allocate device memory (no counterpart
  * in the reference, which has no GPU linear of its own to mirror here).

@@ -43,17 +43,7 @@ int make_plan(int K, int block, HadPlan* p) {
   return PF_OK;
 }
 
-int row_words_of(int fmt, int K) {
-  switch (fmt) {
-    case PF_FMT_INT4_G128: return (K / 128) * 16;
-    case PF_FMT_INT3_G128: return (K / 128) * 13;
-    case PF_FMT_INT2_G128: return (K / 128) * 8;
-    case PF_FMT_INT4: return K / 8;
-    case PF_FMT_INT3: return 3 * K / 32;
-    case PF_FMT_INT2: return K / 16;
-    default: return 0;
-  }
-}
+int row_words_of(int fmt, int K) { return row_words_of_tma(fmt, K); }
 
 struct PolarShape {
   int d, tb, row_bytes;
@@ -143,10 +133,23 @@ int nt_of(int np) { return np <= 4 ? 1 : np <= 8 ? 2 : 4; }
 // one prepare can serve several runs over weights of different M.
 constexpr size_t kCounterBytes = kWsCounterBytes;
 
-// TMA-pipelined GEMV for INT4/INT3/INT2 group-128 and the INT4/INT2 reference
-// streams when K % 512 == 0; chosen from format and K only, so a prepare and
-// every run that shares it take the same path.  PF_GEMV_PATH=ldg forces the
-// register-prefetch GEMV.
+TmaWeight tma_weight(const pf_qweight* w) {
+  TmaWeight t;
+  t.format = w->format;
+  t.M = w->M;
+  t.K = w->K;
+  t.had_block = w->had_block;
+  t.codes = w->codes;
+  t.scales = w->scales;
+  t.mins = w->mins;
+  t.signs = w->had_signs;
+  t.tensor_scale = (float)w->tensor_scale;
+  return t;
+}
+
+// The streaming GEMV (gemv_tma.cu) serves INT4/INT3/INT2 group-128 and the
+// INT4/INT2 reference streams when K % 512 == 0 and the rotation block is at
+// most 512; PF_GEMV_PATH=ldg forces the register-prefetch GEMV.
 bool use_tma(const pf_qweight* w) {
   static int mode = -1;
   if (mode < 0) {
@@ -154,11 +157,11 @@ bool use_tma(const pf_qweight* w) {
     mode = (e && strcmp(e, "ldg") == 0) ? 0 : 1;
   }
   if (!mode) return false;
-  return tma_eligible(w->format, 1, w->K, reinterpret_cast<const void*>(16));
+  return tma_eligible(tma_weight(w));
 }
 
-// The TMA GEMV decodes codes to exact subnormal fp16 (q * 2^(p-24)).
-int tma_subnormal() { return 1; }
+// x alignment of the streaming GEMV's vector loads (else the other path runs)
+bool x_tma_aligned(const void* x, int x_dtype) { return aligned(x, x_dtype == PF_DTYPE_F32 ? 16 : 8); }
 
 struct IntPlan {
   int NT, rpi, n_row_items, CG, n_chunks, Gp;
@@ -180,16 +183,8 @@ IntPlan plan_int(const pf_qweight* w, int np) {
   return p;
 }
 
-size_t tma_partials_bytes(const pf_qweight* w, int np) {
-  const int rows = tma_block_rows();
-  const int spb = (w->K / 128) / tma_stage_groups(w->format);
-  const int n_units = ((w->M + rows - 1) / rows) * spb;
-  return round_up((size_t)2 * tma_grid(w->format, nt_of(np), n_units) * rows * np * sizeof(float), 256);
-}
-
 size_t xprep_bytes(const pf_qweight* w, int np) {
   size_t Gp = (size_t)(w->K + 127) / 128;
-  if (use_tma(w)) return round_up(Gp * tma_record_bytes(np, nt_of(np)), 256);
   if (is_int_format(w->format)) {
     int NT = nt_of(np);
     return round_up((size_t)NT * Gp * 2048, 256) + round_up(Gp * 8 * NT * sizeof(float), 256);
@@ -197,12 +192,22 @@ size_t xprep_bytes(const pf_qweight* w, int np) {
   return round_up((size_t)np * Gp * 128 * sizeof(float), 256);
 }
 
-size_t pass_bytes(const pf_qweight* w, int np) {
+// One pass of the register-prefetch / CUDA-core path.
+size_t ldg_pass_bytes(const pf_qweight* w, int np) {
   size_t b = kCounterBytes + xprep_bytes(w, np);
-  if (use_tma(w)) return b + tma_partials_bytes(w, np);
   if (is_int_format(w->format)) {
     IntPlan p = plan_int(w, np);
     if (p.n_chunks > 1) b += round_up((size_t)p.n_chunks * np * w->M * sizeof(float), 256);
+  }
+  return b;
+}
+
+// Streaming-GEMV weights also fit the other path (taken for misaligned x).
+size_t pass_bytes(const pf_qweight* w, int np) {
+  size_t b = ldg_pass_bytes(w, np);
+  if (use_tma(w)) {
+    size_t t = kCounterBytes + tma_partial_bytes(tma_weight(w), np);
+    if (t > b) b = t;
   }
   return b;
 }
@@ -236,22 +241,6 @@ int do_prepare(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dt
   pa.fmt = w->format;
   pa.M = w->M;
   pa.init_y = 0;
-  if (use_tma(w)) {
-    Prep2Args p2;
-    memset(&p2, 0, sizeof(p2));
-    p2.x = x;
-    p2.x_dtype = x_dtype;
-    p2.N = N;
-    p2.NT = nt_of(N);
-    p2.K = w->K;
-    p2.G = Gp;
-    p2.plan = plan;
-    p2.signs = w->had_signs;
-    p2.fmt = w->format;
-    p2.subnormal = tma_subnormal();
-    p2.rec = reinterpret_cast<unsigned char*>(base);
-    return cuda_status(launch_prep2(p2, s));
-  }
   if (is_int_format(w->format)) {
     const int NT = nt_of(N);
     pa.mode = 0;
@@ -271,33 +260,6 @@ int do_run(const pf_qweight* w, int N, const float* bias, float* y, void* ws, cu
   const int K = w->K, M = w->M;
   const int Gp = (K + 127) / 128;
   char* base = static_cast<char*>(ws) + kCounterBytes;
-  if (use_tma(w)) {
-    if (!tma_eligible(w->format, M, K, w->codes)) return PF_ERR_ALIGNMENT;
-    TmaArgs ta;
-    memset(&ta, 0, sizeof(ta));
-    ta.codes = w->codes;
-    ta.scales = w->scales;
-    ta.mins = static_cast<const __half*>(w->mins);
-    ta.tensor_scale = (float)w->tensor_scale;
-    ta.M = M;
-    ta.K = K;
-    ta.N = N;
-    ta.NT = nt_of(N);
-    ta.G = Gp;
-    ta.row_words = row_words_of(w->format, K);
-    ta.rows = tma_block_rows();
-    ta.n_rb = (M + ta.rows - 1) / ta.rows;
-    ta.spb = Gp / tma_stage_groups(w->format);
-    ta.n_units = ta.n_rb * ta.spb;
-    ta.rec = reinterpret_cast<const unsigned char*>(base);
-    ta.rec_bytes = (int)tma_record_bytes(N, ta.NT);
-    ta.bias = bias;
-    ta.y = y;
-    ta.partials = reinterpret_cast<float*>(base + xprep_bytes(w, N));
-    ta.counters = static_cast<unsigned*>(ws);
-    int smode = is_group_int_format(w->format) ? kScaleGroup : (w->scales ? kScaleRow : kScaleTensor);
-    return cuda_status(launch_gemv_tma(w->format, ta, smode, tma_subnormal(), s));
-  }
   if (is_int_format(w->format)) {
     IntPlan p = plan_int(w, N);
     GemvIntArgs ga;
@@ -393,28 +355,20 @@ static int common_args(const pf_qweight* w, int N, void* ws, size_t ws_bytes) {
   return PF_OK;
 }
 
-int pf_qlinear_prepare(const pf_qweight* w, const void* x, int x_dtype, int N, void* workspace,
-                       size_t ws_bytes, void* stream) {
-  int st = common_args(w, N, workspace, ws_bytes);
-  if (st || N == 0) return st;
-  if (N > kMaxGemvTokens) return PF_ERR_SHAPE;
-  if (x_dtype < PF_DTYPE_F32 || x_dtype > PF_DTYPE_BF16) return PF_ERR_INVALID_ARGUMENT;
-  if (!x) return PF_ERR_INVALID_ARGUMENT;
-  if (!aligned(x, dtype_size(x_dtype))) return PF_ERR_ALIGNMENT;
-  HadPlan plan;
-  st = make_plan(w->K, w->had_block, &plan);
+// One pass (N <= 16 tokens) of pf_qlinear.
+static int qlinear_pass(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, int np,
+                        const float* bias, float* y, void* ws, cudaStream_t s) {
+  if (use_tma(w) && x_tma_aligned(x, x_dtype)) {
+    TmaWeight tw = tma_weight(w);
+    TmaIO io = {x, bias, y};
+    cudaError_t e = cudaSuccess;
+    int st = launch_gemv_tma(&tw, &io, 1, np, x_dtype, ws, s, &e);
+    if (st == PF_ERR_CUDA) return cuda_status(e);
+    return st;
+  }
+  int st = do_prepare(w, plan, x, x_dtype, np, ws, s);
   if (st) return st;
-  return do_prepare(w, plan, x, x_dtype, N, workspace, static_cast<cudaStream_t>(stream));
-}
-
-int pf_qlinear_run(const pf_qweight* w, int N, const float* bias, float* y, void* workspace, size_t ws_bytes,
-                   void* stream) {
-  int st = common_args(w, N, workspace, ws_bytes);
-  if (st || N == 0) return st;
-  if (N > kMaxGemvTokens) return PF_ERR_SHAPE;
-  if (!y) return PF_ERR_INVALID_ARGUMENT;
-  if (!aligned(y, 4) || (bias && !aligned(bias, 4))) return PF_ERR_ALIGNMENT;
-  return do_run(w, N, bias, y, workspace, static_cast<cudaStream_t>(stream));
+  return do_run(w, np, bias, y, ws, s);
 }
 
 int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias, float* y,
@@ -431,10 +385,103 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
   const size_t xs = dtype_size(x_dtype);
   for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {
     int np = N - t0 < kMaxGemvTokens ? N - t0 : kMaxGemvTokens;
-    st = do_prepare(w, plan, static_cast<const char*>(x) + (size_t)t0 * w->K * xs, x_dtype, np, workspace, s);
+    st = qlinear_pass(w, plan, static_cast<const char*>(x) + (size_t)t0 * w->K * xs, x_dtype, np, bias,
+                      y + (size_t)t0 * w->M, workspace, s);
     if (st) return st;
-    st = do_run(w, np, bias, y + (size_t)t0 * w->M, workspace, s);
+  }
+  return PF_OK;
+}
+
+// ---- grouped linears: members [c, c + 4) of a group share one launch when
+// every member takes the streaming GEMV with one format and scale mode.
+static bool group_streams(int count, const pf_qweight* const* ws) {
+  if (count < 1) return false;
+  for (int i = 0; i < count; ++i) {
+    if (!use_tma(ws[i])) return false;
+    if (ws[i]->format != ws[0]->format) return false;
+    if (!is_group_int_format(ws[0]->format) && ((ws[i]->scales != nullptr) != (ws[0]->scales != nullptr)))
+      return false;
+  }
+  for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
+    size_t slots = 0;
+    for (int i = c0; i < count && i < c0 + kTmaMaxJobs; ++i) slots += tma_counter_slots(tma_weight(ws[i]));
+    if (slots >= kWsStatusSlot) return false;
+  }
+  return true;
+}
+
+static size_t group_bytes(int count, const pf_qweight* const* ws, int N) {
+  size_t b = 0;
+  for (int i = 0; i < count; ++i) {
+    size_t t = workspace_bytes(ws[i], N);
+    if (t > b) b = t;
+  }
+  if (group_streams(count, ws)) {
+    int np = tokens_per_pass(N < 1 ? 1 : N);
+    for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
+      size_t t = kCounterBytes;
+      for (int i = c0; i < count && i < c0 + kTmaMaxJobs; ++i) t += tma_partial_bytes(tma_weight(ws[i]), np);
+      if (t > b) b = t;
+    }
+  }
+  return b;
+}
+
+int pf_qlinear_group_workspace_size(int count, const pf_qweight* const* ws, int N, size_t* bytes) {
+  if (count < 1 || !ws || !bytes || N < 0) return PF_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < count; ++i) {
+    int st = check(ws[i]);
     if (st) return st;
+  }
+  *bytes = group_bytes(count, ws, N);
+  return PF_OK;
+}
+
+int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* const* xs, int x_dtype, int N,
+                     const float* const* biases, float* const* ys, void* workspace, size_t ws_bytes, void* stream) {
+  if (count < 1 || !ws || !xs || !ys || N < 0) return PF_ERR_INVALID_ARGUMENT;
+  if (x_dtype < PF_DTYPE_F32 || x_dtype > PF_DTYPE_BF16) return PF_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < count; ++i) {
+    int st = check(ws[i]);
+    if (st) return st;
+    if (!xs[i] || !ys[i]) return PF_ERR_INVALID_ARGUMENT;
+    const float* b = biases ? biases[i] : nullptr;
+    if (!aligned(xs[i], dtype_size(x_dtype)) || !aligned(ys[i], 4) || (b && !aligned(b, 4)))
+      return PF_ERR_ALIGNMENT;
+  }
+  if (N == 0) return PF_OK;
+  if (!workspace || ws_bytes < group_bytes(count, ws, N)) return PF_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return PF_ERR_ALIGNMENT;
+  bool grouped = group_streams(count, ws);
+  for (int i = 0; i < count && grouped; ++i) grouped = x_tma_aligned(xs[i], x_dtype);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t xsz = dtype_size(x_dtype);
+  if (!grouped) {
+    for (int i = 0; i < count; ++i) {
+      int st = pf_qlinear(ws[i], xs[i], x_dtype, N, biases ? biases[i] : nullptr, ys[i], workspace, ws_bytes,
+                          stream);
+      if (st) return st;
+    }
+    return PF_OK;
+  }
+  for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {
+    const int np = N - t0 < kMaxGemvTokens ? N - t0 : kMaxGemvTokens;
+    for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
+      const int n = count - c0 < kTmaMaxJobs ? count - c0 : kTmaMaxJobs;
+      TmaWeight tw[kTmaMaxJobs];
+      TmaIO io[kTmaMaxJobs];
+      for (int k = 0; k < n; ++k) {
+        const pf_qweight* w = ws[c0 + k];
+        tw[k] = tma_weight(w);
+        io[k].x = static_cast<const char*>(xs[c0 + k]) + (size_t)t0 * w->K * xsz;
+        io[k].bias = biases ? biases[c0 + k] : nullptr;
+        io[k].y = ys[c0 + k] + (size_t)t0 * w->M;
+      }
+      cudaError_t e = cudaSuccess;
+      int st = launch_gemv_tma(tw, io, n, np, x_dtype, workspace, s, &e);
+      if (st == PF_ERR_CUDA) return cuda_status(e);
+      if (st) return st;
+    }
   }
   return PF_OK;
 }

@@ -57,49 +57,59 @@ struct GemvCCArgs {
 
 cudaError_t launch_gemv_cc(const GemvCCArgs& a, cudaStream_t s);
 
-// ---- TMA-pipelined integer GEMV (gemv_tma.cu) and its x-prep (prep.cu) ----
-// x' record per 128-column group: [NT tiles][8 k-steps][Lp lanes] uint2 B
-// fragments (Lp = 8 for N = 1, else 32), then float4 {Sx, f, SB, 0} per
-// token slot (4 * NT).  Sx = sum of x' over the group, f = 2^E the group's
-// power-of-two normaliser, SB = sum of the B values (normal-magic decode).
-__host__ __device__ inline int tma_lanes(int N, int NT) { return (NT == 1 && N == 1) ? 8 : 32; }
-__host__ __device__ inline size_t tma_record_bytes(int N, int NT) {
-  return (size_t)NT * 8 * tma_lanes(N, NT) * 8 + (size_t)64 * NT;
-}
+// ---- streaming integer GEMV (gemv_tma.cu): up to kTmaMaxJobs weights of one
+// format per launch, x' computed inside the kernel.
+constexpr int kTmaMaxJobs = 4;
 
-struct Prep2Args {
-  const void* x;
-  int x_dtype;
-  int N, NT, K, G;
-  HadPlan plan;
-  const int8_t* signs;
-  int fmt;
-  int subnormal;  // B scale 2^(14-p) (subnormal codes) or 2^(10-p) (1 + q 2^(p-10) codes)
-  unsigned char* rec;
+struct TmaJob {  // device view of one weight of a launch
+  const void* scales;   // fp16 [M][G] (group) or fp32 [M] (row)
+  const __half* mins;   // fp16 [M][G] (group)
+  const void* x;        // [N][K] activations (x_dtype)
+  const int8_t* signs;  // RWHT column signs, or nullptr
+  const float* bias;
+  float* y;             // [N][M] fp32
+  float* partials;      // [n_rb][spb][128][N] stage partial sums (spb > 1)
+  unsigned* counters;   // [n_rb][8] arrival counters, zero on entry and exit
+  float tensor_scale;
+  float had_rscale;     // 1/sqrt(had_block), 1 when not rotated
+  int had_block;        // 0 or a power of two <= 512 dividing K
+  int M, K, G, n_rb, spb;
+  int unit0, run0;      // first unit and first (job, stage) run of the job
 };
-cudaError_t launch_prep2(const Prep2Args& a, cudaStream_t s);
 
 struct TmaArgs {
+  TmaJob job[kTmaMaxJobs];
+  unsigned* status;     // workspace status word
+  int n_jobs, n_units, N, x_dtype;
+  int NS, XS;           // ring stages, resident x' stage slots
+  int chunk_max;        // largest x-prep chunk (columns)
+};
+
+struct TmaWeight {  // host view of one weight
+  int format, M, K, had_block;
   const void* codes;
   const void* scales;
-  const __half* mins;
+  const void* mins;
+  const int8_t* signs;
   float tensor_scale;
-  int M, K, N, NT, G;
-  int row_words;
-  int n_rb, spb, n_units;  // row blocks, stages per row block, units
-  int rows;                // rows per row block
-  const unsigned char* rec;  // x' records
-  int rec_bytes;
+};
+struct TmaIO {
+  const void* x;
   const float* bias;
   float* y;
-  float* partials;         // [2 * grid][rows][N]
-  unsigned* counters;      // per (row block, consumer warp); status word at kWsStatusSlot
 };
-bool tma_eligible(int fmt, int M, int K, const void* codes);
-int tma_grid(int fmt, int NT, int n_units);
+
+bool tma_eligible(const TmaWeight& w);
+size_t tma_counter_slots(const TmaWeight& w);
+size_t tma_partial_bytes(const TmaWeight& w, int N);
 int tma_block_rows();
-cudaError_t launch_gemv_tma(int fmt, const TmaArgs& a, int smode, int subnormal, cudaStream_t s);
 int tma_stage_groups(int fmt);
+int row_words_of_tma(int fmt, int K);
+// One launch for `count` weights (same format) and N <= 16 tokens; the
+// workspace holds the counters (kWsCounterBytes) followed by every job's
+// partial sums.  Returns a pf_status; *err receives a CUDA launch error.
+int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int x_dtype, void* workspace,
+                    cudaStream_t s, cudaError_t* err);
 
 struct DequantArgs {
   int fmt;

@@ -1,30 +1,39 @@
-// TMA-pipelined fused dequant-GEMV for the INT formats (N <= 16 tokens).
+// Streaming fused dequant-GEMV for the INT formats (N <= 16 tokens): one
+// launch computes y = x W^T for up to four weights ("jobs") of one format.
 //
-// CTA = 4 consumer warps + 1 producer warp.  The producer streams
-// (64*TR)-row x S-group tiles of packed codes with 2-D TMA copies, the
-// matching x' records with 1-D bulk copies, and (with its other lanes) the
-// tiles' fp16 scales and zero points into a 2-4 stage shared-memory ring
-// guarded by mbarriers; the weights of the first stages are requested before
-// the kernel waits for the x-prep grid (programmatic dependent launch), so
-// weight streaming overlaps the preceding kernel.  Consumers never touch
-// global memory until they write y: they read their rows' words from shared
-// memory (128B-swizzled tiles, row order permuted so the reads are
-// bank-conflict free) with 32-bit shared addresses, keep a few registers per
-// row from which every code pair is one AND (codes already below mantissa
-// bit 10 are not shifted; the per-position power of two lives in x'), and
-// multiply on the tensor cores (mma.sync m16n8k16, register A) for TR
-// independent 16-row tiles per warp.
+// CTA = 8 consumer warps + 1 producer warp, one CTA per SM and at most
+// ~110 KB of shared memory, so the CTAs of the next launch on the stream fit
+// beside this one and stream their weights while this launch drains
+// (programmatic dependent launch: every CTA signals its dependents at once;
+// only the consumer warps wait for the preceding grid, before they read x or
+// write to global memory; packed weights and scales are never written by a
+// kernel that precedes a GEMV in this library).
 //
-// Codes become exact subnormal fp16 values  h = q 2^(p-24)  and x' was scaled
-// by 2^(14-p-E), so  sum h B = 2^-10 sum q x'/2^E  with no bias term.  Per
-// 128-column group:   sum w x' = s 2^E Q + m Sx,   Q = sum q x'/2^E.
-// Work is split stream-K style: the (row block, stage) units are dealt out
-// evenly to the CTAs; row blocks split between CTAs are combined through
-// per-warp partial slots and arrival counters in chunk order (deterministic).
-// Every wait is bounded (2 s, %globaltimer); on expiry the kernel records
-// PF_ERR_TIMEOUT in the workspace status word and returns.
+// Work unit = (job, 128-row block, stage of S groups of 128 columns), dealt to
+// the CTAs stream-K style in stage-major order: a CTA's consecutive units
+// share a column stage, so it transforms only the one or two stages of x it
+// needs (x' = forward block RWHT of x, scaled and split for the tensor cores)
+// straight into shared memory; there is no separate x-prep launch.
+//   producer warp: lane 0 issues the 2-D TMA copy of a unit's packed codes
+//     (L2 evict-first); all lanes copy the unit's fp16 scales / zero points
+//     with cp.async and let the copies themselves arrive on the stage's
+//     mbarrier, so no lane ever waits for a global load.
+//   consumer warps: 16 rows each.  A unit's code words are read from shared
+//     memory into registers at once (the ring slot is released right away),
+//     every code pair becomes one AND (exact subnormal fp16 q 2^(p-24)), and
+//     mma.sync m16n8k16 multiplies two groups at a time against the B
+//     fragments of x' (fp16 hi / lo halves of x' in the two columns of each
+//     token).
+// Per 128-column group:  sum w x' = s 2^E Q + m Sx  with  Q = sum q x'/2^E.
+// Each unit's 128 x N partial sums go to the workspace; the last of a row
+// block's stage units (per-warp arrival counters) adds them in stage order
+// (deterministic) and writes y.  Every wait is bounded (2 s, %globaltimer):
+// on expiry the kernel records PF_ERR_TIMEOUT in the workspace status word,
+// skips every later wait and finishes.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <mutex>
 
@@ -37,8 +46,12 @@ namespace {
 
 constexpr int kCWarps = 8;                     // consumer warps per CTA
 constexpr int kThreadsT = (kCWarps + 1) * 32;  // + 1 producer warp
-constexpr int kMaxCtasPerSm = 4;
+constexpr int kRowsBlk = 16 * kCWarps;         // rows per unit
+constexpr int kBarConsumers = 1;               // named barrier of the consumer warps
 constexpr unsigned long long kWaitNs = 2000000000ull;
+constexpr int kSmemBudget = 110 * 1024;  // dynamic smem per CTA (two CTAs per SM)
+constexpr int kMaxStages = 8;
+constexpr int kMaxXSlots = 3;
 
 template <int FMT>
 struct TmaFmt;
@@ -65,6 +78,24 @@ struct TmaFmt<PF_FMT_INT3_G128> {
 constexpr bool is_int4(int f) { return f == PF_FMT_INT4_G128 || f == PF_FMT_INT4; }
 constexpr bool is_int2(int f) { return f == PF_FMT_INT2_G128 || f == PF_FMT_INT2; }
 
+// Shared-memory layout of one ring stage: packed codes, then scales.
+template <int FMT, int SMODE>
+struct StageL {
+  static constexpr int S = TmaFmt<FMT>::S;
+  static constexpr uint32_t W = kRowsBlk * S * TmaFmt<FMT>::WPG * 4;
+  static constexpr uint32_t SROW = SMODE == kScaleGroup ? S * 4 : (SMODE == kScaleRow ? 4 : 0);  // bytes per row
+  static constexpr uint32_t BYTES = (W + kRowsBlk * SROW + 1023u) & ~1023u;
+};
+
+// x' record of one 128-column group: [NT tiles][4 k-step pairs][LP lanes]
+// uint4 (the B fragments of two k-steps), then float4 {Sx, 1024 2^E, -, -}
+// per token slot.
+template <int NT, int LP>
+struct XRec {
+  static constexpr uint32_t FRAG = NT * 4 * LP * 16;
+  static constexpr uint32_t R = FRAG + 64 * NT;
+};
+
 // Box row of quad-row rq: under the 128B swizzle a warp's smem reads are
 // split into 8-lane (128-bit) or 16-lane (64-bit) phases; these orders put
 // rows whose swizzle masks differ in the right bits into one phase.
@@ -81,25 +112,9 @@ __device__ __forceinline__ int row_perm(int rq) {
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-  uint32_t v;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint2 lds64(uint32_t a) {
-  uint2 v;
-  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-  return v;
-}
-__device__ __forceinline__ float4 lds128f(uint32_t a) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
-  return v;
+template <class T>
+__device__ __forceinline__ T lds(const unsigned char* p) {
+  return *reinterpret_cast<const T*>(p);
 }
 
 __device__ __forceinline__ unsigned long long now_ns() {
@@ -108,7 +123,9 @@ __device__ __forceinline__ unsigned long long now_ns() {
   return t;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait on an mbarrier phase; false when it gave up (or another warp
+// of the CTA already did).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const volatile int* abort_flag) {
   unsigned long long t0 = 0;
   for (unsigned it = 0;; ++it) {
     uint32_t done;
@@ -119,7 +136,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     if (done) return true;
     if ((it & 63) == 63) {
-      unsigned long long t = now_ns();
+      if (*abort_flag) return false;
+      const unsigned long long t = now_ns();
       if (t0 == 0)
         t0 = t;
       else if (t - t0 > kWaitNs)
@@ -134,42 +152,53 @@ __device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar,
+                                       uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
       : "memory");
 }
-__device__ __forceinline__ void bulk_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
+// cp.async of 4 / 8 bytes (src_bytes = 0: zero fill, nothing read)
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// arrive on `bar` once this thread's earlier cp.async copies have landed
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kBarConsumers), "n"(kCWarps * 32) : "memory");
+}
+
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // ---- per-row decode state: the few registers from which every code pair of
-// a group is one AND (codes land as exact subnormal fp16 q * 2^(p-24)).
+// a group is one AND (codes land as exact subnormal fp16 q * 2^(p-24)); the
+// pair -> column map is frag_cols2 (common.cuh).
 template <int FMT>
 struct RowCodes;
 
 template <>
 struct RowCodes<PF_FMT_INT4_G128> {
   uint32_t w[4], v[4];
-  __device__ __forceinline__ void load(uint32_t addr_j) {  // 16 bytes of the row's group
-    const uint4 q = lds128(addr_j);
-    w[0] = q.x; w[1] = q.y; w[2] = q.z; w[3] = q.w;
+  __device__ __forceinline__ void set(const uint32_t (&raw)[4], int) {
 #pragma unroll
-    for (int t = 0; t < 4; ++t) v[t] = w[t] >> 8;
+    for (int t = 0; t < 4; ++t) {
+      w[t] = raw[t];
+      v[t] = raw[t] >> 8;
+    }
   }
-  // half2 i (frag_cols2): word i/4; sub 0,1 from w, 2,3 from w >> 8
   __device__ __forceinline__ uint32_t h(int i) const {
     const int t = i >> 2, sub = i & 3;
     const uint32_t src = sub < 2 ? w[t] : v[t];
@@ -182,11 +211,12 @@ struct RowCodes<PF_FMT_INT4> : RowCodes<PF_FMT_INT4_G128> {};
 template <>
 struct RowCodes<PF_FMT_INT2_G128> {
   uint32_t w[2], v[2];
-  __device__ __forceinline__ void load(uint32_t addr_j) {
-    const uint2 q = lds64(addr_j);
-    w[0] = q.x; w[1] = q.y;
-    v[0] = w[0] >> 10;
-    v[1] = w[1] >> 10;
+  __device__ __forceinline__ void set(const uint32_t (&raw)[4], int) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      w[t] = raw[t];
+      v[t] = raw[t] >> 10;
+    }
   }
   __device__ __forceinline__ uint32_t h(int i) const {
     const int t = i >> 3, sub = i & 7;
@@ -199,18 +229,13 @@ struct RowCodes<PF_FMT_INT2> : RowCodes<PF_FMT_INT2_G128> {};
 template <>
 struct RowCodes<PF_FMT_INT3_G128> {
   uint32_t g[3], v[3], h15;
-  __device__ __forceinline__ void load3(uint32_t a0, uint32_t a12, int c) {  // words c, c+4, c+8 and 12
-    uint32_t w[3];
-    w[0] = lds32(a0);
-    w[1] = lds32(a0 + 16);
-    w[2] = lds32(a0 + 32);
-    const uint32_t w12 = lds32(a12);
+  __device__ __forceinline__ void set(const uint32_t (&raw)[4], int c) {
 #pragma unroll
     for (int t = 0; t < 3; ++t) {
-      g[t] = (w[t] & 0x0000FFFFu) | ((w[t] << 1) & 0xFFFF0000u);
+      g[t] = (raw[t] & 0x0000FFFFu) | ((raw[t] << 1) & 0xFFFF0000u);
       v[t] = g[t] >> 9;
     }
-    const uint32_t t12 = w12 >> (6 * c);
+    const uint32_t t12 = raw[3] >> (6 * c);
     h15 = (t12 & 7u) | ((t12 << 13) & 0x00070000u);
   }
   __device__ __forceinline__ uint32_t h(int i) const {
@@ -226,44 +251,202 @@ struct RowCodes<PF_FMT_INT3_G128> {
   }
 };
 
-__device__ __forceinline__ long long cta_of(long long u, long long U, long long P) {
-  return ((u + 1) * P + U - 1) / U - 1;
+// Raw words of row r, group j of a ring stage: INT3 words c, c+4, c+8 and 12;
+// INT4 words 4c..4c+3; INT2 words 2c, 2c+1 (128B-swizzled rows for INT4/INT2).
+template <int FMT>
+__device__ __forceinline__ void load_words(const unsigned char* stg, int r, int j, int c, uint32_t (&raw)[4]) {
+  constexpr int S = TmaFmt<FMT>::S;
+  if constexpr (FMT == PF_FMT_INT3_G128) {
+    const unsigned char* p = stg + r * (S * 52) + 52 * j;
+    raw[0] = lds<uint32_t>(p + 4 * c);
+    raw[1] = lds<uint32_t>(p + 16 + 4 * c);
+    raw[2] = lds<uint32_t>(p + 32 + 4 * c);
+    raw[3] = lds<uint32_t>(p + 48);
+  } else if constexpr (is_int4(FMT)) {
+    const uint32_t chunk = (uint32_t)((4 * j + c) ^ (r & 7));
+    const uint4 q = lds<uint4>(stg + r * 128 + (chunk << 4));
+    raw[0] = q.x; raw[1] = q.y; raw[2] = q.z; raw[3] = q.w;
+  } else {
+    const uint32_t chunk = (uint32_t)((2 * j + (c >> 1)) ^ (r & 7));
+    const uint2 q = lds<uint2>(stg + r * 128 + (chunk << 4) + ((c & 1) << 3));
+    raw[0] = q.x; raw[1] = q.y; raw[2] = 0u; raw[3] = 0u;
+  }
 }
 
-// Compile-time layout of one pipeline stage.
-template <int FMT, int NT, int LP, int TR, int SMODE>
-struct Stage {
-  static constexpr int S = TmaFmt<FMT>::S;
-  static constexpr int kRowsBlk = 16 * kCWarps * TR;
-  static constexpr uint32_t W = kRowsBlk * S * TmaFmt<FMT>::WPG * 4;
-  static constexpr uint32_t R = NT * 8 * LP * 8 + 64 * NT;  // x' record per group
-  static constexpr uint32_t X = S * R;
-  static constexpr uint32_t SC = SMODE == kScaleGroup ? kRowsBlk * S * 4 : (SMODE == kScaleRow ? kRowsBlk * 4 : 0);
-  static constexpr uint32_t XOFF = W;
-  static constexpr uint32_t SOFF = (XOFF + X + 127u) & ~127u;
-  static constexpr uint32_t BYTES = ((SOFF + SC + 1023u) & ~1023u);
-  static constexpr int NS = BYTES * 4 <= 112 * 1024 ? 4 : (BYTES * 3 <= 112 * 1024 ? 3 : 2);
-  static constexpr size_t SMEM = 1024 + (size_t)NS * BYTES + 2 * NS * 8;
+__device__ __forceinline__ const TmaJob& job_ref(const TmaArgs& a, int j) {
+  return j == 0 ? a.job[0] : j == 1 ? a.job[1] : j == 2 ? a.job[2] : a.job[3];
+}
+
+// Job holding global unit u.
+__device__ __forceinline__ int job_of(const TmaArgs& a, int u) {
+  int j = 0;
+#pragma unroll
+  for (int k = 1; k < kTmaMaxJobs; ++k)
+    if (k < a.n_jobs && u >= a.job[k].unit0) j = k;
+  return j;
+}
+
+// Group-relative columns (lo0, hi0, lo1, hi1) of a lane's B fragment and the
+// mantissa positions of its two code pairs.
+struct LaneCols {
+  int col[4];
+  int p[2];
 };
 
-template <int FMT, int NT, int LP, int TR, int SMODE>
+// ---- x' of one prep chunk (C = 32 E columns of token t, one warp): forward
+// block RWHT of x (signs, Walsh-Hadamard butterflies in registers and across
+// lanes, 1/sqrt(b)), then for every group of the chunk inside [g_lo, g_hi):
+// the group's power-of-two normaliser E (|x'| < 2^E), the tensor-core B
+// fragments of x' 2^(14 - p - E) split into fp16 hi + lo, and {Sx, 1024 2^E}.
+// Tokens t >= N write zeros.
+template <int NT, int LP, int E>
+__device__ __noinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype, int col0, int g_lo, int g_hi, int t,
+                                        unsigned char* xslot, float* scratch, int lane, LaneCols lc) {
+  constexpr int C = 32 * E;
+  constexpr int LG = 128 / E;  // lanes per 128-column group
+  const int b = jb.had_block;
+  float v[E];
+  if (t < N) {
+    const size_t base = (size_t)t * jb.K + col0 + E * lane;
+    if (x_dtype == PF_DTYPE_F32) {
+      const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(jb.x) + base);
+#pragma unroll
+      for (int q = 0; q < E / 4; ++q) {
+        const float4 f = __ldg(xp + q);
+        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+      }
+    } else {
+      const uint2* xp = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(jb.x) + base);
+#pragma unroll
+      for (int q = 0; q < E / 4; ++q) {
+        const uint2 r = __ldg(xp + q);
+        if (x_dtype == PF_DTYPE_F16) {
+          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+          const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+          v[4 * q] = f0.x; v[4 * q + 1] = f0.y; v[4 * q + 2] = f1.x; v[4 * q + 3] = f1.y;
+        } else {  // bf16: the upper half of an fp32
+          v[4 * q] = __uint_as_float(r.x << 16);
+          v[4 * q + 1] = __uint_as_float(r.x & 0xFFFF0000u);
+          v[4 * q + 2] = __uint_as_float(r.y << 16);
+          v[4 * q + 3] = __uint_as_float(r.y & 0xFFFF0000u);
+        }
+      }
+    }
+    if (b > 0) {
+      const int* sp = reinterpret_cast<const int*>(jb.signs + col0 + E * lane);
+#pragma unroll
+      for (int q = 0; q < E / 4; ++q) {
+        const int s4 = __ldg(sp + q);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if ((s4 >> (8 * e + 7)) & 1) v[4 * q + e] = -v[4 * q + e];
+      }
+#pragma unroll
+      for (int h = 1; h < E; h *= 2) {
+        if (h < b) {
+#pragma unroll
+          for (int e = 0; e < E; ++e)
+            if (!(e & h)) {
+              const float u = v[e], w = v[e + h];
+              v[e] = u + w;
+              v[e + h] = u - w;
+            }
+        }
+      }
+#pragma unroll
+      for (int m = 1; m < 32; m *= 2) {
+        if (m * E < b) {
+          const float sg = (lane & m) ? -1.f : 1.f;
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const float p = __shfl_xor_sync(0xffffffffu, v[e], m);
+            v[e] = fmaf(sg, v[e], p);
+          }
+        }
+      }
+      const float rs = jb.had_rscale;
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] *= rs;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = 0.f;
+  }
+  float amax = 0.f, sx = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    amax = fmaxf(amax, fabsf(v[e]));
+    sx += v[e];
+  }
+#pragma unroll
+  for (int o = 1; o < LG; o *= 2) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    sx += __shfl_xor_sync(0xffffffffu, sx, o);
+  }
+  int ex = 0;
+  if (amax > 0.f) frexpf(amax, &ex);  // amax < 2^ex
+#pragma unroll
+  for (int q = 0; q < E / 4; ++q)
+    *reinterpret_cast<float4*>(scratch + E * lane + 4 * q) =
+        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  __syncwarp();
+  const int j8 = lane >> 2, c = lane & 3;
+  const int fl = 8 * (t & 3) + c;  // B-fragment lane of the token's hi column (lo: + 4)
+  const int tile = t >> 2;
+#pragma unroll
+  for (int gi = 0; gi < C / 128; ++gi) {
+    const int g = col0 / 128 + gi;
+    const int eg = __shfl_sync(0xffffffffu, ex, gi * LG);
+    const float sg = __shfl_sync(0xffffffffu, sx, gi * LG);
+    if (g < g_lo || g >= g_hi) continue;
+    const float f0 = ldexpf(1.f, 14 - lc.p[0] - eg), f1 = ldexpf(1.f, 14 - lc.p[1] - eg);
+    const float* xs = scratch + gi * 128;
+    const float xv[4] = {xs[lc.col[0]] * f0, xs[lc.col[1]] * f0, xs[lc.col[2]] * f1, xs[lc.col[3]] * f1};
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const __half h0 = __float2half_rn(xv[2 * k]), h1 = __float2half_rn(xv[2 * k + 1]);
+      const __half l0 = __float2half_rn(xv[2 * k] - __half2float(h0));
+      const __half l1 = __float2half_rn(xv[2 * k + 1] - __half2float(h1));
+      hw[k] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      lw[k] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    unsigned char* rec = xslot + (size_t)(g - g_lo) * XRec<NT, LP>::R;
+    unsigned char* fr = rec + (tile * 4 + (j8 >> 1)) * LP * 16 + (j8 & 1) * 8;
+    *reinterpret_cast<uint2*>(fr + fl * 16) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(fr + (fl + 4) * 16) = make_uint2(lw[0], lw[1]);
+    if (lane == 0)
+      *reinterpret_cast<float2*>(rec + XRec<NT, LP>::FRAG + t * 16) = make_float2(sg, ldexpf(1024.f, eg));
+  }
+  __syncwarp();
+}
+
+template <int FMT, int NT, int LP, int SMODE>
 __global__ void __launch_bounds__(kThreadsT, 2)
-    gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap, const TmaArgs a) {
+    gemv_tma_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
+                    const __grid_constant__ CUtensorMap map2, const __grid_constant__ CUtensorMap map3,
+                    const __grid_constant__ TmaArgs a) {
   using F = TmaFmt<FMT>;
-  using L = Stage<FMT, NT, LP, TR, SMODE>;
+  using L = StageL<FMT, SMODE>;
+  using XR = XRec<NT, LP>;
   constexpr int S = F::S;
-  constexpr int NS = L::NS;
-  constexpr int kRowsBlk = L::kRowsBlk;
   constexpr int kOffset = IntFmt<FMT>::kOffset;
 
   asm volatile("griddepcontrol.launch_dependents;");
 
-  extern __shared__ unsigned char smem_raw[];
-  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t full0 = base + NS * L::BYTES, empty0 = full0 + 8 * NS;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ int abort_flag;
+  unsigned char* const base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int NS = a.NS, XS = a.XS;
+  constexpr uint32_t X = S * XR::R;
+  unsigned char* const xarea = base + NS * L::BYTES;
+  float* const scratch0 = reinterpret_cast<float*>(xarea + XS * X);
+  const uint32_t full0 = smem_u32(scratch0 + kCWarps * a.chunk_max);
+  const uint32_t empty0 = full0 + 8 * NS;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    abort_flag = 0;
     for (int s = 0; s < NS; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full0 + 8 * s), "r"(33));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty0 + 8 * s), "r"(kCWarps));
@@ -272,269 +455,336 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   }
   __syncthreads();
 
-  const long long U = a.n_units, P = gridDim.x, cta = blockIdx.x;
-  const int u0 = (int)(cta * U / P), u1 = (int)((cta + 1) * U / P);
+  const int U = a.n_units, P = gridDim.x, cta = blockIdx.x;
+  const int u0 = (int)((long long)cta * U / P), u1 = (int)((long long)(cta + 1) * U / P);
   const int nunits = u1 - u0;
-  const int spb = a.spb, M = a.M, G = a.G, N = a.N;
+  if (nunits <= 0) return;
+  const int N = a.N;
+
+  // unit walk: job, stage, row block (stage-major inside a job)
+  int j = job_of(a, u0);
+  int st, rb;
+  {
+    const TmaJob& jb = job_ref(a, j);
+    const int v = u0 - jb.unit0;
+    st = v / jb.n_rb;
+    rb = v - st * jb.n_rb;
+  }
 
   if (warp == kCWarps) {
     // ------------------------------------------------------------ producer
-    // lane 0 issues the copies; all lanes stage the units' scales in smem
-    int rb = u0 / spb, st = u0 % spb;
-    const int first = nunits < NS ? nunits : NS;
-    for (int it = 0; it < nunits; ++it) {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    if (lane == 0) {
+      for (int k = 0; k < a.n_jobs; ++k) {
+        const CUtensorMap* m = k == 0 ? &map0 : k == 1 ? &map1 : k == 2 ? &map2 : &map3;
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+      }
+    }
+    int it = 0;
+    for (; it < nunits; ++it) {
       const int slot = it % NS;
-      const uint32_t sb = base + slot * L::BYTES;
+      const uint32_t sb = smem_u32(base + slot * L::BYTES);
       if (it >= NS) {
         bool ok = true;
-        if (lane == 0) ok = mbar_wait(empty0 + 8 * slot, ((it / NS) & 1) ^ 1);
+        if (lane == 0) ok = mbar_wait(empty0 + 8 * slot, ((it / NS) & 1) ^ 1, &abort_flag);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) {
-          if (lane == 0) atomicExch(a.counters + kWsStatusSlot, (unsigned)PF_ERR_TIMEOUT);
-          return;
+          if (lane == 0) {
+            abort_flag = 1;
+            atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+          }
+          break;
         }
       }
+      const TmaJob& jb = job_ref(a, j);
       if (lane == 0) {
-        mbar_expect(full0 + 8 * slot, L::W + L::X);
-        tma_2d(sb, &tmap, st * S * F::WPG, rb * kRowsBlk, full0 + 8 * slot);
-        if (it >= first) bulk_1d(sb + L::XOFF, a.rec + (size_t)st * L::X, L::X, full0 + 8 * slot);
+        const CUtensorMap* m = j == 0 ? &map0 : j == 1 ? &map1 : j == 2 ? &map2 : &map3;
+        mbar_expect(full0 + 8 * slot, L::W);
+        tma_2d(sb, m, st * S * F::WPG, rb * kRowsBlk, full0 + 8 * slot, policy);
       }
       if constexpr (SMODE == kScaleGroup) {
-        const uint32_t* sc = static_cast<const uint32_t*>(a.scales);
-        const uint32_t* mn = reinterpret_cast<const uint32_t*>(a.mins);
+        const __half* sc = static_cast<const __half*>(jb.scales);
+        const __half* mn = jb.mins;
 #pragma unroll
         for (int k = 0; k < kRowsBlk / 32; ++k) {
           const int row = lane + 32 * k, grow = rb * kRowsBlk + row;
-          const size_t o = ((size_t)grow * G + (size_t)st * S) / 2;
-          uint32_t sv[S / 2], mv[S / 2];
-#pragma unroll
-          for (int q = 0; q < S / 2; ++q) {
-            sv[q] = grow < M ? __ldg(sc + o + q) : 0u;
-            mv[q] = grow < M ? __ldg(mn + o + q) : 0u;
-          }
-          const uint32_t d = sb + L::SOFF + row * (S * 4);
-#pragma unroll
-          for (int q = 0; q < S / 2; ++q) {
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(d + 4 * q), "r"(sv[q]));
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(d + 2 * S + 4 * q), "r"(mv[q]));
+          const bool ok = grow < jb.M;
+          const size_t o = ok ? (size_t)grow * jb.G + (size_t)st * S : 0;
+          const uint32_t d = sb + L::W + row * L::SROW;
+          if constexpr (S == 4) {
+            cp_async8(d, sc + o, ok ? 8u : 0u);
+            cp_async8(d + 8, mn + o, ok ? 8u : 0u);
+          } else {
+            cp_async4(d, sc + o, ok ? 4u : 0u);
+            cp_async4(d + 4, mn + o, ok ? 4u : 0u);
           }
         }
       } else if constexpr (SMODE == kScaleRow) {
-        const float* sc = static_cast<const float*>(a.scales);
+        const float* sc = static_cast<const float*>(jb.scales);
 #pragma unroll
         for (int k = 0; k < kRowsBlk / 32; ++k) {
           const int row = lane + 32 * k, grow = rb * kRowsBlk + row;
-          const float v = grow < M ? __ldg(sc + grow) : 0.f;
-          asm volatile("st.shared.f32 [%0], %1;" ::"r"(sb + L::SOFF + row * 4), "f"(v));
+          const bool ok = grow < jb.M;
+          cp_async4(sb + L::W + row * 4, sc + (ok ? grow : 0), ok ? 4u : 0u);
         }
       }
-      mbar_arrive(full0 + 8 * slot);
-      if (it == first - 1) {
-        // x' comes from the x-prep grid: wait for it, then fetch the records
-        // of the stages already in flight
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        if (lane == 0) {
-          int rb2 = u0 / spb, st2 = u0 % spb;
-          for (int k = 0; k < first; ++k) {
-            bulk_1d(base + k * L::BYTES + L::XOFF, a.rec + (size_t)st2 * L::X, L::X, full0 + 8 * k);
-            if (++st2 == spb) { st2 = 0; ++rb2; }
-          }
+      cp_async_arrive(full0 + 8 * slot);
+      if (++rb == jb.n_rb) {
+        rb = 0;
+        if (++st == jb.spb) {
+          st = 0;
+          ++j;
         }
       }
-      if (++st == spb) { st = 0; ++rb; }
+    }
+    // every copy this warp started lands before the CTA may exit (after a
+    // timeout: bounded waits on the code tiles that may still be in flight)
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (abort_flag && lane == 0) {
+      volatile int keep_waiting = 0;
+      for (int k = it > NS ? it - NS : 0; k < it; ++k) mbar_wait(full0 + 8 * (k % NS), (k / NS) & 1, &keep_waiting);
     }
     return;
   }
 
   // -------------------------------------------------------------- consumers
   const int c = lane & 3, rq = lane >> 2;
-  int rowb[TR][2];  // box rows of the thread
-#pragma unroll
-  for (int tr = 0; tr < TR; ++tr) {
-    rowb[tr][0] = warp * 16 * TR + tr * 16 + row_perm<FMT>(rq);
-    rowb[tr][1] = rowb[tr][0] + 8;
+  int rowb[2];  // the thread's two rows within the unit's block
+  rowb[0] = warp * 16 + row_perm<FMT>(rq);
+  rowb[1] = rowb[0] + 8;
+  LaneCols lc;
+  {
+    int lo, hi, p;
+    frag_cols2(FMT, c, 2 * rq, lo, hi, p);
+    lc.col[0] = lo; lc.col[1] = hi; lc.p[0] = p;
+    frag_cols2(FMT, c, 2 * rq + 1, lo, hi, p);
+    lc.col[2] = lo; lc.col[3] = hi; lc.p[1] = p;
   }
-  // per-row smem byte offsets of the thread's words (group 0), relative to the stage
-  uint32_t woff[TR][2], woff12[TR][2];
-#pragma unroll
-  for (int tr = 0; tr < TR; ++tr)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int r = rowb[tr][hh];
-      if constexpr (FMT == PF_FMT_INT3_G128) {
-        woff[tr][hh] = r * (S * 52) + 4 * c;
-        woff12[tr][hh] = r * (S * 52) + 48;
-      } else {
-        woff[tr][hh] = r * 128;
-        woff12[tr][hh] = r & 7;
+  float* const scratch = scratch0 + warp * a.chunk_max;
+  const uint32_t blane = (uint32_t)(lane & (LP - 1)) * 16;
+
+  // x' windows over the CTA's runs (consecutive units with one job and stage);
+  // XS runs are resident, in slot run % XS
+  int nruns;
+  {
+    const int jl = job_of(a, u1 - 1);
+    const TmaJob& jf = job_ref(a, j);
+    const TmaJob& jL = job_ref(a, jl);
+    nruns = (jL.run0 + (u1 - 1 - jL.unit0) / jL.n_rb) - (jf.run0 + (u0 - jf.unit0) / jf.n_rb) + 1;
+  }
+  int pj = j, pst = st;  // (job, stage) of the next run to prepare
+  int win_end = 0;
+  auto prep_window = [&](int r0) {
+    const int r1 = (r0 + XS < nruns) ? r0 + XS : nruns;
+    const int tslots = LP == 8 ? 1 : 4 * NT;
+    int task = 0;
+    for (int r = r0; r < r1; ++r) {
+      const TmaJob& jb = job_ref(a, pj);
+      const int b = jb.had_block;
+      const int E = b > 256 ? 16 : (b > 128 ? 8 : 4);
+      const int Cc = 32 * E;
+      const int g_lo = pst * S, g_hi = g_lo + S;
+      const int nchunk = (S * 128) / Cc > 0 ? (S * 128) / Cc : 1;
+      const int cbase = ((g_lo * 128) / Cc) * Cc;
+      unsigned char* xslot = xarea + (size_t)(r % XS) * X;
+      for (int ci = 0; ci < nchunk; ++ci)
+        for (int t = 0; t < tslots; ++t, ++task) {
+          if (task % kCWarps != warp) continue;
+          const int col0 = cbase + ci * Cc;
+          if (E == 4)
+            prep_chunk<NT, LP, 4>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
+          else if (E == 8)
+            prep_chunk<NT, LP, 8>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
+          else
+            prep_chunk<NT, LP, 16>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
+        }
+      if (++pst == jb.spb) {
+        pst = 0;
+        ++pj;
       }
     }
-  const uint32_t blane = (uint32_t)(lane & (LP - 1)) * 8;  // B fragment byte offset within a k-step row
+    win_end = r1;
+  };
 
-  float y[TR][NT][2];
-  int seg_st0 = 0;
-  int rb = u0 / spb, st = u0 % spb;
+  // x may be written by the preceding grid, and so may the workspace and y
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  prep_window(0);
+  consumers_sync();
+
+  // last stage unit of a row block for this warp's 16 rows: add the stage
+  // partials in order and write y (+ bias)
+  auto signal = [&](int jj, int rbb) {
+    const TmaJob& jb = job_ref(a, jj);
+    __threadfence();
+    __syncwarp();
+    unsigned* ctr = jb.counters + (size_t)rbb * kCWarps + warp;
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(ctr, 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev == (unsigned)jb.spb - 1) {
+      __threadfence();
+      const size_t stride = (size_t)kRowsBlk * N;
+      for (int idx = lane; idx < 16 * N; idx += 32) {
+        const int row = idx / N, t = idx - row * N;
+        const int grow = rbb * kRowsBlk + warp * 16 + row;
+        if (grow >= jb.M) continue;
+        const float* p = jb.partials + ((size_t)rbb * jb.spb * kRowsBlk + warp * 16 + row) * N + t;
+        float acc = 0.f;
+#pragma unroll 4
+        for (int s2 = 0; s2 < jb.spb; ++s2) acc += __ldcg(p + s2 * stride);
+        jb.y[(size_t)t * jb.M + grow] = acc + (jb.bias ? jb.bias[grow] : 0.f);
+      }
+      __syncwarp();
+      if (lane == 0) *ctr = 0u;
+    }
+  };
+
+  int run = 0, prev_j = j, prev_st = st;
+  int pend_j = -1, pend_rb = 0;  // unit whose partials are written but not yet counted
+  bool live = true;
   for (int it = 0; it < nunits; ++it) {
+    if (j != prev_j || st != prev_st) {
+      ++run;
+      prev_j = j;
+      prev_st = st;
+    }
+    if (run >= win_end) {  // same decision in every consumer warp
+      consumers_sync();
+      prep_window(win_end);
+      consumers_sync();
+    }
+    const TmaJob& jb = job_ref(a, j);
     const int slot = it % NS;
-    const uint32_t sb = base + slot * L::BYTES;
-    if (it == 0 || st == 0) {
-      seg_st0 = st;
-#pragma unroll
-      for (int tr = 0; tr < TR; ++tr)
-#pragma unroll
-        for (int i = 0; i < NT; ++i) y[tr][i][0] = y[tr][i][1] = 0.f;
+    const unsigned char* stg = base + slot * L::BYTES;
+    const unsigned char* xs = xarea + (size_t)(run % XS) * X;
+    if (live && !mbar_wait(full0 + 8 * slot, (it / NS) & 1, &abort_flag)) {
+      live = false;
+      if (lane == 0) {
+        abort_flag = 1;
+        atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+      }
     }
-    if (!mbar_wait(full0 + 8 * slot, (it / NS) & 1)) {
-      atomicExch(a.counters + kWsStatusSlot, (unsigned)PF_ERR_TIMEOUT);
-      return;
-    }
-    // scales / zero points of the thread's rows (fp32 row scale: per row)
-    uint32_t srow[TR][2][S / 2], mrow[TR][2][S / 2];
-    float frow[TR][2];
-#pragma unroll
-    for (int tr = 0; tr < TR; ++tr)
+    if (live) {
+      // scales / zero points of the thread's rows, then every code word of the unit
+      uint32_t sw[2][4];
+      float frow[2];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const int r = rowb[tr][hh];
+        const unsigned char* sp = stg + L::W + rowb[hh] * L::SROW;
         if constexpr (SMODE == kScaleGroup) {
-          const uint32_t d = sb + L::SOFF + r * (S * 4);
-#pragma unroll
-          for (int q = 0; q < S / 2; ++q) {
-            srow[tr][hh][q] = lds32(d + 4 * q);
-            mrow[tr][hh][q] = lds32(d + 2 * S + 4 * q);
-          }
-        } else if constexpr (SMODE == kScaleRow) {
-          frow[tr][hh] = __uint_as_float(lds32(sb + L::SOFF + r * 4));
-        } else {
-          frow[tr][hh] = a.tensor_scale;
-        }
-      }
-#pragma unroll
-    for (int j = 0; j < S; ++j) {
-      RowCodes<FMT> rc[TR][2];
-#pragma unroll
-      for (int tr = 0; tr < TR; ++tr)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          if constexpr (FMT == PF_FMT_INT3_G128) {
-            rc[tr][hh].load3(sb + woff[tr][hh] + 52 * j, sb + woff12[tr][hh] + 52 * j, c);
-          } else if constexpr (is_int4(FMT)) {
-            const uint32_t chunk = (uint32_t)((4 * j + c) ^ woff12[tr][hh]);
-            rc[tr][hh].load(sb + woff[tr][hh] + (chunk << 4));
+          if constexpr (S == 4) {
+            const uint4 q = lds<uint4>(sp);
+            sw[hh][0] = q.x; sw[hh][1] = q.y; sw[hh][2] = q.z; sw[hh][3] = q.w;
           } else {
-            const uint32_t chunk = (uint32_t)((2 * j + (c >> 1)) ^ woff12[tr][hh]);
-            rc[tr][hh].load(sb + woff[tr][hh] + (chunk << 4) + ((c & 1) << 3));
+            const uint2 q = lds<uint2>(sp);
+            sw[hh][0] = q.x; sw[hh][1] = 0u; sw[hh][2] = q.y; sw[hh][3] = 0u;
           }
+          frow[hh] = 0.f;
+        } else if constexpr (SMODE == kScaleRow) {
+          frow[hh] = lds<float>(sp);
+          sw[hh][0] = sw[hh][1] = sw[hh][2] = sw[hh][3] = 0u;
+        } else {
+          frow[hh] = jb.tensor_scale;
+          sw[hh][0] = sw[hh][1] = sw[hh][2] = sw[hh][3] = 0u;
         }
-      const uint32_t rec = sb + L::XOFF + j * L::R;
-#pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        // two independent accumulator chains per tile (even / odd k-steps);
-        // lanes whose B columns carry no token read a valid finite value
-        // (columns of an MMA are independent, the extra outputs are unused)
-        float acc[TR][2][4];
-#pragma unroll
-        for (int tr = 0; tr < TR; ++tr)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) acc[tr][e][0] = acc[tr][e][1] = acc[tr][e][2] = acc[tr][e][3] = 0.f;
-#pragma unroll
-        for (int j8 = 0; j8 < 8; ++j8) {
-          const uint2 b = lds64(rec + (uint32_t)((i * 8 + j8) * LP * 8) + blane);
-#pragma unroll
-          for (int tr = 0; tr < TR; ++tr)
-            mma16816(acc[tr][j8 & 1], rc[tr][0].h(2 * j8), rc[tr][1].h(2 * j8), rc[tr][0].h(2 * j8 + 1),
-                     rc[tr][1].h(2 * j8 + 1), b.x, b.y);
-        }
-        const int t = 4 * i + c;
-        const float4 g4 = lds128f(rec + NT * 8 * LP * 8 + (t < N ? t : 0) * 16);
-#pragma unroll
-        for (int tr = 0; tr < TR; ++tr)
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            float sv, mv;
-            if constexpr (SMODE == kScaleGroup) {
-              const float2 s2 = __half22float2(*reinterpret_cast<const __half2*>(&srow[tr][hh][j >> 1]));
-              const float2 m2 = __half22float2(*reinterpret_cast<const __half2*>(&mrow[tr][hh][j >> 1]));
-              sv = (j & 1) ? s2.y : s2.x;
-              mv = (j & 1) ? m2.y : m2.x;
-            } else {
-              sv = frow[tr][hh];
-              mv = -(float)kOffset * sv;
-            }
-            const float q = 1024.f * ((acc[tr][0][2 * hh] + acc[tr][1][2 * hh]) +
-                                      (acc[tr][0][2 * hh + 1] + acc[tr][1][2 * hh + 1]));
-            y[tr][i][hh] += (sv * g4.y) * q + mv * g4.x;
-          }
       }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8 * slot);
+      uint32_t raw[S][2][4];
+#pragma unroll
+      for (int g = 0; g < S; ++g)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) load_words<FMT>(stg, rowb[hh], g, c, raw[g][hh]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * slot);
 
-    // -------------------------------------------------- end of a row-block segment
-    const bool seg_end = (st == spb - 1 || it == nunits - 1);
-    if (seg_end) {
-      const bool whole = (seg_st0 == 0 && st == spb - 1);
-      if (whole) {
+      float y[NT][2];
 #pragma unroll
-        for (int tr = 0; tr < TR; ++tr)
+      for (int i = 0; i < NT; ++i) y[i][0] = y[i][1] = 0.f;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int grow = rb * kRowsBlk + rowb[tr][hh];
-            if (grow >= M) continue;
-            const float bv = a.bias ? a.bias[grow] : 0.f;
+      for (int pp = 0; pp < S / 2; ++pp) {
+        RowCodes<FMT> rc[2][2];
 #pragma unroll
-            for (int i = 0; i < NT; ++i) {
-              const int t = 4 * i + c;
-              if (t < N) a.y[(size_t)t * M + grow] = y[tr][i][hh] + bv;
+        for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) rc[gg][hh].set(raw[2 * pp + gg][hh], c);
+        float acc[2][NT][4];
+#pragma unroll
+        for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+          for (int i = 0; i < NT; ++i) acc[gg][i][0] = acc[gg][i][1] = acc[gg][i][2] = acc[gg][i][3] = 0.f;
+#pragma unroll
+        for (int jp = 0; jp < 4; ++jp)
+#pragma unroll
+          for (int i = 0; i < NT; ++i)
+#pragma unroll
+            for (int gg = 0; gg < 2; ++gg) {
+              const uint4 bq = lds<uint4>(xs + (2 * pp + gg) * XR::R + (i * 4 + jp) * LP * 16 + blane);
+              const RowCodes<FMT>& r0 = rc[gg][0];
+              const RowCodes<FMT>& r1 = rc[gg][1];
+              mma16816(acc[gg][i], r0.h(4 * jp), r1.h(4 * jp), r0.h(4 * jp + 1), r1.h(4 * jp + 1), bq.x, bq.y);
+              mma16816(acc[gg][i], r0.h(4 * jp + 2), r1.h(4 * jp + 2), r0.h(4 * jp + 3), r1.h(4 * jp + 3), bq.z,
+                       bq.w);
             }
-          }
-      } else {
-        const int my_slot = (rb == u0 / spb) ? (int)(2 * cta) : (int)(2 * cta + 1);
-        float* part = a.partials + (size_t)my_slot * kRowsBlk * N;
 #pragma unroll
-        for (int tr = 0; tr < TR; ++tr)
+        for (int gg = 0; gg < 2; ++gg) {
+          const int g = 2 * pp + gg;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-            for (int i = 0; i < NT; ++i) {
-              const int t = 4 * i + c;
-              if (t < N) part[(size_t)rowb[tr][hh] * N + t] = y[tr][i][hh];
-            }
-        __threadfence();
-        __syncwarp();
-        const long long first = cta_of((long long)rb * spb, U, P);
-        const long long last = cta_of((long long)(rb + 1) * spb - 1, U, P);
-        const unsigned n_share = (unsigned)(last - first + 1);
-        unsigned* ctr = a.counters + (size_t)rb * kCWarps + warp;
-        unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(ctr, 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == n_share - 1) {
-          __threadfence();
-#pragma unroll
-          for (int tr = 0; tr < TR; ++tr)
+          for (int i = 0; i < NT; ++i) {
+            const int t = LP == 8 ? 0 : 4 * i + c;
+            const float2 gs = lds<float2>(xs + g * XR::R + XR::FRAG + t * 16);
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              const int r = rowb[tr][hh], grow = rb * kRowsBlk + r;
-#pragma unroll
-              for (int i = 0; i < NT; ++i) {
-                const int t = 4 * i + c;
-                if (t >= N) continue;
-                float accv = 0.f;
-                for (long long k = first; k <= last; ++k) {
-                  const long long ku0 = k * U / P;
-                  const int ks = (rb == (int)(ku0 / spb)) ? (int)(2 * k) : (int)(2 * k + 1);
-                  accv += __ldcg(a.partials + ((size_t)ks * kRowsBlk + r) * N + t);
-                }
-                if (grow < M) a.y[(size_t)t * M + grow] = accv + (a.bias ? a.bias[grow] : 0.f);
+              float sv, mv;
+              if constexpr (SMODE == kScaleGroup) {
+                const uint32_t s2 = sw[hh][g >> 1], m2 = sw[hh][2 + (g >> 1)];
+                sv = __half2float(__ushort_as_half((unsigned short)((g & 1) ? (s2 >> 16) : (s2 & 0xFFFFu))));
+                mv = __half2float(__ushort_as_half((unsigned short)((g & 1) ? (m2 >> 16) : (m2 & 0xFFFFu))));
+              } else {
+                sv = frow[hh];
+                mv = -(float)kOffset * sv;
               }
+              const float q = acc[gg][i][2 * hh] + acc[gg][i][2 * hh + 1];
+              y[i][hh] += (sv * gs.y) * q + mv * gs.x;
             }
-          if (lane == 0) *ctr = 0u;
+          }
         }
       }
+
+      if (jb.spb == 1) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int grow = rb * kRowsBlk + rowb[hh];
+          if (grow >= jb.M) continue;
+          const float bv = jb.bias ? jb.bias[grow] : 0.f;
+#pragma unroll
+          for (int i = 0; i < NT; ++i) {
+            const int t = 4 * i + c;
+            if (t < N && (LP == 32 || c == 0)) jb.y[(size_t)t * jb.M + grow] = y[i][hh] + bv;
+          }
+        }
+      } else {
+        if (pend_j >= 0) signal(pend_j, pend_rb);
+        float* part = jb.partials + ((size_t)rb * jb.spb + st) * kRowsBlk * N;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int i = 0; i < NT; ++i) {
+            const int t = 4 * i + c;
+            if (t < N && (LP == 32 || c == 0)) part[(size_t)rowb[hh] * N + t] = y[i][hh];
+          }
+        pend_j = j;
+        pend_rb = rb;
+      }
     }
-    if (++st == spb) { st = 0; ++rb; }
+    if (++rb == jb.n_rb) {
+      rb = 0;
+      if (++st == jb.spb) {
+        st = 0;
+        ++j;
+      }
+    }
   }
+  if (live && pend_j >= 0) signal(pend_j, pend_rb);
 }
 
 // ------------------------------------------------------------------ host side
@@ -547,6 +797,17 @@ int sm_count() {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
   });
   return n;
+}
+
+// CTAs per SM of one launch (1 leaves room for the next launch's CTAs).
+int ctas_per_sm() {
+  static int v = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* e = getenv("PF_TMA_CTAS_PER_SM");
+    v = (e && atoi(e) == 2) ? 2 : 1;
+  });
+  return v;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -562,39 +823,79 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-constexpr int kTR = 1;  // 16-row MMA tiles per consumer warp (rows per block = 16 * kCWarps * kTR)
+int stage_groups(int fmt) { return is_int4(fmt) ? 2 : 4; }
+
+// Prep chunk (columns) of a rotation block size.
+int chunk_cols(int had_block) { return had_block > 256 ? 512 : (had_block > 128 ? 256 : 128); }
+
+// Global run index (job, stage) of unit u.
+int run_of(const TmaArgs& a, int u) {
+  int j = 0;
+  for (int k = 1; k < a.n_jobs; ++k)
+    if (u >= a.job[k].unit0) j = k;
+  return a.job[j].run0 + (u - a.job[j].unit0) / a.job[j].n_rb;
+}
 
 template <int FMT, int NT, int LP, int SMODE>
-cudaError_t launch_one(const TmaArgs& a, cudaStream_t s) {
+cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_words, cudaStream_t s) {
   using F = TmaFmt<FMT>;
-  using L = Stage<FMT, NT, LP, kTR, SMODE>;
+  using L = StageL<FMT, SMODE>;
+  using XR = XRec<NT, LP>;
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
-  CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)a.row_words, (cuuint64_t)a.M};
-  cuuint64_t strides[1] = {(cuuint64_t)a.row_words * 4};
-  cuuint32_t box[2] = {(cuuint32_t)(F::S * F::WPG), (cuuint32_t)L::kRowsBlk};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(a.codes), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  F::SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  const size_t smem = L::SMEM;
-  auto kern = gemv_tma_kernel<FMT, NT, LP, kTR, SMODE>;
-  static int occ = 0;
-  if (occ == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreadsT, smem) != cudaSuccess || n < 1) n = 1;
-    occ = n < kMaxCtasPerSm ? n : kMaxCtasPerSm;
+  CUtensorMap maps[kTmaMaxJobs];
+  for (int k = 0; k < a.n_jobs; ++k) {
+    cuuint64_t dims[2] = {(cuuint64_t)row_words[k], (cuuint64_t)a.job[k].M};
+    cuuint64_t strides[1] = {(cuuint64_t)row_words[k] * 4};
+    cuuint32_t box[2] = {(cuuint32_t)(F::S * F::WPG), (cuuint32_t)kRowsBlk};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&maps[k], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes[k]), dims, strides, box,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    F::SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   }
-  int grid = sm_count() * occ;
-  if (grid > a.n_units) grid = a.n_units;
-  if (grid < 1) grid = 1;
+  for (int k = a.n_jobs; k < kTmaMaxJobs; ++k) maps[k] = maps[0];
+
+  int P = sm_count() * ctas_per_sm();
+  if (P > a.n_units) P = a.n_units;
+  if (P < 1) P = 1;
+  int max_runs = 1;
+  for (int cta = 0; cta < P; ++cta) {
+    const int u0 = (int)((long long)cta * a.n_units / P), u1 = (int)((long long)(cta + 1) * a.n_units / P);
+    if (u1 <= u0) continue;
+    const int r = run_of(a, u1 - 1) - run_of(a, u0) + 1;
+    if (r > max_runs) max_runs = r;
+  }
+  const uint32_t X = F::S * XR::R;
+  const uint32_t fixed = (uint32_t)kCWarps * a.chunk_max * 4 + 16 * kMaxStages + 1024;
+  int XS = max_runs < kMaxXSlots ? max_runs : kMaxXSlots;
+  while (XS > 1 && fixed + XS * X + 3 * L::BYTES > (uint32_t)kSmemBudget) --XS;
+  int NS = (int)(((uint32_t)kSmemBudget - fixed - XS * X) / L::BYTES);
+  if (NS > kMaxStages) NS = kMaxStages;
+  if (NS < 2) return cudaErrorInvalidConfiguration;
+  a.NS = NS;
+  a.XS = XS;
+  const size_t smem = (size_t)1024 + (size_t)NS * L::BYTES + (size_t)XS * X + (size_t)kCWarps * a.chunk_max * 4 +
+                      16 * (size_t)NS;
+
+  auto kern = gemv_tma_kernel<FMT, NT, LP, SMODE>;
+  {
+    // the shared-memory opt-in is per device
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !done[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) done[dev] = true;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(P);
   cfg.blockDim = dim3(kThreadsT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -603,72 +904,143 @@ cudaError_t launch_one(const TmaArgs& a, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, map, a);
+  return cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], (const TmaArgs)a);
 }
 
 template <int FMT, int NT, int LP>
-cudaError_t launch_sm(const TmaArgs& a, int smode, cudaStream_t s) {
+cudaError_t launch_sm(TmaArgs& a, int smode, const void* const* codes, const int* rw, cudaStream_t s) {
   if constexpr (FMT == PF_FMT_INT4 || FMT == PF_FMT_INT2) {
-    if (smode == kScaleRow) return launch_one<FMT, NT, LP, kScaleRow>(a, s);
-    return launch_one<FMT, NT, LP, kScaleTensor>(a, s);
+    if (smode == kScaleRow) return launch_one<FMT, NT, LP, kScaleRow>(a, codes, rw, s);
+    return launch_one<FMT, NT, LP, kScaleTensor>(a, codes, rw, s);
   } else {
-    return launch_one<FMT, NT, LP, kScaleGroup>(a, s);
+    return launch_one<FMT, NT, LP, kScaleGroup>(a, codes, rw, s);
   }
 }
 
 template <int FMT>
-cudaError_t launch_fmt(const TmaArgs& a, int smode, cudaStream_t s) {
-  if (a.NT == 1) return a.N == 1 ? launch_sm<FMT, 1, 8>(a, smode, s) : launch_sm<FMT, 1, 32>(a, smode, s);
-  if (a.NT == 2) return launch_sm<FMT, 2, 32>(a, smode, s);
-  return launch_sm<FMT, 4, 32>(a, smode, s);
+cudaError_t launch_fmt(TmaArgs& a, int smode, const void* const* codes, const int* rw, cudaStream_t s) {
+  const int NT = a.N <= 4 ? 1 : (a.N <= 8 ? 2 : 4);
+  if (NT == 1) return a.N == 1 ? launch_sm<FMT, 1, 8>(a, smode, codes, rw, s) : launch_sm<FMT, 1, 32>(a, smode, codes, rw, s);
+  if (NT == 2) return launch_sm<FMT, 2, 32>(a, smode, codes, rw, s);
+  return launch_sm<FMT, 4, 32>(a, smode, codes, rw, s);
 }
 
 }  // namespace
 
-int tma_stage_groups(int fmt) {
+int tma_block_rows() { return kRowsBlk; }
+
+int row_words_of_tma(int fmt, int K) {
   switch (fmt) {
-    case PF_FMT_INT4_G128:
-    case PF_FMT_INT4: return TmaFmt<PF_FMT_INT4_G128>::S;
-    case PF_FMT_INT2_G128:
-    case PF_FMT_INT2: return TmaFmt<PF_FMT_INT2_G128>::S;
-    default: return TmaFmt<PF_FMT_INT3_G128>::S;
+    case PF_FMT_INT4_G128: return (K / 128) * 16;
+    case PF_FMT_INT3_G128: return (K / 128) * 13;
+    case PF_FMT_INT2_G128: return (K / 128) * 8;
+    case PF_FMT_INT4: return K / 8;
+    case PF_FMT_INT3: return 3 * K / 32;
+    case PF_FMT_INT2: return K / 16;
+    default: return 0;
   }
 }
+int tma_stage_groups(int fmt) { return stage_groups(fmt); }
 
-bool tma_eligible(int fmt, int M, int K, const void* codes) {
-  if (!(fmt == PF_FMT_INT4_G128 || fmt == PF_FMT_INT3_G128 || fmt == PF_FMT_INT2_G128 || fmt == PF_FMT_INT4 ||
-        fmt == PF_FMT_INT2))
+bool tma_eligible(const TmaWeight& w) {
+  const int f = w.format;
+  if (!(f == PF_FMT_INT4_G128 || f == PF_FMT_INT3_G128 || f == PF_FMT_INT2_G128 || f == PF_FMT_INT4 ||
+        f == PF_FMT_INT2))
     return false;
-  if (K % 512 != 0) return false;
-  if (reinterpret_cast<uintptr_t>(codes) % 16) return false;
-  const long long n_rb = (M + 16 * kCWarps * kTR - 1) / (16 * kCWarps * kTR);
+  if (w.K <= 0 || w.K % 512 != 0 || w.M <= 0) return false;
+  if (reinterpret_cast<uintptr_t>(w.codes) % 16) return false;
+  const uintptr_t sal = is_group_int_format(f) ? (uintptr_t)(stage_groups(f) * 2) : 4;
+  if (w.scales && reinterpret_cast<uintptr_t>(w.scales) % sal) return false;
+  if (w.mins && reinterpret_cast<uintptr_t>(w.mins) % sal) return false;
+  if (w.had_block != 0) {
+    if (w.had_block > 512 || (w.had_block & (w.had_block - 1)) || w.K % w.had_block) return false;
+    if (!w.signs || reinterpret_cast<uintptr_t>(w.signs) % 4) return false;
+  }
+  const long long n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
   if (n_rb * kCWarps >= (long long)kWsStatusSlot) return false;
   return encode_fn() != nullptr;
 }
 
-// CTAs of one launch: never more than the units, at most kMaxCtasPerSm per SM
-// (shared memory bounds the real residency; the partial-slot area is sized
-// for this count).
-int tma_block_rows() { return 16 * kCWarps * kTR; }
+size_t tma_counter_slots(const TmaWeight& w) { return (size_t)((w.M + kRowsBlk - 1) / kRowsBlk) * kCWarps; }
 
-int tma_grid(int fmt, int NT, int n_units) {
-  (void)fmt;
-  (void)NT;
-  long long g = (long long)sm_count() * kMaxCtasPerSm;
-  if (g > n_units) g = n_units;
-  return (int)(g < 1 ? 1 : g);
+size_t tma_partial_bytes(const TmaWeight& w, int N) {
+  const size_t n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
+  const size_t spb = (size_t)(w.K / 128) / stage_groups(w.format);
+  if (spb <= 1) return 0;
+  const size_t b = n_rb * spb * kRowsBlk * (size_t)N * sizeof(float);
+  return (b + 255) / 256 * 256;
 }
 
-cudaError_t launch_gemv_tma(int fmt, const TmaArgs& a, int smode, int subnormal, cudaStream_t s) {
-  (void)subnormal;
-  switch (fmt) {
-    case PF_FMT_INT4_G128: return launch_fmt<PF_FMT_INT4_G128>(a, smode, s);
-    case PF_FMT_INT3_G128: return launch_fmt<PF_FMT_INT3_G128>(a, smode, s);
-    case PF_FMT_INT2_G128: return launch_fmt<PF_FMT_INT2_G128>(a, smode, s);
-    case PF_FMT_INT4: return launch_fmt<PF_FMT_INT4>(a, smode, s);
-    case PF_FMT_INT2: return launch_fmt<PF_FMT_INT2>(a, smode, s);
-    default: return cudaErrorInvalidValue;
+int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int x_dtype, void* workspace,
+                    cudaStream_t s, cudaError_t* err) {
+  *err = cudaSuccess;
+  if (count < 1 || count > kTmaMaxJobs || N < 1 || N > kMaxGemvTokens) return PF_ERR_INVALID_ARGUMENT;
+  TmaArgs a;
+  memset(&a, 0, sizeof(a));
+  const void* codes[kTmaMaxJobs];
+  int rw[kTmaMaxJobs];
+  unsigned* counters = static_cast<unsigned*>(workspace);
+  char* part = static_cast<char*>(workspace) + kWsCounterBytes;
+  size_t slot = 0;
+  int unit0 = 0, run0 = 0, chunk = 128;
+  const int fmt = ws[0].format;
+  const int S = stage_groups(fmt);
+  for (int k = 0; k < count; ++k) {
+    const TmaWeight& w = ws[k];
+    TmaJob& jb = a.job[k];
+    if (w.format != fmt) return PF_ERR_INVALID_ARGUMENT;
+    jb.scales = w.scales;
+    jb.mins = static_cast<const __half*>(w.mins);
+    jb.tensor_scale = w.tensor_scale;
+    jb.x = io[k].x;
+    jb.signs = w.had_block ? w.signs : nullptr;
+    jb.had_block = w.had_block;
+    jb.had_rscale = w.had_block ? 1.f / sqrtf((float)w.had_block) : 1.f;
+    jb.bias = io[k].bias;
+    jb.y = io[k].y;
+    jb.M = w.M;
+    jb.K = w.K;
+    jb.G = w.K / 128;
+    jb.n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
+    jb.spb = jb.G / S;
+    jb.unit0 = unit0;
+    jb.run0 = run0;
+    jb.counters = counters + slot;
+    jb.partials = reinterpret_cast<float*>(part);
+    slot += tma_counter_slots(w);
+    part += tma_partial_bytes(w, N);
+    unit0 += jb.n_rb * jb.spb;
+    run0 += jb.spb;
+    const int cc = chunk_cols(w.had_block);
+    if (cc > chunk) chunk = cc;
+    codes[k] = w.codes;
+    rw[k] = row_words_of_tma(fmt, w.K);
   }
+  if (slot >= kWsStatusSlot) return PF_ERR_SHAPE;
+  a.n_jobs = count;
+  a.n_units = unit0;
+  a.N = N;
+  a.x_dtype = x_dtype;
+  a.chunk_max = chunk;
+  a.status = counters + kWsStatusSlot;
+  cudaError_t e;
+  switch (fmt) {
+    case PF_FMT_INT4_G128: e = launch_fmt<PF_FMT_INT4_G128>(a, kScaleGroup, codes, rw, s); break;
+    case PF_FMT_INT3_G128: e = launch_fmt<PF_FMT_INT3_G128>(a, kScaleGroup, codes, rw, s); break;
+    case PF_FMT_INT2_G128: e = launch_fmt<PF_FMT_INT2_G128>(a, kScaleGroup, codes, rw, s); break;
+    case PF_FMT_INT4:
+      e = launch_fmt<PF_FMT_INT4>(a, ws[0].scales ? kScaleRow : kScaleTensor, codes, rw, s);
+      break;
+    case PF_FMT_INT2:
+      e = launch_fmt<PF_FMT_INT2>(a, ws[0].scales ? kScaleRow : kScaleTensor, codes, rw, s);
+      break;
+    default: return PF_ERR_UNSUPPORTED;
+  }
+  if (e != cudaSuccess) {
+    *err = e;
+    return PF_ERR_CUDA;
+  }
+  return PF_OK;
 }
 
 }  // namespace pfb

@@ -39,7 +39,8 @@ ERR_TIMEOUT = 7
 # Every symbol include/polarflash_b200.h declares.
 EXPORTS = (
     "pf_version", "pf_status_string", "pf_last_cuda_error", "pf_qweight_check",
-    "pf_qlinear_workspace_size", "pf_qlinear_prepare", "pf_qlinear_run", "pf_qlinear", "pf_dequant", "pf_unpack_codes", "pf_rwht",
+    "pf_qlinear_workspace_size", "pf_qlinear", "pf_qlinear_group_workspace_size", "pf_qlinear_group",
+    "pf_dequant", "pf_unpack_codes", "pf_rwht",
     "pf_native_gemv_int4", "pf_native_gemv_int2", "pf_native_gemm_int4", "pf_qlinear_noalloc",
 )
 
@@ -92,10 +93,12 @@ def load():
     L.pf_qlinear_workspace_size.argtypes = [QW, I, ctypes.POINTER(SZ)]
     L.pf_qlinear.restype = I
     L.pf_qlinear.argtypes = [QW, P, I, I, P, P, P, SZ, P]
-    L.pf_qlinear_prepare.restype = I
-    L.pf_qlinear_prepare.argtypes = [QW, P, I, I, P, SZ, P]
-    L.pf_qlinear_run.restype = I
-    L.pf_qlinear_run.argtypes = [QW, I, P, P, P, SZ, P]
+    PP = ctypes.POINTER(ctypes.c_void_p)
+    QWP = ctypes.POINTER(QW)
+    L.pf_qlinear_group_workspace_size.restype = I
+    L.pf_qlinear_group_workspace_size.argtypes = [I, QWP, I, ctypes.POINTER(SZ)]
+    L.pf_qlinear_group.restype = I
+    L.pf_qlinear_group.argtypes = [I, QWP, PP, I, I, PP, PP, P, SZ, P]
     L.pf_dequant.restype = I
     L.pf_dequant.argtypes = [QW, P, I, P]
     L.pf_unpack_codes.restype = I

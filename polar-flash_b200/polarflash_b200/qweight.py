@@ -249,36 +249,67 @@ def qlinear(qw: QWeight, x: torch.Tensor, bias: Optional[torch.Tensor] = None,
     return y.reshape(*lead, qw.M)
 
 
-def qlinear_multi(qws, x: torch.Tensor, biases=None, workspace: Optional[torch.Tensor] = None, outs=None):
-    """[x @ W_i^T (+ b_i)] for weights sharing format, K and rotation (q/k/v,
-    gate/up): x is prepared once (pf_qlinear_prepare), then one pf_qlinear_run
-    per weight.  N <= 16 rows per call."""
-    qw0 = qws[0]
-    for q in qws[1:]:
-        if (q.format, q.K, q.had_block) != (qw0.format, qw0.K, qw0.had_block):
-            raise ValueError("qlinear_multi needs weights with the same format, K and rotation")
-    lead = x.shape[:-1]
-    x2 = _x2(qw0, x)
-    N = x2.shape[0]
-    if N > 16:
-        return [qlinear(q, x, None if biases is None else biases[i]) for i, q in enumerate(qws)]
-    need = max(q.workspace_bytes(N) for q in qws)
-    stream = torch.cuda.current_stream(x.device)
-    ws = workspace if workspace is not None else globals()["workspace"](x.device, need, stream)
-    L = _lib.load()
-    sp = ctypes.c_void_p(stream.cuda_stream)
-    _lib.check(L.pf_qlinear_prepare(ctypes.byref(qw0.descriptor()), _ptr(x2), _X_DTYPES[x2.dtype], N, _ptr(ws),
-                                    ws.numel(), sp), "pf_qlinear_prepare")
-    ys = []
+def _desc_array(qws):
+    n = len(qws)
+    arr = (ctypes.POINTER(_lib.PFQWeight) * n)()
     for i, q in enumerate(qws):
-        y = outs[i] if outs is not None else torch.empty(N, q.M, dtype=torch.float32, device=x.device)
-        b = None
-        if biases is not None and biases[i] is not None:
-            b = biases[i].to(device=x.device, dtype=torch.float32).contiguous()
-        _lib.check(L.pf_qlinear_run(ctypes.byref(q.descriptor()), N, _ptr(b), _ptr(y), _ptr(ws), ws.numel(), sp),
-                   "pf_qlinear_run")
-        ys.append(y.reshape(*lead, q.M))
-    return ys
+        arr[i] = ctypes.pointer(q.descriptor())
+    return arr
+
+
+def group_workspace_bytes(qws, N: int) -> int:
+    """Device workspace bytes of one qlinear_group call over `qws`."""
+    out = ctypes.c_size_t(0)
+    _lib.check(_lib.load().pf_qlinear_group_workspace_size(len(qws), _desc_array(qws), N, ctypes.byref(out)),
+               "pf_qlinear_group_workspace_size")
+    return int(out.value)
+
+
+def qlinear_group(qws, xs, biases=None, workspace: Optional[torch.Tensor] = None, outs=None):
+    """[x_i @ W_i^T (+ b_i)] through one pf_qlinear_group call: weights of one
+    INT format that the streaming GEMV serves run as ONE launch per 16 tokens
+    (up to four weights per launch); other weights run one after another.
+    Every x_i has the same leading shape and dtype."""
+    n = len(qws)
+    if n == 0:
+        return []
+    lead = xs[0].shape[:-1]
+    x2s = [_x2(q, x) for q, x in zip(qws, xs)]
+    dt = x2s[0].dtype
+    if any(x.dtype != dt for x in x2s):
+        x2s = [x.float() for x in x2s]
+        dt = torch.float32
+    N = x2s[0].shape[0]
+    if any(x.shape[0] != N for x in x2s):
+        raise ValueError("qlinear_group inputs need the same number of rows")
+    dev = x2s[0].device
+    ys = [outs[i] if outs is not None else torch.empty(N, q.M, dtype=torch.float32, device=dev)
+          for i, q in enumerate(qws)]
+    if N == 0:
+        return [y.reshape(*lead, q.M) for y, q in zip(ys, qws)]
+    bs = []
+    for i in range(n):
+        b = None if biases is None else biases[i]
+        bs.append(b.to(device=dev, dtype=torch.float32).contiguous() if b is not None else None)
+    need = group_workspace_bytes(qws, N)
+    stream = torch.cuda.current_stream(dev)
+    ws = workspace if workspace is not None else globals()["workspace"](dev, need, stream)
+    if ws.numel() < need:
+        raise ValueError(f"workspace of {ws.numel()} bytes < {need} needed")
+    VP = ctypes.c_void_p * n
+    xa = VP(*[x.data_ptr() for x in x2s])
+    ya = VP(*[y.data_ptr() for y in ys])
+    ba = VP(*[b.data_ptr() if b is not None else None for b in bs])
+    st = _lib.load().pf_qlinear_group(n, _desc_array(qws), xa, _X_DTYPES[dt], N, ba, ya, _ptr(ws), ws.numel(),
+                                      ctypes.c_void_p(stream.cuda_stream))
+    _lib.check(st, "pf_qlinear_group")
+    return [y.reshape(*lead, q.M) for y, q in zip(ys, qws)]
+
+
+def qlinear_multi(qws, x: torch.Tensor, biases=None, workspace: Optional[torch.Tensor] = None, outs=None):
+    """[x @ W_i^T (+ b_i)] for weights sharing one input (q/k/v, gate/up):
+    qlinear_group with the same x for every weight."""
+    return qlinear_group(qws, [x] * len(qws), biases, workspace, outs)
 
 
 def dequantize(qw: QWeight, inverse_rwht: bool = True) -> torch.Tensor:
