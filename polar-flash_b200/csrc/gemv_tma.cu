@@ -1,35 +1,33 @@
 // Streaming fused dequant-GEMV for the INT formats (N <= 16 tokens): one
 // launch computes y = x W^T for up to four weights ("jobs") of one format.
 //
-// CTA = 8 consumer warps + 1 producer warp, one CTA per SM and at most
-// ~110 KB of shared memory, so the CTAs of the next launch on the stream fit
-// beside this one and stream their weights while this launch drains
-// (programmatic dependent launch: every CTA signals its dependents at once;
-// only the consumer warps wait for the preceding grid, before they read x or
-// write to global memory; packed weights and scales are never written by a
-// kernel that precedes a GEMV in this library).
-//
 // Work unit = (job, 128-row block, stage of S groups of 128 columns), dealt to
 // the CTAs stream-K style in stage-major order: a CTA's consecutive units
 // share a column stage, so it transforms only the one or two stages of x it
 // needs (x' = forward block RWHT of x, scaled and split for the tensor cores)
 // straight into shared memory; there is no separate x-prep launch.
-//   producer warp: lane 0 issues the 2-D TMA copy of a unit's packed codes
-//     (L2 evict-first); all lanes copy the unit's fp16 scales / zero points
-//     with cp.async and let the copies themselves arrive on the stage's
-//     mbarrier, so no lane ever waits for a global load.
-//   consumer warps: 16 rows each.  A unit's code words are read from shared
-//     memory into registers at once (the ring slot is released right away),
-//     every code pair becomes one AND (exact subnormal fp16 q 2^(p-24)), and
-//     mma.sync m16n8k16 multiplies two groups at a time against the B
-//     fragments of x' (fp16 hi / lo halves of x' in the two columns of each
-//     token).
+//
+// CTA = 8 warps, two CTAs per SM.  Every warp owns 16 rows of each unit and
+// streams them itself through a private ring of shared-memory slots: lane 0
+// issues the 2-D TMA copy of its 16 x (S groups) tile of packed codes (L2
+// evict-first), all lanes copy the tile's fp16 scales / zero points with
+// cp.async, and the copies themselves arrive on the slot's mbarrier.  A warp
+// refills a slot it has just consumed, so warps never wait for each other
+// except at the x' preparation barrier, and the weights of the first slots
+// are requested before the kernel waits for the preceding grid
+// (programmatic dependent launch; packed weights and scales are never written
+// by a kernel that precedes a GEMV in this library).
+//
+// Compute: the unit's code words are read into registers, every code pair
+// becomes one AND (exact subnormal fp16 q 2^(p-24)), and mma.sync m16n8k16
+// multiplies two groups at a time against the B fragments of x' (fp16 hi / lo
+// halves of x' in the two columns of each token).
 // Per 128-column group:  sum w x' = s 2^E Q + m Sx  with  Q = sum q x'/2^E.
-// Each unit's 128 x N partial sums go to the workspace; the last of a row
-// block's stage units (per-warp arrival counters) adds them in stage order
-// (deterministic) and writes y.  Every wait is bounded (2 s, %globaltimer):
-// on expiry the kernel records PF_ERR_TIMEOUT in the workspace status word,
-// skips every later wait and finishes.
+// Each unit's 16 x N partial sums per warp go to the workspace; a per-warp
+// arrival counter per row block finds the last stage unit, whose warp adds the
+// stage partials in stage order (deterministic) and writes y.  Every wait is
+// bounded (2 s, %globaltimer): on expiry the kernel records PF_ERR_TIMEOUT in
+// the workspace status word, skips every later wait and finishes.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdlib.h>
@@ -44,14 +42,16 @@ namespace pfb {
 
 namespace {
 
-constexpr int kCWarps = 8;                     // consumer warps per CTA
-constexpr int kThreadsT = (kCWarps + 1) * 32;  // + 1 producer warp
-constexpr int kRowsBlk = 16 * kCWarps;         // rows per unit
-constexpr int kBarConsumers = 1;               // named barrier of the consumer warps
+constexpr int kWarps = 8;                  // warps per CTA
+constexpr int kThreadsT = kWarps * 32;
+constexpr int kWarpRows = 16;              // rows per warp and unit (one MMA row tile)
+constexpr int kRowsBlk = kWarpRows * kWarps;  // rows per unit
 constexpr unsigned long long kWaitNs = 2000000000ull;
-constexpr int kSmemBudget = 110 * 1024;  // dynamic smem per CTA (two CTAs per SM)
 constexpr int kMaxStages = 8;
 constexpr int kMaxXSlots = 3;
+
+// Dynamic shared memory per CTA: two CTAs share an SM's 228 KB.
+int smem_budget(int ctas_per_sm) { return ctas_per_sm >= 2 ? 110 * 1024 : 200 * 1024; }
 
 template <int FMT>
 struct TmaFmt;
@@ -78,13 +78,15 @@ struct TmaFmt<PF_FMT_INT3_G128> {
 constexpr bool is_int4(int f) { return f == PF_FMT_INT4_G128 || f == PF_FMT_INT4; }
 constexpr bool is_int2(int f) { return f == PF_FMT_INT2_G128 || f == PF_FMT_INT2; }
 
-// Shared-memory layout of one ring stage: packed codes, then scales.
+// One slot of a warp's ring: the 16-row code tile, then its scales.  Tiles
+// under the 128B swizzle start on a 1024-byte boundary.
 template <int FMT, int SMODE>
-struct StageL {
+struct WarpSlot {
   static constexpr int S = TmaFmt<FMT>::S;
-  static constexpr uint32_t W = kRowsBlk * S * TmaFmt<FMT>::WPG * 4;
+  static constexpr uint32_t W = kWarpRows * S * TmaFmt<FMT>::WPG * 4;
   static constexpr uint32_t SROW = SMODE == kScaleGroup ? S * 4 : (SMODE == kScaleRow ? 4 : 0);  // bytes per row
-  static constexpr uint32_t BYTES = (W + kRowsBlk * SROW + 1023u) & ~1023u;
+  static constexpr uint32_t ALIGN = TmaFmt<FMT>::SW128 ? 1024u : 128u;
+  static constexpr uint32_t BYTES = (W + kWarpRows * SROW + ALIGN - 1) & ~(ALIGN - 1);
 };
 
 // x' record of one 128-column group: [NT tiles][4 k-step pairs][LP lanes]
@@ -149,9 +151,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const v
 __device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar,
                                        uint64_t policy) {
   asm volatile(
@@ -170,9 +169,6 @@ __device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, uint32_
 // arrive on `bar` once this thread's earlier cp.async copies have landed
 __device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void consumers_sync() {
-  asm volatile("bar.sync %0, %1;" ::"n"(kBarConsumers), "n"(kCWarps * 32) : "memory");
 }
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -427,7 +423,7 @@ __global__ void __launch_bounds__(kThreadsT, 2)
                     const __grid_constant__ CUtensorMap map2, const __grid_constant__ CUtensorMap map3,
                     const __grid_constant__ TmaArgs a) {
   using F = TmaFmt<FMT>;
-  using L = StageL<FMT, SMODE>;
+  using L = WarpSlot<FMT, SMODE>;
   using XR = XRec<NT, LP>;
   constexpr int S = F::S;
   constexpr int kOffset = IntFmt<FMT>::kOffset;
@@ -439,18 +435,15 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   unsigned char* const base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int NS = a.NS, XS = a.XS;
   constexpr uint32_t X = S * XR::R;
-  unsigned char* const xarea = base + NS * L::BYTES;
-  float* const scratch0 = reinterpret_cast<float*>(xarea + XS * X);
-  const uint32_t full0 = smem_u32(scratch0 + kCWarps * a.chunk_max);
-  const uint32_t empty0 = full0 + 8 * NS;
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    abort_flag = 0;
-    for (int s = 0; s < NS; ++s) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full0 + 8 * s), "r"(33));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty0 + 8 * s), "r"(kCWarps));
-    }
+  unsigned char* const ring = base + (size_t)warp * NS * L::BYTES;  // this warp's slots
+  unsigned char* const xarea = base + (size_t)kWarps * NS * L::BYTES;
+  float* const scratch = reinterpret_cast<float*>(xarea + XS * X) + warp * a.chunk_max;
+  const uint32_t full0 = smem_u32(reinterpret_cast<float*>(xarea + XS * X) + kWarps * a.chunk_max) + warp * NS * 8;
+
+  if (threadIdx.x == 0) abort_flag = 0;
+  if (lane == 0) {
+    for (int s = 0; s < NS; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full0 + 8 * s), "r"(33));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -460,99 +453,84 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   const int nunits = u1 - u0;
   if (nunits <= 0) return;
   const int N = a.N;
+  const int c = lane & 3, rq = lane >> 2;
 
-  // unit walk: job, stage, row block (stage-major inside a job)
-  int j = job_of(a, u0);
-  int st, rb;
+  // ---- load side: this warp's next unit to request (job, stage, row block)
+  int fj = job_of(a, u0), fst, frb;
+  {
+    const TmaJob& jb = job_ref(a, fj);
+    const int v = u0 - jb.unit0;
+    fst = v / jb.n_rb;
+    frb = v - fst * jb.n_rb;
+  }
+  const CUtensorMap* fmap = nullptr;
+  const __half* fsc = nullptr;
+  const __half* fmn = nullptr;
+  int fM = 0, fG = 0, fnrb = 1, fspb = 1;
+  auto load_fjob = [&]() {
+    const TmaJob& jb = job_ref(a, fj);
+    fmap = fj == 0 ? &map0 : fj == 1 ? &map1 : fj == 2 ? &map2 : &map3;
+    fsc = static_cast<const __half*>(jb.scales);
+    fmn = jb.mins;
+    fM = jb.M;
+    fG = jb.G;
+    fnrb = jb.n_rb;
+    fspb = jb.spb;
+  };
+  load_fjob();
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  const uint32_t ring_s = smem_u32(ring);
+  // request the next unit into `slot` (which this warp no longer reads)
+  auto request = [&](int slot) {
+    const uint32_t sb = ring_s + slot * L::BYTES, bar = full0 + 8 * slot;
+    const int row0 = frb * kRowsBlk + warp * kWarpRows;
+    __syncwarp();
+    if (lane == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_expect(bar, L::W);
+      tma_2d(sb, fmap, fst * S * F::WPG, row0, bar, policy);
+    }
+    if constexpr (SMODE == kScaleGroup) {
+      const int row = lane & 15, which = lane >> 4, grow = row0 + row;
+      const bool ok = grow < fM;
+      const __half* src = (which ? fmn : fsc) + (ok ? (size_t)grow * fG + (size_t)fst * S : 0);
+      const uint32_t d = sb + L::W + row * L::SROW + which * (S * 2);
+      if constexpr (S == 4)
+        cp_async8(d, src, ok ? 8u : 0u);
+      else
+        cp_async4(d, src, ok ? 4u : 0u);
+    } else if constexpr (SMODE == kScaleRow) {
+      const int grow = row0 + (lane & 15);
+      const bool ok = lane < 16 && grow < fM;
+      if (lane < 16)
+        cp_async4(sb + L::W + lane * 4, reinterpret_cast<const float*>(fsc) + (ok ? grow : 0), ok ? 4u : 0u);
+    }
+    cp_async_arrive(bar);
+    if (++frb == fnrb) {
+      frb = 0;
+      if (++fst == fspb) {
+        fst = 0;
+        ++fj;
+        if (fj < a.n_jobs) load_fjob();
+      }
+    }
+  };
+  // the first NS - 1 units: weights and scales never come from the preceding grid
+  int requested = 0;
+  for (; requested < NS - 1 && requested < nunits; ++requested) request(requested);
+
+  // ---- compute side: unit walk (job, stage, row block) and its x' runs
+  int j = job_of(a, u0), st, rb;
   {
     const TmaJob& jb = job_ref(a, j);
     const int v = u0 - jb.unit0;
     st = v / jb.n_rb;
     rb = v - st * jb.n_rb;
   }
-
-  if (warp == kCWarps) {
-    // ------------------------------------------------------------ producer
-    uint64_t policy;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-    if (lane == 0) {
-      for (int k = 0; k < a.n_jobs; ++k) {
-        const CUtensorMap* m = k == 0 ? &map0 : k == 1 ? &map1 : k == 2 ? &map2 : &map3;
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
-      }
-    }
-    int it = 0;
-    for (; it < nunits; ++it) {
-      const int slot = it % NS;
-      const uint32_t sb = smem_u32(base + slot * L::BYTES);
-      if (it >= NS) {
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait(empty0 + 8 * slot, ((it / NS) & 1) ^ 1, &abort_flag);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) {
-          if (lane == 0) {
-            abort_flag = 1;
-            atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
-          }
-          break;
-        }
-      }
-      const TmaJob& jb = job_ref(a, j);
-      if (lane == 0) {
-        const CUtensorMap* m = j == 0 ? &map0 : j == 1 ? &map1 : j == 2 ? &map2 : &map3;
-        mbar_expect(full0 + 8 * slot, L::W);
-        tma_2d(sb, m, st * S * F::WPG, rb * kRowsBlk, full0 + 8 * slot, policy);
-      }
-      if constexpr (SMODE == kScaleGroup) {
-        const __half* sc = static_cast<const __half*>(jb.scales);
-        const __half* mn = jb.mins;
-#pragma unroll
-        for (int k = 0; k < kRowsBlk / 32; ++k) {
-          const int row = lane + 32 * k, grow = rb * kRowsBlk + row;
-          const bool ok = grow < jb.M;
-          const size_t o = ok ? (size_t)grow * jb.G + (size_t)st * S : 0;
-          const uint32_t d = sb + L::W + row * L::SROW;
-          if constexpr (S == 4) {
-            cp_async8(d, sc + o, ok ? 8u : 0u);
-            cp_async8(d + 8, mn + o, ok ? 8u : 0u);
-          } else {
-            cp_async4(d, sc + o, ok ? 4u : 0u);
-            cp_async4(d + 4, mn + o, ok ? 4u : 0u);
-          }
-        }
-      } else if constexpr (SMODE == kScaleRow) {
-        const float* sc = static_cast<const float*>(jb.scales);
-#pragma unroll
-        for (int k = 0; k < kRowsBlk / 32; ++k) {
-          const int row = lane + 32 * k, grow = rb * kRowsBlk + row;
-          const bool ok = grow < jb.M;
-          cp_async4(sb + L::W + row * 4, sc + (ok ? grow : 0), ok ? 4u : 0u);
-        }
-      }
-      cp_async_arrive(full0 + 8 * slot);
-      if (++rb == jb.n_rb) {
-        rb = 0;
-        if (++st == jb.spb) {
-          st = 0;
-          ++j;
-        }
-      }
-    }
-    // every copy this warp started lands before the CTA may exit (after a
-    // timeout: bounded waits on the code tiles that may still be in flight)
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    if (abort_flag && lane == 0) {
-      volatile int keep_waiting = 0;
-      for (int k = it > NS ? it - NS : 0; k < it; ++k) mbar_wait(full0 + 8 * (k % NS), (k / NS) & 1, &keep_waiting);
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers
-  const int c = lane & 3, rq = lane >> 2;
-  int rowb[2];  // the thread's two rows within the unit's block
-  rowb[0] = warp * 16 + row_perm<FMT>(rq);
-  rowb[1] = rowb[0] + 8;
+  int rl[2];  // the thread's two rows within the warp's 16
+  rl[0] = row_perm<FMT>(rq);
+  rl[1] = rl[0] + 8;
   LaneCols lc;
   {
     int lo, hi, p;
@@ -561,11 +539,10 @@ __global__ void __launch_bounds__(kThreadsT, 2)
     frag_cols2(FMT, c, 2 * rq + 1, lo, hi, p);
     lc.col[2] = lo; lc.col[3] = hi; lc.p[1] = p;
   }
-  float* const scratch = scratch0 + warp * a.chunk_max;
   const uint32_t blane = (uint32_t)(lane & (LP - 1)) * 16;
 
   // x' windows over the CTA's runs (consecutive units with one job and stage);
-  // XS runs are resident, in slot run % XS
+  // XS runs are resident, run r in slot r % XS
   int nruns;
   {
     const int jl = job_of(a, u1 - 1);
@@ -590,7 +567,7 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       unsigned char* xslot = xarea + (size_t)(r % XS) * X;
       for (int ci = 0; ci < nchunk; ++ci)
         for (int t = 0; t < tslots; ++t, ++task) {
-          if (task % kCWarps != warp) continue;
+          if (task % kWarps != warp) continue;
           const int col0 = cbase + ci * Cc;
           if (E == 4)
             prep_chunk<NT, LP, 4>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
@@ -610,55 +587,77 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   // x may be written by the preceding grid, and so may the workspace and y
   asm volatile("griddepcontrol.wait;" ::: "memory");
   prep_window(0);
-  consumers_sync();
+  __syncthreads();
 
-  // last stage unit of a row block for this warp's 16 rows: add the stage
-  // partials in order and write y (+ bias)
-  auto signal = [&](int jj, int rbb) {
-    const TmaJob& jb = job_ref(a, jj);
+  // Stage partial sums reach the row block's counter one unit late: at the
+  // end of unit i the warp fences (unit i-1's partial stores are long done),
+  // adds unit i-1 to its counter, and reads the value returned for unit i-2;
+  // the warp that completes a counter adds the row block's stage partials in
+  // order and writes y (+ bias).
+  struct Pend {
+    int j, rb;
+    unsigned prev;
+  };
+  auto issue = [&](Pend& p) {
+    const TmaJob& jb = job_ref(a, p.j);
     __threadfence();
     __syncwarp();
-    unsigned* ctr = jb.counters + (size_t)rbb * kCWarps + warp;
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(ctr, 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev == (unsigned)jb.spb - 1) {
-      __threadfence();
-      const size_t stride = (size_t)kRowsBlk * N;
-      for (int idx = lane; idx < 16 * N; idx += 32) {
-        const int row = idx / N, t = idx - row * N;
-        const int grow = rbb * kRowsBlk + warp * 16 + row;
-        if (grow >= jb.M) continue;
-        const float* p = jb.partials + ((size_t)rbb * jb.spb * kRowsBlk + warp * 16 + row) * N + t;
-        float acc = 0.f;
+    unsigned v = 0;
+    if (lane == 0) v = atomicAdd(jb.counters + (size_t)p.rb * kWarps + warp, 1u);
+    p.prev = v;
+  };
+  auto finish = [&](const Pend& p) {
+    const TmaJob& jb = job_ref(a, p.j);
+    const unsigned prev = __shfl_sync(0xffffffffu, p.prev, 0);
+    if (prev != (unsigned)jb.spb - 1) return;
+    __threadfence();
+    const size_t stride = (size_t)kRowsBlk * N;
+    for (int idx = lane; idx < kWarpRows * N; idx += 32) {
+      const int row = idx / N, t = idx - row * N;
+      const int grow = p.rb * kRowsBlk + warp * kWarpRows + row;
+      if (grow >= jb.M) continue;
+      const float* src = jb.partials + ((size_t)p.rb * jb.spb * kRowsBlk + warp * kWarpRows + row) * N + t;
+      float acc = 0.f;
 #pragma unroll 4
-        for (int s2 = 0; s2 < jb.spb; ++s2) acc += __ldcg(p + s2 * stride);
-        jb.y[(size_t)t * jb.M + grow] = acc + (jb.bias ? jb.bias[grow] : 0.f);
-      }
-      __syncwarp();
-      if (lane == 0) *ctr = 0u;
+      for (int s2 = 0; s2 < jb.spb; ++s2) acc += __ldcg(src + s2 * stride);
+      jb.y[(size_t)t * jb.M + grow] = acc + (jb.bias ? jb.bias[grow] : 0.f);
     }
+    __syncwarp();
+    if (lane == 0) jb.counters[(size_t)p.rb * kWarps + warp] = 0u;
   };
 
-  int run = 0, prev_j = j, prev_st = st;
-  int pend_j = -1, pend_rb = 0;  // unit whose partials are written but not yet counted
+  // the current job's fields, reloaded when the walk enters the next job
+  float* jpart = nullptr;
+  float jts = 0.f;
+  int jM = 0, jnrb = 1, jspb = 1;
+  auto load_job = [&]() {
+    const TmaJob& jb = job_ref(a, j);
+    jpart = jb.partials;
+    jts = jb.tensor_scale;
+    jM = jb.M;
+    jnrb = jb.n_rb;
+    jspb = jb.spb;
+  };
+  load_job();
+
+  int run = 0, xslot = 0, slot = 0;
+  uint32_t phase = 0;
+  Pend pend1 = {0, 0, 0u}, pend2 = {0, 0, 0u};
+  bool has1 = false, has2 = false;
   bool live = true;
   for (int it = 0; it < nunits; ++it) {
-    if (j != prev_j || st != prev_st) {
-      ++run;
-      prev_j = j;
-      prev_st = st;
+    if (live && requested < nunits) {  // refill the slot of unit it - 1
+      request(requested % NS);
+      ++requested;
     }
-    if (run >= win_end) {  // same decision in every consumer warp
-      consumers_sync();
+    if (run >= win_end) {  // same decision in every warp of the CTA
+      __syncthreads();
       prep_window(win_end);
-      consumers_sync();
+      __syncthreads();
     }
-    const TmaJob& jb = job_ref(a, j);
-    const int slot = it % NS;
-    const unsigned char* stg = base + slot * L::BYTES;
-    const unsigned char* xs = xarea + (size_t)(run % XS) * X;
-    if (live && !mbar_wait(full0 + 8 * slot, (it / NS) & 1, &abort_flag)) {
+    const unsigned char* stg = ring + slot * L::BYTES;
+    const unsigned char* xs = xarea + xslot * X;
+    if (live && !mbar_wait(full0 + 8 * slot, phase, &abort_flag)) {
       live = false;
       if (lane == 0) {
         abort_flag = 1;
@@ -666,47 +665,38 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       }
     }
     if (live) {
-      // scales / zero points of the thread's rows, then every code word of the unit
-      uint32_t sw[2][4];
-      float frow[2];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const unsigned char* sp = stg + L::W + rowb[hh] * L::SROW;
-        if constexpr (SMODE == kScaleGroup) {
-          if constexpr (S == 4) {
-            const uint4 q = lds<uint4>(sp);
-            sw[hh][0] = q.x; sw[hh][1] = q.y; sw[hh][2] = q.z; sw[hh][3] = q.w;
-          } else {
-            const uint2 q = lds<uint2>(sp);
-            sw[hh][0] = q.x; sw[hh][1] = 0u; sw[hh][2] = q.y; sw[hh][3] = 0u;
-          }
-          frow[hh] = 0.f;
-        } else if constexpr (SMODE == kScaleRow) {
-          frow[hh] = lds<float>(sp);
-          sw[hh][0] = sw[hh][1] = sw[hh][2] = sw[hh][3] = 0u;
-        } else {
-          frow[hh] = jb.tensor_scale;
-          sw[hh][0] = sw[hh][1] = sw[hh][2] = sw[hh][3] = 0u;
-        }
-      }
-      uint32_t raw[S][2][4];
-#pragma unroll
-      for (int g = 0; g < S; ++g)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) load_words<FMT>(stg, rowb[hh], g, c, raw[g][hh]);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * slot);
-
       float y[NT][2];
 #pragma unroll
       for (int i = 0; i < NT; ++i) y[i][0] = y[i][1] = 0.f;
 #pragma unroll
       for (int pp = 0; pp < S / 2; ++pp) {
+        // scales / zero points of the pair's two groups, then their code words
+        uint32_t sv2[2], mv2[2];
+        float frow[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const unsigned char* sp = stg + L::W + rl[hh] * L::SROW;
+          if constexpr (SMODE == kScaleGroup) {
+            sv2[hh] = lds<uint32_t>(sp + 4 * pp);
+            mv2[hh] = lds<uint32_t>(sp + 2 * S + 4 * pp);
+            frow[hh] = 0.f;
+          } else if constexpr (SMODE == kScaleRow) {
+            frow[hh] = lds<float>(sp);
+            sv2[hh] = mv2[hh] = 0u;
+          } else {
+            frow[hh] = jts;
+            sv2[hh] = mv2[hh] = 0u;
+          }
+        }
         RowCodes<FMT> rc[2][2];
 #pragma unroll
         for (int gg = 0; gg < 2; ++gg)
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) rc[gg][hh].set(raw[2 * pp + gg][hh], c);
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t raw[4];
+            load_words<FMT>(stg, rl[hh], 2 * pp + gg, c, raw);
+            rc[gg][hh].set(raw, c);
+          }
         float acc[2][NT][4];
 #pragma unroll
         for (int gg = 0; gg < 2; ++gg)
@@ -736,9 +726,8 @@ __global__ void __launch_bounds__(kThreadsT, 2)
             for (int hh = 0; hh < 2; ++hh) {
               float sv, mv;
               if constexpr (SMODE == kScaleGroup) {
-                const uint32_t s2 = sw[hh][g >> 1], m2 = sw[hh][2 + (g >> 1)];
-                sv = __half2float(__ushort_as_half((unsigned short)((g & 1) ? (s2 >> 16) : (s2 & 0xFFFFu))));
-                mv = __half2float(__ushort_as_half((unsigned short)((g & 1) ? (m2 >> 16) : (m2 & 0xFFFFu))));
+                sv = __half2float(__ushort_as_half((unsigned short)(gg ? (sv2[hh] >> 16) : (sv2[hh] & 0xFFFFu))));
+                mv = __half2float(__ushort_as_half((unsigned short)(gg ? (mv2[hh] >> 16) : (mv2[hh] & 0xFFFFu))));
               } else {
                 sv = frow[hh];
                 mv = -(float)kOffset * sv;
@@ -750,41 +739,70 @@ __global__ void __launch_bounds__(kThreadsT, 2)
         }
       }
 
-      if (jb.spb == 1) {
+      if (jspb == 1) {
+        const TmaJob& jb = job_ref(a, j);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const int grow = rb * kRowsBlk + rowb[hh];
-          if (grow >= jb.M) continue;
+          const int grow = rb * kRowsBlk + warp * kWarpRows + rl[hh];
+          if (grow >= jM) continue;
           const float bv = jb.bias ? jb.bias[grow] : 0.f;
 #pragma unroll
           for (int i = 0; i < NT; ++i) {
             const int t = 4 * i + c;
-            if (t < N && (LP == 32 || c == 0)) jb.y[(size_t)t * jb.M + grow] = y[i][hh] + bv;
+            if (t < N && (LP == 32 || c == 0)) jb.y[(size_t)t * jM + grow] = y[i][hh] + bv;
           }
         }
       } else {
-        if (pend_j >= 0) signal(pend_j, pend_rb);
-        float* part = jb.partials + ((size_t)rb * jb.spb + st) * kRowsBlk * N;
+        if (has2) {
+          finish(pend2);
+          has2 = false;
+        }
+        if (has1) {
+          issue(pend1);
+          pend2 = pend1;
+          has2 = true;
+        }
+        float* part = jpart + (((size_t)rb * jspb + st) * kRowsBlk + warp * kWarpRows) * N;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
           for (int i = 0; i < NT; ++i) {
             const int t = 4 * i + c;
-            if (t < N && (LP == 32 || c == 0)) part[(size_t)rowb[hh] * N + t] = y[i][hh];
+            if (t < N && (LP == 32 || c == 0)) part[(size_t)rl[hh] * N + t] = y[i][hh];
           }
-        pend_j = j;
-        pend_rb = rb;
+        pend1.j = j;
+        pend1.rb = rb;
+        has1 = true;
       }
     }
-    if (++rb == jb.n_rb) {
+    if (++slot == NS) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    if (++rb == jnrb) {
       rb = 0;
-      if (++st == jb.spb) {
+      ++run;
+      if (++xslot == XS) xslot = 0;
+      if (++st == jspb) {
         st = 0;
         ++j;
+        if (j < a.n_jobs) load_job();
       }
     }
   }
-  if (live && pend_j >= 0) signal(pend_j, pend_rb);
+  if (live) {
+    if (has2) finish(pend2);
+    if (has1) {
+      issue(pend1);
+      finish(pend1);
+    }
+  } else if (lane == 0) {
+    // after a timeout: bounded waits on this warp's tiles that may still be in flight
+    volatile int keep_waiting = 0;
+    for (int k = requested > NS ? requested - NS : 0; k < requested; ++k)
+      mbar_wait(full0 + 8 * (k % NS), (k / NS) & 1, &keep_waiting);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ------------------------------------------------------------------ host side
@@ -799,13 +817,14 @@ int sm_count() {
   return n;
 }
 
-// CTAs per SM of one launch (1 leaves room for the next launch's CTAs).
+// CTAs per SM of one launch (PF_TMA_CTAS_PER_SM=1 gives each CTA the whole
+// SM's shared memory).
 int ctas_per_sm() {
   static int v = 0;
   static std::once_flag once;
   std::call_once(once, [] {
     const char* e = getenv("PF_TMA_CTAS_PER_SM");
-    v = (e && atoi(e) == 2) ? 2 : 1;
+    v = (e && atoi(e) == 1) ? 1 : 2;
   });
   return v;
 }
@@ -839,7 +858,7 @@ int run_of(const TmaArgs& a, int u) {
 template <int FMT, int NT, int LP, int SMODE>
 cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_words, cudaStream_t s) {
   using F = TmaFmt<FMT>;
-  using L = StageL<FMT, SMODE>;
+  using L = WarpSlot<FMT, SMODE>;
   using XR = XRec<NT, LP>;
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
@@ -847,7 +866,7 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   for (int k = 0; k < a.n_jobs; ++k) {
     cuuint64_t dims[2] = {(cuuint64_t)row_words[k], (cuuint64_t)a.job[k].M};
     cuuint64_t strides[1] = {(cuuint64_t)row_words[k] * 4};
-    cuuint32_t box[2] = {(cuuint32_t)(F::S * F::WPG), (cuuint32_t)kRowsBlk};
+    cuuint32_t box[2] = {(cuuint32_t)(F::S * F::WPG), (cuuint32_t)kWarpRows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(&maps[k], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes[k]), dims, strides, box,
                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -857,7 +876,8 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   }
   for (int k = a.n_jobs; k < kTmaMaxJobs; ++k) maps[k] = maps[0];
 
-  int P = sm_count() * ctas_per_sm();
+  const int cps = ctas_per_sm();
+  int P = sm_count() * cps;
   if (P > a.n_units) P = a.n_units;
   if (P < 1) P = 1;
   int max_runs = 1;
@@ -867,17 +887,19 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
     const int r = run_of(a, u1 - 1) - run_of(a, u0) + 1;
     if (r > max_runs) max_runs = r;
   }
+  const int budget = smem_budget(cps);
   const uint32_t X = F::S * XR::R;
-  const uint32_t fixed = (uint32_t)kCWarps * a.chunk_max * 4 + 16 * kMaxStages + 1024;
+  const uint32_t fixed = (uint32_t)kWarps * a.chunk_max * 4 + 1024;
+  const uint32_t per_stage = (uint32_t)kWarps * (L::BYTES + 8);
   int XS = max_runs < kMaxXSlots ? max_runs : kMaxXSlots;
-  while (XS > 1 && fixed + XS * X + 3 * L::BYTES > (uint32_t)kSmemBudget) --XS;
-  int NS = (int)(((uint32_t)kSmemBudget - fixed - XS * X) / L::BYTES);
+  while (XS > 1 && fixed + XS * X + 3 * per_stage > (uint32_t)budget) --XS;
+  int NS = (int)(((uint32_t)budget - fixed - XS * X) / per_stage);
   if (NS > kMaxStages) NS = kMaxStages;
   if (NS < 2) return cudaErrorInvalidConfiguration;
   a.NS = NS;
   a.XS = XS;
-  const size_t smem = (size_t)1024 + (size_t)NS * L::BYTES + (size_t)XS * X + (size_t)kCWarps * a.chunk_max * 4 +
-                      16 * (size_t)NS;
+  const size_t smem = (size_t)1024 + (size_t)kWarps * NS * L::BYTES + (size_t)XS * X +
+                      (size_t)kWarps * a.chunk_max * 4 + (size_t)kWarps * NS * 8;
 
   auto kern = gemv_tma_kernel<FMT, NT, LP, SMODE>;
   {
@@ -889,7 +911,7 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(mu);
     if (dev < 0 || dev >= 64 || !done[dev]) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_budget(1) + 1024);
       if (e != cudaSuccess) return e;
       if (dev >= 0 && dev < 64) done[dev] = true;
     }
@@ -957,11 +979,11 @@ bool tma_eligible(const TmaWeight& w) {
     if (!w.signs || reinterpret_cast<uintptr_t>(w.signs) % 4) return false;
   }
   const long long n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
-  if (n_rb * kCWarps >= (long long)kWsStatusSlot) return false;
+  if (n_rb * kWarps >= (long long)kWsStatusSlot) return false;
   return encode_fn() != nullptr;
 }
 
-size_t tma_counter_slots(const TmaWeight& w) { return (size_t)((w.M + kRowsBlk - 1) / kRowsBlk) * kCWarps; }
+size_t tma_counter_slots(const TmaWeight& w) { return (size_t)((w.M + kRowsBlk - 1) / kRowsBlk) * kWarps; }
 
 size_t tma_partial_bytes(const TmaWeight& w, int N) {
   const size_t n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
