@@ -402,11 +402,6 @@ static bool group_streams(int count, const pf_qweight* const* ws) {
     if (!is_group_int_format(ws[0]->format) && ((ws[i]->scales != nullptr) != (ws[0]->scales != nullptr)))
       return false;
   }
-  for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
-    size_t slots = 0;
-    for (int i = c0; i < count && i < c0 + kTmaMaxJobs; ++i) slots += tma_counter_slots(tma_weight(ws[i]));
-    if (slots >= kWsStatusSlot) return false;
-  }
   return true;
 }
 

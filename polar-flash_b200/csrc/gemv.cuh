@@ -69,7 +69,6 @@ struct TmaJob {  // device view of one weight of a launch
   const float* bias;
   float* y;             // [N][M] fp32
   float* partials;      // [n_rb][spb][128][N] stage partial sums (spb > 1)
-  unsigned* counters;   // [n_rb][8] arrival counters, zero on entry and exit
   float tensor_scale;
   float had_rscale;     // 1/sqrt(had_block), 1 when not rotated
   int had_block;        // 0 or a power of two <= 512 dividing K
@@ -100,14 +99,14 @@ struct TmaIO {
 };
 
 bool tma_eligible(const TmaWeight& w);
-size_t tma_counter_slots(const TmaWeight& w);
 size_t tma_partial_bytes(const TmaWeight& w, int N);
 int tma_block_rows();
 int tma_stage_groups(int fmt);
 int row_words_of_tma(int fmt, int K);
-// One launch for `count` weights (same format) and N <= 16 tokens; the
-// workspace holds the counters (kWsCounterBytes) followed by every job's
-// partial sums.  Returns a pf_status; *err receives a CUDA launch error.
+// One GEMV launch for `count` weights (same format) and N <= 16 tokens, then
+// (when K spans more than one column stage) one combine launch; the workspace
+// holds the status word (in its first kWsCounterBytes) followed by every
+// job's stage partial sums.  Returns a pf_status; *err receives a CUDA error.
 int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int x_dtype, void* workspace,
                     cudaStream_t s, cudaError_t* err);
 

@@ -589,43 +589,6 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   prep_window(0);
   __syncthreads();
 
-  // Stage partial sums reach the row block's counter one unit late: at the
-  // end of unit i the warp fences (unit i-1's partial stores are long done),
-  // adds unit i-1 to its counter, and reads the value returned for unit i-2;
-  // the warp that completes a counter adds the row block's stage partials in
-  // order and writes y (+ bias).
-  struct Pend {
-    int j, rb;
-    unsigned prev;
-  };
-  auto issue = [&](Pend& p) {
-    const TmaJob& jb = job_ref(a, p.j);
-    __threadfence();
-    __syncwarp();
-    unsigned v = 0;
-    if (lane == 0) v = atomicAdd(jb.counters + (size_t)p.rb * kWarps + warp, 1u);
-    p.prev = v;
-  };
-  auto finish = [&](const Pend& p) {
-    const TmaJob& jb = job_ref(a, p.j);
-    const unsigned prev = __shfl_sync(0xffffffffu, p.prev, 0);
-    if (prev != (unsigned)jb.spb - 1) return;
-    __threadfence();
-    const size_t stride = (size_t)kRowsBlk * N;
-    for (int idx = lane; idx < kWarpRows * N; idx += 32) {
-      const int row = idx / N, t = idx - row * N;
-      const int grow = p.rb * kRowsBlk + warp * kWarpRows + row;
-      if (grow >= jb.M) continue;
-      const float* src = jb.partials + ((size_t)p.rb * jb.spb * kRowsBlk + warp * kWarpRows + row) * N + t;
-      float acc = 0.f;
-#pragma unroll 4
-      for (int s2 = 0; s2 < jb.spb; ++s2) acc += __ldcg(src + s2 * stride);
-      jb.y[(size_t)t * jb.M + grow] = acc + (jb.bias ? jb.bias[grow] : 0.f);
-    }
-    __syncwarp();
-    if (lane == 0) jb.counters[(size_t)p.rb * kWarps + warp] = 0u;
-  };
-
   // the current job's fields, reloaded when the walk enters the next job
   float* jpart = nullptr;
   float jts = 0.f;
@@ -642,8 +605,6 @@ __global__ void __launch_bounds__(kThreadsT, 2)
 
   int run = 0, xslot = 0, slot = 0;
   uint32_t phase = 0;
-  Pend pend1 = {0, 0, 0u}, pend2 = {0, 0, 0u};
-  bool has1 = false, has2 = false;
   bool live = true;
   for (int it = 0; it < nunits; ++it) {
     if (live && requested < nunits) {  // refill the slot of unit it - 1
@@ -753,26 +714,15 @@ __global__ void __launch_bounds__(kThreadsT, 2)
           }
         }
       } else {
-        if (has2) {
-          finish(pend2);
-          has2 = false;
-        }
-        if (has1) {
-          issue(pend1);
-          pend2 = pend1;
-          has2 = true;
-        }
+        // the stage partial sums; the combine kernel adds them in stage order
         float* part = jpart + (((size_t)rb * jspb + st) * kRowsBlk + warp * kWarpRows) * N;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
           for (int i = 0; i < NT; ++i) {
             const int t = 4 * i + c;
-            if (t < N && (LP == 32 || c == 0)) part[(size_t)rl[hh] * N + t] = y[i][hh];
+            if (t < N && (LP == 32 || c == 0)) __stcg(part + (size_t)rl[hh] * N + t, y[i][hh]);
           }
-        pend1.j = j;
-        pend1.rb = rb;
-        has1 = true;
       }
     }
     if (++slot == NS) {
@@ -790,19 +740,41 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       }
     }
   }
-  if (live) {
-    if (has2) finish(pend2);
-    if (has1) {
-      issue(pend1);
-      finish(pend1);
-    }
-  } else if (lane == 0) {
+  if (!live && lane == 0) {
     // after a timeout: bounded waits on this warp's tiles that may still be in flight
     volatile int keep_waiting = 0;
     for (int k = requested > NS ? requested - NS : 0; k < requested; ++k)
       mbar_wait(full0 + 8 * (k % NS), (k / NS) & 1, &keep_waiting);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// y = sum of a job's stage partial sums in stage order (+ bias): one thread per
+// (job, row), all tokens.  Launched after the GEMV as a programmatic dependent;
+// it lets its own dependents start at once and waits for the GEMV's partials.
+__global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ TmaArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  int row = blockIdx.x * blockDim.x + threadIdx.x;
+  int j = 0;
+  for (; j < a.n_jobs; ++j) {
+    const int Mp = (a.job[j].M + 255) & ~255;
+    if (row < Mp) break;
+    row -= Mp;
+  }
+  if (j >= a.n_jobs) return;
+  const TmaJob& jb = a.job[j];
+  if (jb.spb <= 1 || row >= jb.M) return;
+  const int N = a.N, rb = row / kRowsBlk, r = row - rb * kRowsBlk;
+  const float* p = jb.partials + ((size_t)rb * jb.spb * kRowsBlk + r) * N;
+  const size_t stride = (size_t)kRowsBlk * N;
+  const float bv = jb.bias ? jb.bias[row] : 0.f;
+  for (int t = 0; t < N; ++t) {
+    float acc = 0.f;
+#pragma unroll 4
+    for (int s2 = 0; s2 < jb.spb; ++s2) acc += __ldcg(p + s2 * stride + t);
+    jb.y[(size_t)t * jb.M + row] = acc + bv;
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -978,12 +950,8 @@ bool tma_eligible(const TmaWeight& w) {
     if (w.had_block > 512 || (w.had_block & (w.had_block - 1)) || w.K % w.had_block) return false;
     if (!w.signs || reinterpret_cast<uintptr_t>(w.signs) % 4) return false;
   }
-  const long long n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
-  if (n_rb * kWarps >= (long long)kWsStatusSlot) return false;
   return encode_fn() != nullptr;
 }
-
-size_t tma_counter_slots(const TmaWeight& w) { return (size_t)((w.M + kRowsBlk - 1) / kRowsBlk) * kWarps; }
 
 size_t tma_partial_bytes(const TmaWeight& w, int N) {
   const size_t n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
@@ -1003,7 +971,6 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
   int rw[kTmaMaxJobs];
   unsigned* counters = static_cast<unsigned*>(workspace);
   char* part = static_cast<char*>(workspace) + kWsCounterBytes;
-  size_t slot = 0;
   int unit0 = 0, run0 = 0, chunk = 128;
   const int fmt = ws[0].format;
   const int S = stage_groups(fmt);
@@ -1027,9 +994,7 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
     jb.spb = jb.G / S;
     jb.unit0 = unit0;
     jb.run0 = run0;
-    jb.counters = counters + slot;
     jb.partials = reinterpret_cast<float*>(part);
-    slot += tma_counter_slots(w);
     part += tma_partial_bytes(w, N);
     unit0 += jb.n_rb * jb.spb;
     run0 += jb.spb;
@@ -1038,7 +1003,6 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
     codes[k] = w.codes;
     rw[k] = row_words_of_tma(fmt, w.K);
   }
-  if (slot >= kWsStatusSlot) return PF_ERR_SHAPE;
   a.n_jobs = count;
   a.n_units = unit0;
   a.N = N;
@@ -1061,6 +1025,27 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
   if (e != cudaSuccess) {
     *err = e;
     return PF_ERR_CUDA;
+  }
+  int rows = 0, split = 0;
+  for (int k = 0; k < count; ++k) {
+    rows += (a.job[k].M + 255) & ~255;
+    split |= a.job[k].spb > 1;
+  }
+  if (split) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows / 256);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, combine_kernel, (const TmaArgs)a);
+    if (e != cudaSuccess) {
+      *err = e;
+      return PF_ERR_CUDA;
+    }
   }
   return PF_OK;
 }
