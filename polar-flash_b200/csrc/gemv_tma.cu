@@ -289,54 +289,66 @@ struct LaneCols {
   int p[2];
 };
 
+// 2^e as a float for an unbiased exponent e clamped to the normal range.
+__device__ __forceinline__ float pow2f(int e) {
+  e = e < -126 ? -126 : (e > 127 ? 127 : e);
+  return __int_as_float((e + 127) << 23);
+}
+
 // ---- x' of one prep chunk (C = 32 E columns of token t, one warp): forward
 // block RWHT of x (signs, Walsh-Hadamard butterflies in registers and across
 // lanes, 1/sqrt(b)), then for every group of the chunk inside [g_lo, g_hi):
 // the group's power-of-two normaliser E (|x'| < 2^E), the tensor-core B
 // fragments of x' 2^(14 - p - E) split into fp16 hi + lo, and {Sx, 1024 2^E}.
-// Tokens t >= N write zeros.
+// Tokens t >= N write zeros.  Every global load is issued before any is used.
 template <int NT, int LP, int E>
-__device__ __noinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype, int col0, int g_lo, int g_hi, int t,
-                                        unsigned char* xslot, float* scratch, int lane, LaneCols lc) {
+__device__ __forceinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype, int col0, int g_lo, int g_hi, int t,
+                                           unsigned char* xslot, float* scratch, int lane, const LaneCols& lc) {
   constexpr int C = 32 * E;
   constexpr int LG = 128 / E;  // lanes per 128-column group
   const int b = jb.had_block;
   float v[E];
   if (t < N) {
     const size_t base = (size_t)t * jb.K + col0 + E * lane;
+    int s4[E / 4];
+    const int* sp = reinterpret_cast<const int*>((b > 0 ? jb.signs : static_cast<const int8_t*>(jb.x)) + col0 +
+                                                 E * lane);
+#pragma unroll
+    for (int q = 0; q < E / 4; ++q) s4[q] = __ldg(sp + q);
     if (x_dtype == PF_DTYPE_F32) {
       const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(jb.x) + base);
+      float4 f[E / 4];
+#pragma unroll
+      for (int q = 0; q < E / 4; ++q) f[q] = __ldg(xp + q);
 #pragma unroll
       for (int q = 0; q < E / 4; ++q) {
-        const float4 f = __ldg(xp + q);
-        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+        v[4 * q] = f[q].x; v[4 * q + 1] = f[q].y; v[4 * q + 2] = f[q].z; v[4 * q + 3] = f[q].w;
       }
     } else {
       const uint2* xp = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(jb.x) + base);
+      uint2 r[E / 4];
+#pragma unroll
+      for (int q = 0; q < E / 4; ++q) r[q] = __ldg(xp + q);
 #pragma unroll
       for (int q = 0; q < E / 4; ++q) {
-        const uint2 r = __ldg(xp + q);
         if (x_dtype == PF_DTYPE_F16) {
-          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
-          const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&r[q].x));
+          const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&r[q].y));
           v[4 * q] = f0.x; v[4 * q + 1] = f0.y; v[4 * q + 2] = f1.x; v[4 * q + 3] = f1.y;
         } else {  // bf16: the upper half of an fp32
-          v[4 * q] = __uint_as_float(r.x << 16);
-          v[4 * q + 1] = __uint_as_float(r.x & 0xFFFF0000u);
-          v[4 * q + 2] = __uint_as_float(r.y << 16);
-          v[4 * q + 3] = __uint_as_float(r.y & 0xFFFF0000u);
+          v[4 * q] = __uint_as_float(r[q].x << 16);
+          v[4 * q + 1] = __uint_as_float(r[q].x & 0xFFFF0000u);
+          v[4 * q + 2] = __uint_as_float(r[q].y << 16);
+          v[4 * q + 3] = __uint_as_float(r[q].y & 0xFFFF0000u);
         }
       }
     }
     if (b > 0) {
-      const int* sp = reinterpret_cast<const int*>(jb.signs + col0 + E * lane);
 #pragma unroll
-      for (int q = 0; q < E / 4; ++q) {
-        const int s4 = __ldg(sp + q);
+      for (int q = 0; q < E / 4; ++q)
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if ((s4 >> (8 * e + 7)) & 1) v[4 * q + e] = -v[4 * q + e];
-      }
+        for (int e = 0; e < 4; ++e)  // sign bit of the int8 column sign
+          v[4 * q + e] = __uint_as_float(__float_as_uint(v[4 * q + e]) ^ (((uint32_t)s4[q] << (24 - 8 * e)) & 0x80000000u));
 #pragma unroll
       for (int h = 1; h < E; h *= 2) {
         if (h < b) {
@@ -368,19 +380,24 @@ __device__ __noinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype, in
 #pragma unroll
     for (int e = 0; e < E; ++e) v[e] = 0.f;
   }
-  float amax = 0.f, sx = 0.f;
+  // group statistics: max |x'| (as ordered bit patterns of non-negative floats) and sum
+  uint32_t amax = 0u;
+  float sx = 0.f;
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    amax = fmaxf(amax, fabsf(v[e]));
+    amax = max(amax, __float_as_uint(v[e]) & 0x7FFFFFFFu);
     sx += v[e];
   }
+  if constexpr (LG == 32) {
+    amax = __reduce_max_sync(0xffffffffu, amax);
+  } else {
 #pragma unroll
-  for (int o = 1; o < LG; o *= 2) {
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    for (int o = 1; o < LG; o *= 2) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   }
-  int ex = 0;
-  if (amax > 0.f) frexpf(amax, &ex);  // amax < 2^ex
+#pragma unroll
+  for (int o = 1; o < LG; o *= 2) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+  // |x'| < 2^ex: one more than the exponent of amax (any value for amax = 0)
+  const int ex = amax == 0u ? 0 : (amax < 0x00800000u ? -125 : (int)(amax >> 23) - 126);
 #pragma unroll
   for (int q = 0; q < E / 4; ++q)
     *reinterpret_cast<float4*>(scratch + E * lane + 4 * q) =
@@ -395,7 +412,7 @@ __device__ __noinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype, in
     const int eg = __shfl_sync(0xffffffffu, ex, gi * LG);
     const float sg = __shfl_sync(0xffffffffu, sx, gi * LG);
     if (g < g_lo || g >= g_hi) continue;
-    const float f0 = ldexpf(1.f, 14 - lc.p[0] - eg), f1 = ldexpf(1.f, 14 - lc.p[1] - eg);
+    const float f0 = pow2f(14 - lc.p[0] - eg), f1 = pow2f(14 - lc.p[1] - eg);
     const float* xs = scratch + gi * 128;
     const float xv[4] = {xs[lc.col[0]] * f0, xs[lc.col[1]] * f0, xs[lc.col[2]] * f1, xs[lc.col[3]] * f1};
     uint32_t hw[2], lw[2];
@@ -412,7 +429,7 @@ __device__ __noinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype, in
     *reinterpret_cast<uint2*>(fr + fl * 16) = make_uint2(hw[0], hw[1]);
     *reinterpret_cast<uint2*>(fr + (fl + 4) * 16) = make_uint2(lw[0], lw[1]);
     if (lane == 0)
-      *reinterpret_cast<float2*>(rec + XRec<NT, LP>::FRAG + t * 16) = make_float2(sg, ldexpf(1024.f, eg));
+      *reinterpret_cast<float2*>(rec + XRec<NT, LP>::FRAG + t * 16) = make_float2(sg, 1024.f * pow2f(eg));
   }
   __syncwarp();
 }
@@ -429,6 +446,10 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   constexpr int kOffset = IntFmt<FMT>::kOffset;
 
   asm volatile("griddepcontrol.launch_dependents;");
+  if (threadIdx.x < (unsigned)a.n_jobs) {
+    const CUtensorMap* m = threadIdx.x == 0 ? &map0 : threadIdx.x == 1 ? &map1 : threadIdx.x == 2 ? &map2 : &map3;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+  }
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ int abort_flag;
