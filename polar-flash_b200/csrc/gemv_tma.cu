@@ -537,9 +537,9 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       }
     }
   };
-  // the first NS - 1 units: weights and scales never come from the preceding grid
+  // the first NS units: weights and scales never come from the preceding grid
   int requested = 0;
-  for (; requested < NS - 1 && requested < nunits; ++requested) request(requested);
+  for (; requested < NS && requested < nunits; ++requested) request(requested);
 
   // ---- compute side: unit walk (job, stage, row block) and its x' runs
   int j = job_of(a, u0), st, rb;
@@ -628,10 +628,6 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   uint32_t phase = 0;
   bool live = true;
   for (int it = 0; it < nunits; ++it) {
-    if (live && requested < nunits) {  // refill the slot of unit it - 1
-      request(requested % NS);
-      ++requested;
-    }
     if (run >= win_end) {  // same decision in every warp of the CTA
       __syncthreads();
       prep_window(win_end);
@@ -746,6 +742,10 @@ __global__ void __launch_bounds__(kThreadsT, 2)
           }
       }
     }
+    if (live && requested < nunits) {  // refill the slot just consumed
+      request(slot);
+      ++requested;
+    }
     if (++slot == NS) {
       slot = 0;
       phase ^= 1u;
@@ -773,13 +773,13 @@ __global__ void __launch_bounds__(kThreadsT, 2)
 // y = sum of a job's stage partial sums in stage order (+ bias): one thread per
 // (job, row), all tokens.  Launched after the GEMV as a programmatic dependent;
 // it lets its own dependents start at once and waits for the GEMV's partials.
-__global__ void __launch_bounds__(256) combine_kernel(const __grid_constant__ TmaArgs a) {
+__global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ TmaArgs a) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   int row = blockIdx.x * blockDim.x + threadIdx.x;
   int j = 0;
   for (; j < a.n_jobs; ++j) {
-    const int Mp = (a.job[j].M + 255) & ~255;
+    const int Mp = (a.job[j].M + 127) & ~127;
     if (row < Mp) break;
     row -= Mp;
   }
@@ -1049,13 +1049,13 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
   }
   int rows = 0, split = 0;
   for (int k = 0; k < count; ++k) {
-    rows += (a.job[k].M + 255) & ~255;
+    rows += (a.job[k].M + 127) & ~127;
     split |= a.job[k].spb > 1;
   }
   if (split) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(rows / 256);
-    cfg.blockDim = dim3(256);
+    cfg.gridDim = dim3(rows / 128);
+    cfg.blockDim = dim3(128);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
