@@ -446,8 +446,17 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   constexpr int kOffset = IntFmt<FMT>::kOffset;
 
   asm volatile("griddepcontrol.launch_dependents;");
-  if (threadIdx.x < (unsigned)a.n_jobs) {
-    const CUtensorMap* m = threadIdx.x == 0 ? &map0 : threadIdx.x == 1 ? &map1 : threadIdx.x == 2 ? &map2 : &map3;
+  // the launch's parameters are cold in every SM's constant cache: touch each
+  // 64-byte line once, in parallel, before the dependent reads that follow
+  if (threadIdx.x < (sizeof(TmaArgs) + 63) / 64) {
+    constexpr unsigned kLast = sizeof(TmaArgs) / 4 - 1;
+    const unsigned i = threadIdx.x * 16 < kLast ? threadIdx.x * 16 : kLast;
+    const uint32_t w = reinterpret_cast<const uint32_t*>(&a)[i];
+    asm volatile("" ::"r"(w));
+  }
+  if (threadIdx.x >= 32 && threadIdx.x < 32 + kTmaMaxJobs) {
+    const int k = threadIdx.x - 32;
+    const CUtensorMap* m = k == 0 ? &map0 : k == 1 ? &map1 : k == 2 ? &map2 : &map3;
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
   }
 
@@ -469,8 +478,8 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   }
   __syncthreads();
 
-  const int U = a.n_units, P = gridDim.x, cta = blockIdx.x;
-  const int u0 = (int)((long long)cta * U / P), u1 = (int)((long long)(cta + 1) * U / P);
+  const unsigned U = (unsigned)a.n_units, P = gridDim.x, cta = blockIdx.x;
+  const int u0 = (int)(cta * U / P), u1 = (int)((cta + 1) * U / P);  // U * P < 2^32 (host-checked)
   const int nunits = u1 - u0;
   if (nunits <= 0) return;
   const int N = a.N;
@@ -1024,6 +1033,8 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
     codes[k] = w.codes;
     rw[k] = row_words_of_tma(fmt, w.K);
   }
+  if ((unsigned long long)unit0 * (unsigned long long)(sm_count() * ctas_per_sm() + 1) >= (1ull << 32))
+    return PF_ERR_SHAPE;
   a.n_jobs = count;
   a.n_units = unit0;
   a.N = N;
