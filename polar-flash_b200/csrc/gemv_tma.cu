@@ -546,9 +546,11 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       }
     }
   };
-  // the first NS units: weights and scales never come from the preceding grid
+  // the first two units (weights and scales never come from the preceding
+  // grid); the rest of the ring is requested after the x' preparation, when
+  // the copy engine's queue has drained
   int requested = 0;
-  for (; requested < NS && requested < nunits; ++requested) request(requested);
+  for (; requested < 2 && requested < NS && requested < nunits; ++requested) request(requested);
 
   // ---- compute side: unit walk (job, stage, row block) and its x' runs
   int j = job_of(a, u0), st, rb;
@@ -617,6 +619,7 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   // x may be written by the preceding grid, and so may the workspace and y
   asm volatile("griddepcontrol.wait;" ::: "memory");
   prep_window(0);
+  for (; requested < NS && requested < nunits; ++requested) request(requested);
   __syncthreads();
 
   // the current job's fields, reloaded when the walk enters the next job
