@@ -782,31 +782,54 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-// y = sum of a job's stage partial sums in stage order (+ bias): one thread per
-// (job, row), all tokens.  Launched after the GEMV as a programmatic dependent;
-// it lets its own dependents start at once and waits for the GEMV's partials.
-__global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ TmaArgs a) {
+// y = the sum of a job's stage partial sums (+ bias).  A block covers 32
+// consecutive (row, token) elements of one job; warp w adds stages w, w + 8,
+// ... (all its loads in flight at once) and warp 0 adds the eight warp sums
+// in warp order, so the result is the same on every run.  Launched after the
+// GEMV as a programmatic dependent: it lets its own dependents start at once
+// and waits for the GEMV's partial sums.
+constexpr int kCombineWarps = 8;
+
+__global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(const __grid_constant__ TmaArgs a) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  int row = blockIdx.x * blockDim.x + threadIdx.x;
-  int j = 0;
+  __shared__ float red[kCombineWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int N = a.N;
+  int blk = blockIdx.x, j = 0;
   for (; j < a.n_jobs; ++j) {
-    const int Mp = (a.job[j].M + 127) & ~127;
-    if (row < Mp) break;
-    row -= Mp;
+    const int nb = (((a.job[j].M + kRowsBlk - 1) / kRowsBlk) * kRowsBlk * N + 31) / 32;
+    if (blk < nb) break;
+    blk -= nb;
   }
   if (j >= a.n_jobs) return;
   const TmaJob& jb = a.job[j];
-  if (jb.spb <= 1 || row >= jb.M) return;
-  const int N = a.N, rb = row / kRowsBlk, r = row - rb * kRowsBlk;
-  const float* p = jb.partials + ((size_t)rb * jb.spb * kRowsBlk + r) * N;
-  const size_t stride = (size_t)kRowsBlk * N;
-  const float bv = jb.bias ? jb.bias[row] : 0.f;
-  for (int t = 0; t < N; ++t) {
-    float acc = 0.f;
-#pragma unroll 4
-    for (int s2 = 0; s2 < jb.spb; ++s2) acc += __ldcg(p + s2 * stride + t);
-    jb.y[(size_t)t * jb.M + row] = acc + bv;
+  if (jb.spb <= 1) return;
+  const int e = blk * 32 + lane;  // element row * N + t of the job
+  const int row = e / N, t = e - row * N;
+  const bool valid = row < jb.M;
+  float acc = 0.f;
+  if (valid) {
+    const int rb = row / kRowsBlk, r = row - rb * kRowsBlk;
+    const float* p = jb.partials + (size_t)rb * jb.spb * kRowsBlk * N + (size_t)r * N + t;
+    const size_t stride = (size_t)kRowsBlk * N;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int st = warp + k * kCombineWarps;
+      v[k] = st < jb.spb ? __ldcg(p + st * stride) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc += v[k];
+    for (int st = warp + 8 * kCombineWarps; st < jb.spb; st += kCombineWarps) acc += __ldcg(p + st * stride);
+  }
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && valid) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCombineWarps; ++w) s += red[w][lane];
+    jb.y[(size_t)t * jb.M + row] = s + (jb.bias ? jb.bias[row] : 0.f);
   }
 }
 
@@ -1061,15 +1084,15 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
     *err = e;
     return PF_ERR_CUDA;
   }
-  int rows = 0, split = 0;
+  int blocks = 0, split = 0;
   for (int k = 0; k < count; ++k) {
-    rows += (a.job[k].M + 127) & ~127;
+    blocks += (((a.job[k].M + kRowsBlk - 1) / kRowsBlk) * kRowsBlk * N + 31) / 32;
     split |= a.job[k].spb > 1;
   }
   if (split) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(rows / 128);
-    cfg.blockDim = dim3(128);
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(kCombineWarps * 32);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
