@@ -353,7 +353,7 @@ def main():
     achieved = step_bytes / (ms_run / 1e3) / 1e9
     traffic = None
     try:
-        with open(os.path.join(ROOT, "profiles", "gemv_int_traffic.json")) as f:
+        with open(os.path.join(ROOT, "profiles", "gemv_tma_traffic.json")) as f:
             traffic = json.load(f).get("bytes_per_step")
     except Exception:  # noqa: BLE001
         pass
@@ -381,6 +381,7 @@ def main():
                              "inputs > 126 MB L2", "parallelism": f"column-shard x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                         "traffic_unit": "DRAM bytes per step (8 GEMV launches, ncu)",
                          "kernel": "gemv_tma_kernel (8 grouped launches per step: q|k|v, o, gate|up, down at "
                                    "INT3 and INT2; CUDA events over the timed region)",
                          "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback"},
