@@ -212,8 +212,30 @@ size_t pass_bytes(const pf_qweight* w, int np) {
   return b;
 }
 
+// Batches of more than 16 tokens of the group-128 INT and E8 formats run on
+// the tensor-core dequant-GEMM, kGemmChunk tokens per launch; its workspace
+// holds fp32 x' and the per-token-scaled fp16 copy the GEMM reads.
+constexpr int kGemmChunk = 512;
+bool use_gemm(const pf_qweight* w, int N) {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("PF_GEMM");
+    mode = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  if (!mode || N <= kMaxGemvTokens || !gemm_eligible(w->format, w->K)) return false;
+  // the GEMM reads packed rows with 16-byte loads (INT3: 4-byte), E8 scales as fp16 pairs
+  if (w->format != PF_FMT_INT3_G128 && !aligned(w->codes, 16)) return false;
+  return w->format != PF_FMT_E8_RVQ2_G128 || aligned(w->scales, 4);
+}
+size_t gemm_bytes(const pf_qweight* w, int N) {
+  const int nc = N < kGemmChunk ? N : kGemmChunk;
+  const size_t Kp = (size_t)((w->K + 127) / 128) * 128;
+  return kCounterBytes + round_up((size_t)nc * Kp * sizeof(float), 256) + gemm_x16_bytes(nc, w->K);
+}
+
 size_t workspace_bytes(const pf_qweight* w, int N) {
   if (N < 1) N = 1;
+  if (use_gemm(w, N)) return gemm_bytes(w, N);
   size_t b = pass_bytes(w, tokens_per_pass(N));
   int tail = N % kMaxGemvTokens;
   if (N > kMaxGemvTokens && tail) {
@@ -371,6 +393,57 @@ static int qlinear_pass(const pf_qweight* w, const HadPlan& plan, const void* x,
   return do_run(w, np, bias, y, ws, s);
 }
 
+// Tokens [0, N) through the tensor-core GEMM, kGemmChunk at a time.
+static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, int N,
+                        const float* bias, float* y, void* ws, cudaStream_t s) {
+  const int K = w->K, Kp = ((K + 127) / 128) * 128;
+  const size_t xs = dtype_size(x_dtype);
+  char* base = static_cast<char*>(ws) + kCounterBytes;
+  const int cmax = N < kGemmChunk ? N : kGemmChunk;
+  float* xplain = reinterpret_cast<float*>(base);
+  __half* x16 = reinterpret_cast<__half*>(base + round_up((size_t)cmax * Kp * sizeof(float), 256));
+  float* tsc = reinterpret_cast<float*>(reinterpret_cast<char*>(x16) + round_up((size_t)cmax * K * 2, 256));
+  for (int t0 = 0; t0 < N; t0 += kGemmChunk) {
+    const int nc = N - t0 < kGemmChunk ? N - t0 : kGemmChunk;
+    PrepArgs pa;
+    memset(&pa, 0, sizeof(pa));
+    pa.x = static_cast<const char*>(x) + (size_t)t0 * K * xs;
+    pa.x_dtype = x_dtype;
+    pa.N = nc;
+    pa.K = K;
+    pa.Kp = Kp;
+    pa.plan = plan;
+    pa.signs = w->had_signs;
+    pa.fmt = w->format;
+    pa.M = w->M;
+    pa.mode = 1;
+    pa.slots = nc;
+    pa.xplain = xplain;
+    int st = cuda_status(launch_prep(pa, s));
+    if (st) return st;
+    GemmIn g;
+    memset(&g, 0, sizeof(g));
+    g.fmt = w->format;
+    g.codes = w->codes;
+    g.scales = static_cast<const __half*>(w->scales);
+    g.mins = static_cast<const __half*>(w->mins);
+    g.M = w->M;
+    g.K = K;
+    g.Kp = Kp;
+    g.N = nc;
+    g.row_words = row_words_of(w->format, K);
+    g.xplain = xplain;
+    g.x16 = x16;
+    g.tok_scale = tsc;
+    g.bias = bias;
+    g.y = y + (size_t)t0 * w->M;
+    g.status = static_cast<unsigned*>(ws) + kWsStatusSlot;
+    st = cuda_status(launch_gemm(g, s));
+    if (st) return st;
+  }
+  return PF_OK;
+}
+
 int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias, float* y,
                void* workspace, size_t ws_bytes, void* stream) {
   int st = common_args(w, N, workspace, ws_bytes);
@@ -382,6 +455,7 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
   st = make_plan(w->K, w->had_block, &plan);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (use_gemm(w, N)) return qlinear_gemm(w, plan, x, x_dtype, N, bias, y, workspace, s);
   const size_t xs = dtype_size(x_dtype);
   for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {
     int np = N - t0 < kMaxGemvTokens ? N - t0 : kMaxGemvTokens;
@@ -411,7 +485,7 @@ static size_t group_bytes(int count, const pf_qweight* const* ws, int N) {
     size_t t = workspace_bytes(ws[i], N);
     if (t > b) b = t;
   }
-  if (group_streams(count, ws)) {
+  if (N <= kMaxGemvTokens && group_streams(count, ws)) {
     int np = tokens_per_pass(N < 1 ? 1 : N);
     for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
       size_t t = kCounterBytes;
@@ -447,7 +521,7 @@ int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* const* 
   if (N == 0) return PF_OK;
   if (!workspace || ws_bytes < group_bytes(count, ws, N)) return PF_ERR_WORKSPACE;
   if (!aligned(workspace, 256)) return PF_ERR_ALIGNMENT;
-  bool grouped = group_streams(count, ws);
+  bool grouped = N <= kMaxGemvTokens && group_streams(count, ws);
   for (int i = 0; i < count && grouped; ++i) grouped = x_tma_aligned(xs[i], x_dtype);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t xsz = dtype_size(x_dtype);

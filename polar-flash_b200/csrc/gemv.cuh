@@ -110,6 +110,24 @@ int row_words_of_tma(int fmt, int K);
 int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int x_dtype, void* workspace,
                     cudaStream_t s, cudaError_t* err);
 
+// ---- tensor-core dequant-GEMM (gemm_tc.cu) for N > 16 tokens
+struct GemmIn {
+  int fmt;
+  const void* codes;
+  const __half* scales;
+  const __half* mins;
+  int M, K, Kp, N, row_words;
+  const float* xplain;  // [N][Kp] fp32 x' (prep_kernel, plain mode)
+  __half* x16;          // [N][K] fp16 x' scaled per token (written here)
+  float* tok_scale;     // [N]
+  const float* bias;
+  float* y;
+  unsigned* status;
+};
+bool gemm_eligible(int fmt, int K);
+size_t gemm_x16_bytes(int N, int K);
+cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s);
+
 struct DequantArgs {
   int fmt;
   const void* codes;
