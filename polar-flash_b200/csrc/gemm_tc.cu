@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   __shared__ uint64_t bars[3 * kStages + 1];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
-  __shared__ float roots[240][8];
+  __shared__ __align__(16) float roots[240][8];  // read as float4
   __shared__ float tscale[kBN];
 
   unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
