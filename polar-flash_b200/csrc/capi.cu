@@ -222,7 +222,10 @@ bool use_gemm(const pf_qweight* w, int N) {
     const char* e = getenv("PF_GEMM");
     mode = (e && strcmp(e, "0") == 0) ? 0 : 1;
   }
-  if (!mode || N <= kMaxGemvTokens || !gemm_eligible(w->format, w->K)) return false;
+  // E8 decodes through a shared-memory root table: the tensor-core kernel
+  // serves it at every batch size; the INT formats use it above 16 tokens
+  const int min_tokens = w->format == PF_FMT_E8_RVQ2_G128 ? 1 : kMaxGemvTokens + 1;
+  if (!mode || N < min_tokens || !gemm_eligible(w->format, w->K)) return false;
   // the GEMM reads packed rows with 16-byte loads (INT3: 4-byte), E8 scales as fp16 pairs
   if (w->format != PF_FMT_INT3_G128 && !aligned(w->codes, 16)) return false;
   return w->format != PF_FMT_E8_RVQ2_G128 || aligned(w->scales, 4);

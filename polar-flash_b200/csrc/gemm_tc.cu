@@ -91,8 +91,11 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
          (2ull << 61);
 }
 
-// Instruction descriptor: fp16 A and B (K-major), fp32 D, M = 128, N = 128.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+// Instruction descriptor: fp16 A and B (K-major), fp32 D, M = 128, N = n
+// (a multiple of 16 up to kBN).
+__host__ __device__ constexpr uint32_t gemm_idesc(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
 
 // Byte offset of 16-byte chunk c (8 fp16, columns 8c..8c+7 of the stage) of
 // tile row r: two 64-column atoms, rows of 128 bytes, chunk index XOR (r & 7).
@@ -152,6 +155,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = tmem_base_slot;
   const int G = a.G;
+  // tokens of this CTA, rounded up to the MMA's N granularity
+  const int nv = a.N - n0 < kBN ? a.N - n0 : kBN;
+  const int nmma = (nv + 15) & ~15;
 
   if (warp == 0) {
     // ------------------------------------------------------------ x' via TMA
@@ -195,7 +201,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           asm volatile(
               "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
                   tmem),
-              "l"(da), "l"(db), "r"(kIdesc), "r"(acc));
+              "l"(da), "l"(db), "r"(gemm_idesc(nmma)), "r"(acc));
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(free0 +
                                                                                                         8 * slot)
@@ -213,7 +219,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     bool live = true;
     uint4 pk[4];  // the row's packed group (E8: 32 index bytes)
     uint32_t p13 = 0;
+    uint32_t psc = 0;  // its fp16 scale and zero point (E8: the two stage scales)
+    constexpr int kL2Ahead = 4;  // groups requested into L2 ahead of the register loads
+    auto row_bytes = [&]() -> size_t {
+      return FMT == PF_FMT_E8_RVQ2_G128 ? (size_t)a.K / 4 : (size_t)a.row_words * 4;
+    };
+    constexpr int kGroupBytes = FMT == PF_FMT_INT4_G128 ? 64 : (FMT == PF_FMT_INT3_G128 ? 52 : 32);
+    auto l2_ahead = [&](int g) {
+      if (g >= G) return;
+      const char* p = static_cast<const char*>(a.codes) + (size_t)growc * row_bytes() + (size_t)g * kGroupBytes;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p + kGroupBytes - 1));
+    };
     auto load_group = [&](int g) {
+      if constexpr (FMT == PF_FMT_E8_RVQ2_G128) {
+        psc = __ldg(reinterpret_cast<const unsigned*>(a.scales + ((size_t)growc * G + g) * 2));
+      } else {
+        const uint32_t lo = __half_as_ushort(__ldg(a.scales + (size_t)growc * G + g));
+        const uint32_t hi = __half_as_ushort(__ldg(a.mins + (size_t)growc * G + g));
+        psc = lo | (hi << 16);
+      }
       if constexpr (FMT == PF_FMT_INT4_G128) {
         const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(a.codes) +
                                                         (size_t)growc * a.row_words + (size_t)g * 16);
@@ -245,21 +270,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       const int q = i & 3;
       return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
     };
+    for (int g = 0; g < kL2Ahead; ++g) l2_ahead(g);
     if (G > 0) load_group(0);
     for (int s = 0; s < G; ++s) {
       const int slot = s % kStages;
       unsigned char* at = base + slot * kStageBytes;
-      // the codes of this stage; the next stage's are requested before decoding
+      // the codes and scales of this stage; the next stage's are requested
+      // into registers before decoding, the one after that into L2
       uint32_t cw[16];
       uint32_t c12 = p13;
+      const uint32_t sc = psc;
 #pragma unroll
       for (int i = 0; i < 16; ++i) cw[i] = word(i);
       float sv = 0.f, s2v = 0.f;
       if constexpr (FMT == PF_FMT_E8_RVQ2_G128) {
-        const __half2 ss = *reinterpret_cast<const __half2*>(a.scales + ((size_t)growc * G + s) * 2);
+        const __half2 ss = *reinterpret_cast<const __half2*>(&sc);
         sv = __low2float(ss);
         s2v = __high2float(ss);
       }
+      l2_ahead(s + kL2Ahead);
       if (s + 1 < G) load_group(s + 1);
       if (live && s >= kStages && !bar_wait(free0 + 8 * slot, ((s / kStages) - 1) & 1, &abort_flag)) {
         live = false;
@@ -292,8 +321,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           }
         } else {
           // the stored fp16 scale / zero point
-          const __half2 sx = __half2half2(a.scales[(size_t)growc * G + s]);
-          const __half2 mx = __half2half2(a.mins[(size_t)growc * G + s]);
+          const __half2 sx = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
+          const __half2 mx = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             uint32_t q[8];
@@ -329,7 +358,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
       const float bv = (rvalid && a.bias) ? a.bias[grow] : 0.f;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kBN; c0 += 16) {
+      for (int c0 = 0; c0 < nmma; c0 += 16) {
         uint32_t v[16];
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"

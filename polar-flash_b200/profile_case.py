@@ -21,6 +21,7 @@ def main():
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--N", type=int, default=1)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--time", action="store_true", help="report device time per call (CUDA events)")
     a = ap.parse_args()
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
@@ -32,6 +33,18 @@ def main():
         y = qlinear(qw, x)
     torch.cuda.synchronize()
     print(f"{a.fmt} {a.M}x{a.K} N={a.N}: packed {qw.nbytes()} B, y[0,:4] = {y[0, :4].tolist()}")
+    if a.time:
+        out = torch.empty_like(y)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(5, a.iters)
+        e0.record()
+        for _ in range(reps):
+            qlinear(qw, x, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        flops = 2.0 * a.M * a.K * a.N
+        print(f"time {us:.1f} us  {flops / us / 1e6:.1f} TFLOP/s  {qw.nbytes() / us / 1e3:.1f} GB/s packed")
 
 
 if __name__ == "__main__":
