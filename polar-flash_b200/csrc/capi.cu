@@ -406,8 +406,37 @@ static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x,
   float* xplain = reinterpret_cast<float*>(base);
   __half* x16 = reinterpret_cast<__half*>(base + round_up((size_t)cmax * Kp * sizeof(float), 256));
   float* tsc = reinterpret_cast<float*>(reinterpret_cast<char*>(x16) + round_up((size_t)cmax * K * 2, 256));
+  // rotation blocks that tile K: x' straight from x in the GEMM's own prep
+  const bool direct = plan.ncasc == 0 && (plan.block == 0 || plan.rot_end == K) && K <= kGemmPrepMaxK;
   for (int t0 = 0; t0 < N; t0 += kGemmChunk) {
     const int nc = N - t0 < kGemmChunk ? N - t0 : kGemmChunk;
+    if (direct) {
+      GemmIn g;
+      memset(&g, 0, sizeof(g));
+      g.fmt = w->format;
+      g.codes = w->codes;
+      g.scales = static_cast<const __half*>(w->scales);
+      g.mins = static_cast<const __half*>(w->mins);
+      g.M = w->M;
+      g.K = K;
+      g.Kp = Kp;
+      g.N = nc;
+      g.row_words = row_words_of(w->format, K);
+      g.xplain = nullptr;
+      g.x = static_cast<const char*>(x) + (size_t)t0 * K * xs;
+      g.x_dtype = x_dtype;
+      g.signs = w->had_signs;
+      g.block = plan.block;
+      g.rscale = plan.block > 1 ? 1.f / sqrtf((float)plan.block) : 1.f;
+      g.x16 = x16;
+      g.tok_scale = tsc;
+      g.bias = bias;
+      g.y = y + (size_t)t0 * w->M;
+      g.status = static_cast<unsigned*>(ws) + kWsStatusSlot;
+      int st = cuda_status(launch_gemm(g, s));
+      if (st) return st;
+      continue;
+    }
     PrepArgs pa;
     memset(&pa, 0, sizeof(pa));
     pa.x = static_cast<const char*>(x) + (size_t)t0 * K * xs;

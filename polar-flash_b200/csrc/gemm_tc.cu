@@ -4,16 +4,19 @@
 // asymmetric and E8 RVQ2), X' = the forward block RWHT of X in fp16 with a
 // power-of-two scale per token (the same fusion identity as the GEMV).
 //
-// CTA = 128 weight rows x 128 tokens, one CTA per SM, six warps:
+// CTA = 128 weight rows x 128 tokens, one CTA per SM, ten warps:
 //   warp 0    TMA producer: the x' tile of each 128-column stage, two
 //             64-column boxes, 128B-swizzled (K-major canonical layout).
-//   warps 1-4 one weight row per thread: load the row's packed group with
-//             plain 16-byte loads (one stage ahead), decode every weight to
-//             fp16 q*s + m (one rounding: an fp16 FMA of the exact code) or,
-//             for E8, s1*r[i1] + s2*r[i2] (fp32, one rounding), and write it
-//             into the A tile in the same swizzled K-major layout; then the
-//             epilogue (tcgen05.ld of their 32 TMEM lanes, token scale, bias).
-//   warp 5    allocates 128 TMEM columns and issues tcgen05.mma (kind::f16,
+//   warps 1-8 two groups of four dequantising alternate stages, one weight
+//             row per thread: the row's packed group is loaded with plain
+//             loads one own stage ahead (and into L2 four ahead), every code
+//             pair that sits 16 bits apart in its word becomes an fp16x2 with
+//             one shift + LOP3, and w = q s + m is one fp16 FMA of the exact
+//             code (one rounding; E8: s2 r[i2] + s1 r[i1], s1 r[i1] exact), written
+//             into the A tile in the swizzled K-major layout (columns permuted
+//             within each group, x' permuted alike); then the epilogue
+//             (tcgen05.ld of their 32 TMEM lanes, token scale, bias).
+//   warp 9    allocates 128 TMEM columns and issues tcgen05.mma (kind::f16,
 //             M = 128, N = 128, K = 16; fp32 accumulator in TMEM) from one
 //             lane; tcgen05.commit releases each stage's smem slot.
 // Every wait is bounded (2 s on %globaltimer): on expiry the kernel records
@@ -37,7 +40,9 @@ constexpr int kBM = 128;  // weight rows per CTA (MMA M)
 constexpr int kBN = 128;  // tokens per CTA (MMA N)
 constexpr int kBK = 128;  // columns per stage: one scale group
 constexpr int kStages = 3;
-constexpr int kGemmThreads = 192;
+constexpr int kDqWarps = 8;                          // two groups of four: alternate stages
+constexpr int kGemmThreads = (kDqWarps + 2) * 32;  // + TMA warp + MMA warp
+constexpr int kMmaWarp = kDqWarps + 1;
 constexpr uint32_t kATile = kBM * kBK * 2;  // two 64-column swizzle atoms of 16 KB
 constexpr uint32_t kBTile = kBN * kBK * 2;
 constexpr uint32_t kStageBytes = kATile + kBTile;
@@ -103,9 +108,25 @@ __device__ __forceinline__ uint32_t a_chunk(int r, int c) {
   return (uint32_t)((c >> 3) * (kBM * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-// fp16 pair (q0, q1) from two small codes: 1024 + q as fp16 bits, minus 1024.
-__device__ __forceinline__ __half2 code_pair(uint32_t q0, uint32_t q1) {
-  const uint32_t b = q0 | (q1 << 16) | 0x64006400u;
+// Column order of the A tile inside each 128-column group: slot s holds the
+// code of group column gemm_slot_col(fmt, s).  Code pairs that sit 16 bits
+// apart in their word fill one fp16x2 slot pair, so a pair decodes with one
+// shift and one LOP3; the fp16 x' is written in the same order.
+__host__ __device__ __forceinline__ int gemm_slot_col(int fmt, int s) {
+  const int hi = s & 1;
+  if (fmt == PF_FMT_INT4_G128) return 8 * (s >> 3) + ((s & 7) >> 1) + 4 * hi;
+  if (fmt == PF_FMT_INT2_G128) return 16 * (s >> 4) + ((s & 15) >> 1) + 8 * hi;
+  if (fmt == PF_FMT_INT3_G128) {
+    const int p = s >> 1;
+    return p < 60 ? 10 * (p / 5) + (p % 5) + 5 * hi : 120 + (p - 60) + 4 * hi;
+  }
+  return s;
+}
+
+// fp16x2 (q0, q1) from a word holding the codes at bits 0.. and 16.., already
+// masked: 1024 + q as fp16 bits, minus 1024 (exact).
+__device__ __forceinline__ __half2 pair_fp16(uint32_t masked) {
+  const uint32_t b = masked | 0x64006400u;
   return __hsub2(*reinterpret_cast<const __half2*>(&b), __half2half2(__ushort_as_half(0x6400)));
 }
 
@@ -116,7 +137,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   __shared__ uint64_t bars[3 * kStages + 1];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
-  __shared__ __align__(16) float roots[240][8];  // read as float4
+  __shared__ uint4 roots16[240];  // E8 roots as 8 fp16
   __shared__ float tscale[kBN];
 
   unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
@@ -129,7 +150,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bfull0 + 8 * s));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(128));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(kBM));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(free0 + 8 * s));
     }
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(accbar));
@@ -140,12 +161,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     for (int k = threadIdx.x; k < 240; k += blockDim.x) {
       float r[8];
       e8_root(k, r);
+      uint32_t h[4];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) roots[k][q] = r[q];
+      for (int q = 0; q < 4; ++q) {
+        const __half2 v = __floats2half2_rn(r[2 * q], r[2 * q + 1]);
+        h[q] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+      roots16[k] = make_uint4(h[0], h[1], h[2], h[3]);
     }
   }
   for (int t = threadIdx.x; t < kBN; t += blockDim.x) tscale[t] = (n0 + t < a.N) ? a.tok_scale[n0 + t] : 0.f;
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_slot)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -180,7 +206,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
               : "memory");
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       for (int s = 0; s < G; ++s) {
@@ -212,22 +238,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     }
   } else {
     // ------------------------------------------------ dequant rows, epilogue
+    const int grp = (warp - 1) >> 2;       // this group dequantises stages s with s % 2 == grp
     const int r = 32 * (warp & 3) + lane;  // tile row == this warp's TMEM lanes
     const int grow = m0 + r;
     const bool rvalid = grow < a.M;
     const int growc = rvalid ? grow : 0;
     bool live = true;
-    uint4 pk[4];  // the row's packed group (E8: 32 index bytes)
-    uint32_t p13 = 0;
-    uint32_t psc = 0;  // its fp16 scale and zero point (E8: the two stage scales)
-    constexpr int kL2Ahead = 4;  // groups requested into L2 ahead of the register loads
-    auto row_bytes = [&]() -> size_t {
-      return FMT == PF_FMT_E8_RVQ2_G128 ? (size_t)a.K / 4 : (size_t)a.row_words * 4;
-    };
     constexpr int kGroupBytes = FMT == PF_FMT_INT4_G128 ? 64 : (FMT == PF_FMT_INT3_G128 ? 52 : 32);
+    constexpr int kL2Ahead = 4;  // own stages requested into L2 ahead of the register loads
+    const size_t rowb = FMT == PF_FMT_E8_RVQ2_G128 ? (size_t)a.K / 4 : (size_t)a.row_words * 4;
+    const char* rowp = static_cast<const char*>(a.codes) + (size_t)growc * rowb;
+    uint32_t pw[16];  // packed words of the next own stage (E8: 32 index bytes)
+    uint32_t psc = 0;  // its fp16 scale and zero point (E8: the two stage scales)
+#pragma unroll
+    for (int q = 0; q < 16; ++q) pw[q] = 0u;
     auto l2_ahead = [&](int g) {
       if (g >= G) return;
-      const char* p = static_cast<const char*>(a.codes) + (size_t)growc * row_bytes() + (size_t)g * kGroupBytes;
+      const char* p = rowp + (size_t)g * kGroupBytes;
       asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
       asm volatile("prefetch.global.L2 [%0];" ::"l"(p + kGroupBytes - 1));
     };
@@ -239,57 +266,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         const uint32_t hi = __half_as_ushort(__ldg(a.mins + (size_t)growc * G + g));
         psc = lo | (hi << 16);
       }
-      if constexpr (FMT == PF_FMT_INT4_G128) {
-        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(a.codes) +
-                                                        (size_t)growc * a.row_words + (size_t)g * 16);
+      const char* p = rowp + (size_t)g * kGroupBytes;
+      if constexpr (FMT == PF_FMT_INT3_G128) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) pk[q] = __ldg(p + q);
-      } else if constexpr (FMT == PF_FMT_INT2_G128) {
-        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(a.codes) +
-                                                        (size_t)growc * a.row_words + (size_t)g * 8);
-        pk[0] = __ldg(p);
-        pk[1] = __ldg(p + 1);
-      } else if constexpr (FMT == PF_FMT_INT3_G128) {
-        const uint32_t* p = static_cast<const uint32_t*>(a.codes) + (size_t)growc * a.row_words + (size_t)g * 13;
-        uint32_t w[13];
+        for (int q = 0; q < 13; ++q) pw[q] = __ldg(reinterpret_cast<const uint32_t*>(p) + q);
+      } else {
 #pragma unroll
-        for (int q = 0; q < 13; ++q) w[q] = __ldg(p + q);
-        pk[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        pk[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        pk[2] = make_uint4(w[8], w[9], w[10], w[11]);
-        p13 = w[12];
-      } else {  // E8: [M][K/8][2] bytes, 32 per group
-        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.codes) +
-                                                        (size_t)growc * (a.K / 4) + (size_t)g * 32);
-        pk[0] = __ldg(p);
-        pk[1] = __ldg(p + 1);
+        for (int q = 0; q < kGroupBytes / 16; ++q) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + q);
+          pw[4 * q] = v.x; pw[4 * q + 1] = v.y; pw[4 * q + 2] = v.z; pw[4 * q + 3] = v.w;
+        }
       }
     };
-    auto word = [&](int i) -> uint32_t {  // i-th 32-bit word of pk
-      const uint4 v = pk[i >> 2];
-      const int q = i & 3;
-      return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
-    };
-    for (int g = 0; g < kL2Ahead; ++g) l2_ahead(g);
-    if (G > 0) load_group(0);
-    for (int s = 0; s < G; ++s) {
+    for (int k = 0; k < kL2Ahead; ++k) l2_ahead(grp + 2 * k);
+    if (grp < G) load_group(grp);
+    for (int s = grp; s < G; s += 2) {
       const int slot = s % kStages;
       unsigned char* at = base + slot * kStageBytes;
-      // the codes and scales of this stage; the next stage's are requested
-      // into registers before decoding, the one after that into L2
+      // this stage's codes and scales; the group's next stage is requested into
+      // registers before decoding, the ones after it into L2
       uint32_t cw[16];
-      uint32_t c12 = p13;
-      const uint32_t sc = psc;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) cw[i] = word(i);
-      float sv = 0.f, s2v = 0.f;
-      if constexpr (FMT == PF_FMT_E8_RVQ2_G128) {
-        const __half2 ss = *reinterpret_cast<const __half2*>(&sc);
-        sv = __low2float(ss);
-        s2v = __high2float(ss);
-      }
-      l2_ahead(s + kL2Ahead);
-      if (s + 1 < G) load_group(s + 1);
+      for (int q = 0; q < 16; ++q) cw[q] = pw[q];
+      const uint32_t sc = psc;
+      l2_ahead(s + 2 * kL2Ahead);
+      if (s + 2 < G) load_group(s + 2);
       if (live && s >= kStages && !bar_wait(free0 + 8 * slot, ((s / kStages) - 1) & 1, &abort_flag)) {
         live = false;
         if (lane == 0) {
@@ -297,68 +298,72 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
         }
       }
-      if (live) {
-        if constexpr (FMT == PF_FMT_E8_RVQ2_G128) {
-          // 16 vectors of 8 columns: chunk c = vector c
+      if (!live) continue;
+      if constexpr (FMT == PF_FMT_E8_RVQ2_G128) {
+        // w = s1 r[i1] + s2 r[i2] in one fp16 FMA (s1 r[i1] is exact: r in {0, +-1/2, +-1})
+        const __half2 s1 = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
+        const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const uint32_t wv = cw[c >> 1];
-            const int i1 = (wv >> (16 * (c & 1))) & 0xFF, i2 = (wv >> (16 * (c & 1) + 8)) & 0xFF;
-            const float4 r1a = *reinterpret_cast<const float4*>(&roots[i1 < 240 ? i1 : 0][0]);
-            const float4 r1b = *reinterpret_cast<const float4*>(&roots[i1 < 240 ? i1 : 0][4]);
-            const float4 r2a = *reinterpret_cast<const float4*>(&roots[i2 < 240 ? i2 : 0][0]);
-            const float4 r2b = *reinterpret_cast<const float4*>(&roots[i2 < 240 ? i2 : 0][4]);
-            const __half2 h0 = __floats2half2_rn(fmaf(sv, r1a.x, s2v * r2a.x), fmaf(sv, r1a.y, s2v * r2a.y));
-            const __half2 h1 = __floats2half2_rn(fmaf(sv, r1a.z, s2v * r2a.z), fmaf(sv, r1a.w, s2v * r2a.w));
-            const __half2 h2 = __floats2half2_rn(fmaf(sv, r1b.x, s2v * r2b.x), fmaf(sv, r1b.y, s2v * r2b.y));
-            const __half2 h3 = __floats2half2_rn(fmaf(sv, r1b.z, s2v * r2b.z), fmaf(sv, r1b.w, s2v * r2b.w));
-            uint4 o;
-            o.x = *reinterpret_cast<const uint32_t*>(&h0);
-            o.y = *reinterpret_cast<const uint32_t*>(&h1);
-            o.z = *reinterpret_cast<const uint32_t*>(&h2);
-            o.w = *reinterpret_cast<const uint32_t*>(&h3);
-            *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = rvalid ? o : make_uint4(0, 0, 0, 0);
+        for (int c = 0; c < 16; ++c) {
+          const uint32_t wv = cw[c >> 1] >> (16 * (c & 1));
+          const uint32_t i1 = wv & 0xFFu, i2 = (wv >> 8) & 0xFFu;
+          const uint4 ra = roots16[i1 < 240u ? i1 : 0u], rb = roots16[i2 < 240u ? i2 : 0u];
+          const uint32_t* pa = reinterpret_cast<const uint32_t*>(&ra);
+          const uint32_t* pb = reinterpret_cast<const uint32_t*>(&rb);
+          uint4 o;
+          uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __half2 h = __hfma2(s2, *reinterpret_cast<const __half2*>(&pb[e]),
+                                      __hmul2(s1, *reinterpret_cast<const __half2*>(&pa[e])));
+            ov[e] = *reinterpret_cast<const uint32_t*>(&h);
           }
-        } else {
-          // the stored fp16 scale / zero point
-          const __half2 sx = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
-          const __half2 mx = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            uint32_t q[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int k = 8 * c + e;  // column in the group
-              if constexpr (FMT == PF_FMT_INT4_G128) {
-                q[e] = (cw[k >> 3] >> (4 * (k & 7))) & 15u;
-              } else if constexpr (FMT == PF_FMT_INT2_G128) {
-                q[e] = (cw[k >> 4] >> (2 * (k & 15))) & 3u;
-              } else {
-                const int wi = k / 10, sh = 3 * (k % 10);
-                q[e] = ((wi < 12 ? cw[wi] : c12) >> sh) & 7u;
-              }
-            }
-            uint4 o;
-            uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __half2 h = __hfma2(code_pair(q[2 * e], q[2 * e + 1]), sx, mx);
-              ov[e] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-            *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = rvalid ? o : make_uint4(0, 0, 0, 0);
-          }
+          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = rvalid ? o : make_uint4(0, 0, 0, 0);
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(afull0 + 8 * slot) : "memory");
+      } else {
+        // w = q s + m as one fp16 FMA of the exact code (the stored fp16 s and m)
+        const __half2 sx = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
+        const __half2 mx = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
+        uint32_t g3[13];
+        if constexpr (FMT == PF_FMT_INT3_G128) {
+#pragma unroll
+          for (int t = 0; t < 12; ++t) g3[t] = (cw[t] & 0x0000FFFFu) | ((cw[t] << 1) & 0xFFFF0000u);
+          g3[12] = (cw[12] & 0x0000FFFFu) | ((cw[12] << 4) & 0xFFFF0000u);
+        }
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          uint4 o;
+          uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint32_t mk;
+            if constexpr (FMT == PF_FMT_INT4_G128) {
+              mk = (cw[c] >> (4 * e)) & 0x000F000Fu;
+            } else if constexpr (FMT == PF_FMT_INT2_G128) {
+              mk = (cw[c >> 1] >> (2 * (4 * (c & 1) + e))) & 0x00030003u;
+            } else {
+              const int p = 4 * c + e;
+              mk = p < 60 ? (g3[p / 5] >> (3 * (p % 5))) & 0x00070007u : (g3[12] >> (3 * (p - 60))) & 0x00070007u;
+            }
+            const __half2 h = __hfma2(pair_fp16(mk), sx, mx);
+            ov[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = rvalid ? o : make_uint4(0, 0, 0, 0);
+        }
       }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(afull0 + 8 * slot) : "memory");
     }
-    // ------------------------------------------------ epilogue
-    if (live && bar_wait(accbar, 0, &abort_flag)) {
+    // ------------------------------------------------ epilogue (16-column chunks split between the groups)
+    bool ok = live;
+    if (ok) ok = bar_wait(accbar, 0, &abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
       asm volatile("tcgen05.fence::after_thread_sync;");
       const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
       const float bv = (rvalid && a.bias) ? a.bias[grow] : 0.f;
 #pragma unroll 1
-      for (int c0 = 0; c0 < nmma; c0 += 16) {
+      for (int c0 = 16 * grp; c0 < nmma; c0 += 32) {
         uint32_t v[16];
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -381,20 +386,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.fence::after_thread_sync;");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
-// x'' (fp16) = x' * 2^e per token with max |x'| 2^e in [2^14, 2^15); tok_scale = 2^-e.
-__global__ void __launch_bounds__(256) xhalf_kernel(const float* __restrict__ xp, int Kp, int K, __half* out,
-                                                    float* tok_scale) {
-  const int t = blockIdx.x;
-  const float* row = xp + (size_t)t * Kp;
-  float mx = 0.f;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(row[k]));
-  __shared__ float red[8];
+// Block-wide max of a non-negative float (all threads get it).
+__device__ __forceinline__ float block_max(float mx, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
@@ -406,13 +405,62 @@ __global__ void __launch_bounds__(256) xhalf_kernel(const float* __restrict__ xp
     if (threadIdx.x == 0) red[0] = v;
   }
   __syncthreads();
-  mx = red[0];
+  return red[0];
+}
+
+// fp16 x'' of one token in the GEMM's slot order: x'' = x' 2^(15 - e) with
+// max |x'| < 2^e, tok_scale = 2^(e - 15).
+__device__ __forceinline__ void write_x16(const float* row, float mx, float rs, int K, int fmt, __half* out,
+                                          float* tok_scale) {
   int ex = 0;
   if (mx > 0.f) frexpf(mx, &ex);  // mx < 2^ex
-  const float sc = ldexpf(1.f, 15 - ex), inv = ldexpf(1.f, ex - 15);
-  __half* o = out + (size_t)t * K;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) o[k] = __float2half_rn(row[k] * sc);
-  if (threadIdx.x == 0) tok_scale[t] = mx > 0.f ? inv : 1.f;
+  const float sc = ldexpf(1.f, 15 - ex) * rs, inv = ldexpf(1.f, ex - 15);
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const int g = k & ~127, sl = k & 127;
+    out[k] = __float2half_rn(row[g + gemm_slot_col(fmt, sl)] * sc);
+  }
+  if (threadIdx.x == 0) *tok_scale = mx > 0.f ? inv : 1.f;
+}
+
+// From fp32 x' (prep_kernel, any rotation plan): one CTA per token.
+__global__ void __launch_bounds__(256) xhalf_kernel(const float* __restrict__ xp, int Kp, int K, int fmt, __half* out,
+                                                    float* tok_scale) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const float* row = xp + (size_t)t * Kp;
+  float mx = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(row[k]));
+  mx = block_max(mx, red);
+  write_x16(row, mx, 1.f, K, fmt, out + (size_t)t * K, tok_scale + t);
+}
+
+// From x directly, for rotation blocks that tile K (no remainder cascade): one
+// CTA per token, the token's row in shared memory, sign flip, Walsh-Hadamard
+// butterflies of every block (one pass per level), 1/sqrt(b), max, fp16 out.
+__global__ void __launch_bounds__(512) xprep16_kernel(const void* x, int x_dtype, const int8_t* signs, int K,
+                                                      int block, float rs, int fmt, __half* out, float* tok_scale) {
+  extern __shared__ float xrow[];
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    float v = load_x(x, x_dtype, (size_t)t * K + k);
+    if (block > 1 && signs[k] < 0) v = -v;
+    xrow[k] = v;
+  }
+  __syncthreads();
+  for (int h = 1; h < block; h <<= 1) {
+    for (int j = threadIdx.x; j < K / 2; j += blockDim.x) {
+      const int lo = (j / h) * 2 * h + (j % h);
+      const float u = xrow[lo], w = xrow[lo + h];
+      xrow[lo] = u + w;
+      xrow[lo + h] = u - w;
+    }
+    __syncthreads();
+  }
+  float mx = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(xrow[k]));
+  mx = block_max(mx * rs, red);
+  write_x16(xrow, mx, rs, K, fmt, out + (size_t)t * K, tok_scale + t);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn_gemm() {
@@ -473,7 +521,26 @@ bool gemm_eligible(int fmt, int K) {
 size_t gemm_x16_bytes(int N, int K) { return ((size_t)N * K * 2 + 255) / 256 * 256 + ((size_t)N * 4 + 255) / 256 * 256; }
 
 cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s) {
-  xhalf_kernel<<<in.N, 256, 0, s>>>(in.xplain, in.Kp, in.K, in.x16, in.tok_scale);
+  if (in.xplain) {
+    xhalf_kernel<<<in.N, 256, 0, s>>>(in.xplain, in.Kp, in.K, in.fmt, in.x16, in.tok_scale);
+  } else {
+    const size_t smem = (size_t)in.K * sizeof(float);
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaError_t e0 = cudaGetDevice(&dev);
+    if (e0 != cudaSuccess) return e0;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (dev < 0 || dev >= 64 || !done[dev]) {
+        e0 = cudaFuncSetAttribute(xprep16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmPrepMaxK * 4);
+        if (e0 != cudaSuccess) return e0;
+        if (dev >= 0 && dev < 64) done[dev] = true;
+      }
+    }
+    xprep16_kernel<<<in.N, 512, smem, s>>>(in.x, in.x_dtype, in.signs, in.K, in.block, in.rscale, in.fmt, in.x16,
+                                           in.tok_scale);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   GemmArgs a;

@@ -117,13 +117,19 @@ struct GemmIn {
   const __half* scales;
   const __half* mins;
   int M, K, Kp, N, row_words;
-  const float* xplain;  // [N][Kp] fp32 x' (prep_kernel, plain mode)
+  const float* xplain;  // [N][Kp] fp32 x' (prep_kernel, plain mode), or nullptr: x' made from x here
+  const void* x;        // [N][K] activations (when xplain == nullptr)
+  int x_dtype;
+  const int8_t* signs;  // RWHT column signs (block > 1)
+  int block;            // rotation block tiling K (0 / 1: none)
+  float rscale;         // 1/sqrt(block)
   __half* x16;          // [N][K] fp16 x' scaled per token (written here)
   float* tok_scale;     // [N]
   const float* bias;
   float* y;
   unsigned* status;
 };
+constexpr int kGemmPrepMaxK = 49152;  // K of the one-kernel x' preparation (K floats of smem)
 bool gemm_eligible(int fmt, int K);
 size_t gemm_x16_bytes(int N, int K);
 cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s);
