@@ -23,11 +23,12 @@
 // multiplies two groups at a time against the B fragments of x' (fp16 hi / lo
 // halves of x' in the two columns of each token).
 // Per 128-column group:  sum w x' = s 2^E Q + m Sx  with  Q = sum q x'/2^E.
-// Each unit's 16 x N partial sums per warp go to the workspace; a per-warp
-// arrival counter per row block finds the last stage unit, whose warp adds the
-// stage partials in stage order (deterministic) and writes y.  Every wait is
-// bounded (2 s, %globaltimer): on expiry the kernel records PF_ERR_TIMEOUT in
-// the workspace status word, skips every later wait and finishes.
+// Each unit's 16 x N partial sums per warp go to the workspace (plain
+// stores); combine_kernel, launched next as a programmatic dependent, adds a
+// row block's stage partials in a fixed order (deterministic) and writes y.
+// Every wait is bounded (2 s, %globaltimer): on expiry the kernel records
+// PF_ERR_TIMEOUT in the workspace status word, skips every later wait and
+// finishes.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdlib.h>
