@@ -137,7 +137,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   __shared__ uint64_t bars[3 * kStages + 1];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
-  __shared__ uint4 roots16[240];  // E8 roots as 8 fp16
+  // E8 roots as 8 fp16, indices 240..255 zero, four copies per root in
+  // consecutive 16-byte slots: lane l reads copy l & 3, so the lanes of one
+  // 8-lane phase of a 16-byte load mostly fall in different bank groups
+  __shared__ uint4 roots16[256 * 4];
   __shared__ float tscale[kBN];
 
   unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
@@ -158,16 +161,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
   }
   if (FMT == PF_FMT_E8_RVQ2_G128) {
-    for (int k = threadIdx.x; k < 240; k += blockDim.x) {
+    for (int k = threadIdx.x; k < 256; k += blockDim.x) {
       float r[8];
-      e8_root(k, r);
+      if (k < 240) {
+        e8_root(k, r);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) r[q] = 0.f;
+      }
       uint32_t h[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const __half2 v = __floats2half2_rn(r[2 * q], r[2 * q + 1]);
         h[q] = *reinterpret_cast<const uint32_t*>(&v);
       }
-      roots16[k] = make_uint4(h[0], h[1], h[2], h[3]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) roots16[4 * k + c] = make_uint4(h[0], h[1], h[2], h[3]);
     }
   }
   for (int t = threadIdx.x; t < kBN; t += blockDim.x) tscale[t] = (n0 + t < a.N) ? a.tok_scale[n0 + t] : 0.f;
@@ -307,7 +316,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         for (int c = 0; c < 16; ++c) {
           const uint32_t wv = cw[c >> 1] >> (16 * (c & 1));
           const uint32_t i1 = wv & 0xFFu, i2 = (wv >> 8) & 0xFFu;
-          const uint4 ra = roots16[i1 < 240u ? i1 : 0u], rb = roots16[i2 < 240u ? i2 : 0u];
+          const uint4 ra = roots16[4 * i1 + (lane & 3)], rb = roots16[4 * i2 + (lane & 3)];
           const uint32_t* pa = reinterpret_cast<const uint32_t*>(&ra);
           const uint32_t* pb = reinterpret_cast<const uint32_t*>(&rb);
           uint4 o;
@@ -318,7 +327,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                                       __hmul2(s1, *reinterpret_cast<const __half2*>(&pa[e])));
             ov[e] = *reinterpret_cast<const uint32_t*>(&h);
           }
-          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = rvalid ? o : make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = o;  // rows past M: row 0's codes, never written out
         }
       } else {
         // w = q s + m as one fp16 FMA of the exact code (the stored fp16 s and m)
@@ -348,7 +357,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             const __half2 h = __hfma2(pair_fp16(mk), sx, mx);
             ov[e] = *reinterpret_cast<const uint32_t*>(&h);
           }
-          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = rvalid ? o : make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = o;  // rows past M: row 0's codes, never written out
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
