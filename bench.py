@@ -197,6 +197,7 @@ def main():
     from polarflash_b200 import encoders
     from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
     from polarflash_b200.qweight import QWeight, group_workspace_bytes, qlinear_multi, workspace
+    from polarflash_b200._lib import kernel_launches
 
     N = args.batch
     # --- encode one set per format (this rank's column shard of the N-times-wider
@@ -242,7 +243,6 @@ def main():
     ws = workspace(dev, ws_need)  # zero-filled once; every launch leaves its counters zero
     step_bytes = sum(alg_bytes(qw, N) for qw in base.values())
     packed_bytes = sum(qw.nbytes() for qw in base.values())
-    launches_per_step = len(FORMATS) * len(SHARED)
 
     def step(cp):
         for fmt in FORMATS:
@@ -256,11 +256,16 @@ def main():
 
     stream = torch.cuda.Stream(device=dev)
     graphs = []
+    launches_per_step = None
     with torch.cuda.stream(stream):
         for cp in copies:
             gr = torch.cuda.CUDAGraph()
+            n0 = kernel_launches()
             with torch.cuda.graph(gr, stream=stream):
                 step(cp)
+            # the library's own count of the kernels one step's graph holds
+            # (every grouped GEMV launch plus its partial-sum combine)
+            launches_per_step = kernel_launches() - n0
             graphs.append(gr)
     torch.cuda.synchronize()
 
@@ -290,28 +295,40 @@ def main():
         e1.record(stream)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
-        # keep sampling clocks for at least ~1.5 s of the same replays when the
-        # timed region is shorter than the sampling interval allows
+        # keep sampling clocks for at least ~1.5 s of the same GEMV graphs when
+        # the timed region is shorter than the sampling interval allows (local
+        # replays only: ranks may stop at different counts, so no collective)
         extra = 0
         while time.perf_counter() - t_wall0 < 1.5 and extra < 200000:
             for k in range(200):
-                replay(k, graphs)
+                graphs[k % len(graphs)].replay()
             extra += 200
             torch.cuda.synchronize()
         clk = clocks.stop()
         if extra:
             clk["window"] = "timed region + same-graph replays to 1.5 s"
 
-        # the step holds nothing but the GEMV kernel's launches, so the dominant
-        # kernel's time per step is the timed region's (CUDA events, stream above)
-        ms_run = ms / args.steps
+        # kernel-only time per step: at one GPU the step holds nothing but the
+        # library's launches, so it is the timed region's; at N GPUs the same
+        # graphs are timed again without the all-gather
+        if world > 1:
+            r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            r0.record(stream)
+            for k in range(args.steps):
+                graphs[k % len(graphs)].replay()
+            r1.record(stream)
+            torch.cuda.synchronize()
+            ms_run = r0.elapsed_time(r1) / args.steps
+        else:
+            ms_run = ms / args.steps
 
         # e2e through the public API with host buffers: pinned x in, y out,
         # copies inside the timed region (graph of H2D -> GEMVs -> D2H)
         x_host = {grp: torch.empty(N, xs[grp].shape[1], dtype=torch.float16, pin_memory=True) for grp in xs}
         for grp in x_host:
             x_host[grp].copy_(xs[grp].cpu())
-        y_host = torch.empty(N * y_total, dtype=torch.float32, pin_memory=True)
+        # at N GPUs the step's result is the all-gathered y of every rank's shard
+        y_host = torch.empty(world * N * y_total, dtype=torch.float32, pin_memory=True)
         e2e_graphs = []
         for cp in copies[:4]:
             gr = torch.cuda.CUDAGraph()
@@ -319,16 +336,26 @@ def main():
                 for grp in xs:
                     xs[grp].copy_(x_host[grp], non_blocking=True)
                 step(cp)
-                y_host.copy_(y_all, non_blocking=True)
+                if world == 1:
+                    y_host.copy_(y_all, non_blocking=True)
             e2e_graphs.append(gr)
+
+        def e2e_step(k):
+            e2e_graphs[k % len(e2e_graphs)].replay()
+            if world > 1:
+                dist.all_gather_into_tensor(gather_buf, y_all)
+                y_host.copy_(gather_buf, non_blocking=True)
+
         for k in range(5):
-            e2e_graphs[k % 4].replay()
+            e2e_step(k)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         n_e2e = max(50, min(args.steps, 2000))
         q0.record(stream)
         for k in range(n_e2e):
-            e2e_graphs[k % 4].replay()
+            e2e_step(k)
         q1.record(stream)
         torch.cuda.synchronize()
         ms_e2e = q0.elapsed_time(q1) / n_e2e
@@ -388,7 +415,8 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": round(world * step_bytes / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "how": "CUDA graph of public-API calls: pinned x H2D, 8 grouped GEMV launches, y D2H"},
+                    "how": "CUDA graph of public-API calls: pinned x H2D, 8 grouped GEMV launches"
+                           + (", NCCL all-gather of the column shards" if world > 1 else "") + ", y D2H"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }

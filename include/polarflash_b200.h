@@ -111,6 +111,10 @@ typedef struct pf_qweight {
 PF_API const char* pf_version(void);
 PF_API const char* pf_status_string(int status);
 PF_API int pf_last_cuda_error(void);
+/* Kernel launches this library has issued in this process, over all devices
+ * and streams.  A launch recorded into a CUDA graph counts once, at capture;
+ * graph replays add nothing. */
+PF_API unsigned long long pf_kernel_launches(void);
 
 /* Checks a descriptor (shapes, pointers, alignment) without launching. */
 PF_API int pf_qweight_check(const pf_qweight* w);

@@ -1,6 +1,7 @@
 // C ABI entry points: argument validation on the host, then the launch
 // sequence (x-prep, GEMV) on the caller's stream.  Nothing here allocates.
 #include <stdlib.h>
+#include <atomic>
 #include <string.h>
 
 #include "gemv.cuh"
@@ -340,7 +341,12 @@ int do_run(const pf_qweight* w, int N, const float* bias, float* y, void* ws, cu
 
 }  // namespace
 
+static std::atomic<unsigned long long> g_launches{0};
+void pfb::note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 extern "C" {
+
+unsigned long long pf_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* pf_version(void) { return "polarflash_b200 0.1.0 (sm_100a)"; }
 

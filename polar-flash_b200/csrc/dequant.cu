@@ -167,6 +167,7 @@ cudaError_t launch_dequant(const DequantArgs& a, cudaStream_t s) {
     dequant_e8_kernel<<<blocks, 256, 0, s>>>(a);
   else
     dequant_polar_kernel<<<blocks, 256, 0, s>>>(a);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -182,6 +183,7 @@ cudaError_t launch_rwht_rows(const float* in, float* out, int rows, int K, const
   }
   dim3 grid((K + CH - 1) / CH, rows);
   rwht_rows_kernel<<<grid, 256, smem, s>>>(in, out, K, plan, signs, inverse, CH);
+  note_launch();
   return cudaGetLastError();
 }
 

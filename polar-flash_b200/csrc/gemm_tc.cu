@@ -515,6 +515,7 @@ cudaError_t launch_gemm_fmt(const GemmArgs& a, const __half* x16, cudaStream_t s
   }
   dim3 grid((a.M + kBM - 1) / kBM, (a.N + kBN - 1) / kBN);
   kern<<<grid, kGemmThreads, smem, s>>>(map, a);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -550,6 +551,7 @@ cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s) {
     xprep16_kernel<<<in.N, 512, smem, s>>>(in.x, in.x_dtype, in.signs, in.K, in.block, in.rscale, in.fmt, in.x16,
                                            in.tok_scale);
   }
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   GemmArgs a;

@@ -5,6 +5,10 @@
 
 namespace pfb {
 
+// Adds one to the library's count of kernel launches (read by
+// pf_kernel_launches); called after every launch this library makes.
+void note_launch();
+
 // Workspace head: split-K arrival counters (zero-filled once by the owner of
 // the workspace, left zero by every call); the last slot records a device
 // status word (PF_ERR_TIMEOUT when a bounded pipeline wait gave up).

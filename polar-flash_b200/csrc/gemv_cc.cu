@@ -108,6 +108,7 @@ cudaError_t launch_gemv_cc(const GemvCCArgs& a, cudaStream_t s) {
     gemv_e8_kernel<<<grid, kWarpsCC * 32, 0, s>>>(a);
   else
     gemv_polar_kernel<<<grid, kWarpsCC * 32, 0, s>>>(a);
+  note_launch();
   return cudaGetLastError();
 }
 

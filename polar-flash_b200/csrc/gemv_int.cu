@@ -374,6 +374,7 @@ cudaError_t launch_fmt_nt(const GemvIntArgs& a, int smode, cudaStream_t s) {
     gemv_int_kernel<FMT, NT, TR, kScaleRow><<<grid, kWarps * 32, 0, s>>>(a);
   else
     gemv_int_kernel<FMT, NT, TR, kScaleTensor><<<grid, kWarps * 32, 0, s>>>(a);
+  note_launch();
   return cudaGetLastError();
 }
 

@@ -955,7 +955,9 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], (const TmaArgs)a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], (const TmaArgs)a);
+  if (e == cudaSuccess) note_launch();
+  return e;
 }
 
 template <int FMT, int NT, int LP>
@@ -1101,6 +1103,7 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, combine_kernel, (const TmaArgs)a);
+    if (e == cudaSuccess) note_launch();
     if (e != cudaSuccess) {
       *err = e;
       return PF_ERR_CUDA;

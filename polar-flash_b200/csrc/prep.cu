@@ -164,6 +164,7 @@ cudaError_t launch_prep(const PrepArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
   }
   prep_kernel<<<grid, kPrepThreads, smem, stream>>>(a, CH);
+  note_launch();
   return cudaGetLastError();
 }
 

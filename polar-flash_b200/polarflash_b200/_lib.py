@@ -38,7 +38,7 @@ ERR_TIMEOUT = 7
 
 # Every symbol include/polarflash_b200.h declares.
 EXPORTS = (
-    "pf_version", "pf_status_string", "pf_last_cuda_error", "pf_qweight_check",
+    "pf_version", "pf_status_string", "pf_last_cuda_error", "pf_kernel_launches", "pf_qweight_check",
     "pf_qlinear_workspace_size", "pf_qlinear", "pf_qlinear_group_workspace_size", "pf_qlinear_group",
     "pf_dequant", "pf_unpack_codes", "pf_rwht",
     "pf_native_gemv_int4", "pf_native_gemv_int2", "pf_native_gemm_int4", "pf_qlinear_noalloc",
@@ -87,6 +87,8 @@ def load():
     L.pf_status_string.argtypes = [I]
     L.pf_last_cuda_error.restype = I
     L.pf_last_cuda_error.argtypes = []
+    L.pf_kernel_launches.restype = ctypes.c_ulonglong
+    L.pf_kernel_launches.argtypes = []
     L.pf_qweight_check.restype = I
     L.pf_qweight_check.argtypes = [QW]
     L.pf_qlinear_workspace_size.restype = I
@@ -131,3 +133,9 @@ def check(status: int, what: str = "polarflash_b200") -> None:
 
 def version() -> str:
     return load().pf_version().decode()
+
+
+def kernel_launches() -> int:
+    """Kernel launches the library has issued in this process (graph captures
+    count once; replays add nothing)."""
+    return int(load().pf_kernel_launches())
