@@ -237,8 +237,44 @@ size_t gemm_bytes(const pf_qweight* w, int N) {
   return kCounterBytes + round_up((size_t)nc * Kp * sizeof(float), 256) + gemm_x16_bytes(nc, w->K);
 }
 
+// Batch-1 E8 runs on the lookup-table GEMV when its shapes and alignments
+// allow (PF_E8_LUT=0 keeps it on the GEMM).
+bool e8_lut_enabled() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("PF_E8_LUT");
+    mode = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return mode == 1;
+}
+E8In e8_in(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, const float* bias, float* y) {
+  E8In e;
+  e.codes = w->codes;
+  e.scales = w->scales;
+  e.x = x;
+  e.x_dtype = x_dtype;
+  e.signs = w->had_signs;
+  e.had_block = plan.block > 1 ? plan.block : 0;
+  e.bias = bias;
+  e.y = y;
+  e.M = w->M;
+  e.K = w->K;
+  return e;
+}
+bool use_e8_lut(const pf_qweight* w, int N, const HadPlan& plan, const void* x, int x_dtype) {
+  if (N != 1 || w->format != PF_FMT_E8_RVQ2_G128 || !e8_lut_enabled()) return false;
+  if (plan.ncasc != 0 || (plan.block > 1 && plan.rot_end != w->K)) return false;
+  return e8_lut_eligible(e8_in(w, plan, x, x_dtype, nullptr, nullptr));
+}
+
 size_t workspace_bytes(const pf_qweight* w, int N) {
   if (N < 1) N = 1;
+  if (w->format == PF_FMT_E8_RVQ2_G128 && N == 1) {
+    // either path, depending on the input's alignment
+    const size_t lut = kCounterBytes + e8_lut_partial_bytes(w->M, w->K);
+    const size_t other = use_gemm(w, N) ? gemm_bytes(w, N) : pass_bytes(w, 1);
+    return lut > other ? lut : other;
+  }
   if (use_gemm(w, N)) return gemm_bytes(w, N);
   size_t b = pass_bytes(w, tokens_per_pass(N));
   int tail = N % kMaxGemvTokens;
@@ -493,6 +529,11 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
   st = make_plan(w->K, w->had_block, &plan);
   if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (use_e8_lut(w, N, plan, x, x_dtype)) {
+    cudaError_t e = cudaSuccess;
+    st = launch_e8_lut(e8_in(w, plan, x, x_dtype, bias, y), workspace, s, &e);
+    return st == PF_ERR_CUDA ? cuda_status(e) : st;
+  }
   if (use_gemm(w, N)) return qlinear_gemm(w, plan, x, x_dtype, N, bias, y, workspace, s);
   const size_t xs = dtype_size(x_dtype);
   for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {

@@ -114,6 +114,26 @@ int row_words_of_tma(int fmt, int K);
 int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int x_dtype, void* workspace,
                     cudaStream_t s, cudaError_t* err);
 
+// ---- streaming lookup-table GEMV for E8 RVQ2 weights at batch 1 (gemv_e8.cu)
+struct E8In {
+  const void* codes;     // uint16 [M][K/8]: stage-1 root index (low byte), stage-2 (high byte)
+  const void* scales;    // half2 [M][K/128]: (stage-1, stage-2) scale per 128-column group
+  const void* x;         // [K] activations (x_dtype)
+  int x_dtype;
+  const int8_t* signs;   // RWHT column signs (had_block > 0)
+  int had_block;         // 0 or a power of two <= 512 dividing K
+  const float* bias;
+  float* y;              // [M] fp32
+  int M, K;
+};
+// Shapes, alignments and rotation blocks the kernel takes (else the GEMM serves E8).
+bool e8_lut_eligible(const E8In& in);
+// Workspace bytes after the counter/status head: the stage partial sums.
+size_t e8_lut_partial_bytes(int M, int K);
+// One GEMV launch (+ one partial-sum combine launch when K spans several
+// 256-column stages); workspace as for launch_gemv_tma.  Returns a pf_status.
+int launch_e8_lut(const E8In& in, void* workspace, cudaStream_t s, cudaError_t* err);
+
 // ---- tensor-core dequant-GEMM (gemm_tc.cu) for N > 16 tokens
 struct GemmIn {
   int fmt;

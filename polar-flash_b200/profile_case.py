@@ -22,6 +22,8 @@ def main():
     ap.add_argument("--N", type=int, default=1)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="report device time per call (CUDA events)")
+    ap.add_argument("--copies", type=int, default=1,
+                    help="resident copies of the weight cycled by the timed calls (more than L2 holds: 126 MB)")
     a = ap.parse_args()
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
@@ -34,12 +36,20 @@ def main():
     torch.cuda.synchronize()
     print(f"{a.fmt} {a.M}x{a.K} N={a.N}: packed {qw.nbytes()} B, y[0,:4] = {y[0, :4].tolist()}")
     if a.time:
+        from polarflash_b200.qweight import QWeight
+
+        qws = [qw] + [QWeight(qw.format, qw.M, qw.K, qw.codes.clone(),
+                              qw.scales.clone() if qw.scales is not None else None,
+                              qw.mins.clone() if qw.mins is not None else None, qw.had_block, qw.had_signs,
+                              qw.tensor_scale, list(qw.params)) for _ in range(a.copies - 1)]
         out = torch.empty_like(y)
+        for i in range(len(qws)):
+            qlinear(qws[i], x, out=out)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = max(5, a.iters)
         e0.record()
-        for _ in range(reps):
-            qlinear(qw, x, out=out)
+        for i in range(reps):
+            qlinear(qws[i % len(qws)], x, out=out)
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / reps
