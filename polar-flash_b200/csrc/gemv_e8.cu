@@ -166,6 +166,14 @@ __device__ __forceinline__ void stage_xprime(const E8Args& a, int c0, float* xs,
   }
 }
 
+// Table entry `idx` of the table row at shared address `row` (a constant
+// offset from the lane's row block, which folds into the load's immediate).
+__device__ __forceinline__ float tab_read(uint32_t row, uint32_t idx) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(row + (idx << 2)));
+  return v;
+}
+
 __global__ void __launch_bounds__(kET, 1)
     gemv_e8_lut_kernel(const __grid_constant__ CUtensorMap map, const __grid_constant__ E8Args a) {
   asm volatile("griddepcontrol.launch_dependents;");
@@ -282,8 +290,8 @@ __global__ void __launch_bounds__(kET, 1)
     }
     if (live) {
       const unsigned char* tile = ring + slot * kESlot;
-      // this lane's vectors 8q .. 8q + 7 of the stage
-      const float* tab = tabs + (size_t)(run % XS) * (kEVec * 256) + (8 * q) * 256;
+      // this lane's vectors 8q .. 8q + 7 of the stage: table rows 1 KB apart
+      const uint32_t tab = smem_u32(tabs) + (uint32_t)(run % XS) * kETab + (uint32_t)(8 * q) * 1024u;
       float rs[4];
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
@@ -297,9 +305,10 @@ __global__ void __launch_bounds__(kET, 1)
         for (int j = 0; j < 4; ++j)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const float* tv = tab + (2 * j + h) * 256;
-            A1 += tv[(w[j] >> (16 * h)) & 0xFFu];
-            A2 += tv[(w[j] >> (16 * h + 8)) & 0xFFu];
+            // index bytes 2h (stage 1) and 2h + 1 (stage 2) of word j: vector 2j + h
+            const uint32_t row = tab + (uint32_t)(2 * j + h) * 1024u;
+            A1 += tab_read(row, __byte_perm(w[j], 0u, 0x4440u + 2 * h));
+            A2 += tab_read(row, __byte_perm(w[j], 0u, 0x4441u + 2 * h));
           }
         float part = fmaf(s.x, A1, s.y * A2);
         part += __shfl_xor_sync(0xffffffffu, part, 1);
