@@ -266,12 +266,45 @@ bool use_e8_lut(const pf_qweight* w, int N, const HadPlan& plan, const void* x, 
   if (plan.ncasc != 0 || (plan.block > 1 && plan.rot_end != w->K)) return false;
   return e8_lut_eligible(e8_in(w, plan, x, x_dtype, nullptr, nullptr));
 }
+// Batch-1 recursive polar with 8-column blocks at 1.75 bpw likewise runs on a
+// lookup-table GEMV (PF_POLAR_LUT=0 keeps it on the CUDA-core kernel).
+bool polar_lut_enabled() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("PF_POLAR_LUT");
+    mode = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return mode == 1;
+}
+Polar8In polar8_in(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, const float* bias, float* y) {
+  Polar8In p;
+  memset(&p, 0, sizeof(p));
+  p.codes = w->codes;
+  for (int i = 0; i < 8; ++i) p.alloc[i] = w->params[1 + i];
+  p.r_scale = (float)w->tensor_scale;
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.signs = w->had_signs;
+  p.had_block = plan.block > 1 ? plan.block : 0;
+  p.bias = bias;
+  p.y = y;
+  p.M = w->M;
+  p.K = w->K;
+  return p;
+}
+bool use_polar_lut(const pf_qweight* w, int N, const HadPlan& plan, const void* x, int x_dtype) {
+  if (N != 1 || w->format != PF_FMT_POLAR_RECURSIVE || w->params[0] != 8 || !polar_lut_enabled()) return false;
+  if (plan.ncasc != 0 || (plan.block > 1 && plan.rot_end != w->K)) return false;
+  return polar8_lut_eligible(polar8_in(w, plan, x, x_dtype, nullptr, nullptr));
+}
 
 size_t workspace_bytes(const pf_qweight* w, int N) {
   if (N < 1) N = 1;
-  if (w->format == PF_FMT_E8_RVQ2_G128 && N == 1) {
+  if ((w->format == PF_FMT_E8_RVQ2_G128 || (w->format == PF_FMT_POLAR_RECURSIVE && w->params[0] == 8)) && N == 1) {
     // either path, depending on the input's alignment
-    const size_t lut = kCounterBytes + e8_lut_partial_bytes(w->M, w->K);
+    const size_t part = w->format == PF_FMT_E8_RVQ2_G128 ? e8_lut_partial_bytes(w->M, w->K)
+                                                         : polar8_lut_partial_bytes(w->M, w->K);
+    const size_t lut = kCounterBytes + part;
     const size_t other = use_gemm(w, N) ? gemm_bytes(w, N) : pass_bytes(w, 1);
     return lut > other ? lut : other;
   }
@@ -532,6 +565,11 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
   if (use_e8_lut(w, N, plan, x, x_dtype)) {
     cudaError_t e = cudaSuccess;
     st = launch_e8_lut(e8_in(w, plan, x, x_dtype, bias, y), workspace, s, &e);
+    return st == PF_ERR_CUDA ? cuda_status(e) : st;
+  }
+  if (use_polar_lut(w, N, plan, x, x_dtype)) {
+    cudaError_t e = cudaSuccess;
+    st = launch_polar8_lut(polar8_in(w, plan, x, x_dtype, bias, y), workspace, s, &e);
     return st == PF_ERR_CUDA ? cuda_status(e) : st;
   }
   if (use_gemm(w, N)) return qlinear_gemm(w, plan, x, x_dtype, N, bias, y, workspace, s);

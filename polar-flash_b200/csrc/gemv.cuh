@@ -114,7 +114,8 @@ int row_words_of_tma(int fmt, int K);
 int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int x_dtype, void* workspace,
                     cudaStream_t s, cudaError_t* err);
 
-// ---- streaming lookup-table GEMV for E8 RVQ2 weights at batch 1 (gemv_e8.cu)
+// ---- streaming lookup-table GEMVs at batch 1 (gemv_lut.cu): E8 RVQ2, and
+// recursive polar with block 8 and allocation [3 | 2 2 2 2 | 1 1 | 1]
 struct E8In {
   const void* codes;     // uint16 [M][K/8]: stage-1 root index (low byte), stage-2 (high byte)
   const void* scales;    // half2 [M][K/128]: (stage-1, stage-2) scale per 128-column group
@@ -133,6 +134,22 @@ size_t e8_lut_partial_bytes(int M, int K);
 // One GEMV launch (+ one partial-sum combine launch when K spans several
 // 256-column stages); workspace as for launch_gemv_tma.  Returns a pf_status.
 int launch_e8_lut(const E8In& in, void* workspace, cudaStream_t s, cudaError_t* err);
+
+struct Polar8In {
+  const void* codes;     // rows of K/8 14-bit MSB-first block codes (K * 7 / 32 bytes per row)
+  int alloc[8];          // the block allocation (must be 3 2 2 2 2 1 1 1)
+  float r_scale;
+  const void* x;
+  int x_dtype;
+  const int8_t* signs;
+  int had_block;
+  const float* bias;
+  float* y;
+  int M, K;
+};
+bool polar8_lut_eligible(const Polar8In& in);
+size_t polar8_lut_partial_bytes(int M, int K);
+int launch_polar8_lut(const Polar8In& in, void* workspace, cudaStream_t s, cudaError_t* err);
 
 // ---- tensor-core dequant-GEMM (gemm_tc.cu) for N > 16 tokens
 struct GemmIn {
