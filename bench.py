@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--copies", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode tokens/s figures")
     return ap.parse_args()
 
 
@@ -62,6 +63,79 @@ def synth_weight(M, K, seed, device):
     sg = torch.randint(0, 2, (n,), generator=g, device=device).float() * 2 - 1
     W.view(-1)[pos] = sg * 0.4
     return W
+
+
+def time_tokens(graphs, stream, tokens):
+    """Device ms per token of a decode step that replays every graph once (one
+    graph per layer), over `tokens` tokens after two untimed ones."""
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            for gr in graphs:
+                gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(tokens):
+            for gr in graphs:
+                gr.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / tokens
+
+
+def decode_rates(copies, xs, outs, ws, stream, dev, layers, tokens=20):
+    """Tokens/s of the linears of one batch-1 decode token of the Llama-3-8B
+    shape (`layers` layers of q|k|v, o, gate|up, down, each layer its own
+    resident weight copy): INT3 g128 and INT2 g128 (the bench's weights), and
+    recursive polar at 1.75 bpw (block 8, RWHT-128) encoded here."""
+    from polarflash_b200 import encoders
+    from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
+    from polarflash_b200.qweight import QWeight, qlinear, qlinear_multi
+
+    res = {}
+    for fmt in FORMATS:
+        graphs = []
+        with torch.cuda.stream(stream):
+            for li in range(layers):
+                cp = copies[li % len(copies)]
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for grp in SHARED:
+                        qlinear_multi([cp[(fmt, n)] for n in grp], xs[grp], workspace=ws,
+                                      outs=[outs[(fmt, n)] for n in grp])
+                graphs.append(gr)
+        ms = time_tokens(graphs, stream, tokens)
+        nb = sum(alg_bytes(copies[0][(fmt, n)], 1) for n, _, _ in LINEARS) * layers
+        res[fmt] = {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4), "GB_s": round(nb / ms / 1e6, 1)}
+        del graphs
+    # recursive polar 1.75 bpw: one encoded layer, `layers` resident copies
+    base = {}
+    for i, (name, M, K) in enumerate(LINEARS):
+        W = synth_weight(M, K, 2000 + i, dev)
+        payload, meta = encoders.polar_encode(BlockHadamardTransform(K, 128, device=dev).forward(W), 8, 1.75)
+        base[name] = QWeight(8, M, K, payload, None, None, effective_block(128, K), column_signs(K, 128, dev),
+                             meta["r_scale"], [8] + meta["alloc"])
+        del W
+    pc = [base] + [{n: QWeight(q.format, q.M, q.K, q.codes.clone(), None, None, q.had_block, q.had_signs,
+                               q.tensor_scale, list(q.params)) for n, q in base.items()} for _ in range(layers - 1)]
+    need = max(q.workspace_bytes(1) for q in base.values())
+    pws = torch.zeros(need, dtype=torch.uint8, device=dev)
+    pout = {n: torch.empty(1, M, device=dev) for n, M, _ in LINEARS}
+    xin = {n: xs[next(g for g in SHARED if n in g)] for n, _, _ in LINEARS}
+    graphs = []
+    with torch.cuda.stream(stream):
+        for cp in pc:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for n, _, _ in LINEARS:
+                    qlinear(cp[n], xin[n], workspace=pws, out=pout[n])
+            graphs.append(gr)
+    ms = time_tokens(graphs, stream, tokens)
+    nb = sum(q.nbytes() + q.K * 2 + q.M * 4 for q in base.values()) * layers
+    res["polar_recursive_1.75"] = {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
+                                   "GB_s": round(nb / ms / 1e6, 1)}
+    del graphs, pc
+    return res
 
 
 def alg_bytes(qw, N):
@@ -362,6 +436,13 @@ def main():
         h2d = sum(t.numel() * t.element_size() for t in x_host.values())
         d2h = y_host.numel() * 4
 
+    decode = None
+    if world == 1 and not args.no_decode and N == 1:
+        decode = decode_rates(copies, xs, outs, ws, stream, dev, layers=32)
+        decode["what"] = ("linears of one batch-1 decode token, Llama-3-8B shape: 32 layers x (q|k|v, o, gate|up, "
+                          "down), one resident weight copy per layer, CUDA-graph replays; attention, norms and "
+                          "lm_head not included")
+
     # max over ranks
     t = torch.tensor([ms, ms_run, ms_e2e], device=dev, dtype=torch.float64)
     if world > 1:
@@ -418,6 +499,7 @@ def main():
                     "how": "CUDA graph of public-API calls: pinned x H2D, 8 grouped GEMV launches"
                            + (", NCCL all-gather of the column shards" if world > 1 else "") + ", y D2H"},
             "gpu_launches": launches_per_step * args.steps,
+            "decode_tok_s": decode,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
