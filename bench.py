@@ -90,7 +90,7 @@ def decode_rates(copies, xs, outs, ws, stream, dev, layers, tokens=20):
     recursive polar at 1.75 bpw (block 8, RWHT-128) encoded here."""
     from polarflash_b200 import encoders
     from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
-    from polarflash_b200.qweight import QWeight, qlinear, qlinear_multi
+    from polarflash_b200.qweight import QWeight, group_workspace_bytes, qlinear_multi
 
     res = {}
     for fmt in FORMATS:
@@ -118,17 +118,16 @@ def decode_rates(copies, xs, outs, ws, stream, dev, layers, tokens=20):
         del W
     pc = [base] + [{n: QWeight(q.format, q.M, q.K, q.codes.clone(), None, None, q.had_block, q.had_signs,
                                q.tensor_scale, list(q.params)) for n, q in base.items()} for _ in range(layers - 1)]
-    need = max(q.workspace_bytes(1) for q in base.values())
+    need = max(group_workspace_bytes([base[n] for n in grp], 1) for grp in SHARED)
     pws = torch.zeros(need, dtype=torch.uint8, device=dev)
     pout = {n: torch.empty(1, M, device=dev) for n, M, _ in LINEARS}
-    xin = {n: xs[next(g for g in SHARED if n in g)] for n, _, _ in LINEARS}
     graphs = []
     with torch.cuda.stream(stream):
         for cp in pc:
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr, stream=stream):
-                for n, _, _ in LINEARS:
-                    qlinear(cp[n], xin[n], workspace=pws, out=pout[n])
+                for grp in SHARED:  # one launch per shared input, as for the INT formats
+                    qlinear_multi([cp[n] for n in grp], xs[grp], workspace=pws, outs=[pout[n] for n in grp])
             graphs.append(gr)
     ms = time_tokens(graphs, stream, tokens)
     nb = sum(q.nbytes() + q.K * 2 + q.M * 4 for q in base.values()) * layers

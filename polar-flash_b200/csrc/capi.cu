@@ -564,12 +564,14 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_e8_lut(w, N, plan, x, x_dtype)) {
     cudaError_t e = cudaSuccess;
-    st = launch_e8_lut(e8_in(w, plan, x, x_dtype, bias, y), workspace, s, &e);
+    const E8In in = e8_in(w, plan, x, x_dtype, bias, y);
+    st = launch_e8_lut(&in, 1, workspace, s, &e);
     return st == PF_ERR_CUDA ? cuda_status(e) : st;
   }
   if (use_polar_lut(w, N, plan, x, x_dtype)) {
     cudaError_t e = cudaSuccess;
-    st = launch_polar8_lut(polar8_in(w, plan, x, x_dtype, bias, y), workspace, s, &e);
+    const Polar8In in = polar8_in(w, plan, x, x_dtype, bias, y);
+    st = launch_polar8_lut(&in, 1, workspace, s, &e);
     return st == PF_ERR_CUDA ? cuda_status(e) : st;
   }
   if (use_gemm(w, N)) return qlinear_gemm(w, plan, x, x_dtype, N, bias, y, workspace, s);
@@ -596,11 +598,36 @@ static bool group_streams(int count, const pf_qweight* const* ws) {
   return true;
 }
 
+// Batch-1 groups of E8 or block-8 polar weights that read one x share a
+// table-GEMV launch (tables depend on x only), four weights at a time.
+static int group_lut_kind(int count, const pf_qweight* const* ws, int N) {
+  if (count < 2 || N != 1) return 0;
+  const int f = ws[0]->format;
+  const bool e8 = f == PF_FMT_E8_RVQ2_G128 && e8_lut_enabled();
+  const bool pol = f == PF_FMT_POLAR_RECURSIVE && ws[0]->params[0] == 8 && polar_lut_enabled();
+  if (!e8 && !pol) return 0;
+  for (int i = 1; i < count; ++i) {
+    const pf_qweight* w = ws[i];
+    if (w->format != f || w->K != ws[0]->K || w->had_block != ws[0]->had_block || w->had_signs != ws[0]->had_signs)
+      return 0;
+    if (pol && memcmp(w->params, ws[0]->params, 9 * sizeof(int32_t)) != 0) return 0;
+  }
+  return e8 ? 1 : 2;
+}
+
 static size_t group_bytes(int count, const pf_qweight* const* ws, int N) {
   size_t b = 0;
   for (int i = 0; i < count; ++i) {
     size_t t = workspace_bytes(ws[i], N);
     if (t > b) b = t;
+  }
+  if (const int kind = group_lut_kind(count, ws, N)) {
+    for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
+      size_t t = kCounterBytes;
+      for (int i = c0; i < count && i < c0 + kTmaMaxJobs; ++i)
+        t += kind == 1 ? e8_lut_partial_bytes(ws[i]->M, ws[i]->K) : polar8_lut_partial_bytes(ws[i]->M, ws[i]->K);
+      if (t > b) b = t;
+    }
   }
   if (N <= kMaxGemvTokens && group_streams(count, ws)) {
     int np = tokens_per_pass(N < 1 ? 1 : N);
@@ -638,9 +665,35 @@ int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* const* 
   if (N == 0) return PF_OK;
   if (!workspace || ws_bytes < group_bytes(count, ws, N)) return PF_ERR_WORKSPACE;
   if (!aligned(workspace, 256)) return PF_ERR_ALIGNMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (const int kind = group_lut_kind(count, ws, N)) {
+    // every member eligible and reading the same x: table-GEMV launches of up to four
+    HadPlan plan;
+    bool ok = make_plan(ws[0]->K, ws[0]->had_block, &plan) == PF_OK &&
+              (kind == 1 ? use_e8_lut(ws[0], 1, plan, xs[0], x_dtype) : use_polar_lut(ws[0], 1, plan, xs[0], x_dtype));
+    for (int i = 1; i < count && ok; ++i) ok = xs[i] == xs[0];
+    for (int c0 = 0; ok && c0 < count; c0 += kTmaMaxJobs) {
+      const int n = count - c0 < kTmaMaxJobs ? count - c0 : kTmaMaxJobs;
+      cudaError_t e = cudaSuccess;
+      int st;
+      if (kind == 1) {
+        E8In in[kTmaMaxJobs];
+        for (int k = 0; k < n; ++k)
+          in[k] = e8_in(ws[c0 + k], plan, xs[0], x_dtype, biases ? biases[c0 + k] : nullptr, ys[c0 + k]);
+        st = launch_e8_lut(in, n, workspace, s, &e);
+      } else {
+        Polar8In in[kTmaMaxJobs];
+        for (int k = 0; k < n; ++k)
+          in[k] = polar8_in(ws[c0 + k], plan, xs[0], x_dtype, biases ? biases[c0 + k] : nullptr, ys[c0 + k]);
+        st = launch_polar8_lut(in, n, workspace, s, &e);
+      }
+      if (st == PF_ERR_CUDA) return cuda_status(e);
+      if (st) return st;
+    }
+    if (ok) return PF_OK;
+  }
   bool grouped = N <= kMaxGemvTokens && group_streams(count, ws);
   for (int i = 0; i < count && grouped; ++i) grouped = x_tma_aligned(xs[i], x_dtype);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t xsz = dtype_size(x_dtype);
   if (!grouped) {
     for (int i = 0; i < count; ++i) {

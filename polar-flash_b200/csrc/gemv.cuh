@@ -131,9 +131,11 @@ struct E8In {
 bool e8_lut_eligible(const E8In& in);
 // Workspace bytes after the counter/status head: the stage partial sums.
 size_t e8_lut_partial_bytes(int M, int K);
-// One GEMV launch (+ one partial-sum combine launch when K spans several
-// 256-column stages); workspace as for launch_gemv_tma.  Returns a pf_status.
-int launch_e8_lut(const E8In& in, void* workspace, cudaStream_t s, cudaError_t* err);
+// One GEMV launch over `count` <= 4 weights that share x, K and the rotation
+// (+ one partial-sum combine launch when K spans several 256-column stages);
+// the workspace holds the status word in its head, then every weight's stage
+// partial sums.  Returns a pf_status.
+int launch_e8_lut(const E8In* in, int count, void* workspace, cudaStream_t s, cudaError_t* err);
 
 struct Polar8In {
   const void* codes;     // rows of K/8 14-bit MSB-first block codes (K * 7 / 32 bytes per row)
@@ -149,7 +151,7 @@ struct Polar8In {
 };
 bool polar8_lut_eligible(const Polar8In& in);
 size_t polar8_lut_partial_bytes(int M, int K);
-int launch_polar8_lut(const Polar8In& in, void* workspace, cudaStream_t s, cudaError_t* err);
+int launch_polar8_lut(const Polar8In* in, int count, void* workspace, cudaStream_t s, cudaError_t* err);
 
 // ---- tensor-core dequant-GEMM (gemm_tc.cu) for N > 16 tokens
 struct GemmIn {

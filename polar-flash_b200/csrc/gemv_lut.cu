@@ -11,17 +11,19 @@
 //    inverse_recursive: psi splits the radius between the two halves, phi_h
 //    each half between its two pairs, theta_j each pair), so
 //      <w, x'_v> = r (Q0[th0 th1 phi0 psi] + Q1[th2 th3 phi1 psi])
-//    with Q_h = r_scale (cos | sin psi)(cos phi_h P_2h[th] + sin phi_h P_2h+1[th'])
+//    with Q_h = (cos | sin psi)(cos phi_h P_2h[th] + sin phi_h P_2h+1[th'])
 //    and P_j[c] = cos th_j(c) x'_2j + sin th_j(c) x'_2j+1: two 64-entry
-//    tables per vector.
+//    tables per vector (r_scale multiplies the row sums).
 //
 // The weight's block RWHT is folded into x (x' = forward RWHT of x).  A CTA
 // builds the tables of a column stage in shared memory from x' (fp32), then
 // a weight vector costs two table reads and two adds: no weight is decoded.
 //
-// Work unit = (stage, block of 512 rows), dealt to the CTAs stream-K style in
-// stage-major order, so a CTA's consecutive units share a stage and its
-// tables.  One 16-warp CTA per SM; every warp owns 32 rows of a unit and
+// A launch serves up to four weights ("jobs") that read the same x (q|k|v,
+// gate|up): the tables depend on x and the stage only, so the jobs share
+// them.  Work unit = (stage, block of 512 rows of one job), dealt to the CTAs
+// stream-K style in stage-major order (every job's row blocks of a stage, then
+// the next stage), so a CTA's consecutive units share a stage and its tables.  One 16-warp CTA per SM; every warp owns 32 rows of a unit and
 // streams them through its own ring of shared-memory slots: lane 0 issues the
 // TMA copy of the 32-row code tile (L2 evict-first), E8 lanes copy their row's
 // group scales with cp.async, and the copies arrive on the slot's mbarrier.
@@ -56,18 +58,37 @@ constexpr int kLMaxStages = 8;
 constexpr int kLMaxTabs = 3;
 constexpr int kLSmemBudget = 216 * 1024;
 
-struct LutArgs {
+constexpr int kLutMaxJobs = 4;
+
+struct LutJob {  // one weight of a launch
   const uint32_t* scales;  // E8: half2 [M][G] as words
-  const void* x;
-  const int8_t* signs;
   const float* bias;
   float* y;
   float* partials;  // [n_rb][spb][kLRows] stage row sums (spb > 1)
+  float out_scale;  // polar r_scale (1 for E8)
+  int M, n_rb, rb0;  // rows, row blocks, first row block of the launch's block list
+};
+
+struct LutArgs {
+  LutJob job[kLutMaxJobs];
+  const void* x;  // shared by the jobs
+  const int8_t* signs;
   unsigned* status;
   float had_rscale;
-  float r_scale;  // polar
-  int had_block, x_dtype, M, K, G, n_rb, spb, n_units, NS, XS;
+  int n_jobs, had_block, x_dtype, K, G, n_rb, spb, n_units, NS, XS;
 };
+
+__device__ __forceinline__ const LutJob& lut_job(const LutArgs& a, int j) {
+  return j == 0 ? a.job[0] : j == 1 ? a.job[1] : j == 2 ? a.job[2] : a.job[3];
+}
+// Job holding row block `grb` of the launch's block list.
+__device__ __forceinline__ int lut_job_of(const LutArgs& a, int grb) {
+  int j = 0;
+#pragma unroll
+  for (int k = 1; k < kLutMaxJobs; ++k)
+    if (k < a.n_jobs && grb >= a.job[k].rb0) j = k;
+  return j;
+}
 
 // Table entry `idx` of the table row at shared address `row` (a constant
 // offset from the lane's row block, which folds into the load's immediate).
@@ -170,7 +191,7 @@ struct Polar8Pol {
       const int ta = e >> 4, tb = (e >> 2) & 3, ph = (e >> 1) & 1, ps = e & 1;
       const float2 fph = cs[(4 + h) * kPolarTabPerCol + ph], fps = cs[6 * kPolarTabPerCol + ps];
       const float half = fmaf(fph.x, Pa[ta], fph.y * Pb[tb]);
-      out[e] = a.r_scale * ((h == 0 ? fps.x : fps.y) * half);
+      out[e] = (h == 0 ? fps.x : fps.y) * half;
     }
   }
   __device__ static float part(const unsigned char* tile, int r, int q, uint32_t tab) {
@@ -301,11 +322,17 @@ __device__ __forceinline__ void stage_xprime(const LutArgs& a, int c0, int cols,
 
 template <class Pol>
 __global__ void __launch_bounds__(kLT, 1)
-    lut_gemv_kernel(const __grid_constant__ CUtensorMap map, const __grid_constant__ LutArgs a) {
+    lut_gemv_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
+                    const __grid_constant__ CUtensorMap map2, const __grid_constant__ CUtensorMap map3,
+                    const __grid_constant__ LutArgs a) {
   constexpr uint32_t kSlot = Pol::kCodes + Pol::kScales;
   constexpr uint32_t kTab = Pol::kTabFloats * 4;
   asm volatile("griddepcontrol.launch_dependents;");
-  if (threadIdx.x == 32) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map)) : "memory");
+  if (threadIdx.x >= 32 && threadIdx.x < 32 + kLutMaxJobs) {
+    const int k = threadIdx.x - 32;
+    const CUtensorMap* m = k == 0 ? &map0 : k == 1 ? &map1 : k == 2 ? &map2 : &map3;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+  }
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ int abort_flag;
@@ -334,28 +361,31 @@ __global__ void __launch_bounds__(kLT, 1)
   const int nunits = u1 - u0;
   if (nunits <= 0) return;
 
-  // ---- load side: this warp's next unit to request
-  int fst = u0 / a.n_rb, frb = u0 - fst * a.n_rb;
+  // ---- load side: this warp's next unit to request (stage, block of the list)
+  int fst = u0 / a.n_rb, fgrb = u0 - fst * a.n_rb;
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   const uint32_t ring_s = smem_u32(ring);
   auto request = [&](int slot) {
+    const int fj = lut_job_of(a, fgrb);
+    const LutJob& jb = lut_job(a, fj);
+    const CUtensorMap* map = fj == 0 ? &map0 : fj == 1 ? &map1 : fj == 2 ? &map2 : &map3;
     const uint32_t sb = ring_s + slot * kSlot, bar = full0 + 8 * slot;
-    const int row0 = frb * kLRows + warp * kLRowsW;
+    const int row0 = (fgrb - jb.rb0) * kLRows + warp * kLRowsW;
     __syncwarp();
     if (lane == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_expect(bar, Pol::kCodes);
-      tma_2d(sb, &map, fst * (int)(Pol::kRowCode / 4), row0, bar, policy);
+      tma_2d(sb, map, fst * (int)(Pol::kRowCode / 4), row0, bar, policy);
     }
     if constexpr (Pol::kScales > 0) {
       const int grow = row0 + lane;
-      const bool ok = grow < a.M;
-      cp_async8(sb + Pol::kCodes + lane * 8, a.scales + (ok ? (size_t)grow * a.G + 2 * fst : 0), ok ? 8u : 0u);
+      const bool ok = grow < jb.M;
+      cp_async8(sb + Pol::kCodes + lane * 8, jb.scales + (ok ? (size_t)grow * a.G + 2 * fst : 0), ok ? 8u : 0u);
       cp_async_arrive(bar);
     }
-    if (++frb == a.n_rb) {
-      frb = 0;
+    if (++fgrb == a.n_rb) {
+      fgrb = 0;
       ++fst;
     }
   };
@@ -383,7 +413,7 @@ __global__ void __launch_bounds__(kLT, 1)
   for (; requested < NS && requested < nunits; ++requested) request(requested);
 
   const int r8 = lane >> 2, q = lane & 3;
-  int st = st_first, rb = u0 - st_first * a.n_rb, run = 0, slot = 0;
+  int st = st_first, grb = u0 - st_first * a.n_rb, run = 0, slot = 0;
   uint32_t phase = 0;
   bool live = true;
   for (int it = 0; it < nunits; ++it) {
@@ -410,14 +440,17 @@ __global__ void __launch_bounds__(kLT, 1)
         rs[p] = v;
       }
       if (q == 0) {
+        const LutJob& jb = lut_job(a, lut_job_of(a, grb));
+        const int rb = grb - jb.rb0;
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
           const int rl = warp * kLRowsW + 8 * p + r8;
           const int row = rb * kLRows + rl;
+          const float v = rs[p] * jb.out_scale;
           if (a.spb == 1) {
-            if (row < a.M) a.y[row] = rs[p] + (a.bias ? a.bias[row] : 0.f);
+            if (row < jb.M) jb.y[row] = v + (jb.bias ? jb.bias[row] : 0.f);
           } else {
-            __stcg(a.partials + ((size_t)rb * a.spb + st) * kLRows + rl, rs[p]);
+            __stcg(jb.partials + ((size_t)rb * a.spb + st) * kLRows + rl, v);
           }
         }
       }
@@ -430,8 +463,8 @@ __global__ void __launch_bounds__(kLT, 1)
       slot = 0;
       phase ^= 1u;
     }
-    if (++rb == a.n_rb) {
-      rb = 0;
+    if (++grb == a.n_rb) {
+      grb = 0;
       ++st;
       ++run;
     }
@@ -445,14 +478,23 @@ __global__ void __launch_bounds__(kLT, 1)
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-// y = the sum of a row's stage sums in stage order (+ bias).
+// y = the sum of a row's stage sums in stage order (+ bias).  Block b of the
+// grid covers 256 rows of one job (jobs start on a new block).
 __global__ void __launch_bounds__(256) lut_combine_kernel(const __grid_constant__ LutArgs a) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int row = blockIdx.x * 256 + threadIdx.x;
-  if (row >= a.M) return;
+  int blk = blockIdx.x, j = 0;
+  for (; j < a.n_jobs; ++j) {
+    const int nb = (lut_job(a, j).M + 255) / 256;
+    if (blk < nb) break;
+    blk -= nb;
+  }
+  if (j >= a.n_jobs) return;
+  const LutJob& jb = lut_job(a, j);
+  const int row = blk * 256 + threadIdx.x;
+  if (row >= jb.M) return;
   const int rb = row / kLRows, r = row - rb * kLRows;
-  const float* p = a.partials + (size_t)rb * a.spb * kLRows + r;
+  const float* p = jb.partials + (size_t)rb * a.spb * kLRows + r;
   float sum = 0.f;
   int st = 0;
   for (; st + 8 <= a.spb; st += 8) {
@@ -463,7 +505,7 @@ __global__ void __launch_bounds__(256) lut_combine_kernel(const __grid_constant_
     for (int k = 0; k < 8; ++k) sum += v[k];
   }
   for (; st < a.spb; ++st) sum += __ldcg(p + (size_t)st * kLRows);
-  a.y[row] = sum + (a.bias ? a.bias[row] : 0.f);
+  jb.y[row] = sum + (jb.bias ? jb.bias[row] : 0.f);
 }
 
 int lut_sm_count() {
@@ -510,30 +552,39 @@ size_t lut_partial_bytes(int M, int K, int cols) {
   return (n_rb * spb * kLRows * sizeof(float) + 255) / 256 * 256;
 }
 
+// One launch over a.n_jobs weights sharing x, K and the rotation (the jobs'
+// scales, bias, y, out_scale and M set by the caller).
 template <class Pol>
-int launch_lut(LutArgs& a, const void* codes, void* workspace, cudaStream_t s, cudaError_t* err) {
+int launch_lut(LutArgs& a, const void* const* codes, void* workspace, cudaStream_t s, cudaError_t* err) {
   constexpr uint32_t kSlot = Pol::kCodes + Pol::kScales;
   constexpr size_t kTab = (size_t)Pol::kTabFloats * 4;
   auto fn = lut_encode_fn();
   a.G = a.K / 128;
-  a.n_rb = (a.M + kLRows - 1) / kLRows;
   a.spb = a.K / Pol::kCols;
-  a.n_units = a.n_rb * a.spb;
   a.status = static_cast<unsigned*>(workspace) + kWsStatusSlot;
-  a.partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsCounterBytes);
   const size_t row_bytes = (size_t)(a.K / Pol::kCols) * Pol::kRowCode;
-
-  CUtensorMap map;
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)a.M};
+  char* part = static_cast<char*>(workspace) + kWsCounterBytes;
+  int rb0 = 0;
+  CUtensorMap maps[kLutMaxJobs];
+  for (int k = 0; k < a.n_jobs; ++k) {
+    LutJob& jb = a.job[k];
+    jb.n_rb = (jb.M + kLRows - 1) / kLRows;
+    jb.rb0 = rb0;
+    rb0 += jb.n_rb;
+    jb.partials = reinterpret_cast<float*>(part);
+    part += lut_partial_bytes(jb.M, a.K, Pol::kCols);
+    cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)jb.M};
     cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
     cuuint32_t box[2] = {(cuuint32_t)(Pol::kRowCode / 4), (cuuint32_t)kLRowsW};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(&maps[k], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes[k]), dims, strides, box,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return PF_ERR_UNSUPPORTED;
   }
+  for (int k = a.n_jobs; k < kLutMaxJobs; ++k) maps[k] = maps[0];
+  a.n_rb = rb0;
+  a.n_units = a.n_rb * a.spb;
   int P = lut_sm_count();
   if (P > a.n_units) P = a.n_units;
   if ((unsigned long long)a.n_units * (unsigned long long)(P + 1) >= (1ull << 32)) return PF_ERR_SHAPE;
@@ -584,15 +635,17 @@ int launch_lut(LutArgs& a, const void* codes, void* workspace, cudaStream_t s, c
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, map, (const LutArgs)a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], (const LutArgs)a);
   if (e != cudaSuccess) {
     *err = e;
     return PF_ERR_CUDA;
   }
   note_launch();
   if (a.spb > 1) {
+    int blocks = 0;
+    for (int k = 0; k < a.n_jobs; ++k) blocks += (a.job[k].M + 255) / 256;
     cudaLaunchConfig_t cc = {};
-    cc.gridDim = dim3((a.M + 255) / 256);
+    cc.gridDim = dim3(blocks);
     cc.blockDim = dim3(256);
     cc.stream = s;
     cc.attrs = attr;
@@ -607,8 +660,7 @@ int launch_lut(LutArgs& a, const void* codes, void* workspace, cudaStream_t s, c
   return PF_OK;
 }
 
-LutArgs lut_args(const void* x, int x_dtype, const int8_t* signs, int had_block, const float* bias, float* y, int M,
-                 int K) {
+LutArgs lut_args(const void* x, int x_dtype, const int8_t* signs, int had_block, int K) {
   LutArgs a;
   memset(&a, 0, sizeof(a));
   a.x = x;
@@ -616,9 +668,6 @@ LutArgs lut_args(const void* x, int x_dtype, const int8_t* signs, int had_block,
   a.signs = had_block ? signs : nullptr;
   a.had_block = had_block;
   a.had_rscale = had_block ? 1.f / sqrtf((float)had_block) : 1.f;
-  a.bias = bias;
-  a.y = y;
-  a.M = M;
   a.K = K;
   return a;
 }
@@ -633,14 +682,6 @@ bool e8_lut_eligible(const E8In& in) {
 
 size_t e8_lut_partial_bytes(int M, int K) { return lut_partial_bytes(M, K, E8Pol::kCols); }
 
-int launch_e8_lut(const E8In& in, void* workspace, cudaStream_t s, cudaError_t* err) {
-  *err = cudaSuccess;
-  if (!e8_lut_eligible(in)) return PF_ERR_UNSUPPORTED;
-  LutArgs a = lut_args(in.x, in.x_dtype, in.signs, in.had_block, in.bias, in.y, in.M, in.K);
-  a.scales = static_cast<const uint32_t*>(in.scales);
-  return launch_lut<E8Pol>(a, in.codes, workspace, s, err);
-}
-
 bool polar8_lut_eligible(const Polar8In& in) {
   static const int kAlloc[8] = {3, 2, 2, 2, 2, 1, 1, 1};
   for (int i = 0; i < 8; ++i)
@@ -650,12 +691,45 @@ bool polar8_lut_eligible(const Polar8In& in) {
 
 size_t polar8_lut_partial_bytes(int M, int K) { return lut_partial_bytes(M, K, Polar8Pol::kCols); }
 
-int launch_polar8_lut(const Polar8In& in, void* workspace, cudaStream_t s, cudaError_t* err) {
+int launch_e8_lut(const E8In* in, int count, void* workspace, cudaStream_t s, cudaError_t* err) {
   *err = cudaSuccess;
-  if (!polar8_lut_eligible(in)) return PF_ERR_UNSUPPORTED;
-  LutArgs a = lut_args(in.x, in.x_dtype, in.signs, in.had_block, in.bias, in.y, in.M, in.K);
-  a.r_scale = in.r_scale;
-  return launch_lut<Polar8Pol>(a, in.codes, workspace, s, err);
+  if (count < 1 || count > kLutMaxJobs) return PF_ERR_INVALID_ARGUMENT;
+  LutArgs a = lut_args(in[0].x, in[0].x_dtype, in[0].signs, in[0].had_block, in[0].K);
+  const void* codes[kLutMaxJobs];
+  for (int k = 0; k < count; ++k) {
+    if (!e8_lut_eligible(in[k]) || in[k].x != in[0].x || in[k].K != in[0].K || in[k].had_block != in[0].had_block ||
+        in[k].signs != in[0].signs || in[k].x_dtype != in[0].x_dtype)
+      return PF_ERR_UNSUPPORTED;
+    LutJob& jb = a.job[k];
+    jb.scales = static_cast<const uint32_t*>(in[k].scales);
+    jb.bias = in[k].bias;
+    jb.y = in[k].y;
+    jb.M = in[k].M;
+    jb.out_scale = 1.f;
+    codes[k] = in[k].codes;
+  }
+  a.n_jobs = count;
+  return launch_lut<E8Pol>(a, codes, workspace, s, err);
+}
+
+int launch_polar8_lut(const Polar8In* in, int count, void* workspace, cudaStream_t s, cudaError_t* err) {
+  *err = cudaSuccess;
+  if (count < 1 || count > kLutMaxJobs) return PF_ERR_INVALID_ARGUMENT;
+  LutArgs a = lut_args(in[0].x, in[0].x_dtype, in[0].signs, in[0].had_block, in[0].K);
+  const void* codes[kLutMaxJobs];
+  for (int k = 0; k < count; ++k) {
+    if (!polar8_lut_eligible(in[k]) || in[k].x != in[0].x || in[k].K != in[0].K ||
+        in[k].had_block != in[0].had_block || in[k].signs != in[0].signs || in[k].x_dtype != in[0].x_dtype)
+      return PF_ERR_UNSUPPORTED;
+    LutJob& jb = a.job[k];
+    jb.bias = in[k].bias;
+    jb.y = in[k].y;
+    jb.M = in[k].M;
+    jb.out_scale = in[k].r_scale;
+    codes[k] = in[k].codes;
+  }
+  a.n_jobs = count;
+  return launch_lut<Polar8Pol>(a, codes, workspace, s, err);
 }
 
 }  // namespace pfb

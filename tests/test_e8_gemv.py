@@ -151,3 +151,25 @@ def test_full_size_against_tensor_core_path(tmp_path):
     assert_rel(res["1"]["y"][:, :4096], ref)
     assert_rel(res["0"]["y"][:, :4096], ref)
     assert_rel(res["1"]["y"], res["0"]["y"])
+
+
+def test_group_launch_bit_identical_to_single():
+    """q|k|v-like members reading one x share the table-GEMV launches (four per
+    launch, here 4 + 1) and give exactly the single-weight results."""
+    from polarflash_b200 import qlinear
+    from polarflash_b200.qweight import qlinear_group
+
+    K = 2048
+    qws, pays, metas, bs = [], [], [], []
+    for i, M in enumerate((1000, 256, 256, 700, 512)):
+        qw, pay, meta = _e8_qweight(M, K, 40 + i)
+        qws.append(qw)
+        pays.append(pay)
+        metas.append(meta)
+        bs.append((torch.randn(M, generator=torch.Generator().manual_seed(i)) * 0.1).cuda())
+    x = _x(1, K, 6).cuda()
+    ys = qlinear_group(qws, [x] * len(qws), bs)
+    for i, qw in enumerate(qws):
+        assert torch.equal(ys[i], qlinear(qw, x, bs[i])), f"weight {i}"
+        assert_rel(ys[i].cpu().numpy(), oracle.linear("e8_rvq2_g128", pays[i], qw.M, K, metas[i],
+                                                      x.float().cpu().numpy(), bs[i].cpu().numpy()))

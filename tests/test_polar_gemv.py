@@ -151,3 +151,24 @@ def test_full_size_against_cuda_core_kernel(tmp_path):
     assert_rel(res["1"]["y"][:, :R], ref)
     assert_rel(res["0"]["y"][:, :R], ref)
     assert_rel(res["1"]["y"], res["0"]["y"])
+
+
+def test_group_launch_bit_identical_to_single():
+    """gate|up-like members reading one x share the table-GEMV launches (each
+    member's r_scale applied to its row sums) and give exactly the
+    single-weight results."""
+    from polarflash_b200 import qlinear
+    from polarflash_b200.qweight import qlinear_group
+
+    K = 4096
+    qws, pays, metas = [], [], []
+    for i, M in enumerate((1500, 512, 512, 2048, 100)):
+        qw, pay, meta = _polar_qweight(M, K, 60 + i)
+        qws.append(qw)
+        pays.append(pay)
+        metas.append(meta)
+    x = _x(1, K, 12).cuda()
+    ys = qlinear_group(qws, [x] * len(qws))
+    for i, qw in enumerate(qws):
+        assert torch.equal(ys[i], qlinear(qw, x)), f"weight {i}"
+        assert_rel(ys[i].cpu().numpy(), _ref(pays[i], qw.M, K, metas[i], x.float().cpu().numpy()))
