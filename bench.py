@@ -54,14 +54,14 @@ def parse():
     return ap.parse_args()
 
 
-def synth_weight(M, K, seed, device):
-    """W ~ N(0, 0.02^2) with 0.1% of entries at +-20 sigma (seeded positions)."""
+def synth_weight(M, K, seed, device, std=0.02):
+    """W ~ N(0, std^2) with 0.1% of entries at +-20 sigma (seeded positions)."""
     g = torch.Generator(device=device).manual_seed(seed)
-    W = torch.randn(M, K, generator=g, device=device) * 0.02
+    W = torch.randn(M, K, generator=g, device=device) * std
     n = max(1, int(0.001 * M * K))
     pos = torch.randint(0, M * K, (n,), generator=g, device=device)
     sg = torch.randint(0, 2, (n,), generator=g, device=device).float() * 2 - 1
-    W.view(-1)[pos] = sg * 0.4
+    W.view(-1)[pos] = sg * (20.0 * std)
     return W
 
 
@@ -133,7 +133,54 @@ def decode_rates(copies, xs, outs, ws, stream, dev, layers, tokens=20):
     nb = sum(q.nbytes() + q.K * 2 + q.M * 4 for q in base.values()) * layers
     res["polar_recursive_1.75"] = {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
                                    "GB_s": round(nb / ms / 1e6, 1)}
-    del graphs, pc
+    del graphs, pc, base
+    res.update(decode_rates_70b_e8(stream, dev, tokens))
+    return res
+
+
+LINEARS_70B = [("q", 8192, 8192), ("k", 1024, 8192), ("v", 1024, 8192), ("o", 8192, 8192),
+               ("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672)]
+
+
+def decode_rates_70b_e8(stream, dev, tokens, layers=80):
+    """Tokens/s of the linears of a Llama-3-70B-shaped decode step (80 layers of
+    q|k|v, o, gate|up, down; W ~ N(0, 0.01^2) with 0.1 % outliers, RWHT-128,
+    E8 RVQ2) at batch 1 (table GEMV) and batch 32 (tensor-core GEMM): one
+    encoded layer, one resident copy per layer (19.3 GB)."""
+    from polarflash_b200 import encoders
+    from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
+    from polarflash_b200.qweight import QWeight, group_workspace_bytes, qlinear_multi
+
+    base = {}
+    for i, (name, M, K) in enumerate(LINEARS_70B):
+        W = synth_weight(M, K, 3000 + i, dev, std=0.01)
+        idx, sc = encoders.e8_encode(BlockHadamardTransform(K, 128, device=dev).forward(W))
+        base[name] = QWeight(7, M, K, idx.reshape(-1), sc, None, effective_block(128, K), column_signs(K, 128, dev))
+        del W
+    pc = [base] + [{n: QWeight(q.format, q.M, q.K, q.codes.clone(), q.scales.clone(), None, q.had_block,
+                               q.had_signs) for n, q in base.items()} for _ in range(layers - 1)]
+    kdim = {n: K for n, _, K in LINEARS_70B}
+    layer_bytes = sum(q.nbytes() for q in base.values())
+    res = {}
+    for B in (1, 32):
+        g = torch.Generator().manual_seed(B)
+        xs = {grp: torch.randn(B, kdim[grp[0]], generator=g).half().to(dev) for grp in SHARED}
+        outs = {n: torch.empty(B, M, device=dev) for n, M, _ in LINEARS_70B}
+        need = max(group_workspace_bytes([base[n] for n in grp], B) for grp in SHARED)
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+        graphs = []
+        with torch.cuda.stream(stream):
+            for cp in pc:
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for grp in SHARED:
+                        qlinear_multi([cp[n] for n in grp], xs[grp], workspace=ws, outs=[outs[n] for n in grp])
+                graphs.append(gr)
+        ms = time_tokens(graphs, stream, max(4, tokens // (4 if B > 1 else 1)))
+        res[f"e8_rvq2_70b_batch{B}"] = {"tok_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+                                        "GB_s": round(layer_bytes * layers / ms / 1e6, 1)}
+        del graphs
+    del pc, base
     return res
 
 
@@ -438,8 +485,9 @@ def main():
     decode = None
     if world == 1 and not args.no_decode and N == 1:
         decode = decode_rates(copies, xs, outs, ws, stream, dev, layers=32)
-        decode["what"] = ("linears of one batch-1 decode token, Llama-3-8B shape: 32 layers x (q|k|v, o, gate|up, "
-                          "down), one resident weight copy per layer, CUDA-graph replays; attention, norms and "
+        decode["what"] = ("linears of one decode step: Llama-3-8B shape (32 layers x q|k|v, o, gate|up, down) at "
+                          "batch 1 for INT3 / INT2 / polar 1.75, Llama-3-70B shape (80 layers, E8 RVQ2) at batch 1 "
+                          "and 32; one resident weight copy per layer, CUDA-graph replays; attention, norms and "
                           "lm_head not included")
 
     # max over ranks

@@ -173,3 +173,26 @@ def test_group_launch_bit_identical_to_single():
         assert torch.equal(ys[i], qlinear(qw, x, bs[i])), f"weight {i}"
         assert_rel(ys[i].cpu().numpy(), oracle.linear("e8_rvq2_g128", pays[i], qw.M, K, metas[i],
                                                       x.float().cpu().numpy(), bs[i].cpu().numpy()))
+
+
+@pytest.mark.parametrize("N", [1, 32, 2048])
+def test_llama70b_down_projection(N):
+    """The 70B stack's longest linear (down, 8192 x 28672, W ~ N(0, 0.01^2) with
+    0.1 % outliers, RWHT-128) at decode batch 1 (table GEMV) and 32 and at a
+    2048-token prefill (tensor-core GEMM), against the oracle on its first rows."""
+    from polarflash_b200 import encoders, qlinear
+    from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
+    from polarflash_b200.qweight import QWeight
+
+    M, K = 8192, 28672
+    dev = torch.device("cuda")
+    W = _w(M, K, 70, std=0.01).to(dev)
+    idx, sc = encoders.e8_encode(BlockHadamardTransform(K, 128, device=dev).forward(W))
+    del W
+    qw = QWeight(7, M, K, idx.reshape(-1), sc, None, effective_block(128, K), column_signs(K, 128, dev))
+    x = _x(N, K, 71)
+    y = qlinear(qw, x.to(dev)).cpu().numpy()
+    R = 256 if N <= 32 else 32
+    meta = {"hadamard_rotation": True, "hadamard_block_size": 128}
+    pay = {"idx": idx[:R].cpu().numpy(), "scales": sc[:R].cpu().numpy()}
+    assert_rel(y[:, :R], oracle.linear("e8_rvq2_g128", pay, R, K, meta, x.float().numpy()))
