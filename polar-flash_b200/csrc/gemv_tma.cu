@@ -92,11 +92,12 @@ struct WarpSlot {
 
 // x' record of one 128-column group: [NT tiles][4 k-step pairs][LP lanes]
 // uint4 (the B fragments of two k-steps), then float4 {Sx, 1024 2^E, -, -}
-// per token slot.
-template <int NT, int LP>
+// per token slot.  A tile's 8 B columns hold TPT tokens: 4 tokens as fp16
+// hi / lo pairs (N <= 4), or 8 tokens as one fp16 each (N > 4).
+template <int NT, int LP, int TPT = 4>
 struct XRec {
   static constexpr uint32_t FRAG = NT * 4 * LP * 16;
-  static constexpr uint32_t R = FRAG + 64 * NT;
+  static constexpr uint32_t R = FRAG + 16 * TPT * NT;
 };
 
 // Box row of quad-row rq: under the 128B swizzle a warp's smem reads are
@@ -242,7 +243,7 @@ __device__ __forceinline__ float pow2f(int e) {
 // the group's power-of-two normaliser E (|x'| < 2^E), the tensor-core B
 // fragments of x' 2^(14 - p - E) split into fp16 hi + lo, and {Sx, 1024 2^E}.
 // Tokens t >= N write zeros.  Every global load is issued before any is used.
-template <int NT, int LP, int E>
+template <int NT, int LP, int E, int TPT>
 __device__ __forceinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype, int col0, int g_lo, int g_hi, int t,
                                            unsigned char* xslot, float* scratch, int lane, const LaneCols& lc) {
   constexpr int C = 32 * E;
@@ -345,8 +346,10 @@ __device__ __forceinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype,
         make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   __syncwarp();
   const int j8 = lane >> 2, c = lane & 3;
-  const int fl = 8 * (t & 3) + c;  // B-fragment lane of the token's hi column (lo: + 4)
-  const int tile = t >> 2;
+  // B-fragment lane of the token's column: hi at column 2 (t % 4), lo next to
+  // it, or the token's own column t % 8
+  const int fl = TPT == 4 ? 8 * (t & 3) + c : 4 * (t & 7) + c;
+  const int tile = TPT == 4 ? t >> 2 : t >> 3;
 #pragma unroll
   for (int gi = 0; gi < C / 128; ++gi) {
     const int g = col0 / 128 + gi;
@@ -365,26 +368,27 @@ __device__ __forceinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype,
       hw[k] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       lw[k] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    unsigned char* rec = xslot + (size_t)(g - g_lo) * XRec<NT, LP>::R;
+    using XR = XRec<NT, LP, TPT>;
+    unsigned char* rec = xslot + (size_t)(g - g_lo) * XR::R;
     unsigned char* fr = rec + (tile * 4 + (j8 >> 1)) * LP * 16 + (j8 & 1) * 8;
     *reinterpret_cast<uint2*>(fr + fl * 16) = make_uint2(hw[0], hw[1]);
-    *reinterpret_cast<uint2*>(fr + (fl + 4) * 16) = make_uint2(lw[0], lw[1]);
-    if (lane == 0)
-      *reinterpret_cast<float2*>(rec + XRec<NT, LP>::FRAG + t * 16) = make_float2(sg, 1024.f * pow2f(eg));
+    if (TPT == 4) *reinterpret_cast<uint2*>(fr + (fl + 4) * 16) = make_uint2(lw[0], lw[1]);
+    if (lane == 0) *reinterpret_cast<float2*>(rec + XR::FRAG + t * 16) = make_float2(sg, 1024.f * pow2f(eg));
   }
   __syncwarp();
 }
 
-template <int FMT, int NT, int LP, int SMODE>
+template <int FMT, int NT, int LP, int SMODE, int TPT>
 __global__ void __launch_bounds__(kThreadsT, 2)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
                     const __grid_constant__ CUtensorMap map2, const __grid_constant__ CUtensorMap map3,
                     const __grid_constant__ TmaArgs a) {
   using F = TmaFmt<FMT>;
   using L = WarpSlot<FMT, SMODE>;
-  using XR = XRec<NT, LP>;
+  using XR = XRec<NT, LP, TPT>;
   constexpr int S = F::S;
   constexpr int kOffset = IntFmt<FMT>::kOffset;
+  constexpr int YT = TPT / 4;  // tokens of a thread per tile
 
   asm volatile("griddepcontrol.launch_dependents;");
   // the launch's parameters are cold in every SM's constant cache: touch each
@@ -527,7 +531,7 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   int win_end = 0;
   auto prep_window = [&](int r0) {
     const int r1 = (r0 + XS < nruns) ? r0 + XS : nruns;
-    const int tslots = LP == 8 ? 1 : 4 * NT;
+    const int tslots = LP == 8 ? 1 : TPT * NT;
     int task = 0;
     for (int r = r0; r < r1; ++r) {
       const TmaJob& jb = job_ref(a, pj);
@@ -543,11 +547,11 @@ __global__ void __launch_bounds__(kThreadsT, 2)
           if (task % kWarps != warp) continue;
           const int col0 = cbase + ci * Cc;
           if (E == 4)
-            prep_chunk<NT, LP, 4>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
+            prep_chunk<NT, LP, 4, TPT>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
           else if (E == 8)
-            prep_chunk<NT, LP, 8>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
+            prep_chunk<NT, LP, 8, TPT>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
           else
-            prep_chunk<NT, LP, 16>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
+            prep_chunk<NT, LP, 16, TPT>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
         }
       if (++pst == jb.spb) {
         pst = 0;
@@ -596,9 +600,11 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       }
     }
     if (live) {
-      float y[NT][2];
+      float y[NT][2][YT];
 #pragma unroll
-      for (int i = 0; i < NT; ++i) y[i][0] = y[i][1] = 0.f;
+      for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int u = 0; u < YT; ++u) y[i][0][u] = y[i][1][u] = 0.f;
 #pragma unroll
       for (int pp = 0; pp < S / 2; ++pp) {
         // scales / zero points of the pair's two groups, then their code words
@@ -651,20 +657,24 @@ __global__ void __launch_bounds__(kThreadsT, 2)
           const int g = 2 * pp + gg;
 #pragma unroll
           for (int i = 0; i < NT; ++i) {
-            const int t = LP == 8 ? 0 : 4 * i + c;
-            const float2 gs = lds<float2>(xs + g * XR::R + XR::FRAG + t * 16);
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              float sv, mv;
-              if constexpr (SMODE == kScaleGroup) {
-                sv = __half2float(__ushort_as_half((unsigned short)(gg ? (sv2[hh] >> 16) : (sv2[hh] & 0xFFFFu))));
-                mv = __half2float(__ushort_as_half((unsigned short)(gg ? (mv2[hh] >> 16) : (mv2[hh] & 0xFFFFu))));
-              } else {
-                sv = frow[hh];
-                mv = -(float)kOffset * sv;
+            for (int u = 0; u < YT; ++u) {
+              // token of accumulator columns 2c, 2c + 1: one token as hi + lo, or two tokens
+              const int t = LP == 8 ? 0 : (TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u);
+              const float2 gs = lds<float2>(xs + g * XR::R + XR::FRAG + t * 16);
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                float sv, mv;
+                if constexpr (SMODE == kScaleGroup) {
+                  sv = __half2float(__ushort_as_half((unsigned short)(gg ? (sv2[hh] >> 16) : (sv2[hh] & 0xFFFFu))));
+                  mv = __half2float(__ushort_as_half((unsigned short)(gg ? (mv2[hh] >> 16) : (mv2[hh] & 0xFFFFu))));
+                } else {
+                  sv = frow[hh];
+                  mv = -(float)kOffset * sv;
+                }
+                const float q = TPT == 4 ? acc[gg][i][2 * hh] + acc[gg][i][2 * hh + 1] : acc[gg][i][2 * hh + u];
+                y[i][hh][u] += (sv * gs.y) * q + mv * gs.x;
               }
-              const float q = acc[gg][i][2 * hh] + acc[gg][i][2 * hh + 1];
-              y[i][hh] += (sv * gs.y) * q + mv * gs.x;
             }
           }
         }
@@ -678,10 +688,12 @@ __global__ void __launch_bounds__(kThreadsT, 2)
           if (grow >= jM) continue;
           const float bv = jb.bias ? jb.bias[grow] : 0.f;
 #pragma unroll
-          for (int i = 0; i < NT; ++i) {
-            const int t = 4 * i + c;
-            if (t < N && (LP == 32 || c == 0)) jb.y[(size_t)t * jM + grow] = y[i][hh] + bv;
-          }
+          for (int i = 0; i < NT; ++i)
+#pragma unroll
+            for (int u = 0; u < YT; ++u) {
+              const int t = TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u;
+              if (t < N && (LP == 32 || c == 0)) jb.y[(size_t)t * jM + grow] = y[i][hh][u] + bv;
+            }
         }
       } else {
         // the stage partial sums; the combine kernel adds them in stage order
@@ -689,10 +701,12 @@ __global__ void __launch_bounds__(kThreadsT, 2)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-          for (int i = 0; i < NT; ++i) {
-            const int t = 4 * i + c;
-            if (t < N && (LP == 32 || c == 0)) __stcg(part + (size_t)rl[hh] * N + t, y[i][hh]);
-          }
+          for (int i = 0; i < NT; ++i)
+#pragma unroll
+            for (int u = 0; u < YT; ++u) {
+              const int t = TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u;
+              if (t < N && (LP == 32 || c == 0)) __stcg(part + (size_t)rl[hh] * N + t, y[i][hh][u]);
+            }
       }
     }
     if (live && requested < nunits) {  // refill the slot just consumed
@@ -824,11 +838,11 @@ int run_of(const TmaArgs& a, int u) {
   return a.job[j].run0 + (u - a.job[j].unit0) / a.job[j].n_rb;
 }
 
-template <int FMT, int NT, int LP, int SMODE>
+template <int FMT, int NT, int LP, int SMODE, int TPT>
 cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_words, cudaStream_t s) {
   using F = TmaFmt<FMT>;
   using L = WarpSlot<FMT, SMODE>;
-  using XR = XRec<NT, LP>;
+  using XR = XRec<NT, LP, TPT>;
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
   CUtensorMap maps[kTmaMaxJobs];
@@ -870,7 +884,7 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   const size_t smem = (size_t)1024 + (size_t)kWarps * NS * L::BYTES + (size_t)XS * X +
                       (size_t)kWarps * a.chunk_max * 4 + (size_t)kWarps * NS * 8;
 
-  auto kern = gemv_tma_kernel<FMT, NT, LP, SMODE>;
+  auto kern = gemv_tma_kernel<FMT, NT, LP, SMODE, TPT>;
   {
     // the shared-memory opt-in is per device
     static std::mutex mu;
@@ -900,22 +914,24 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   return e;
 }
 
-template <int FMT, int NT, int LP>
+template <int FMT, int NT, int LP, int TPT>
 cudaError_t launch_sm(TmaArgs& a, int smode, const void* const* codes, const int* rw, cudaStream_t s) {
   if constexpr (FMT == PF_FMT_INT4 || FMT == PF_FMT_INT2) {
-    if (smode == kScaleRow) return launch_one<FMT, NT, LP, kScaleRow>(a, codes, rw, s);
-    return launch_one<FMT, NT, LP, kScaleTensor>(a, codes, rw, s);
+    if (smode == kScaleRow) return launch_one<FMT, NT, LP, kScaleRow, TPT>(a, codes, rw, s);
+    return launch_one<FMT, NT, LP, kScaleTensor, TPT>(a, codes, rw, s);
   } else {
-    return launch_one<FMT, NT, LP, kScaleGroup>(a, codes, rw, s);
+    return launch_one<FMT, NT, LP, kScaleGroup, TPT>(a, codes, rw, s);
   }
 }
 
 template <int FMT>
 cudaError_t launch_fmt(TmaArgs& a, int smode, const void* const* codes, const int* rw, cudaStream_t s) {
-  const int NT = a.N <= 4 ? 1 : (a.N <= 8 ? 2 : 4);
-  if (NT == 1) return a.N == 1 ? launch_sm<FMT, 1, 8>(a, smode, codes, rw, s) : launch_sm<FMT, 1, 32>(a, smode, codes, rw, s);
-  if (NT == 2) return launch_sm<FMT, 2, 32>(a, smode, codes, rw, s);
-  return launch_sm<FMT, 4, 32>(a, smode, codes, rw, s);
+  // up to 4 tokens: fp16 hi / lo halves of x' (4 tokens per MMA tile); more:
+  // one fp16 per token (8 per tile), half the MMAs and x' reads per token
+  if (a.N == 1) return launch_sm<FMT, 1, 8, 4>(a, smode, codes, rw, s);
+  if (a.N <= 4) return launch_sm<FMT, 1, 32, 4>(a, smode, codes, rw, s);
+  if (a.N <= 8) return launch_sm<FMT, 1, 32, 8>(a, smode, codes, rw, s);
+  return launch_sm<FMT, 2, 32, 8>(a, smode, codes, rw, s);
 }
 
 }  // namespace
