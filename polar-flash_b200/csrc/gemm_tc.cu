@@ -401,6 +401,342 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   }
 }
 
+// ---------------------------------------------------------------------------
+// Variant with the packed codes and scales staged by TMA (shapes whose row
+// strides allow 2-D tensor maps).  The producer warp also copies, per box of
+// CB groups, the CTA's 128 rows of packed codes, and per box of SB groups their
+// scales (and zero points), into double-buffered shared-memory slots; the
+// dequant threads read their row from there, so no thread issues a global
+// load (one 4-byte load per row per lane was the limit of the plain kernel:
+// a warp touched 32 rows, 32 sectors per load).  The A/B ring is two stages.
+template <int FMT>
+struct TcBox;
+template <>
+struct TcBox<PF_FMT_INT4_G128> {
+  static constexpr int GB = 64, CB = 2, SB = 8, SW = 2;  // group bytes, code / scale box groups, scale bytes
+};
+template <>
+struct TcBox<PF_FMT_INT3_G128> {
+  static constexpr int GB = 52, CB = 4, SB = 8, SW = 2;
+};
+template <>
+struct TcBox<PF_FMT_INT2_G128> {
+  static constexpr int GB = 32, CB = 4, SB = 8, SW = 2;
+};
+template <>
+struct TcBox<PF_FMT_E8_RVQ2_G128> {
+  static constexpr int GB = 32, CB = 4, SB = 4, SW = 4;  // scales: (s1, s2) fp16 per group
+};
+constexpr int kStages2 = 2;  // the dequant groups take alternate stages: one slot each
+
+__device__ __forceinline__ void tma2d_plain(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
+                    const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap mmap,
+                    const __grid_constant__ GemmArgs a) {
+  using B = TcBox<FMT>;
+  constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
+  constexpr uint32_t kCodeSlot = kBM * B::CB * B::GB;  // 128 rows x CB groups
+  constexpr uint32_t kScaleSlot = kBM * 16;            // 128 rows x SB groups x SW bytes (16)
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // A/B ring full / A full / free, accumulator, then code full / free and scale full / free (two slots each)
+  __shared__ uint64_t bars[3 * kStages2 + 1 + 8];
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ int abort_flag;
+  __shared__ uint4 roots16[kE8 ? 256 * 4 : 1];
+  __shared__ float tscale[kBN];
+
+  unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
+  unsigned char* const codes = base + kStages2 * kStageBytes;          // [2][kCodeSlot]
+  unsigned char* const scl = codes + 2 * kCodeSlot;                    // [2][kScaleSlot] (+ [2][kScaleSlot] mins)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
+  const uint32_t bfull0 = su32(&bars[0]), afull0 = su32(&bars[kStages2]), free0 = su32(&bars[2 * kStages2]);
+  const uint32_t accbar = su32(&bars[3 * kStages2]);
+  const uint32_t cfull0 = su32(&bars[3 * kStages2 + 1]), cfree0 = cfull0 + 16;
+  const uint32_t sfull0 = cfull0 + 32, sfree0 = cfull0 + 48;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kStages2; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bfull0 + 8 * s));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(kBM));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(free0 + 8 * s));
+    }
+    for (int s = 0; s < 2; ++s) {  // the code and scale boxes are double-buffered
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(cfull0 + 8 * s));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(cfree0 + 8 * s), "r"(2 * kBM));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sfull0 + 8 * s));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sfree0 + 8 * s), "r"(2 * kBM));
+    }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(accbar));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&cmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&smap)) : "memory");
+    if (!kE8) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mmap)) : "memory");
+  }
+  if constexpr (kE8) {
+    for (int k = threadIdx.x; k < 256; k += blockDim.x) {
+      float r[8];
+      if (k < 240) {
+        e8_root(k, r);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) r[q] = 0.f;
+      }
+      uint32_t h[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __half2 v = __floats2half2_rn(r[2 * q], r[2 * q + 1]);
+        h[q] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) roots16[4 * k + c] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+  }
+  for (int t = threadIdx.x; t < kBN; t += blockDim.x) tscale[t] = (n0 + t < a.N) ? a.tok_scale[n0 + t] : 0.f;
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = tmem_base_slot;
+  const int G = a.G;
+  const int nv = a.N - n0 < kBN ? a.N - n0 : kBN;
+  const int nmma = (nv + 15) & ~15;
+
+  if (warp == 0) {
+    // ------------------------------------------------ producer: codes, scales, x'
+    if (lane == 0) {
+      bool ok = true;
+      for (int s = 0; s < G && ok; ++s) {
+        if (s % B::CB == 0) {
+          const int b = s / B::CB, cs = b & 1;
+          if (b >= 2 && !bar_wait(cfree0 + 8 * cs, ((b >> 1) - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(cfull0 + 8 * cs),
+                       "r"(kCodeSlot)
+                       : "memory");
+          tma2d_plain(su32(codes + cs * kCodeSlot), &cmap, s * (B::GB / 4), m0, cfull0 + 8 * cs);
+        }
+        if (s % B::SB == 0) {
+          const int c = s / B::SB, ss = c & 1;
+          if (c >= 2 && !bar_wait(sfree0 + 8 * ss, ((c >> 1) - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sfull0 + 8 * ss),
+                       "r"(kE8 ? kScaleSlot : 2 * kScaleSlot)
+                       : "memory");
+          // x in fp16 elements: E8 keeps two scales per group
+          tma2d_plain(su32(scl + ss * kScaleSlot), &smap, kE8 ? 2 * s : s, m0, sfull0 + 8 * ss);
+          if (!kE8) tma2d_plain(su32(scl + (2 + ss) * kScaleSlot), &mmap, s, m0, sfull0 + 8 * ss);
+        }
+        const int slot = s % kStages2;
+        if (s >= kStages2 && !bar_wait(free0 + 8 * slot, ((s / kStages2) - 1) & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t dst = su32(base + slot * kStageBytes + kATile), bar = bfull0 + 8 * slot;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBTile) : "memory");
+#pragma unroll
+        for (int h = 0; h < 2; ++h) tma2d_plain(dst + h * (kBN * 128), &xmap, s * kBK + h * 64, n0, bar);
+      }
+      if (!ok) {
+        abort_flag = 1;
+        atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      for (int s = 0; s < G; ++s) {
+        const int slot = s % kStages2;
+        const uint32_t par = (s / kStages2) & 1;
+        if (!bar_wait(afull0 + 8 * slot, par, &abort_flag) || !bar_wait(bfull0 + 8 * slot, par, &abort_flag)) {
+          abort_flag = 1;
+          atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const uint32_t sa = su32(base + slot * kStageBytes), sb = sa + kATile;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          const uint32_t off = (k >> 2) * (kBM * 128) + (k & 3) * 32;
+          const uint64_t da = kmajor_desc(sa + off), db = kmajor_desc(sb + off);
+          const uint32_t acc = (s > 0 || k > 0) ? 1u : 0u;
+          asm volatile(
+              "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
+                  tmem),
+              "l"(da), "l"(db), "r"(gemm_idesc(nmma)), "r"(acc));
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(free0 +
+                                                                                                        8 * slot)
+                     : "memory");
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(accbar)
+                   : "memory");
+    }
+  } else {
+    // ------------------------------------------------ dequant rows, epilogue
+    const int grp = (warp - 1) >> 2;       // this group dequantises stages s with s % 2 == grp
+    const int r = 32 * (warp & 3) + lane;  // tile row == this warp's TMEM lanes
+    const int grow = m0 + r;
+    const bool rvalid = grow < a.M;
+    bool live = true;
+    auto fail = [&]() {
+      live = false;
+      if (lane == 0) {
+        abort_flag = 1;
+        atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+      }
+    };
+    for (int s = grp; s < G; s += 2) {
+      const int slot = s % kStages2;
+      const int b = s / B::CB, cs = b & 1, sbx = s / B::SB, ss = sbx & 1;
+      if (live && !bar_wait(cfull0 + 8 * cs, (b >> 1) & 1, &abort_flag)) fail();
+      if (live && !bar_wait(sfull0 + 8 * ss, (sbx >> 1) & 1, &abort_flag)) fail();
+      // this row's codes and scales of stage s
+      uint32_t cw[16];
+      uint32_t sc = 0u;
+      if (live) {
+        const unsigned char* cp = codes + cs * kCodeSlot + r * (B::CB * B::GB) + (s % B::CB) * B::GB;
+        if constexpr (FMT == PF_FMT_INT3_G128) {
+#pragma unroll
+          for (int q = 0; q < 13; ++q) cw[q] = *reinterpret_cast<const uint32_t*>(cp + 4 * q);
+          cw[13] = cw[14] = cw[15] = 0u;
+        } else {
+#pragma unroll
+          for (int q = 0; q < B::GB / 16; ++q) {
+            const uint4 v = *reinterpret_cast<const uint4*>(cp + 16 * q);
+            cw[4 * q] = v.x; cw[4 * q + 1] = v.y; cw[4 * q + 2] = v.z; cw[4 * q + 3] = v.w;
+          }
+#pragma unroll
+          for (int q = B::GB / 4; q < 16; ++q) cw[q] = 0u;
+        }
+        const unsigned char* sp = scl + ss * kScaleSlot + r * 16 + (s % B::SB) * B::SW;
+        if constexpr (kE8) {
+          sc = *reinterpret_cast<const uint32_t*>(sp);
+        } else {
+          const uint32_t lo = *reinterpret_cast<const uint16_t*>(sp);
+          const uint32_t hi = *reinterpret_cast<const uint16_t*>(sp + 2 * kScaleSlot);
+          sc = lo | (hi << 16);
+        }
+      }
+      // hand the code / scale boxes back after this thread's last stage in them
+      if (s + 2 >= (b + 1) * B::CB || s + 2 >= G) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(cfree0 + 8 * cs) : "memory");
+      if (s + 2 >= (sbx + 1) * B::SB || s + 2 >= G) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sfree0 + 8 * ss) : "memory");
+      if (live && s >= kStages2 && !bar_wait(free0 + 8 * slot, ((s / kStages2) - 1) & 1, &abort_flag)) fail();
+      if (!live) continue;
+      unsigned char* at = base + slot * kStageBytes;
+      if constexpr (FMT == PF_FMT_E8_RVQ2_G128) {
+        // w = s1 r[i1] + s2 r[i2] in one fp16 FMA (s1 r[i1] is exact: r in {0, +-1/2, +-1})
+        const __half2 s1 = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
+        const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const uint32_t wv = cw[c >> 1] >> (16 * (c & 1));
+          const uint32_t i1 = wv & 0xFFu, i2 = (wv >> 8) & 0xFFu;
+          const uint4 ra = roots16[4 * i1 + (lane & 3)], rb = roots16[4 * i2 + (lane & 3)];
+          const uint32_t* pa = reinterpret_cast<const uint32_t*>(&ra);
+          const uint32_t* pb = reinterpret_cast<const uint32_t*>(&rb);
+          uint4 o;
+          uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __half2 h = __hfma2(s2, *reinterpret_cast<const __half2*>(&pb[e]),
+                                      __hmul2(s1, *reinterpret_cast<const __half2*>(&pa[e])));
+            ov[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = o;  // rows past M: zero codes (TMA fill)
+        }
+      } else {
+        // w = q s + m as one fp16 FMA of the exact code (the stored fp16 s and m)
+        const __half2 sx = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
+        const __half2 mx = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
+        uint32_t g3[13];
+        if constexpr (FMT == PF_FMT_INT3_G128) {
+#pragma unroll
+          for (int t = 0; t < 12; ++t) g3[t] = (cw[t] & 0x0000FFFFu) | ((cw[t] << 1) & 0xFFFF0000u);
+          g3[12] = (cw[12] & 0x0000FFFFu) | ((cw[12] << 4) & 0xFFFF0000u);
+        }
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          uint4 o;
+          uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint32_t mk;
+            if constexpr (FMT == PF_FMT_INT4_G128) {
+              mk = (cw[c] >> (4 * e)) & 0x000F000Fu;
+            } else if constexpr (FMT == PF_FMT_INT2_G128) {
+              mk = (cw[c >> 1] >> (2 * (4 * (c & 1) + e))) & 0x00030003u;
+            } else {
+              const int p = 4 * c + e;
+              mk = p < 60 ? (g3[p / 5] >> (3 * (p % 5))) & 0x00070007u : (g3[12] >> (3 * (p - 60))) & 0x00070007u;
+            }
+            const __half2 h = __hfma2(pair_fp16(mk), sx, mx);
+            ov[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = o;  // rows past M: zero codes (TMA fill)
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(afull0 + 8 * slot) : "memory");
+    }
+    // ------------------------------------------------ epilogue (16-column chunks split between the groups)
+    bool ok = live;
+    if (ok) ok = bar_wait(accbar, 0, &abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+      const float bv = (rvalid && a.bias) ? a.bias[grow] : 0.f;
+#pragma unroll 1
+      for (int c0 = 16 * grp; c0 < nmma; c0 += 32) {
+        uint32_t v[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(taddr + (uint32_t)c0));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (rvalid) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int t = n0 + c0 + j;
+            if (t < a.N) a.y[(size_t)t * a.M + grow] = __uint_as_float(v[j]) * tscale[c0 + j] + bv;
+          }
+        }
+      }
+    } else if (lane == 0 && !abort_flag) {
+      abort_flag = 1;
+      atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+
 // Block-wide max of a non-negative float (all threads get it).
 __device__ __forceinline__ float block_max(float mx, float* red) {
 #pragma unroll
@@ -485,6 +821,76 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn_gemm() {
   return fn;
 }
 
+// PF_GEMM_TMA=0 keeps every launch on the plain kernel (for comparison).
+bool gemm_tma_enabled() {
+  static int v = -1;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* e = getenv("PF_GEMM_TMA");
+    v = (e && atoi(e) == 0) ? 0 : 1;
+  });
+  return v == 1;
+}
+
+// The TMA-staged variant: 2-D tensor maps over the packed rows and the scale
+// rows need 16-byte aligned bases and row strides.
+template <int FMT>
+cudaError_t launch_gemm_tc2(const GemmArgs& a, const CUtensorMap& xmap, cudaStream_t s, bool* taken) {
+  using B = TcBox<FMT>;
+  constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
+  *taken = false;
+  const size_t row_bytes = (size_t)a.G * B::GB, srow = (size_t)a.G * B::SW;
+  if (!gemm_tma_enabled() || row_bytes % 16 || srow % 16 || reinterpret_cast<uintptr_t>(a.codes) % 16 ||
+      reinterpret_cast<uintptr_t>(a.scales) % 16 || (!kE8 && reinterpret_cast<uintptr_t>(a.mins) % 16))
+    return cudaSuccess;
+  auto fn = encode_fn_gemm();
+  CUtensorMap cmap, smap, mmap;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)a.M};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)(B::CB * B::GB / 4), (cuuint32_t)kBM};
+    cuuint32_t estr[2] = {1, 1};
+    if (fn(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(a.codes), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaSuccess;
+  }
+  for (int k = 0; k < (kE8 ? 1 : 2); ++k) {
+    // scale (and zero-point) rows: SB groups of SW bytes per box row (16 bytes)
+    cuuint64_t dims[2] = {(cuuint64_t)(srow / 2), (cuuint64_t)a.M};
+    cuuint64_t strides[1] = {(cuuint64_t)srow};
+    cuuint32_t box[2] = {8, (cuuint32_t)kBM};
+    cuuint32_t estr[2] = {1, 1};
+    const void* src = k == 0 ? static_cast<const void*>(a.scales) : static_cast<const void*>(a.mins);
+    if (fn(k == 0 ? &smap : &mmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(src), dims, strides, box,
+           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaSuccess;
+  }
+  if (kE8) mmap = smap;
+  const size_t smem = 1024 + (size_t)kStages2 * kStageBytes + 2 * (size_t)kBM * B::CB * B::GB +
+                      (kE8 ? 2 : 4) * (size_t)kBM * 16;
+  auto kern = gemm_tc2_kernel<FMT>;
+  {
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || !done[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) done[dev] = true;
+    }
+  }
+  *taken = true;
+  dim3 grid((a.M + kBM - 1) / kBM, (a.N + kBN - 1) / kBN);
+  kern<<<grid, kGemmThreads, smem, s>>>(xmap, cmap, smap, mmap, a);
+  note_launch();
+  return cudaGetLastError();
+}
+
 template <int FMT>
 cudaError_t launch_gemm_fmt(const GemmArgs& a, const __half* x16, cudaStream_t s) {
   auto fn = encode_fn_gemm();
@@ -498,6 +904,11 @@ cudaError_t launch_gemm_fmt(const GemmArgs& a, const __half* x16, cudaStream_t s
          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
+  {
+    bool taken = false;
+    const cudaError_t e = launch_gemm_tc2<FMT>(a, map, s, &taken);
+    if (taken || e != cudaSuccess) return e;
+  }
   const size_t smem = 1024 + (size_t)kStages * kStageBytes;
   auto kern = gemm_tc_kernel<FMT>;
   {
