@@ -234,7 +234,8 @@ bool use_gemm(const pf_qweight* w, int N) {
 size_t gemm_bytes(const pf_qweight* w, int N) {
   const int nc = N < kGemmChunk ? N : kGemmChunk;
   const size_t Kp = (size_t)((w->K + 127) / 128) * 128;
-  return kCounterBytes + round_up((size_t)nc * Kp * sizeof(float), 256) + gemm_x16_bytes(nc, w->K);
+  return kCounterBytes + round_up((size_t)nc * Kp * sizeof(float), 256) + gemm_x16_bytes(nc, w->K) +
+         gemm_partial_bytes();
 }
 
 // Batch-1 E8 runs on the lookup-table GEMV when its shapes and alignments
@@ -481,6 +482,7 @@ static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x,
   float* xplain = reinterpret_cast<float*>(base);
   __half* x16 = reinterpret_cast<__half*>(base + round_up((size_t)cmax * Kp * sizeof(float), 256));
   float* tsc = reinterpret_cast<float*>(reinterpret_cast<char*>(x16) + round_up((size_t)cmax * K * 2, 256));
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(x16) + gemm_x16_bytes(cmax, K));
   // rotation blocks that tile K: x' straight from x in the GEMM's own prep
   const bool direct = plan.ncasc == 0 && (plan.block == 0 || plan.rot_end == K) && K <= kGemmPrepMaxK;
   for (int t0 = 0; t0 < N; t0 += kGemmChunk) {
@@ -508,6 +510,8 @@ static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x,
       g.bias = bias;
       g.y = y + (size_t)t0 * w->M;
       g.status = static_cast<unsigned*>(ws) + kWsStatusSlot;
+      g.counters = static_cast<unsigned*>(ws);
+      g.partials = partials;
       int st = cuda_status(launch_gemm(g, s));
       if (st) return st;
       continue;
@@ -545,6 +549,8 @@ static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x,
     g.bias = bias;
     g.y = y + (size_t)t0 * w->M;
     g.status = static_cast<unsigned*>(ws) + kWsStatusSlot;
+    g.counters = static_cast<unsigned*>(ws);
+    g.partials = partials;
     st = cuda_status(launch_gemm(g, s));
     if (st) return st;
   }

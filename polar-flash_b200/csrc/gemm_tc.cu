@@ -59,6 +59,12 @@ struct GemmArgs {
   const float* bias;
   float* y;  // [N][M]
   unsigned* status;
+  // persistent stream-K kernel: tiles per token column, (tile, group) units,
+  // per-tile arrival counters (zero, left zero) and 2 partial tiles per CTA
+  int n_mb;
+  long long units;
+  unsigned* counters;
+  float* partials;
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -427,7 +433,21 @@ template <>
 struct TcBox<PF_FMT_E8_RVQ2_G128> {
   static constexpr int GB = 32, CB = 4, SB = 4, SW = 4;  // scales: (s1, s2) fp16 per group
 };
-constexpr int kStages2 = 2;  // the dequant groups take alternate stages: one slot each
+// 128 weight rows x 256 tokens per CTA (one N = 256 MMA per k-step, 256 TMEM
+// columns), so every decoded weight feeds twice the MACs of a 128-token tile;
+// stages of 64 columns (half a scale group, the dequant groups take
+// alternate halves) in a three-slot A/B ring.
+constexpr int kBN2 = 256;
+constexpr int kBK2 = 64;
+constexpr int kStages2 = 3;
+constexpr int kTmemCols2 = 256;
+constexpr uint32_t kATile2 = kBM * kBK2 * 2;  // one 64-column swizzle atom
+constexpr uint32_t kBTile2 = kBN2 * kBK2 * 2;
+constexpr uint32_t kStageBytes2 = kATile2 + kBTile2;
+
+// Token rows of the x' box: 256, or the batch rounded up to 16 when it is
+// smaller (the MMA reads no row past that).
+__host__ __device__ constexpr int tc2_box_rows(int N) { return N >= kBN2 ? kBN2 : ((N + 15) & ~15); }
 
 __device__ __forceinline__ void tma2d_plain(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
@@ -437,32 +457,133 @@ __device__ __forceinline__ void tma2d_plain(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Decodes half H of a row's scale group (A-tile slots 64 H .. 64 H + 63, the
+// 16-byte chunks 8 H .. 8 H + 7) from its packed words at cp into the
+// half-stage A tile at `at` (one 64-column swizzle atom).
+template <int FMT, int H>
+__device__ __forceinline__ void tc2_decode(const unsigned char* cp, uint32_t sc, int r, int lane, unsigned char* at,
+                                           const uint4* roots16) {
+  using B = TcBox<FMT>;
+  uint32_t cw[16];
+  if constexpr (FMT == PF_FMT_INT3_G128) {
+#pragma unroll
+    for (int q = 0; q < 13; ++q) cw[q] = *reinterpret_cast<const uint32_t*>(cp + 4 * q);
+    cw[13] = cw[14] = cw[15] = 0u;
+  } else {
+#pragma unroll
+    for (int q = 0; q < B::GB / 16; ++q) {
+      const uint4 v = *reinterpret_cast<const uint4*>(cp + 16 * q);
+      cw[4 * q] = v.x; cw[4 * q + 1] = v.y; cw[4 * q + 2] = v.z; cw[4 * q + 3] = v.w;
+    }
+#pragma unroll
+    for (int q = B::GB / 4; q < 16; ++q) cw[q] = 0u;
+  }
+  if constexpr (FMT == PF_FMT_E8_RVQ2_G128) {
+    // w = s1 r[i1] + s2 r[i2] in one fp16 FMA (s1 r[i1] is exact: r in {0, +-1/2, +-1})
+    const __half2 s1 = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
+    const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
+#pragma unroll
+    for (int c = 8 * H; c < 8 * H + 8; ++c) {
+      const uint32_t wv = cw[c >> 1] >> (16 * (c & 1));
+      const uint32_t i1 = wv & 0xFFu, i2 = (wv >> 8) & 0xFFu;
+      const uint4 ra = roots16[4 * i1 + (lane & 3)], rb = roots16[4 * i2 + (lane & 3)];
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&ra);
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&rb);
+      uint4 o;
+      uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __half2 h = __hfma2(s2, *reinterpret_cast<const __half2*>(&pb[e]),
+                                  __hmul2(s1, *reinterpret_cast<const __half2*>(&pa[e])));
+        ov[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) = o;  // rows past M: zero codes (TMA fill)
+    }
+  } else {
+    // w = q s + m as one fp16 FMA of the exact code (the stored fp16 s and m)
+    const __half2 sx = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
+    const __half2 mx = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
+    uint32_t g3[13];
+    if constexpr (FMT == PF_FMT_INT3_G128) {
+#pragma unroll
+      for (int t = 0; t < 12; ++t) g3[t] = (cw[t] & 0x0000FFFFu) | ((cw[t] << 1) & 0xFFFF0000u);
+      g3[12] = (cw[12] & 0x0000FFFFu) | ((cw[12] << 4) & 0xFFFF0000u);
+    }
+#pragma unroll
+    for (int c = 8 * H; c < 8 * H + 8; ++c) {
+      uint4 o;
+      uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        uint32_t mk;
+        if constexpr (FMT == PF_FMT_INT4_G128) {
+          mk = (cw[c] >> (4 * e)) & 0x000F000Fu;
+        } else if constexpr (FMT == PF_FMT_INT2_G128) {
+          mk = (cw[c >> 1] >> (2 * (4 * (c & 1) + e))) & 0x00030003u;
+        } else {
+          const int p = 4 * c + e;
+          mk = p < 60 ? (g3[p / 5] >> (3 * (p % 5))) & 0x00070007u : (g3[12] >> (3 * (p - 60))) & 0x00070007u;
+        }
+        const __half2 h = __hfma2(pair_fp16(mk), sx, mx);
+        ov[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) = o;  // rows past M: zero codes (TMA fill)
+    }
+  }
+}
+
+// Stream-K work split of the persistent GEMM: units are (tile, scale group)
+// pairs, tile t = nb * n_mb + mb (128 rows x 256 tokens), and CTA c of P takes
+// units [U c / P, U (c + 1) / P), so every CTA decodes the same number of
+// groups whatever the tile count.  A tile covered by one CTA is written
+// straight to y; the CTAs that share a tile store fp32 partial tiles and the
+// last of them to arrive sums them in k order (deterministic) and writes y.
+__device__ __forceinline__ long long sk_begin(long long U, int P, int c) { return U * c / P; }
+__device__ __forceinline__ int sk_cta_of(long long U, int P, long long u) {
+  const long long c = ((u + 1) * P - 1) / U;
+  return (int)(c < P - 1 ? c : P - 1);
+}
+
+// Warp roles of the persistent kernel: 0 TMA producer, 1-8 dequant, 9 MMA,
+// 10-13 epilogue (one per TMEM lane quarter).
+constexpr int kEpiWarp0 = kDqWarps + 2;
+constexpr int kSkThreads = (kDqWarps + 2 + 4) * 32;
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 template <int FMT>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc2_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
-                    const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap mmap,
-                    const __grid_constant__ GemmArgs a) {
+__global__ void __launch_bounds__(kSkThreads, 1)
+    gemm_sk_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
+                   const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap mmap,
+                   const __grid_constant__ GemmArgs a) {
   using B = TcBox<FMT>;
   constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
   constexpr uint32_t kCodeSlot = kBM * B::CB * B::GB;  // 128 rows x CB groups
   constexpr uint32_t kScaleSlot = kBM * 16;            // 128 rows x SB groups x SW bytes (16)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // A/B ring full / A full / free, accumulator, then code full / free and scale full / free (two slots each)
-  __shared__ uint64_t bars[3 * kStages2 + 1 + 8];
+  // A/B ring full / A full / free, then code full / free and scale full /
+  // free (two slots each), then accumulator full and TMEM-buffer empty (two each)
+  __shared__ uint64_t bars[3 * kStages2 + 8 + 4];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
+  __shared__ unsigned arrival;
   __shared__ uint4 roots16[kE8 ? 256 * 4 : 1];
-  __shared__ float tscale[kBN];
 
   unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
-  unsigned char* const codes = base + kStages2 * kStageBytes;          // [2][kCodeSlot]
-  unsigned char* const scl = codes + 2 * kCodeSlot;                    // [2][kScaleSlot] (+ [2][kScaleSlot] mins)
+  unsigned char* const codes = base + kStages2 * kStageBytes2;  // [2][kCodeSlot]
+  unsigned char* const scl = codes + 2 * kCodeSlot;             // [2][kScaleSlot] (+ [2][kScaleSlot] mins)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
   const uint32_t bfull0 = su32(&bars[0]), afull0 = su32(&bars[kStages2]), free0 = su32(&bars[2 * kStages2]);
-  const uint32_t accbar = su32(&bars[3 * kStages2]);
-  const uint32_t cfull0 = su32(&bars[3 * kStages2 + 1]), cfree0 = cfull0 + 16;
+  const uint32_t cfull0 = su32(&bars[3 * kStages2]), cfree0 = cfull0 + 16;
   const uint32_t sfull0 = cfull0 + 32, sfree0 = cfull0 + 48;
+  const uint32_t accf0 = cfull0 + 64, tempty0 = cfull0 + 80;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -471,13 +592,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(kBM));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(free0 + 8 * s));
     }
-    for (int s = 0; s < 2; ++s) {  // the code and scale boxes are double-buffered
+    for (int s = 0; s < 2; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(cfull0 + 8 * s));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(cfree0 + 8 * s), "r"(2 * kBM));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sfull0 + 8 * s));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sfree0 + 8 * s), "r"(2 * kBM));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(accf0 + 8 * s));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tempty0 + 8 * s), "r"(kBM));
     }
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(accbar));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&cmap)) : "memory");
@@ -503,58 +625,70 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c = 0; c < 4; ++c) roots16[4 * k + c] = make_uint4(h[0], h[1], h[2], h[3]);
     }
   }
-  for (int t = threadIdx.x; t < kBN; t += blockDim.x) tscale[t] = (n0 + t < a.N) ? a.tok_scale[n0 + t] : 0.f;
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_slot)),
-                 "r"(kTmemCols));
+                 "r"(2 * kTmemCols2));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = tmem_base_slot;
-  const int G = a.G;
-  const int nv = a.N - n0 < kBN ? a.N - n0 : kBN;
-  const int nmma = (nv + 15) & ~15;
+  const int G = a.G, P = gridDim.x;
+  const long long U = a.units;
+  const long long u_begin = sk_begin(U, P, blockIdx.x), u_end = sk_begin(U, P, blockIdx.x + 1);
+  const uint32_t xbox_bytes = (uint32_t)tc2_box_rows(a.N) * (kBK2 * 2);
 
   if (warp == 0) {
     // ------------------------------------------------ producer: codes, scales, x'
     if (lane == 0) {
       bool ok = true;
-      for (int s = 0; s < G && ok; ++s) {
-        if (s % B::CB == 0) {
-          const int b = s / B::CB, cs = b & 1;
-          if (b >= 2 && !bar_wait(cfree0 + 8 * cs, ((b >> 1) - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
+      uint32_t q = 0, kc = 0, ks = 0;  // half-stages, code boxes and scale boxes issued
+      for (long long u = u_begin; u < u_end && ok;) {
+        const int t = (int)(u / G), g0 = (int)(u - (long long)t * G);
+        const int g1 = (long long)(G - g0) < u_end - u ? G : g0 + (int)(u_end - u);
+        const int m0 = (t % a.n_mb) * kBM, n0 = (t / a.n_mb) * kBN2;
+        for (int s = g0; s < g1 && ok; ++s) {
+          if (s == g0 || s % B::CB == 0) {
+            const uint32_t cs = kc & 1;
+            if (kc >= 2 && !bar_wait(cfree0 + 8 * cs, ((kc >> 1) - 1) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(cfull0 + 8 * cs),
+                         "r"(kCodeSlot)
+                         : "memory");
+            tma2d_plain(su32(codes + cs * kCodeSlot), &cmap, (s - s % B::CB) * (B::GB / 4), m0, cfull0 + 8 * cs);
+            ++kc;
           }
-          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(cfull0 + 8 * cs),
-                       "r"(kCodeSlot)
-                       : "memory");
-          tma2d_plain(su32(codes + cs * kCodeSlot), &cmap, s * (B::GB / 4), m0, cfull0 + 8 * cs);
-        }
-        if (s % B::SB == 0) {
-          const int c = s / B::SB, ss = c & 1;
-          if (c >= 2 && !bar_wait(sfree0 + 8 * ss, ((c >> 1) - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
+          if (s == g0 || s % B::SB == 0) {
+            const uint32_t ss = ks & 1;
+            if (ks >= 2 && !bar_wait(sfree0 + 8 * ss, ((ks >> 1) - 1) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sfull0 + 8 * ss),
+                         "r"(kE8 ? kScaleSlot : 2 * kScaleSlot)
+                         : "memory");
+            // x in fp16 elements: E8 keeps two scales per group
+            const int sx = s - s % B::SB;
+            tma2d_plain(su32(scl + ss * kScaleSlot), &smap, kE8 ? 2 * sx : sx, m0, sfull0 + 8 * ss);
+            if (!kE8) tma2d_plain(su32(scl + (2 + ss) * kScaleSlot), &mmap, sx, m0, sfull0 + 8 * ss);
+            ++ks;
           }
-          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sfull0 + 8 * ss),
-                       "r"(kE8 ? kScaleSlot : 2 * kScaleSlot)
-                       : "memory");
-          // x in fp16 elements: E8 keeps two scales per group
-          tma2d_plain(su32(scl + ss * kScaleSlot), &smap, kE8 ? 2 * s : s, m0, sfull0 + 8 * ss);
-          if (!kE8) tma2d_plain(su32(scl + (2 + ss) * kScaleSlot), &mmap, s, m0, sfull0 + 8 * ss);
+          for (int h = 0; h < 2; ++h, ++q) {
+            const uint32_t slot = q % kStages2;
+            if (q >= kStages2 && !bar_wait(free0 + 8 * slot, ((q / kStages2) - 1) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t dst = su32(base + slot * kStageBytes2 + kATile2), bar = bfull0 + 8 * slot;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(xbox_bytes)
+                         : "memory");
+            tma2d_plain(dst, &xmap, (2 * s + h) * kBK2, n0, bar);
+          }
         }
-        const int slot = s % kStages2;
-        if (s >= kStages2 && !bar_wait(free0 + 8 * slot, ((s / kStages2) - 1) & 1, &abort_flag)) {
-          ok = false;
-          break;
-        }
-        const uint32_t dst = su32(base + slot * kStageBytes + kATile), bar = bfull0 + 8 * slot;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBTile) : "memory");
-#pragma unroll
-        for (int h = 0; h < 2; ++h) tma2d_plain(dst + h * (kBN * 128), &xmap, s * kBK + h * 64, n0, bar);
+        u += g1 - g0;
       }
       if (!ok) {
         abort_flag = 1;
@@ -564,39 +698,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
-      for (int s = 0; s < G; ++s) {
-        const int slot = s % kStages2;
-        const uint32_t par = (s / kStages2) & 1;
-        if (!bar_wait(afull0 + 8 * slot, par, &abort_flag) || !bar_wait(bfull0 + 8 * slot, par, &abort_flag)) {
-          abort_flag = 1;
-          atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+      bool ok = true;
+      uint32_t q = 0, j = 0;
+      for (long long u = u_begin; u < u_end && ok; ++j) {
+        const int t = (int)(u / G), g0 = (int)(u - (long long)t * G);
+        const int g1 = (long long)(G - g0) < u_end - u ? G : g0 + (int)(u_end - u);
+        const int n0 = (t / a.n_mb) * kBN2;
+        const int nv = a.N - n0 < kBN2 ? a.N - n0 : kBN2;
+        const uint32_t idesc = gemm_idesc((nv + 15) & ~15);
+        const uint32_t buf = j & 1, acc_t = tmem + buf * kTmemCols2;
+        if (j >= 2 && !bar_wait(tempty0 + 8 * buf, ((j >> 1) - 1) & 1, &abort_flag)) {
+          ok = false;
           break;
         }
-        asm volatile("tcgen05.fence::after_thread_sync;");
-        const uint32_t sa = su32(base + slot * kStageBytes), sb = sa + kATile;
+        for (int s = g0; s < g1 && ok; ++s) {
+          for (int h = 0; h < 2; ++h, ++q) {
+            const uint32_t slot = q % kStages2, par = (q / kStages2) & 1;
+            if (!bar_wait(afull0 + 8 * slot, par, &abort_flag) || !bar_wait(bfull0 + 8 * slot, par, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t sa = su32(base + slot * kStageBytes2), sb = sa + kATile2;
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          const uint32_t off = (k >> 2) * (kBM * 128) + (k & 3) * 32;
-          const uint64_t da = kmajor_desc(sa + off), db = kmajor_desc(sb + off);
-          const uint32_t acc = (s > 0 || k > 0) ? 1u : 0u;
-          asm volatile(
-              "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
-                  tmem),
-              "l"(da), "l"(db), "r"(gemm_idesc(nmma)), "r"(acc));
+            for (int k = 0; k < kBK2 / 16; ++k) {
+              const uint64_t da = kmajor_desc(sa + k * 32), db = kmajor_desc(sb + k * 32);
+              const uint32_t acc = (s > g0 || h > 0 || k > 0) ? 1u : 0u;
+              asm volatile(
+                  "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
+                      acc_t),
+                  "l"(da), "l"(db), "r"(idesc), "r"(acc));
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             free0 + 8 * slot)
+                         : "memory");
+          }
         }
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(free0 +
-                                                                                                        8 * slot)
-                     : "memory");
+        if (ok)
+          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(accf0 +
+                                                                                                          8 * buf)
+                       : "memory");
+        u += g1 - g0;
       }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(accbar)
-                   : "memory");
+      if (!ok) {
+        abort_flag = 1;
+        atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+      }
     }
-  } else {
-    // ------------------------------------------------ dequant rows, epilogue
-    const int grp = (warp - 1) >> 2;       // this group dequantises stages s with s % 2 == grp
-    const int r = 32 * (warp & 3) + lane;  // tile row == this warp's TMEM lanes
-    const int grow = m0 + r;
-    const bool rvalid = grow < a.M;
+  } else if (warp <= kDqWarps) {
+    // ------------------------------------------------ dequant rows
+    const int grp = (warp - 1) >> 2;       // this group decodes half grp of every scale group
+    const int r = 32 * (warp & 3) + lane;  // tile row
     bool live = true;
     auto fail = [&]() {
       live = false;
@@ -605,134 +757,168 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
       }
     };
-    for (int s = grp; s < G; s += 2) {
-      const int slot = s % kStages2;
-      const int b = s / B::CB, cs = b & 1, sbx = s / B::SB, ss = sbx & 1;
-      if (live && !bar_wait(cfull0 + 8 * cs, (b >> 1) & 1, &abort_flag)) fail();
-      if (live && !bar_wait(sfull0 + 8 * ss, (sbx >> 1) & 1, &abort_flag)) fail();
-      // this row's codes and scales of stage s
-      uint32_t cw[16];
-      uint32_t sc = 0u;
-      if (live) {
+    uint32_t gs = 0, kc = 0, ks = 0;  // groups, code boxes and scale boxes consumed
+    for (long long u = u_begin; u < u_end;) {
+      const int t = (int)(u / G), g0 = (int)(u - (long long)t * G);
+      const int g1 = (long long)(G - g0) < u_end - u ? G : g0 + (int)(u_end - u);
+      uint32_t cs = 0, ss = 0, cpar = 0, spar = 0;
+      for (int s = g0; s < g1; ++s, ++gs) {
+        if (s == g0 || s % B::CB == 0) {
+          cs = kc & 1;
+          cpar = (kc >> 1) & 1;
+          ++kc;
+        }
+        if (s == g0 || s % B::SB == 0) {
+          ss = ks & 1;
+          spar = (ks >> 1) & 1;
+          ++ks;
+        }
+        const uint32_t q = 2 * gs + grp, slot = q % kStages2;
+        if (live && !bar_wait(cfull0 + 8 * cs, cpar, &abort_flag)) fail();
+        if (live && !bar_wait(sfull0 + 8 * ss, spar, &abort_flag)) fail();
+        // this row's scale (and zero point) of group s
+        uint32_t sc = 0u;
+        if (live) {
+          const unsigned char* sp = scl + ss * kScaleSlot + r * 16 + (s % B::SB) * B::SW;
+          if constexpr (kE8) {
+            sc = *reinterpret_cast<const uint32_t*>(sp);
+          } else {
+            const uint32_t lo = *reinterpret_cast<const uint16_t*>(sp);
+            const uint32_t hi = *reinterpret_cast<const uint16_t*>(sp + 2 * kScaleSlot);
+            sc = lo | (hi << 16);
+          }
+        }
         const unsigned char* cp = codes + cs * kCodeSlot + r * (B::CB * B::GB) + (s % B::CB) * B::GB;
-        if constexpr (FMT == PF_FMT_INT3_G128) {
-#pragma unroll
-          for (int q = 0; q < 13; ++q) cw[q] = *reinterpret_cast<const uint32_t*>(cp + 4 * q);
-          cw[13] = cw[14] = cw[15] = 0u;
-        } else {
-#pragma unroll
-          for (int q = 0; q < B::GB / 16; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4*>(cp + 16 * q);
-            cw[4 * q] = v.x; cw[4 * q + 1] = v.y; cw[4 * q + 2] = v.z; cw[4 * q + 3] = v.w;
-          }
-#pragma unroll
-          for (int q = B::GB / 4; q < 16; ++q) cw[q] = 0u;
+        if (live && q >= kStages2 && !bar_wait(free0 + 8 * slot, ((q / kStages2) - 1) & 1, &abort_flag)) fail();
+        if (live) {
+          unsigned char* at = base + slot * kStageBytes2;
+          if (grp == 0)
+            tc2_decode<FMT, 0>(cp, sc, r, lane, at, roots16);
+          else
+            tc2_decode<FMT, 1>(cp, sc, r, lane, at, roots16);
         }
-        const unsigned char* sp = scl + ss * kScaleSlot + r * 16 + (s % B::SB) * B::SW;
-        if constexpr (kE8) {
-          sc = *reinterpret_cast<const uint32_t*>(sp);
-        } else {
-          const uint32_t lo = *reinterpret_cast<const uint16_t*>(sp);
-          const uint32_t hi = *reinterpret_cast<const uint16_t*>(sp + 2 * kScaleSlot);
-          sc = lo | (hi << 16);
-        }
+        // hand the code / scale boxes back after this thread's last group in them
+        if (s + 1 == g1 || (s + 1) % B::CB == 0)
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(cfree0 + 8 * cs) : "memory");
+        if (s + 1 == g1 || (s + 1) % B::SB == 0)
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sfree0 + 8 * ss) : "memory");
+        if (!live) continue;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(afull0 + 8 * slot) : "memory");
       }
-      // hand the code / scale boxes back after this thread's last stage in them
-      if (s + 2 >= (b + 1) * B::CB || s + 2 >= G) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(cfree0 + 8 * cs) : "memory");
-      if (s + 2 >= (sbx + 1) * B::SB || s + 2 >= G) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sfree0 + 8 * ss) : "memory");
-      if (live && s >= kStages2 && !bar_wait(free0 + 8 * slot, ((s / kStages2) - 1) & 1, &abort_flag)) fail();
-      if (!live) continue;
-      unsigned char* at = base + slot * kStageBytes;
-      if constexpr (FMT == PF_FMT_E8_RVQ2_G128) {
-        // w = s1 r[i1] + s2 r[i2] in one fp16 FMA (s1 r[i1] is exact: r in {0, +-1/2, +-1})
-        const __half2 s1 = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
-        const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint32_t wv = cw[c >> 1] >> (16 * (c & 1));
-          const uint32_t i1 = wv & 0xFFu, i2 = (wv >> 8) & 0xFFu;
-          const uint4 ra = roots16[4 * i1 + (lane & 3)], rb = roots16[4 * i2 + (lane & 3)];
-          const uint32_t* pa = reinterpret_cast<const uint32_t*>(&ra);
-          const uint32_t* pb = reinterpret_cast<const uint32_t*>(&rb);
-          uint4 o;
-          uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __half2 h = __hfma2(s2, *reinterpret_cast<const __half2*>(&pb[e]),
-                                      __hmul2(s1, *reinterpret_cast<const __half2*>(&pa[e])));
-            ov[e] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = o;  // rows past M: zero codes (TMA fill)
-        }
-      } else {
-        // w = q s + m as one fp16 FMA of the exact code (the stored fp16 s and m)
-        const __half2 sx = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
-        const __half2 mx = __half2half2(__ushort_as_half((unsigned short)(sc >> 16)));
-        uint32_t g3[13];
-        if constexpr (FMT == PF_FMT_INT3_G128) {
-#pragma unroll
-          for (int t = 0; t < 12; ++t) g3[t] = (cw[t] & 0x0000FFFFu) | ((cw[t] << 1) & 0xFFFF0000u);
-          g3[12] = (cw[12] & 0x0000FFFFu) | ((cw[12] << 4) & 0xFFFF0000u);
-        }
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint4 o;
-          uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            uint32_t mk;
-            if constexpr (FMT == PF_FMT_INT4_G128) {
-              mk = (cw[c] >> (4 * e)) & 0x000F000Fu;
-            } else if constexpr (FMT == PF_FMT_INT2_G128) {
-              mk = (cw[c >> 1] >> (2 * (4 * (c & 1) + e))) & 0x00030003u;
-            } else {
-              const int p = 4 * c + e;
-              mk = p < 60 ? (g3[p / 5] >> (3 * (p % 5))) & 0x00070007u : (g3[12] >> (3 * (p - 60))) & 0x00070007u;
-            }
-            const __half2 h = __hfma2(pair_fp16(mk), sx, mx);
-            ov[e] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          *reinterpret_cast<uint4*>(at + a_chunk(r, c)) = o;  // rows past M: zero codes (TMA fill)
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(afull0 + 8 * slot) : "memory");
+      u += g1 - g0;
     }
-    // ------------------------------------------------ epilogue (16-column chunks split between the groups)
-    bool ok = live;
-    if (ok) ok = bar_wait(accbar, 0, &abort_flag);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+  } else {
+    // ------------------------------------------------ epilogue warps: TMEM -> y / partial tiles
+    const int quarter = warp & 3;
+    const int r = 32 * quarter + lane;  // tile row == this warp's TMEM lanes
+    const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
+    const int ci = (int)blockIdx.x;
+    uint32_t j = 0;
+    for (long long u = u_begin; u < u_end; ++j) {
+      const int t = (int)(u / G), g0 = (int)(u - (long long)t * G);
+      const int g1 = (long long)(G - g0) < u_end - u ? G : g0 + (int)(u_end - u);
+      const int m0 = (t % a.n_mb) * kBM, n0 = (t / a.n_mb) * kBN2;
+      const uint32_t buf = j & 1, taddr = tmem + buf * kTmemCols2 + lane_off;
+      const int nv = a.N - n0 < kBN2 ? a.N - n0 : kBN2;
+      const int nmma = (nv + 15) & ~15;
+      const int grow = m0 + r;
+      const bool rvalid = grow < a.M;
       const float bv = (rvalid && a.bias) ? a.bias[grow] : 0.f;
+      const bool whole = g0 == 0 && g1 == G;
+      float* const mine = a.partials + ((size_t)(2 * ci + (j > 0 ? 1 : 0)) * kBN2) * kBM;
+      bool ok = bar_wait(accf0 + 8 * buf, (j >> 1) & 1, &abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) {
+        abort_flag = 1;
+        atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;");
 #pragma unroll 1
-      for (int c0 = 16 * grp; c0 < nmma; c0 += 32) {
+      for (int c0 = 0; c0 < nmma && ok; c0 += 16) {
         uint32_t v[16];
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-            : "r"(taddr + (uint32_t)c0));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (rvalid) {
+        tmem_ld16(taddr + (uint32_t)c0, v);
+        if (whole) {
+          if (rvalid) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int t = n0 + c0 + j;
-            if (t < a.N) a.y[(size_t)t * a.M + grow] = __uint_as_float(v[j]) * tscale[c0 + j] + bv;
+            for (int jj = 0; jj < 16; ++jj) {
+              const int tk = n0 + c0 + jj;
+              if (tk < a.N) a.y[(size_t)tk * a.M + grow] = __uint_as_float(v[jj]) * a.tok_scale[tk] + bv;
+            }
           }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) mine[(size_t)(c0 + jj) * kBM + r] = __uint_as_float(v[jj]);
         }
       }
-    } else if (lane == 0 && !abort_flag) {
-      abort_flag = 1;
-      atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+      if (!whole) {
+        // the last CTA of this tile to arrive sums the partials in k order
+        // (its own from TMEM, the others' from the workspace)
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");
+        if (warp == kEpiWarp0 && lane == 0) {
+          unsigned v = 0xFFFFFFFFu;
+          if (ok && !abort_flag) {
+            v = atomicAdd(a.counters + t, 1u);
+            __threadfence();
+          }
+          arrival = v;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");
+        const long long tu0 = (long long)t * G;
+        const int cf = sk_cta_of(U, P, tu0), cl = sk_cta_of(U, P, tu0 + G - 1);
+        const unsigned got = arrival;
+        if (ok && got != 0xFFFFFFFFu && got == (unsigned)(cl - cf)) {
+#pragma unroll 1
+          for (int c0 = 0; c0 < nmma; c0 += 32) {
+            float accv[32];
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) accv[jj] = 0.f;
+#pragma unroll 1
+            for (int c = cf; c <= cl; ++c) {
+              float pv[32];
+              if (c == ci) {
+                uint32_t w0[16], w1[16];
+                tmem_ld16(taddr + (uint32_t)c0, w0);
+                tmem_ld16(taddr + (uint32_t)(c0 + 16), w1);
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) {
+                  pv[jj] = __uint_as_float(w0[jj]);
+                  pv[16 + jj] = __uint_as_float(w1[jj]);
+                }
+              } else {
+                // CTA c holds this tile in its first segment (slot 2c) unless the tile starts after its range does
+                const int first_t = (int)(sk_begin(U, P, c) / G);
+                const float* pp = a.partials + ((size_t)(2 * c + (first_t == t ? 0 : 1)) * kBN2 + c0) * kBM + r;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) pv[jj] = __ldcg(pp + (size_t)jj * kBM);
+              }
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) accv[jj] += pv[jj];
+            }
+            if (rvalid) {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) {
+                const int tk = n0 + c0 + jj;
+                if (tk < a.N) a.y[(size_t)tk * a.M + grow] = accv[jj] * a.tok_scale[tk] + bv;
+              }
+            }
+          }
+          if (warp == kEpiWarp0 && lane == 0) a.counters[t] = 0u;  // left zero for the next call
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");  // arrival is rewritten by the next segment
+      }
+      // TMEM buffer free for the segment after next
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty0 + 8 * buf) : "memory");
+      u += g1 - g0;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.fence::after_thread_sync;");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTmemCols2));
   }
 }
 
@@ -808,6 +994,111 @@ __global__ void __launch_bounds__(512) xprep16_kernel(const void* x, int x_dtype
   write_x16(xrow, mx, rs, K, fmt, out + (size_t)t * K, tok_scale + t);
 }
 
+// V consecutive activations of one token as fp32 (16-byte aligned x).
+template <int V>
+__device__ __forceinline__ void load_vec(const void* x, int dtype, size_t idx, float* v) {
+  if (dtype == PF_DTYPE_F32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + idx);
+#pragma unroll
+    for (int q = 0; q < V / 4; ++q) {
+      const float4 f = p[q];
+      v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+    }
+  } else {
+    const uint2* p = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + idx);
+#pragma unroll
+    for (int q = 0; q < V / 4; ++q) {
+      const uint2 w = p[q];
+      const uint32_t h[2] = {w.x, w.y};
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        if (dtype == PF_DTYPE_F16) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[e]));
+          v[4 * q + 2 * e] = f.x; v[4 * q + 2 * e + 1] = f.y;
+        } else {
+          v[4 * q + 2 * e] = __uint_as_float(h[e] << 16);
+          v[4 * q + 2 * e + 1] = __uint_as_float(h[e] & 0xFFFF0000u);
+        }
+      }
+    }
+  }
+}
+
+// The same x' as xprep16_kernel with the butterflies in registers: each lane
+// holds V consecutive columns of a 32 V-column segment (one segment per warp
+// at a time, V >= block / 32), levels below V in-lane, the others by warp
+// shuffles (same sums and differences in the same order, so the same bits);
+// the rotated row goes to shared memory once for the max and the fp16 pass,
+// which writes 8 slot-ordered fp16 per 16-byte store.
+template <int V>
+__global__ void __launch_bounds__(512) xprep16_vec_kernel(const void* x, int x_dtype, const int8_t* signs, int K,
+                                                          int block, float rs, int fmt, __half* out,
+                                                          float* tok_scale) {
+  extern __shared__ float xrow[];
+  __shared__ float red[32];
+  constexpr int kSeg = 32 * V;
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float mx = 0.f;
+  for (int seg = warp; seg < K / kSeg; seg += nw) {
+    const int k0 = seg * kSeg + lane * V;
+    float v[V];
+    load_vec<V>(x, x_dtype, (size_t)t * K + k0, v);
+    if (block > 1) {
+#pragma unroll
+      for (int q = 0; q < V / 4; ++q) {
+        const uint32_t sg = *reinterpret_cast<const uint32_t*>(signs + k0 + 4 * q);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (sg & (0x80u << (8 * e))) v[4 * q + e] = -v[4 * q + e];
+      }
+    }
+#pragma unroll
+    for (int h = 1; h < V; h <<= 1) {
+      if (h < block) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          if (!(i & h)) {
+            const float u = v[i], w = v[i + h];
+            v[i] = u + w;
+            v[i + h] = u - w;
+          }
+        }
+      }
+    }
+    for (int h = V; h < block; h <<= 1) {
+      const int m = h / V;
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float p = __shfl_xor_sync(0xffffffffu, v[i], m);
+        v[i] = upper ? p - v[i] : v[i] + p;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < V; ++i) mx = fmaxf(mx, fabsf(v[i]));
+#pragma unroll
+    for (int q = 0; q < V / 4; ++q)
+      *reinterpret_cast<float4*>(xrow + k0 + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  }
+  mx = block_max(mx * rs, red);  // also orders the row's shared-memory writes before the reads below
+  int ex = 0;
+  if (mx > 0.f) frexpf(mx, &ex);  // mx < 2^ex
+  const float sc = ldexpf(1.f, 15 - ex) * rs, inv = ldexpf(1.f, ex - 15);
+  __half* o = out + (size_t)t * K;
+  for (int k = 8 * threadIdx.x; k < K; k += 8 * blockDim.x) {
+    const int g = k & ~127, sl = k & 127;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __half2 h2 = __floats2half2_rn(xrow[g + gemm_slot_col(fmt, sl + 2 * e)] * sc,
+                                           xrow[g + gemm_slot_col(fmt, sl + 2 * e + 1)] * sc);
+      w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    *reinterpret_cast<uint4*>(o + k) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  if (threadIdx.x == 0) tok_scale[t] = mx > 0.f ? inv : 1.f;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn_gemm() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -832,19 +1123,51 @@ bool gemm_tma_enabled() {
   return v == 1;
 }
 
-// The TMA-staged variant: 2-D tensor maps over the packed rows and the scale
-// rows need 16-byte aligned bases and row strides.
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+// The persistent stream-K kernel: 2-D tensor maps over the packed rows and
+// the scale rows need 16-byte aligned bases and row strides, and the tile
+// count must fit the workspace's arrival counters.
 template <int FMT>
-cudaError_t launch_gemm_tc2(const GemmArgs& a, const CUtensorMap& xmap, cudaStream_t s, bool* taken) {
+cudaError_t launch_gemm_sk(GemmArgs a, const __half* x16, cudaStream_t s, bool* taken) {
   using B = TcBox<FMT>;
   constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
   *taken = false;
   const size_t row_bytes = (size_t)a.G * B::GB, srow = (size_t)a.G * B::SW;
   if (!gemm_tma_enabled() || row_bytes % 16 || srow % 16 || reinterpret_cast<uintptr_t>(a.codes) % 16 ||
-      reinterpret_cast<uintptr_t>(a.scales) % 16 || (!kE8 && reinterpret_cast<uintptr_t>(a.mins) % 16))
+      reinterpret_cast<uintptr_t>(a.scales) % 16 || (!kE8 && reinterpret_cast<uintptr_t>(a.mins) % 16) ||
+      !a.counters || !a.partials)
     return cudaSuccess;
+  const int n_mb = (a.M + kBM - 1) / kBM, n_nb = (a.N + kBN2 - 1) / kBN2;
+  const long long tiles = (long long)n_mb * n_nb;
+  const int sms = sm_count();
+  if (sms <= 0 || tiles > (long long)kGemmCounterSlots) return cudaSuccess;
+  a.n_mb = n_mb;
+  a.units = tiles * a.G;
+  const int P = a.units < sms ? (int)a.units : sms;
   auto fn = encode_fn_gemm();
-  CUtensorMap cmap, smap, mmap;
+  CUtensorMap xmap, cmap, smap, mmap;
+  {
+    // x' tiles of 64 columns x up to 256 tokens, 128B-swizzled
+    cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.N};
+    cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)tc2_box_rows(a.N)};
+    cuuint32_t estr[2] = {1, 1};
+    if (fn(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaSuccess;
+  }
   {
     cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
@@ -868,9 +1191,9 @@ cudaError_t launch_gemm_tc2(const GemmArgs& a, const CUtensorMap& xmap, cudaStre
       return cudaSuccess;
   }
   if (kE8) mmap = smap;
-  const size_t smem = 1024 + (size_t)kStages2 * kStageBytes + 2 * (size_t)kBM * B::CB * B::GB +
+  const size_t smem = 1024 + (size_t)kStages2 * kStageBytes2 + 2 * (size_t)kBM * B::CB * B::GB +
                       (kE8 ? 2 : 4) * (size_t)kBM * 16;
-  auto kern = gemm_tc2_kernel<FMT>;
+  auto kern = gemm_sk_kernel<FMT>;
   {
     static std::mutex mu;
     static bool done[64] = {false};
@@ -885,8 +1208,7 @@ cudaError_t launch_gemm_tc2(const GemmArgs& a, const CUtensorMap& xmap, cudaStre
     }
   }
   *taken = true;
-  dim3 grid((a.M + kBM - 1) / kBM, (a.N + kBN - 1) / kBN);
-  kern<<<grid, kGemmThreads, smem, s>>>(xmap, cmap, smap, mmap, a);
+  kern<<<P, kSkThreads, smem, s>>>(xmap, cmap, smap, mmap, a);
   note_launch();
   return cudaGetLastError();
 }
@@ -906,7 +1228,7 @@ cudaError_t launch_gemm_fmt(const GemmArgs& a, const __half* x16, cudaStream_t s
     return cudaErrorInvalidValue;
   {
     bool taken = false;
-    const cudaError_t e = launch_gemm_tc2<FMT>(a, map, s, &taken);
+    const cudaError_t e = launch_gemm_sk<FMT>(a, x16, s, &taken);
     if (taken || e != cudaSuccess) return e;
   }
   const size_t smem = 1024 + (size_t)kStages * kStageBytes;
@@ -941,6 +1263,8 @@ bool gemm_eligible(int fmt, int K) {
 
 size_t gemm_x16_bytes(int N, int K) { return ((size_t)N * K * 2 + 255) / 256 * 256 + ((size_t)N * 4 + 255) / 256 * 256; }
 
+size_t gemm_partial_bytes() { return (size_t)2 * sm_count() * kBN2 * kBM * sizeof(float); }
+
 cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s) {
   if (in.xplain) {
     xhalf_kernel<<<in.N, 256, 0, s>>>(in.xplain, in.Kp, in.K, in.fmt, in.x16, in.tok_scale);
@@ -954,13 +1278,32 @@ cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s) {
     {
       std::lock_guard<std::mutex> lock(mu);
       if (dev < 0 || dev >= 64 || !done[dev]) {
-        e0 = cudaFuncSetAttribute(xprep16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmPrepMaxK * 4);
-        if (e0 != cudaSuccess) return e0;
+        for (const void* f : {reinterpret_cast<const void*>(xprep16_kernel),
+                              reinterpret_cast<const void*>(xprep16_vec_kernel<4>),
+                              reinterpret_cast<const void*>(xprep16_vec_kernel<8>),
+                              reinterpret_cast<const void*>(xprep16_vec_kernel<16>)}) {
+          e0 = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmPrepMaxK * 4);
+          if (e0 != cudaSuccess) return e0;
+        }
         if (dev >= 0 && dev < 64) done[dev] = true;
       }
     }
-    xprep16_kernel<<<in.N, 512, smem, s>>>(in.x, in.x_dtype, in.signs, in.K, in.block, in.rscale, in.fmt, in.x16,
-                                           in.tok_scale);
+    // register butterflies for rotation blocks up to 512 columns (16-byte aligned x, 4-byte aligned signs)
+    const int blk = in.block > 1 ? in.block : 1;
+    const bool vec = blk <= 512 && reinterpret_cast<uintptr_t>(in.x) % 16 == 0 &&
+                     (blk == 1 || reinterpret_cast<uintptr_t>(in.signs) % 4 == 0);
+    if (vec && blk <= 128)
+      xprep16_vec_kernel<4><<<in.N, 512, smem, s>>>(in.x, in.x_dtype, in.signs, in.K, blk, in.rscale, in.fmt, in.x16,
+                                                   in.tok_scale);
+    else if (vec && blk == 256)
+      xprep16_vec_kernel<8><<<in.N, 512, smem, s>>>(in.x, in.x_dtype, in.signs, in.K, blk, in.rscale, in.fmt, in.x16,
+                                                   in.tok_scale);
+    else if (vec && blk == 512)
+      xprep16_vec_kernel<16><<<in.N, 512, smem, s>>>(in.x, in.x_dtype, in.signs, in.K, blk, in.rscale, in.fmt,
+                                                    in.x16, in.tok_scale);
+    else
+      xprep16_kernel<<<in.N, 512, smem, s>>>(in.x, in.x_dtype, in.signs, in.K, in.block, in.rscale, in.fmt, in.x16,
+                                             in.tok_scale);
   }
   note_launch();
   cudaError_t e = cudaGetLastError();
@@ -980,6 +1323,8 @@ cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s) {
   a.bias = in.bias;
   a.y = in.y;
   a.status = in.status;
+  a.counters = in.counters;
+  a.partials = in.partials;
   switch (in.fmt) {
     case PF_FMT_INT4_G128: return launch_gemm_fmt<PF_FMT_INT4_G128>(a, in.x16, s);
     case PF_FMT_INT3_G128: return launch_gemm_fmt<PF_FMT_INT3_G128>(a, in.x16, s);

@@ -171,10 +171,14 @@ struct GemmIn {
   const float* bias;
   float* y;
   unsigned* status;
+  unsigned* counters;  // workspace arrival counters (zero; left zero)
+  float* partials;     // gemm_partial_bytes() of split-tile partial sums
 };
 constexpr int kGemmPrepMaxK = 49152;  // K of the one-kernel x' preparation (K floats of smem)
+constexpr int kGemmCounterSlots = (int)kWsStatusSlot;  // tiles one GEMM launch may split
 bool gemm_eligible(int fmt, int K);
 size_t gemm_x16_bytes(int N, int K);
+size_t gemm_partial_bytes();
 cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s);
 
 struct DequantArgs {

@@ -72,3 +72,41 @@ def test_gemm_linearity_and_status_word():
     torch.cuda.synchronize()
     head = workspace(torch.device("cuda"), 1)[: 16384 * 4].view(torch.int32)
     assert int(head.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("hb", [0, 64, 128, 256, 512])
+@pytest.mark.parametrize("xdt", [torch.float16, torch.bfloat16, torch.float32])
+def test_prep_paths_bit_identical(hb, xdt):
+    """The x' preparation with in-register butterflies (16-byte aligned x) and
+    the shared-memory one (x one element off alignment) give the same y to
+    the bit, for every rotation block the register kernel takes."""
+    from polarflash_b200 import qlinear
+
+    M, K, N = 300, 2048, 40
+    qw, pay, _ = _g128_qweight(_w(M, K, 70 + hb), 3, hb=hb)
+    x = _x(N, K, 71 + hb, xdt).cuda()
+    buf = torch.zeros(N * K + 1, dtype=xdt, device="cuda")
+    xm = buf[1:].view(N, K)
+    xm.copy_(x)
+    assert x.data_ptr() % 16 == 0 and xm.data_ptr() % 16 != 0
+    y = qlinear(qw, x)
+    assert torch.equal(y, qlinear(qw, xm))
+    meta = {"hadamard_rotation": bool(hb), "hadamard_block_size": hb}
+    assert_rel(y.cpu().numpy(), oracle.linear("int3_g128", pay, M, K, meta, x.float().cpu().numpy()))
+
+
+def test_split_tiles_deterministic():
+    """Stream-K: 3000 rows x 600 tokens over K = 2048 is 24 x 3 tiles of 16
+    groups split across the CTAs; repeated calls give identical bits, and y
+    matches the oracle on a slice of rows."""
+    from polarflash_b200 import qlinear
+
+    M, K, N = 3000, 2048, 600
+    qw, pay, _ = _g128_qweight(_w(M, K, 81), 2, hb=128)
+    x = _x(N, K, 82).cuda()
+    y0 = qlinear(qw, x)
+    for _ in range(3):
+        assert torch.equal(qlinear(qw, x), y0)
+    meta = {"hadamard_rotation": True, "hadamard_block_size": 128}
+    ref = oracle.linear("int2_g128", pay, M, K, meta, x[:64].float().cpu().numpy())
+    assert_rel(y0[:64].cpu().numpy(), ref)
