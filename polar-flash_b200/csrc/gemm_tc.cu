@@ -544,10 +544,48 @@ __device__ __forceinline__ int sk_cta_of(long long U, int P, long long u) {
   return (int)(c < P - 1 ? c : P - 1);
 }
 
-// Warp roles of the persistent kernel: 0 TMA producer, 1-8 dequant, 9 MMA,
-// 10-13 epilogue (one per TMEM lane quarter).
+// Order of a CTA's segments: the partial ones first (the one ending its
+// range, then the one starting it), whole tiles after, so the tiles it shares
+// are finished early and their reductions overlap the whole tiles' work.
+__device__ __forceinline__ int sk_items(long long ub, long long ue, int G) {
+  const long long e0 = (ub / G + 1) * G;
+  return e0 >= ue ? 1 : 2 + (int)((((ue - 1) / G) * G - e0) / G);
+}
+__device__ __forceinline__ void sk_item(long long ub, long long ue, int G, int j, long long* us, long long* ul) {
+  const long long e0 = (ub / G + 1) * G;
+  if (e0 >= ue) {
+    *us = ub;
+    *ul = ue;
+    return;
+  }
+  const long long l0 = ((ue - 1) / G) * G;
+  const int n = 2 + (int)((l0 - e0) / G);  // segments in range order: 0 = [ub, e0), n - 1 = [l0, ue)
+  const bool p_first = ub % G != 0, p_last = ue % G != 0;
+  int i;
+  if (p_last && j == 0) {
+    i = n - 1;
+  } else {
+    const int k = p_last ? 1 : 0;  // the rest in range order, after the partial ones
+    i = (p_first && j == k) ? 0 : j - k;
+  }
+  if (i == 0) {
+    *us = ub;
+    *ul = e0;
+  } else if (i == n - 1) {
+    *us = l0;
+    *ul = ue;
+  } else {
+    *us = e0 + (long long)(i - 1) * G;
+    *ul = *us + G;
+  }
+}
+
+// Warp roles of the persistent kernel: 0 x' producer, 1-8 dequant, 9 MMA,
+// 10-13 epilogue (one per TMEM lane quarter), 14 code and scale producer
+// (runs ahead of the x' ring, bounded by the two code / scale slots).
 constexpr int kEpiWarp0 = kDqWarps + 2;
-constexpr int kSkThreads = (kDqWarps + 2 + 4) * 32;
+constexpr int kCodeWarp = kDqWarps + 6;
+constexpr int kSkThreads = (kDqWarps + 7) * 32;
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
   asm volatile(
@@ -575,6 +613,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   __shared__ int abort_flag;
   __shared__ unsigned arrival;
   __shared__ uint4 roots16[kE8 ? 256 * 4 : 1];
+  __shared__ float etscale[kBN2];  // token scales of the epilogue's current segment
 
   unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
   unsigned char* const codes = base + kStages2 * kStageBytes2;  // [2][kCodeSlot]
@@ -589,7 +628,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     abort_flag = 0;
     for (int s = 0; s < kStages2; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bfull0 + 8 * s));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(kBM));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(kDqWarps / 2));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(free0 + 8 * s));
     }
     for (int s = 0; s < 2; ++s) {
@@ -637,17 +676,50 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   const int G = a.G, P = gridDim.x;
   const long long U = a.units;
   const long long u_begin = sk_begin(U, P, blockIdx.x), u_end = sk_begin(U, P, blockIdx.x + 1);
+  const int n_items = sk_items(u_begin, u_end, G);
   const uint32_t xbox_bytes = (uint32_t)tc2_box_rows(a.N) * (kBK2 * 2);
 
   if (warp == 0) {
-    // ------------------------------------------------ producer: codes, scales, x'
+    // ------------------------------------------------ producer: x' tiles
+    if (lane == 0) {
+      // x' and the token scales come from the preparation kernel launched just before
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      bool ok = true;
+      uint32_t q = 0;  // half-stages issued
+      for (int it = 0; it < n_items && ok; ++it) {
+        long long us, ul;
+        sk_item(u_begin, u_end, G, it, &us, &ul);
+        const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
+        const int n0 = (t / a.n_mb) * kBN2;
+        for (int s = g0; s < g1 && ok; ++s) {
+          for (int h = 0; h < 2; ++h, ++q) {
+            const uint32_t slot = q % kStages2;
+            if (q >= kStages2 && !bar_wait(free0 + 8 * slot, ((q / kStages2) - 1) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t dst = su32(base + slot * kStageBytes2 + kATile2), bar = bfull0 + 8 * slot;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(xbox_bytes)
+                         : "memory");
+            tma2d_plain(dst, &xmap, (2 * s + h) * kBK2, n0, bar);
+          }
+        }
+      }
+      if (!ok) {
+        abort_flag = 1;
+        atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+      }
+    }
+  } else if (warp == kCodeWarp) {
+    // ------------------------------------------------ producer: code and scale boxes
     if (lane == 0) {
       bool ok = true;
-      uint32_t q = 0, kc = 0, ks = 0;  // half-stages, code boxes and scale boxes issued
-      for (long long u = u_begin; u < u_end && ok;) {
-        const int t = (int)(u / G), g0 = (int)(u - (long long)t * G);
-        const int g1 = (long long)(G - g0) < u_end - u ? G : g0 + (int)(u_end - u);
-        const int m0 = (t % a.n_mb) * kBM, n0 = (t / a.n_mb) * kBN2;
+      uint32_t kc = 0, ks = 0;  // code boxes and scale boxes issued
+      for (int it = 0; it < n_items && ok; ++it) {
+        long long us, ul;
+        sk_item(u_begin, u_end, G, it, &us, &ul);
+        const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
+        const int m0 = (t % a.n_mb) * kBM;
         for (int s = g0; s < g1 && ok; ++s) {
           if (s == g0 || s % B::CB == 0) {
             const uint32_t cs = kc & 1;
@@ -676,19 +748,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             if (!kE8) tma2d_plain(su32(scl + (2 + ss) * kScaleSlot), &mmap, sx, m0, sfull0 + 8 * ss);
             ++ks;
           }
-          for (int h = 0; h < 2; ++h, ++q) {
-            const uint32_t slot = q % kStages2;
-            if (q >= kStages2 && !bar_wait(free0 + 8 * slot, ((q / kStages2) - 1) & 1, &abort_flag)) {
-              ok = false;
-              break;
-            }
-            const uint32_t dst = su32(base + slot * kStageBytes2 + kATile2), bar = bfull0 + 8 * slot;
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(xbox_bytes)
-                         : "memory");
-            tma2d_plain(dst, &xmap, (2 * s + h) * kBK2, n0, bar);
-          }
         }
-        u += g1 - g0;
       }
       if (!ok) {
         abort_flag = 1;
@@ -700,9 +760,10 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     if (lane == 0) {
       bool ok = true;
       uint32_t q = 0, j = 0;
-      for (long long u = u_begin; u < u_end && ok; ++j) {
-        const int t = (int)(u / G), g0 = (int)(u - (long long)t * G);
-        const int g1 = (long long)(G - g0) < u_end - u ? G : g0 + (int)(u_end - u);
+      for (; (int)j < n_items && ok; ++j) {
+        long long us, ul;
+        sk_item(u_begin, u_end, G, (int)j, &us, &ul);
+        const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
         const int n0 = (t / a.n_mb) * kBN2;
         const int nv = a.N - n0 < kBN2 ? a.N - n0 : kBN2;
         const uint32_t idesc = gemm_idesc((nv + 15) & ~15);
@@ -738,7 +799,6 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(accf0 +
                                                                                                           8 * buf)
                        : "memory");
-        u += g1 - g0;
       }
       if (!ok) {
         abort_flag = 1;
@@ -758,9 +818,10 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       }
     };
     uint32_t gs = 0, kc = 0, ks = 0;  // groups, code boxes and scale boxes consumed
-    for (long long u = u_begin; u < u_end;) {
-      const int t = (int)(u / G), g0 = (int)(u - (long long)t * G);
-      const int g1 = (long long)(G - g0) < u_end - u ? G : g0 + (int)(u_end - u);
+    for (int it = 0; it < n_items; ++it) {
+      long long us, ul;
+      sk_item(u_begin, u_end, G, it, &us, &ul);
+      const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
       uint32_t cs = 0, ss = 0, cpar = 0, spar = 0;
       for (int s = g0; s < g1; ++s, ++gs) {
         if (s == g0 || s % B::CB == 0) {
@@ -802,11 +863,11 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(cfree0 + 8 * cs) : "memory");
         if (s + 1 == g1 || (s + 1) % B::SB == 0)
           asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sfree0 + 8 * ss) : "memory");
-        if (!live) continue;
+        // every lane's A-tile stores visible to the tensor core, then one arrival per warp
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(afull0 + 8 * slot) : "memory");
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(afull0 + 8 * slot) : "memory");
       }
-      u += g1 - g0;
     }
   } else {
     // ------------------------------------------------ epilogue warps: TMEM -> y / partial tiles
@@ -814,10 +875,12 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     const int r = 32 * quarter + lane;  // tile row == this warp's TMEM lanes
     const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
     const int ci = (int)blockIdx.x;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     uint32_t j = 0;
-    for (long long u = u_begin; u < u_end; ++j) {
-      const int t = (int)(u / G), g0 = (int)(u - (long long)t * G);
-      const int g1 = (long long)(G - g0) < u_end - u ? G : g0 + (int)(u_end - u);
+    for (; (int)j < n_items; ++j) {
+      long long us, ul;
+      sk_item(u_begin, u_end, G, (int)j, &us, &ul);
+      const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
       const int m0 = (t % a.n_mb) * kBM, n0 = (t / a.n_mb) * kBN2;
       const uint32_t buf = j & 1, taddr = tmem + buf * kTmemCols2 + lane_off;
       const int nv = a.N - n0 < kBN2 ? a.N - n0 : kBN2;
@@ -826,7 +889,13 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       const bool rvalid = grow < a.M;
       const float bv = (rvalid && a.bias) ? a.bias[grow] : 0.f;
       const bool whole = g0 == 0 && g1 == G;
-      float* const mine = a.partials + ((size_t)(2 * ci + (j > 0 ? 1 : 0)) * kBN2) * kBM;
+      // the segment holding the range's first unit keeps slot 2c, the one ending it 2c + 1
+      float* const mine = a.partials + ((size_t)(2 * ci + (us == u_begin ? 0 : 1)) * kBN2) * kBM;
+      // this segment's token scales in shared memory: the y stores below then
+      // need no global load between them
+      asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");
+      for (int i = r; i < kBN2; i += kBM) etscale[i] = n0 + i < a.N ? a.tok_scale[n0 + i] : 0.f;
+      asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");
       bool ok = bar_wait(accf0 + 8 * buf, (j >> 1) & 1, &abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok && lane == 0) {
@@ -843,7 +912,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
               const int tk = n0 + c0 + jj;
-              if (tk < a.N) a.y[(size_t)tk * a.M + grow] = __uint_as_float(v[jj]) * a.tok_scale[tk] + bv;
+              if (tk < a.N) a.y[(size_t)tk * a.M + grow] = __uint_as_float(v[jj]) * etscale[c0 + jj] + bv;
             }
           }
         } else {
@@ -870,37 +939,43 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const unsigned got = arrival;
         if (ok && got != 0xFFFFFFFFu && got == (unsigned)(cl - cf)) {
 #pragma unroll 1
-          for (int c0 = 0; c0 < nmma; c0 += 32) {
-            float accv[32];
+          for (int c0 = 0; c0 < nmma; c0 += 16) {
+            float accv[16];
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) accv[jj] = 0.f;
+            for (int jj = 0; jj < 16; ++jj) accv[jj] = 0.f;
+            // contributors in k order, four at a time so their loads overlap
 #pragma unroll 1
-            for (int c = cf; c <= cl; ++c) {
-              float pv[32];
-              if (c == ci) {
-                uint32_t w0[16], w1[16];
-                tmem_ld16(taddr + (uint32_t)c0, w0);
-                tmem_ld16(taddr + (uint32_t)(c0 + 16), w1);
+            for (int cb = cf; cb <= cl; cb += 4) {
+              float pv[4][16];
 #pragma unroll
-                for (int jj = 0; jj < 16; ++jj) {
-                  pv[jj] = __uint_as_float(w0[jj]);
-                  pv[16 + jj] = __uint_as_float(w1[jj]);
+              for (int i = 0; i < 4; ++i) {
+                const int c = cb + i;
+                if (c > cl) continue;
+                if (c == ci) {
+                  uint32_t w[16];
+                  tmem_ld16(taddr + (uint32_t)c0, w);
+#pragma unroll
+                  for (int jj = 0; jj < 16; ++jj) pv[i][jj] = __uint_as_float(w[jj]);
+                } else {
+                  // CTA c holds this tile in its first segment (slot 2c) unless the tile starts after its range does
+                  const int first_t = (int)(sk_begin(U, P, c) / G);
+                  const float* pp = a.partials + ((size_t)(2 * c + (first_t == t ? 0 : 1)) * kBN2 + c0) * kBM + r;
+#pragma unroll
+                  for (int jj = 0; jj < 16; ++jj) pv[i][jj] = __ldcg(pp + (size_t)jj * kBM);
                 }
-              } else {
-                // CTA c holds this tile in its first segment (slot 2c) unless the tile starts after its range does
-                const int first_t = (int)(sk_begin(U, P, c) / G);
-                const float* pp = a.partials + ((size_t)(2 * c + (first_t == t ? 0 : 1)) * kBN2 + c0) * kBM + r;
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) pv[jj] = __ldcg(pp + (size_t)jj * kBM);
               }
 #pragma unroll
-              for (int jj = 0; jj < 32; ++jj) accv[jj] += pv[jj];
+              for (int i = 0; i < 4; ++i) {
+                if (cb + i > cl) continue;
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) accv[jj] += pv[i][jj];
+              }
             }
             if (rvalid) {
 #pragma unroll
-              for (int jj = 0; jj < 32; ++jj) {
+              for (int jj = 0; jj < 16; ++jj) {
                 const int tk = n0 + c0 + jj;
-                if (tk < a.N) a.y[(size_t)tk * a.M + grow] = accv[jj] * a.tok_scale[tk] + bv;
+                if (tk < a.N) a.y[(size_t)tk * a.M + grow] = accv[jj] * etscale[c0 + jj] + bv;
               }
             }
           }
@@ -911,7 +986,6 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       // TMEM buffer free for the segment after next
       asm volatile("tcgen05.fence::before_thread_sync;");
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty0 + 8 * buf) : "memory");
-      u += g1 - g0;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -958,6 +1032,7 @@ __global__ void __launch_bounds__(256) xhalf_kernel(const float* __restrict__ xp
                                                     float* tok_scale) {
   __shared__ float red[32];
   const int t = blockIdx.x;
+  asm volatile("griddepcontrol.launch_dependents;");  // the GEMM's prologue may start
   const float* row = xp + (size_t)t * Kp;
   float mx = 0.f;
   for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(row[k]));
@@ -973,6 +1048,7 @@ __global__ void __launch_bounds__(512) xprep16_kernel(const void* x, int x_dtype
   extern __shared__ float xrow[];
   __shared__ float red[32];
   const int t = blockIdx.x;
+  asm volatile("griddepcontrol.launch_dependents;");  // the GEMM's prologue may start
   for (int k = threadIdx.x; k < K; k += blockDim.x) {
     float v = load_x(x, x_dtype, (size_t)t * K + k);
     if (block > 1 && signs[k] < 0) v = -v;
@@ -1038,6 +1114,7 @@ __global__ void __launch_bounds__(512) xprep16_vec_kernel(const void* x, int x_d
   __shared__ float red[32];
   constexpr int kSeg = 32 * V;
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  asm volatile("griddepcontrol.launch_dependents;");  // the GEMM's prologue may start
   float mx = 0.f;
   for (int seg = warp; seg < K / kSeg; seg += nw) {
     const int k0 = seg * kSeg + lane * V;
@@ -1208,9 +1285,21 @@ cudaError_t launch_gemm_sk(GemmArgs a, const __half* x16, cudaStream_t s, bool* 
     }
   }
   *taken = true;
-  kern<<<P, kSkThreads, smem, s>>>(xmap, cmap, smap, mmap, a);
+  // programmatic dependent launch: barrier setup, TMEM allocation, the code and
+  // scale loads and the first decodes overlap the x' preparation's tail
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(P);
+  cfg.blockDim = dim3(kSkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, xmap, cmap, smap, mmap, (const GemmArgs)a);
   note_launch();
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int FMT>
