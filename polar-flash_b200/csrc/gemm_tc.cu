@@ -596,6 +596,22 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 32 consecutive fp32 accumulator columns of this thread's TMEM lane, one wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* f) {
+  uint32_t v[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(kSkThreads, 1)
     gemm_sk_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
@@ -903,21 +919,23 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
       }
       asm volatile("tcgen05.fence::after_thread_sync;");
+      // 32 columns per TMEM load (columns past nmma are read, never written out)
 #pragma unroll 1
-      for (int c0 = 0; c0 < nmma && ok; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(taddr + (uint32_t)c0, v);
+      for (int c0 = 0; c0 < nmma && ok; c0 += 32) {
+        float v[32];
+        tmem_ld32(taddr + (uint32_t)c0, v);
         if (whole) {
           if (rvalid) {
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
+            for (int jj = 0; jj < 32; ++jj) {
               const int tk = n0 + c0 + jj;
-              if (tk < a.N) a.y[(size_t)tk * a.M + grow] = __uint_as_float(v[jj]) * etscale[c0 + jj] + bv;
+              if (tk < a.N) a.y[(size_t)tk * a.M + grow] = v[jj] * etscale[c0 + jj] + bv;
             }
           }
         } else {
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) mine[(size_t)(c0 + jj) * kBM + r] = __uint_as_float(v[jj]);
+          for (int jj = 0; jj < 32; ++jj)
+            if (c0 + jj < nmma) mine[(size_t)(c0 + jj) * kBM + r] = v[jj];
         }
       }
       if (!whole) {
@@ -943,12 +961,12 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             float accv[16];
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) accv[jj] = 0.f;
-            // contributors in k order, four at a time so their loads overlap
+            // contributors in k order, two at a time so their loads overlap
 #pragma unroll 1
-            for (int cb = cf; cb <= cl; cb += 4) {
-              float pv[4][16];
+            for (int cb = cf; cb <= cl; cb += 2) {
+              float pv[2][16];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
+              for (int i = 0; i < 2; ++i) {
                 const int c = cb + i;
                 if (c > cl) continue;
                 if (c == ci) {
@@ -965,7 +983,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                 }
               }
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
+              for (int i = 0; i < 2; ++i) {
                 if (cb + i > cl) continue;
 #pragma unroll
                 for (int jj = 0; jj < 16; ++jj) accv[jj] += pv[i][jj];
