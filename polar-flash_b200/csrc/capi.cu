@@ -231,11 +231,13 @@ bool use_gemm(const pf_qweight* w, int N) {
   if (w->format != PF_FMT_INT3_G128 && !aligned(w->codes, 16)) return false;
   return w->format != PF_FMT_E8_RVQ2_G128 || aligned(w->scales, 4);
 }
-size_t gemm_bytes(const pf_qweight* w, int N) {
+// `partials`: room for the stream-K kernel's split-tile partial sums; a
+// workspace without it runs the GEMM on the non-persistent kernel.
+size_t gemm_bytes(const pf_qweight* w, int N, bool partials = true) {
   const int nc = N < kGemmChunk ? N : kGemmChunk;
   const size_t Kp = (size_t)((w->K + 127) / 128) * 128;
   return kCounterBytes + round_up((size_t)nc * Kp * sizeof(float), 256) + gemm_x16_bytes(nc, w->K) +
-         gemm_partial_bytes();
+         (partials ? gemm_partial_bytes() : 0);
 }
 
 // Batch-1 E8 runs on the lookup-table GEMV when its shapes and alignments
@@ -299,17 +301,19 @@ bool use_polar_lut(const pf_qweight* w, int N, const HadPlan& plan, const void* 
   return polar8_lut_eligible(polar8_in(w, plan, x, x_dtype, nullptr, nullptr));
 }
 
-size_t workspace_bytes(const pf_qweight* w, int N) {
+// full: the size pf_qlinear_workspace_size reports (fastest paths); without
+// it, the least pf_qlinear accepts.
+size_t workspace_bytes(const pf_qweight* w, int N, bool full = true) {
   if (N < 1) N = 1;
   if ((w->format == PF_FMT_E8_RVQ2_G128 || (w->format == PF_FMT_POLAR_RECURSIVE && w->params[0] == 8)) && N == 1) {
     // either path, depending on the input's alignment
     const size_t part = w->format == PF_FMT_E8_RVQ2_G128 ? e8_lut_partial_bytes(w->M, w->K)
                                                          : polar8_lut_partial_bytes(w->M, w->K);
     const size_t lut = kCounterBytes + part;
-    const size_t other = use_gemm(w, N) ? gemm_bytes(w, N) : pass_bytes(w, 1);
+    const size_t other = use_gemm(w, N) ? gemm_bytes(w, N, full) : pass_bytes(w, 1);
     return lut > other ? lut : other;
   }
-  if (use_gemm(w, N)) return gemm_bytes(w, N);
+  if (use_gemm(w, N)) return gemm_bytes(w, N, full);
   size_t b = pass_bytes(w, tokens_per_pass(N));
   int tail = N % kMaxGemvTokens;
   if (N > kMaxGemvTokens && tail) {
@@ -411,6 +415,8 @@ int do_run(const pf_qweight* w, int N, const float* bias, float* y, void* ws, cu
 
 }  // namespace
 
+size_t pfb::min_workspace_bytes(const pf_qweight* w, int N) { return workspace_bytes(w, N, false); }
+
 static std::atomic<unsigned long long> g_launches{0};
 void pfb::note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
@@ -451,7 +457,7 @@ static int common_args(const pf_qweight* w, int N, void* ws, size_t ws_bytes) {
   if (st) return st;
   if (N < 0) return PF_ERR_INVALID_ARGUMENT;
   if (N == 0) return PF_OK;
-  if (!ws || ws_bytes < workspace_bytes(w, N)) return PF_ERR_WORKSPACE;
+  if (!ws || ws_bytes < workspace_bytes(w, N, false)) return PF_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return PF_ERR_ALIGNMENT;
   return PF_OK;
 }
@@ -474,7 +480,7 @@ static int qlinear_pass(const pf_qweight* w, const HadPlan& plan, const void* x,
 
 // Tokens [0, N) through the tensor-core GEMM, kGemmChunk at a time.
 static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, int N,
-                        const float* bias, float* y, void* ws, cudaStream_t s) {
+                        const float* bias, float* y, void* ws, bool with_partials, cudaStream_t s) {
   const int K = w->K, Kp = ((K + 127) / 128) * 128;
   const size_t xs = dtype_size(x_dtype);
   char* base = static_cast<char*>(ws) + kCounterBytes;
@@ -482,7 +488,9 @@ static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x,
   float* xplain = reinterpret_cast<float*>(base);
   __half* x16 = reinterpret_cast<__half*>(base + round_up((size_t)cmax * Kp * sizeof(float), 256));
   float* tsc = reinterpret_cast<float*>(reinterpret_cast<char*>(x16) + round_up((size_t)cmax * K * 2, 256));
-  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(x16) + gemm_x16_bytes(cmax, K));
+  // no room for partial tiles: the non-persistent GEMM kernel runs
+  float* partials =
+      with_partials ? reinterpret_cast<float*>(reinterpret_cast<char*>(x16) + gemm_x16_bytes(cmax, K)) : nullptr;
   // rotation blocks that tile K: x' straight from x in the GEMM's own prep
   const bool direct = plan.ncasc == 0 && (plan.block == 0 || plan.rot_end == K) && K <= kGemmPrepMaxK;
   for (int t0 = 0; t0 < N; t0 += kGemmChunk) {
@@ -580,7 +588,8 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
     st = launch_polar8_lut(&in, 1, workspace, s, &e);
     return st == PF_ERR_CUDA ? cuda_status(e) : st;
   }
-  if (use_gemm(w, N)) return qlinear_gemm(w, plan, x, x_dtype, N, bias, y, workspace, s);
+  if (use_gemm(w, N))
+    return qlinear_gemm(w, plan, x, x_dtype, N, bias, y, workspace, ws_bytes >= workspace_bytes(w, N), s);
   const size_t xs = dtype_size(x_dtype);
   for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {
     int np = N - t0 < kMaxGemvTokens ? N - t0 : kMaxGemvTokens;

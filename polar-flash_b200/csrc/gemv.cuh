@@ -9,6 +9,10 @@ namespace pfb {
 // pf_kernel_launches); called after every launch this library makes.
 void note_launch();
 
+// The least workspace pf_qlinear accepts for (w, N) (pf_qlinear_workspace_size
+// reports the size for the fastest paths, which can be larger).
+size_t min_workspace_bytes(const pf_qweight* w, int N);
+
 // Workspace head: split-K arrival counters (zero-filled once by the owner of
 // the workspace, left zero by every call); the last slot records a device
 // status word (PF_ERR_TIMEOUT when a bounded pipeline wait gave up).

@@ -62,8 +62,11 @@ extern "C" int pf_qlinear_noalloc(const pf_qweight* w, const void* x, int x_dtyp
                                   float* y, void* stream) {
   if (!w || N < 0) return PF_ERR_INVALID_ARGUMENT;
   size_t need = 0;
-  int st = pf_qlinear_workspace_size(w, N, &need);
+  int st = pf_qlinear_workspace_size(w, N, &need);  // also validates w
   if (st) return st;
+  // the least workspace the call can run in (batches above 16 tokens then
+  // take the tensor-core GEMM without stream-K partial tiles)
+  need = pfb::min_workspace_bytes(w, N);
   if (need > kNoAllocScratchBytes) return PF_ERR_WORKSPACE;  // request beyond the fixed 8 MiB scratch
   void* scratch = nullptr;
   st = noalloc_scratch(&scratch);
