@@ -442,8 +442,6 @@ constexpr int kBK2 = 64;
 constexpr int kStages2 = 3;
 constexpr int kTmemCols2 = 256;
 constexpr uint32_t kATile2 = kBM * kBK2 * 2;  // one 64-column swizzle atom
-constexpr uint32_t kBTile2 = kBN2 * kBK2 * 2;
-constexpr uint32_t kStageBytes2 = kATile2 + kBTile2;
 
 // Token rows of the x' box: 256, or the batch rounded up to 16 when it is
 // smaller (the MMA reads no row past that).
@@ -580,6 +578,58 @@ __device__ __forceinline__ void sk_item(long long ub, long long ue, int G, int j
   }
 }
 
+// Two-SM (pair) helpers.
+constexpr int kStagesPair = 5;  // A/B ring slots of the pair kernel (32 KB each)
+
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared variable in the cluster's CTA 0.
+__device__ __forceinline__ uint32_t map_rank0(uint32_t saddr) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(d) : "r"(saddr));
+  return d;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// One arrival on a barrier of this CTA (kPair: of the pair's first CTA, by
+// its cluster address).
+template <bool kPair>
+__device__ __forceinline__ void bar_arrive_pair(uint32_t bar) {
+  if constexpr (kPair)
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+  else
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Completion of this thread's earlier MMAs arrives on `bar` (kPair: on the
+// same barrier of both CTAs of the pair).
+template <bool kPair>
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  if constexpr (kPair)
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((unsigned short)0x3)
+        : "memory");
+  else
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// x' half-tile load of a pair CTA; its bytes count on CTA 0's barrier (cluster address).
+__device__ __forceinline__ void tma2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// Instruction descriptor for an M x N kind::f16 MMA (fp16 A, B K-major, fp32 D).
+__host__ __device__ constexpr uint32_t gemm_idesc_m(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
 // Warp roles of the persistent kernel: 0 x' producer, 1-8 dequant, 9 MMA,
 // 10-13 epilogue (one per TMEM lane quarter), 14 code and scale producer
 // (runs ahead of the x' ring, bounded by the two code / scale slots).
@@ -612,19 +662,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* f) {
   for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
 }
 
-template <int FMT>
+// kPair: a cluster of two CTAs on two SMs runs each 256-row tile with
+// tcgen05.mma.cta_group::2 (M = 256): every CTA decodes its own 128 rows and
+// loads half of the x' tile (128 tokens), the first CTA of the pair issues
+// the MMAs (reading both CTAs' shared memory) and each CTA's TMEM holds its
+// rows' accumulators.  Half the x' bytes per CTA leave room for five stages.
+template <int FMT, bool kPair>
 __global__ void __launch_bounds__(kSkThreads, 1)
     gemm_sk_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
                    const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap mmap,
                    const __grid_constant__ GemmArgs a) {
   using B = TcBox<FMT>;
   constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
+  constexpr int kSt = kPair ? kStagesPair : kStages2;    // A/B ring slots
+  constexpr int kXRows = kPair ? kBN2 / 2 : kBN2;       // token rows of this CTA's x' box
+  constexpr uint32_t kSB = kATile2 + kXRows * kBK2 * 2;  // bytes per stage
+  constexpr int kRowsT = kPair ? 2 * kBM : kBM;          // weight rows per tile
   constexpr uint32_t kCodeSlot = kBM * B::CB * B::GB;  // 128 rows x CB groups
   constexpr uint32_t kScaleSlot = kBM * 16;            // 128 rows x SB groups x SW bytes (16)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // A/B ring full / A full / free, then code full / free and scale full /
   // free (two slots each), then accumulator full and TMEM-buffer empty (two each)
-  __shared__ uint64_t bars[3 * kStages2 + 8 + 4];
+  __shared__ uint64_t bars[3 * kSt + 8 + 4];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
   __shared__ unsigned arrival;
@@ -632,19 +691,23 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   __shared__ float etscale[kBN2];  // token scales of the epilogue's current segment
 
   unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
-  unsigned char* const codes = base + kStages2 * kStageBytes2;  // [2][kCodeSlot]
+  unsigned char* const codes = base + kSt * kSB;  // [2][kCodeSlot]
   unsigned char* const scl = codes + 2 * kCodeSlot;             // [2][kScaleSlot] (+ [2][kScaleSlot] mins)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t bfull0 = su32(&bars[0]), afull0 = su32(&bars[kStages2]), free0 = su32(&bars[2 * kStages2]);
-  const uint32_t cfull0 = su32(&bars[3 * kStages2]), cfree0 = cfull0 + 16;
+  const uint32_t bfull0 = su32(&bars[0]), afull0 = su32(&bars[kSt]), free0 = su32(&bars[2 * kSt]);
+  const uint32_t cfull0 = su32(&bars[3 * kSt]), cfree0 = cfull0 + 16;
   const uint32_t sfull0 = cfull0 + 32, sfree0 = cfull0 + 48;
   const uint32_t accf0 = cfull0 + 64, tempty0 = cfull0 + 80;
+  const uint32_t rank = kPair ? cta_rank() : 0u;
+  // barriers of the pair's first CTA as cluster addresses (own ones without kPair)
+  const uint32_t afull_l = kPair ? map_rank0(afull0) : afull0, bfull_l = kPair ? map_rank0(bfull0) : bfull0;
+  const uint32_t tempty_l = kPair ? map_rank0(tempty0) : tempty0;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int s = 0; s < kStages2; ++s) {
+    for (int s = 0; s < kSt; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bfull0 + 8 * s));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(kDqWarps / 2));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(kPair ? kDqWarps : kDqWarps / 2));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(free0 + 8 * s));
     }
     for (int s = 0; s < 2; ++s) {
@@ -653,7 +716,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sfull0 + 8 * s));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sfree0 + 8 * s), "r"(2 * kBM));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(accf0 + 8 * s));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tempty0 + 8 * s), "r"(kBM));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tempty0 + 8 * s), "r"(kPair ? 8 : 4));
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
@@ -681,19 +744,29 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
   }
   if (warp == kMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_slot)),
-                 "r"(2 * kTmemCols2));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (kPair) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_slot)),
+                   "r"(2 * kTmemCols2));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_slot)),
+                   "r"(2 * kTmemCols2));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
+  if constexpr (kPair) cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = tmem_base_slot;
-  const int G = a.G, P = gridDim.x;
+  // stream-K over pairs (kPair) or CTAs
+  const int G = a.G, P = kPair ? (int)gridDim.x / 2 : (int)gridDim.x;
+  const int sk_id = kPair ? (int)blockIdx.x / 2 : (int)blockIdx.x;
   const long long U = a.units;
-  const long long u_begin = sk_begin(U, P, blockIdx.x), u_end = sk_begin(U, P, blockIdx.x + 1);
+  const long long u_begin = sk_begin(U, P, sk_id), u_end = sk_begin(U, P, sk_id + 1);
   const int n_items = sk_items(u_begin, u_end, G);
-  const uint32_t xbox_bytes = (uint32_t)tc2_box_rows(a.N) * (kBK2 * 2);
+  // x' bytes landing on one stage's full barrier (kPair: both CTAs' halves)
+  const uint32_t xbox_bytes = kPair ? 2u * kXRows * (kBK2 * 2) : (uint32_t)tc2_box_rows(a.N) * (kBK2 * 2);
 
   if (warp == 0) {
     // ------------------------------------------------ producer: x' tiles
@@ -706,18 +779,23 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         long long us, ul;
         sk_item(u_begin, u_end, G, it, &us, &ul);
         const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
-        const int n0 = (t / a.n_mb) * kBN2;
+        const int n0 = (t / a.n_mb) * kBN2 + (int)rank * kXRows;
         for (int s = g0; s < g1 && ok; ++s) {
           for (int h = 0; h < 2; ++h, ++q) {
-            const uint32_t slot = q % kStages2;
-            if (q >= kStages2 && !bar_wait(free0 + 8 * slot, ((q / kStages2) - 1) & 1, &abort_flag)) {
+            const uint32_t slot = q % kSt;
+            if (q >= kSt && !bar_wait(free0 + 8 * slot, ((q / kSt) - 1) & 1, &abort_flag)) {
               ok = false;
               break;
             }
-            const uint32_t dst = su32(base + slot * kStageBytes2 + kATile2), bar = bfull0 + 8 * slot;
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(xbox_bytes)
-                         : "memory");
-            tma2d_plain(dst, &xmap, (2 * s + h) * kBK2, n0, bar);
+            const uint32_t dst = su32(base + slot * kSB + kATile2);
+            if (rank == 0)
+              asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bfull0 + 8 * slot),
+                           "r"(xbox_bytes)
+                           : "memory");
+            if constexpr (kPair)
+              tma2d_pair(dst, &xmap, (2 * s + h) * kBK2, n0, bfull_l + 8 * slot);
+            else
+              tma2d_plain(dst, &xmap, (2 * s + h) * kBK2, n0, bfull0 + 8 * slot);
           }
         }
       }
@@ -735,7 +813,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         long long us, ul;
         sk_item(u_begin, u_end, G, it, &us, &ul);
         const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
-        const int m0 = (t % a.n_mb) * kBM;
+        const int m0 = (t % a.n_mb) * kRowsT + (int)rank * kBM;
         for (int s = g0; s < g1 && ok; ++s) {
           if (s == g0 || s % B::CB == 0) {
             const uint32_t cs = kc & 1;
@@ -772,8 +850,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       }
     }
   } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issue (the pair's first CTA)
+    if (lane == 0 && rank == 0) {
       bool ok = true;
       uint32_t q = 0, j = 0;
       for (; (int)j < n_items && ok; ++j) {
@@ -782,7 +860,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
         const int n0 = (t / a.n_mb) * kBN2;
         const int nv = a.N - n0 < kBN2 ? a.N - n0 : kBN2;
-        const uint32_t idesc = gemm_idesc((nv + 15) & ~15);
+        // kPair: N = 256 always (each CTA's half of B is 128 tokens, zero past N)
+        const uint32_t idesc = kPair ? gemm_idesc_m(2 * kBM, kBN2) : gemm_idesc((nv + 15) & ~15);
         const uint32_t buf = j & 1, acc_t = tmem + buf * kTmemCols2;
         if (j >= 2 && !bar_wait(tempty0 + 8 * buf, ((j >> 1) - 1) & 1, &abort_flag)) {
           ok = false;
@@ -790,31 +869,32 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         }
         for (int s = g0; s < g1 && ok; ++s) {
           for (int h = 0; h < 2; ++h, ++q) {
-            const uint32_t slot = q % kStages2, par = (q / kStages2) & 1;
+            const uint32_t slot = q % kSt, par = (q / kSt) & 1;
             if (!bar_wait(afull0 + 8 * slot, par, &abort_flag) || !bar_wait(bfull0 + 8 * slot, par, &abort_flag)) {
               ok = false;
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;");
-            const uint32_t sa = su32(base + slot * kStageBytes2), sb = sa + kATile2;
+            const uint32_t sa = su32(base + slot * kSB), sb = sa + kATile2;
 #pragma unroll
             for (int k = 0; k < kBK2 / 16; ++k) {
               const uint64_t da = kmajor_desc(sa + k * 32), db = kmajor_desc(sb + k * 32);
               const uint32_t acc = (s > g0 || h > 0 || k > 0) ? 1u : 0u;
-              asm volatile(
-                  "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
-                      acc_t),
-                  "l"(da), "l"(db), "r"(idesc), "r"(acc));
+              if constexpr (kPair)
+                asm volatile(
+                    "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
+                        acc_t),
+                    "l"(da), "l"(db), "r"(idesc), "r"(acc));
+              else
+                asm volatile(
+                    "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
+                        acc_t),
+                    "l"(da), "l"(db), "r"(idesc), "r"(acc));
             }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             free0 + 8 * slot)
-                         : "memory");
+            mma_commit<kPair>(free0 + 8 * slot);
           }
         }
-        if (ok)
-          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(accf0 +
-                                                                                                          8 * buf)
-                       : "memory");
+        if (ok) mma_commit<kPair>(accf0 + 8 * buf);
       }
       if (!ok) {
         abort_flag = 1;
@@ -850,7 +930,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           spar = (ks >> 1) & 1;
           ++ks;
         }
-        const uint32_t q = 2 * gs + grp, slot = q % kStages2;
+        const uint32_t q = 2 * gs + grp, slot = q % kSt;
         if (live && !bar_wait(cfull0 + 8 * cs, cpar, &abort_flag)) fail();
         if (live && !bar_wait(sfull0 + 8 * ss, spar, &abort_flag)) fail();
         // this row's scale (and zero point) of group s
@@ -866,9 +946,9 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           }
         }
         const unsigned char* cp = codes + cs * kCodeSlot + r * (B::CB * B::GB) + (s % B::CB) * B::GB;
-        if (live && q >= kStages2 && !bar_wait(free0 + 8 * slot, ((q / kStages2) - 1) & 1, &abort_flag)) fail();
+        if (live && q >= kSt && !bar_wait(free0 + 8 * slot, ((q / kSt) - 1) & 1, &abort_flag)) fail();
         if (live) {
-          unsigned char* at = base + slot * kStageBytes2;
+          unsigned char* at = base + slot * kSB;
           if (grp == 0)
             tc2_decode<FMT, 0>(cp, sc, r, lane, at, roots16);
           else
@@ -882,7 +962,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         // every lane's A-tile stores visible to the tensor core, then one arrival per warp
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(afull0 + 8 * slot) : "memory");
+        if (lane == 0) bar_arrive_pair<kPair>(afull_l + 8 * slot);
       }
     }
   } else {
@@ -890,14 +970,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     const int quarter = warp & 3;
     const int r = 32 * quarter + lane;  // tile row == this warp's TMEM lanes
     const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
-    const int ci = (int)blockIdx.x;
+    const int ci = sk_id;             // this CTA's (kPair: pair's) place in the stream-K split
+    const int cta = (int)blockIdx.x;  // partial slots are per CTA
     asm volatile("griddepcontrol.wait;" ::: "memory");
     uint32_t j = 0;
     for (; (int)j < n_items; ++j) {
       long long us, ul;
       sk_item(u_begin, u_end, G, (int)j, &us, &ul);
       const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
-      const int m0 = (t % a.n_mb) * kBM, n0 = (t / a.n_mb) * kBN2;
+      const int m0 = (t % a.n_mb) * kRowsT + (int)rank * kBM, n0 = (t / a.n_mb) * kBN2;
       const uint32_t buf = j & 1, taddr = tmem + buf * kTmemCols2 + lane_off;
       const int nv = a.N - n0 < kBN2 ? a.N - n0 : kBN2;
       const int nmma = (nv + 15) & ~15;
@@ -906,7 +987,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       const float bv = (rvalid && a.bias) ? a.bias[grow] : 0.f;
       const bool whole = g0 == 0 && g1 == G;
       // the segment holding the range's first unit keeps slot 2c, the one ending it 2c + 1
-      float* const mine = a.partials + ((size_t)(2 * ci + (us == u_begin ? 0 : 1)) * kBN2) * kBM;
+      float* const mine = a.partials + ((size_t)(2 * cta + (us == u_begin ? 0 : 1)) * kBN2) * kBM;
       // this segment's token scales in shared memory: the y stores below then
       // need no global load between them
       asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");
@@ -946,7 +1027,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         if (warp == kEpiWarp0 && lane == 0) {
           unsigned v = 0xFFFFFFFFu;
           if (ok && !abort_flag) {
-            v = atomicAdd(a.counters + t, 1u);
+            v = atomicAdd(a.counters + (kPair ? 2 * t + (int)rank : t), 1u);
             __threadfence();
           }
           arrival = v;
@@ -977,7 +1058,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                 } else {
                   // CTA c holds this tile in its first segment (slot 2c) unless the tile starts after its range does
                   const int first_t = (int)(sk_begin(U, P, c) / G);
-                  const float* pp = a.partials + ((size_t)(2 * c + (first_t == t ? 0 : 1)) * kBN2 + c0) * kBM + r;
+                  const int cc = kPair ? 2 * c + (int)rank : c;  // the contributing CTA holding these rows
+                  const float* pp = a.partials + ((size_t)(2 * cc + (first_t == t ? 0 : 1)) * kBN2 + c0) * kBM + r;
 #pragma unroll
                   for (int jj = 0; jj < 16; ++jj) pv[i][jj] = __ldcg(pp + (size_t)jj * kBM);
                 }
@@ -997,20 +1079,25 @@ __global__ void __launch_bounds__(kSkThreads, 1)
               }
             }
           }
-          if (warp == kEpiWarp0 && lane == 0) a.counters[t] = 0u;  // left zero for the next call
+          if (warp == kEpiWarp0 && lane == 0) a.counters[kPair ? 2 * t + (int)rank : t] = 0u;  // left zero for the next call
         }
         asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");  // arrival is rewritten by the next segment
       }
       // TMEM buffer free for the segment after next
       asm volatile("tcgen05.fence::before_thread_sync;");
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty0 + 8 * buf) : "memory");
+      __syncwarp();
+      if (lane == 0) bar_arrive_pair<kPair>(tempty_l + 8 * buf);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
+  if constexpr (kPair) cluster_sync();  // the partner no longer reads this CTA's shared memory or signals it
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.fence::after_thread_sync;");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTmemCols2));
+    if constexpr (kPair)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTmemCols2));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTmemCols2));
   }
 }
 
@@ -1230,33 +1317,49 @@ int sm_count() {
   return n;
 }
 
+// Batches above 128 tokens run on two-SM pairs; PF_GEMM_PAIR=0 keeps them on
+// the one-SM stream-K kernel.
+bool gemm_pair_enabled() {
+  static int v = -1;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* e = getenv("PF_GEMM_PAIR");
+    v = (e && atoi(e) == 0) ? 0 : 1;
+  });
+  return v == 1;
+}
+
 // The persistent stream-K kernel: 2-D tensor maps over the packed rows and
 // the scale rows need 16-byte aligned bases and row strides, and the tile
-// count must fit the workspace's arrival counters.
-template <int FMT>
-cudaError_t launch_gemm_sk(GemmArgs a, const __half* x16, cudaStream_t s, bool* taken) {
+// count must fit the workspace's arrival counters.  kPair: two-CTA clusters,
+// as many as can be resident at once.
+template <int FMT, bool kPair>
+cudaError_t launch_gemm_sk_impl(GemmArgs a, const __half* x16, cudaStream_t s, bool* taken) {
   using B = TcBox<FMT>;
   constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
+  constexpr int kSt = kPair ? kStagesPair : kStages2;
+  constexpr int kXRows = kPair ? kBN2 / 2 : kBN2;
+  constexpr size_t kSB = kATile2 + (size_t)kXRows * kBK2 * 2;
+  constexpr int kRowsT = kPair ? 2 * kBM : kBM;
   *taken = false;
   const size_t row_bytes = (size_t)a.G * B::GB, srow = (size_t)a.G * B::SW;
   if (!gemm_tma_enabled() || row_bytes % 16 || srow % 16 || reinterpret_cast<uintptr_t>(a.codes) % 16 ||
       reinterpret_cast<uintptr_t>(a.scales) % 16 || (!kE8 && reinterpret_cast<uintptr_t>(a.mins) % 16) ||
       !a.counters || !a.partials)
     return cudaSuccess;
-  const int n_mb = (a.M + kBM - 1) / kBM, n_nb = (a.N + kBN2 - 1) / kBN2;
+  const int n_mb = (a.M + kRowsT - 1) / kRowsT, n_nb = (a.N + kBN2 - 1) / kBN2;
   const long long tiles = (long long)n_mb * n_nb;
   const int sms = sm_count();
-  if (sms <= 0 || tiles > (long long)kGemmCounterSlots) return cudaSuccess;
+  if (sms <= 0 || (kPair ? 2 : 1) * tiles > (long long)kGemmCounterSlots) return cudaSuccess;
   a.n_mb = n_mb;
   a.units = tiles * a.G;
-  const int P = a.units < sms ? (int)a.units : sms;
   auto fn = encode_fn_gemm();
   CUtensorMap xmap, cmap, smap, mmap;
   {
     // x' tiles of 64 columns x up to 256 tokens, 128B-swizzled
     cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.N};
     cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)tc2_box_rows(a.N)};
+    cuuint32_t box[2] = {64, (cuuint32_t)(kPair ? kXRows : tc2_box_rows(a.N))};
     cuuint32_t estr[2] = {1, 1};
     if (fn(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), dims, strides, box, estr,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1286,38 +1389,66 @@ cudaError_t launch_gemm_sk(GemmArgs a, const __half* x16, cudaStream_t s, bool* 
       return cudaSuccess;
   }
   if (kE8) mmap = smap;
-  const size_t smem = 1024 + (size_t)kStages2 * kStageBytes2 + 2 * (size_t)kBM * B::CB * B::GB +
-                      (kE8 ? 2 : 4) * (size_t)kBM * 16;
-  auto kern = gemm_sk_kernel<FMT>;
+  const size_t smem = 1024 + (size_t)kSt * kSB + 2 * (size_t)kBM * B::CB * B::GB + (kE8 ? 2 : 4) * (size_t)kBM * 16;
+  auto kern = gemm_sk_kernel<FMT, kPair>;
+  // programmatic dependent launch: barrier setup, TMEM allocation, the code and
+  // scale loads and the first decodes overlap the x' preparation's tail
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kSkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = kPair ? 2 : 1;
+  static int max_pairs[64] = {0};
+  int dev = 0;
   {
     static std::mutex mu;
     static bool done[64] = {false};
-    int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(mu);
     if (dev < 0 || dev >= 64 || !done[dev]) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
+      if (kPair) {
+        // pairs that fit on the device at once (clusters sit inside one GPC)
+        cfg.gridDim = dim3(2 * (sms / 2));
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) max_pairs[dev] = n;
+      }
       if (dev >= 0 && dev < 64) done[dev] = true;
     }
   }
+  int P = sms;
+  if (kPair) {
+    P = (dev >= 0 && dev < 64) ? max_pairs[dev] : 0;
+    if (P > sms / 2) P = sms / 2;
+    if (P < 1) return cudaSuccess;  // no two-CTA cluster fits: the one-SM kernel runs
+  }
+  if (a.units < P) P = (int)a.units;
   *taken = true;
-  // programmatic dependent launch: barrier setup, TMEM allocation, the code and
-  // scale loads and the first decodes overlap the x' preparation's tail
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(P);
-  cfg.blockDim = dim3(kSkThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.gridDim = dim3((kPair ? 2 : 1) * P);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, xmap, cmap, smap, mmap, (const GemmArgs)a);
   note_launch();
   return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <int FMT>
+cudaError_t launch_gemm_sk(const GemmArgs& a, const __half* x16, cudaStream_t s, bool* taken) {
+  if (a.N > kBN2 / 2 && gemm_pair_enabled()) {
+    const cudaError_t e = launch_gemm_sk_impl<FMT, true>(a, x16, s, taken);
+    if (*taken || e != cudaSuccess) return e;
+  }
+  return launch_gemm_sk_impl<FMT, false>(a, x16, s, taken);
 }
 
 template <int FMT>
