@@ -681,9 +681,9 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   constexpr uint32_t kCodeSlot = kBM * B::CB * B::GB;  // 128 rows x CB groups
   constexpr uint32_t kScaleSlot = kBM * 16;            // 128 rows x SB groups x SW bytes (16)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // A/B ring full / A full / free, then code full / free and scale full /
-  // free (two slots each), then accumulator full and TMEM-buffer empty (two each)
-  __shared__ uint64_t bars[3 * kSt + 8 + 4];
+  // A/B ring full / free, then code full / free and scale full / free (two
+  // slots each), then accumulator full and TMEM-buffer empty (two each)
+  __shared__ uint64_t bars[2 * kSt + 8 + 4];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
   __shared__ unsigned arrival;
@@ -694,20 +694,22 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   unsigned char* const codes = base + kSt * kSB;  // [2][kCodeSlot]
   unsigned char* const scl = codes + 2 * kCodeSlot;             // [2][kScaleSlot] (+ [2][kScaleSlot] mins)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t bfull0 = su32(&bars[0]), afull0 = su32(&bars[kSt]), free0 = su32(&bars[2 * kSt]);
-  const uint32_t cfull0 = su32(&bars[3 * kSt]), cfree0 = cfull0 + 16;
+  // full0: one barrier per ring slot for the decoded A stage and the x' bytes
+  const uint32_t full0 = su32(&bars[0]), free0 = su32(&bars[kSt]);
+  const uint32_t cfull0 = su32(&bars[2 * kSt]), cfree0 = cfull0 + 16;
   const uint32_t sfull0 = cfull0 + 32, sfree0 = cfull0 + 48;
   const uint32_t accf0 = cfull0 + 64, tempty0 = cfull0 + 80;
   const uint32_t rank = kPair ? cta_rank() : 0u;
   // barriers of the pair's first CTA as cluster addresses (own ones without kPair)
-  const uint32_t afull_l = kPair ? map_rank0(afull0) : afull0, bfull_l = kPair ? map_rank0(bfull0) : bfull0;
+  const uint32_t full_l = kPair ? map_rank0(full0) : full0;
   const uint32_t tempty_l = kPair ? map_rank0(tempty0) : tempty0;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     for (int s = 0; s < kSt; ++s) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bfull0 + 8 * s));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(afull0 + 8 * s), "r"(kPair ? kDqWarps : kDqWarps / 2));
+      // the decoding warps (both CTAs' with kPair) and the x' producer's expect-tx
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full0 + 8 * s),
+                   "r"((kPair ? kDqWarps : kDqWarps / 2) + 1));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(free0 + 8 * s));
     }
     for (int s = 0; s < 2; ++s) {
@@ -789,13 +791,13 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             }
             const uint32_t dst = su32(base + slot * kSB + kATile2);
             if (rank == 0)
-              asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bfull0 + 8 * slot),
+              asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full0 + 8 * slot),
                            "r"(xbox_bytes)
                            : "memory");
             if constexpr (kPair)
-              tma2d_pair(dst, &xmap, (2 * s + h) * kBK2, n0, bfull_l + 8 * slot);
+              tma2d_pair(dst, &xmap, (2 * s + h) * kBK2, n0, full_l + 8 * slot);
             else
-              tma2d_plain(dst, &xmap, (2 * s + h) * kBK2, n0, bfull0 + 8 * slot);
+              tma2d_plain(dst, &xmap, (2 * s + h) * kBK2, n0, full0 + 8 * slot);
           }
         }
       }
@@ -870,7 +872,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         for (int s = g0; s < g1 && ok; ++s) {
           for (int h = 0; h < 2; ++h, ++q) {
             const uint32_t slot = q % kSt, par = (q / kSt) & 1;
-            if (!bar_wait(afull0 + 8 * slot, par, &abort_flag) || !bar_wait(bfull0 + 8 * slot, par, &abort_flag)) {
+            if (!bar_wait(full0 + 8 * slot, par, &abort_flag)) {
               ok = false;
               break;
             }
@@ -920,19 +922,21 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       const int t = (int)(us / G), g0 = (int)(us - (long long)t * G), g1 = g0 + (int)(ul - us);
       uint32_t cs = 0, ss = 0, cpar = 0, spar = 0;
       for (int s = g0; s < g1; ++s, ++gs) {
+        // a code / scale box stays put until this thread's last group in it:
+        // wait for it once, on entering it
         if (s == g0 || s % B::CB == 0) {
           cs = kc & 1;
           cpar = (kc >> 1) & 1;
           ++kc;
+          if (live && !bar_wait(cfull0 + 8 * cs, cpar, &abort_flag)) fail();
         }
         if (s == g0 || s % B::SB == 0) {
           ss = ks & 1;
           spar = (ks >> 1) & 1;
           ++ks;
+          if (live && !bar_wait(sfull0 + 8 * ss, spar, &abort_flag)) fail();
         }
         const uint32_t q = 2 * gs + grp, slot = q % kSt;
-        if (live && !bar_wait(cfull0 + 8 * cs, cpar, &abort_flag)) fail();
-        if (live && !bar_wait(sfull0 + 8 * ss, spar, &abort_flag)) fail();
         // this row's scale (and zero point) of group s
         uint32_t sc = 0u;
         if (live) {
@@ -962,7 +966,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         // every lane's A-tile stores visible to the tensor core, then one arrival per warp
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) bar_arrive_pair<kPair>(afull_l + 8 * slot);
+        if (lane == 0) bar_arrive_pair<kPair>(full_l + 8 * slot);
       }
     }
   } else {
