@@ -110,3 +110,40 @@ def test_split_tiles_deterministic():
     meta = {"hadamard_rotation": True, "hadamard_block_size": 128}
     ref = oracle.linear("int2_g128", pay, M, K, meta, x[:64].float().cpu().numpy())
     assert_rel(y0[:64].cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("M,N", [(200, 129), (200, 257), (712, 300), (130, 600)])
+def test_two_sm_pair_edges(M, N):
+    """Batches above 128 tokens run on two-SM pairs (256-row tiles, each CTA
+    holding 128 rows and half of the 256-token x' tile): a pair tile only
+    partly inside M (the second CTA's rows partly or wholly past M), a token
+    tile whose second half is nearly empty (N = 129) or a second token tile
+    of one token (N = 257).  y matches the oracle and repeats bit for bit."""
+    from polarflash_b200 import qlinear
+
+    K = 2048
+    qw, pay, _ = _g128_qweight(_w(M, K, 90 + M + N), 3, hb=128)
+    x = _x(N, K, 91 + N).cuda()
+    y = qlinear(qw, x)
+    assert torch.equal(qlinear(qw, x), y)
+    meta = {"hadamard_rotation": True, "hadamard_block_size": 128}
+    assert_rel(y.cpu().numpy(), oracle.linear("int3_g128", pay, M, K, meta, x.float().cpu().numpy()))
+
+
+def test_two_sm_pair_e8():
+    """E8 RVQ2 on two-SM pairs: 300 rows x 2048 columns at 200 tokens."""
+    from polarflash_b200 import qlinear
+    from polarflash_b200.hadamard import column_signs, effective_block
+    from polarflash_b200.qweight import QWeight
+    from polarflash_b200.quantizer import rwht_cpu
+
+    M, K, N = 300, 2048, 200
+    W = _w(M, K, 93, std=0.015)
+    idx, sc = oracle.e8_encode(rwht_cpu(W, 128).numpy())
+    dev = torch.device("cuda")
+    qw = QWeight(7, M, K, torch.from_numpy(idx.reshape(-1).copy()).to(dev), torch.from_numpy(sc.copy()).to(dev),
+                 None, effective_block(128, K), column_signs(K, 128, dev))
+    x = _x(N, K, 94)
+    y = qlinear(qw, x.cuda()).cpu().numpy()
+    meta = {"hadamard_rotation": True, "hadamard_block_size": 128}
+    assert_rel(y, oracle.linear("e8_rvq2_g128", {"idx": idx, "scales": sc}, M, K, meta, x.float().numpy()))
