@@ -877,11 +877,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;");
-            const uint32_t sa = su32(base + slot * kSB), sb = sa + kATile2;
+            // descriptors of the slot's A and B tiles; each 16-column step
+            // adds 32 bytes (2 in the descriptor's 16-byte address field)
+            const uint32_t sa = su32(base + slot * kSB);
+            const uint64_t da0 = kmajor_desc(sa), db0 = kmajor_desc(sa + kATile2);
+            const uint32_t acc0 = (s > g0 || h > 0) ? 1u : 0u;
 #pragma unroll
             for (int k = 0; k < kBK2 / 16; ++k) {
-              const uint64_t da = kmajor_desc(sa + k * 32), db = kmajor_desc(sb + k * 32);
-              const uint32_t acc = (s > g0 || h > 0 || k > 0) ? 1u : 0u;
+              const uint64_t da = da0 + 2u * k, db = db0 + 2u * k;
+              const uint32_t acc = k > 0 ? 1u : acc0;
               if constexpr (kPair)
                 asm volatile(
                     "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(
