@@ -445,7 +445,7 @@ constexpr uint32_t kATile2 = kBM * kBK2 * 2;  // one 64-column swizzle atom
 
 // Token rows of the x' box: 256, or the batch rounded up to 16 when it is
 // smaller (the MMA reads no row past that).
-__host__ __device__ constexpr int tc2_box_rows(int N) { return N >= kBN2 ? kBN2 : ((N + 15) & ~15); }
+__host__ __device__ constexpr int sk_box_rows(int N) { return N >= kBN2 ? kBN2 : ((N + 15) & ~15); }
 
 __device__ __forceinline__ void tma2d_plain(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
@@ -459,7 +459,7 @@ __device__ __forceinline__ void tma2d_plain(uint32_t dst, const CUtensorMap* map
 // 16-byte chunks 8 H .. 8 H + 7) from its packed words at cp into the
 // half-stage A tile at `at` (one 64-column swizzle atom).
 template <int FMT, int H>
-__device__ __forceinline__ void tc2_decode(const unsigned char* cp, uint32_t sc, int r, int lane, unsigned char* at,
+__device__ __forceinline__ void sk_decode(const unsigned char* cp, uint32_t sc, int r, int lane, unsigned char* at,
                                            const uint4* roots16) {
   using B = TcBox<FMT>;
   uint32_t cw[16];
@@ -768,7 +768,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   const long long u_begin = sk_begin(U, P, sk_id), u_end = sk_begin(U, P, sk_id + 1);
   const int n_items = sk_items(u_begin, u_end, G);
   // x' bytes landing on one stage's full barrier (kPair: both CTAs' halves)
-  const uint32_t xbox_bytes = kPair ? 2u * kXRows * (kBK2 * 2) : (uint32_t)tc2_box_rows(a.N) * (kBK2 * 2);
+  const uint32_t xbox_bytes = kPair ? 2u * kXRows * (kBK2 * 2) : (uint32_t)sk_box_rows(a.N) * (kBK2 * 2);
 
   if (warp == 0) {
     // ------------------------------------------------ producer: x' tiles
@@ -958,9 +958,9 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         if (live) {
           unsigned char* at = base + slot * kSB;
           if (grp == 0)
-            tc2_decode<FMT, 0>(cp, sc, r, lane, at, roots16);
+            sk_decode<FMT, 0>(cp, sc, r, lane, at, roots16);
           else
-            tc2_decode<FMT, 1>(cp, sc, r, lane, at, roots16);
+            sk_decode<FMT, 1>(cp, sc, r, lane, at, roots16);
         }
         // hand the code / scale boxes back after this thread's last group in them
         if (s + 1 == g1 || (s + 1) % B::CB == 0)
@@ -1367,7 +1367,7 @@ cudaError_t launch_gemm_sk_impl(GemmArgs a, const __half* x16, cudaStream_t s, b
     // x' tiles of 64 columns x up to 256 tokens, 128B-swizzled
     cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.N};
     cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)(kPair ? kXRows : tc2_box_rows(a.N))};
+    cuuint32_t box[2] = {64, (cuuint32_t)(kPair ? kXRows : sk_box_rows(a.N))};
     cuuint32_t estr[2] = {1, 1};
     if (fn(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), dims, strides, box, estr,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
