@@ -134,8 +134,52 @@ def decode_rates(copies, xs, outs, ws, stream, dev, layers, tokens=20):
     res["polar_recursive_1.75"] = {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
                                    "GB_s": round(nb / ms / 1e6, 1)}
     del graphs, pc, base
+    res.update(decode_full_step(copies, stream, dev, layers, tokens=tokens))
     res.update(decode_rates_70b_e8(stream, dev, tokens))
     return res
+
+
+def decode_full_step(copies, stream, dev, layers=32, ctx=512, tokens=20):
+    """Tokens/s of a whole batch-1 decode step of the Llama-3-8B shape
+    (polarflash_b200.decode.PFlashDecoder, one CUDA graph per token): the
+    INT3 g128 linears of `layers` layers (the bench's weights), RMSNorms,
+    RoPE, the fp32 KV cache at `ctx` previous tokens, attention (torch SDPA)
+    and a dense fp16 embedding and lm_head (128256 x 4096, 1.05 GB)."""
+    from polarflash_b200.decode import DecoderLayer, PFlashDecoder
+
+    H, V = 4096, 128256
+    cfg = dict(hidden_size=H, num_attention_heads=32, num_key_value_heads=8, intermediate_size=14336, vocab_size=V,
+               rope_theta=500000.0, rms_norm_eps=1e-5)
+    g = torch.Generator(device=dev).manual_seed(5)
+    ones = torch.ones(H, device=dev)
+    lys = []
+    for li in range(layers):
+        cp = copies[li % len(copies)]
+        w = {n: cp[("int3_g128", n)] for n, _, _ in LINEARS}
+        lys.append(DecoderLayer(w["q"], w["k"], w["v"], w["o"], w["gate"], w["up"], w["down"], ones, ones))
+    embed = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
+    head = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
+    dec = PFlashDecoder(cfg, lys, embed, ones, head, max_seq=ctx + 1)
+    with torch.cuda.stream(stream):
+        dec.forward(torch.tensor([1], device=dev))  # one-time set-up of every launch path, outside the capture
+        dec.length = ctx  # attend over `ctx` cached positions (contents are the cache's zeros)
+        dec.capture(stream)
+        for _ in range(2):
+            dec._pos.fill_(ctx)
+            dec._graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(tokens):
+            dec._graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / tokens
+    nb = sum(alg_bytes(copies[0][("int3_g128", n)], 1) for n, _, _ in LINEARS) * layers + V * H * 2 + \
+        layers * 2 * (ctx + 1) * 8 * 128 * 4
+    del dec, embed, head
+    return {"llama3_8b_int3_full_step_ctx512": {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
+                                                "GB_s": round(nb / ms / 1e6, 1)}}
 
 
 LINEARS_70B = [("q", 8192, 8192), ("k", 1024, 8192), ("v", 1024, 8192), ("o", 8192, 8192),
@@ -488,7 +532,9 @@ def main():
         decode["what"] = ("linears of one decode step: Llama-3-8B shape (32 layers x q|k|v, o, gate|up, down) at "
                           "batch 1 for INT3 / INT2 / polar 1.75, Llama-3-70B shape (80 layers, E8 RVQ2) at batch 1 "
                           "and 32; one resident weight copy per layer, CUDA-graph replays; attention, norms and "
-                          "lm_head not included")
+                          "lm_head not included, except llama3_8b_int3_full_step_ctx512: the whole batch-1 step "
+                          "through polarflash_b200.decode (RMSNorms, RoPE, fp32 KV cache at 512 tokens, SDPA "
+                          "attention, fp16 embedding and lm_head), one CUDA graph per token")
 
     # max over ranks
     t = torch.tensor([ms, ms_run, ms_e2e], device=dev, dtype=torch.float64)
