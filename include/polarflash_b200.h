@@ -188,6 +188,40 @@ PF_API int pf_native_gemm_int4(const float* X, const uint8_t* packed, const floa
                         int M, int K, float* Y, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Decode-step helpers around the packed linears (batch 1, fp32 device
+ * buffers; `pos` is a device int64 holding the new token's position, so a
+ * whole step can be captured once as a CUDA graph).
+ *
+ * pf_add_rmsnorm: for each of `rows` rows of h [rows][H]: h += delta (if
+ * delta is non-null, in place), out = h / sqrt(mean(h^2) + eps) * w.
+ * Replaces the residual add of PFlashTransformerLayer.forward and
+ * RMSNorm.forward (polarflash_core/model_integration.py:183-192, 34-37). */
+PF_API int pf_add_rmsnorm(float* h, const float* delta, const float* w, float* out, int rows, int H, float eps,
+                          void* stream);
+/* pf_rope_kv: q [n_heads][head_dim] rotated in place, k [n_kv_heads][head_dim]
+ * rotated into k_cache[*pos] and v copied into v_cache[*pos] (caches
+ * [max_seq][n_kv_heads][head_dim]); angle = *pos * inv_freq[i] for the pair
+ * (i, i + head_dim/2).  Replaces apply_rotary_pos_emb and the cache update of
+ * PFlashAttentionBlock.forward (model_integration.py:40-60, 109-122). */
+PF_API int pf_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                      const long long* pos, const float* inv_freq, int n_heads, int n_kv_heads, int head_dim,
+                      int max_seq, void* stream);
+/* pf_decode_attention: out [n_heads][head_dim] = softmax(q k^T * scale) v over
+ * positions 0..*pos of the caches, query head h reading KV head
+ * h / (n_heads / n_kv_heads); head_dim <= 128, at most 8 query heads per KV
+ * head, max_seq <= 32768.  The positions are split into chunks of 64 whose
+ * partial results go to `workspace` (device, at least
+ * pf_decode_attention_workspace_size bytes) and are merged by a second
+ * launch.  Replaces the GQA attention of PFlashAttentionBlock.forward
+ * (model_integration.py:126-145) for one new token. */
+PF_API size_t pf_decode_attention_workspace_size(int n_heads, int head_dim, int max_seq);
+PF_API int pf_decode_attention(const float* q, const float* k_cache, const float* v_cache, const long long* pos,
+                               float* out, int n_heads, int n_kv_heads, int head_dim, int max_seq, float scale,
+                               void* workspace, size_t workspace_bytes, void* stream);
+/* pf_silu_mul: out = silu(g) * u elementwise.  Replaces the gate of
+ * PFlashMLPBlock.forward (model_integration.py:160-163). */
+PF_API int pf_silu_mul(const float* g, const float* u, float* out, long long n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,293 @@
+// Decode-step kernels around the packed linears (batch 1, fp32): the
+// residual add + RMSNorm, RoPE with the KV-cache write, a GQA attention over
+// the cache and the SwiGLU gate.  They restate the reference decode forward
+// (polarflash_core/model_integration.py: RMSNorm :27-37, apply_rotary_pos_emb
+// :40-60, PFlashAttentionBlock.forward :97-147, PFlashMLPBlock.forward
+// :160-163) for one new token, reading the token's position from device
+// memory so that a whole step can be captured once as a CUDA graph.
+#include <math.h>
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace pfb {
+namespace {
+
+constexpr int kNormThreads = 256;
+constexpr int kAttnThreads = 256;
+constexpr int kDecodeMaxSeq = 32768;  // positions one attention call may cover
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();  // red is reused by consecutive reductions
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+  return s;
+}
+
+// One row per block: h += delta (when given), out = h / sqrt(mean(h^2) + eps) * w.
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ delta,
+                                                                   const float* __restrict__ w, float* __restrict__ out,
+                                                                   int H, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  float* hr = h + (size_t)blockIdx.x * H;
+  const float* dr = delta ? delta + (size_t)blockIdx.x * H : nullptr;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float v = hr[i];
+    if (dr) {
+      v += dr[i];
+      hr[i] = v;
+    }
+    ss += v * v;
+  }
+  const float r = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) out[(size_t)blockIdx.x * H + i] = hr[i] * r * w[i];
+}
+
+// Blocks 0..nh-1 rotate q's heads in place; blocks nh..nh+nkv-1 rotate k's
+// heads into the key cache at position *pos and copy v's heads into the value
+// cache there.  Thread i handles the pair (i, i + hd/2): angle pos * inv_freq[i].
+__global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                               float* __restrict__ kc, float* __restrict__ vc, const long long* __restrict__ pos,
+                               const float* __restrict__ inv_freq, int nh, int nkv, int hd, int max_seq) {
+  const long long p = *pos;
+  if (p < 0 || p >= max_seq) return;  // rejected on the host when it can see it; never written out of range
+  const int half = hd >> 1, i = threadIdx.x;
+  if (i >= half) return;
+  const float f = (float)p * inv_freq[i];
+  const float c = cosf(f), s = sinf(f);
+  const int head = blockIdx.x;
+  if (head < nh) {
+    float* x = q + (size_t)head * hd;
+    const float x1 = x[i], x2 = x[i + half];
+    x[i] = x1 * c - x2 * s;
+    x[i + half] = x1 * s + x2 * c;
+  } else {
+    const int kh = head - nh;
+    const float* x = k + (size_t)kh * hd;
+    const float x1 = x[i], x2 = x[i + half];
+    float* kd = kc + ((size_t)p * nkv + kh) * hd;
+    kd[i] = x1 * c - x2 * s;
+    kd[i + half] = x1 * s + x2 * c;
+    float* vd = vc + ((size_t)p * nkv + kh) * hd;
+    const float* vs = v + (size_t)kh * hd;
+    vd[i] = vs[i];
+    vd[i + half] = vs[i + half];
+  }
+}
+
+// Attention of one new token over positions 0..*pos of the cache, split over
+// chunks of kAttnChunk positions (flash decoding).  attn_chunk_kernel: one
+// block per (KV head, chunk) serves the KV head's G query heads: scores with
+// one warp per position (eight positions per warp in flight), the chunk's
+// softmax statistics, and the value sum with threads over head dimensions;
+// it stores per query head (max, sum of exponentials, unnormalised output).
+// Chunks past *pos store an empty entry.  attn_combine_kernel merges a head's
+// chunks: out = sum_c e^(m_c - m) o_c / sum_c e^(m_c - m) l_c.
+constexpr int kAttnChunk = 64;
+constexpr int kAttnG = 8;  // query heads per KV head handled by one block
+
+__global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* __restrict__ q,
+                                                                  const float* __restrict__ kc,
+                                                                  const float* __restrict__ vc,
+                                                                  const long long* __restrict__ pos,
+                                                                  float* __restrict__ part, int nh, int nkv, int hd,
+                                                                  int max_seq, int nchunk, float scale) {
+  __shared__ float qs[kAttnG][128];
+  __shared__ float sc[kAttnG][kAttnChunk];
+  __shared__ float mx[kAttnG], sm[kAttnG];
+  __shared__ float po[2][kAttnG][128];
+  const int kvh = blockIdx.x, chunk = blockIdx.y, G = nh / nkv;
+  const long long p = *pos;
+  const int T = (p < 0) ? 0 : (p >= max_seq ? max_seq : (int)p + 1);
+  const int t0 = chunk * kAttnChunk, t1 = min(T, t0 + kAttnChunk), n = t1 - t0;
+  const int rec = hd + 2;  // per (head, chunk): m, l, o[hd]
+  if (n <= 0) {
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+      float* r = part + ((size_t)(kvh * G + g) * nchunk + chunk) * rec;
+      r[0] = -INFINITY;
+      r[1] = 0.f;
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i / hd][i % hd] = q[(size_t)(kvh * G + i / hd) * hd + i % hd];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  // scores: warp w takes positions t0 + w, t0 + w + nw, ... (eight at a time)
+  for (int j0 = warp; j0 < n; j0 += 8 * nw) {
+    float kv[8][4];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u * nw;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = lane + 32 * e;
+        kv[u][e] = (j < n && d < hd) ? kc[((size_t)(t0 + j) * nkv + kvh) * hd + d] : 0.f;
+      }
+    }
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = lane + 32 * e;
+          if (d < hd) dot += qs[g][d] * kv[u][e];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const int j = j0 + u * nw;
+        if (lane == 0 && j < n) sc[g][j] = dot * scale;
+      }
+    }
+  }
+  __syncthreads();
+  // per query head: chunk max and exponentials (warp g)
+  if (warp < G) {
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[warp][j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const float e = expf(sc[warp][j] - m);
+      sc[warp][j] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) {
+      mx[warp] = m;
+      sm[warp] = l;
+    }
+  }
+  __syncthreads();
+  // values: thread (half, d) sums positions of parity `half`, for every query head
+  const int d = threadIdx.x % hd, half = threadIdx.x / hd;
+  if (half < 2) {
+    float acc[kAttnG];
+#pragma unroll
+    for (int g = 0; g < kAttnG; ++g) acc[g] = 0.f;
+    for (int j = half; j < n; j += 2) {
+      const float val = vc[((size_t)(t0 + j) * nkv + kvh) * hd + d];
+#pragma unroll
+      for (int g = 0; g < kAttnG; ++g)
+        if (g < G) acc[g] += sc[g][j] * val;
+    }
+#pragma unroll
+    for (int g = 0; g < kAttnG; ++g)
+      if (g < G) po[half][g][d] = acc[g];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+    const int g = i / hd, e = i % hd;
+    float* r = part + ((size_t)(kvh * G + g) * nchunk + chunk) * rec;
+    r[2 + e] = po[0][g][e] + po[1][g][e];
+    if (e == 0) {
+      r[0] = mx[g];
+      r[1] = sm[g];
+    }
+  }
+}
+
+__global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out, int hd, int nchunk) {
+  const int head = blockIdx.x, rec = hd + 2;
+  const float* base = part + (size_t)head * nchunk * rec;
+  float m = -INFINITY;
+  for (int c = 0; c < nchunk; ++c) m = fmaxf(m, base[(size_t)c * rec]);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float o = 0.f, l = 0.f;
+    for (int c = 0; c < nchunk; ++c) {
+      const float* r = base + (size_t)c * rec;
+      if (r[1] > 0.f) {
+        const float w = expf(r[0] - m);
+        o += w * r[2 + d];
+        l += w * r[1];
+      }
+    }
+    out[(size_t)head * hd + d] = l > 0.f ? o / l : 0.f;
+  }
+}
+
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
+                                long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float x = g[i];
+    out[i] = x / (1.f + expf(-x)) * u[i];
+  }
+}
+
+int status_of(cudaError_t e) { return e == cudaSuccess ? PF_OK : PF_ERR_CUDA; }
+bool al4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+}  // namespace
+}  // namespace pfb
+
+using namespace pfb;
+
+int pf_add_rmsnorm(float* h, const float* delta, const float* w, float* out, int rows, int H, float eps, void* stream) {
+  if (!h || !w || !out || rows < 0 || H <= 0 || !(eps >= 0.f)) return PF_ERR_INVALID_ARGUMENT;
+  if (!al4(h) || !al4(w) || !al4(out) || (delta && !al4(delta))) return PF_ERR_ALIGNMENT;
+  if (rows == 0) return PF_OK;
+  add_rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(h, delta, w, out, H, eps);
+  note_launch();
+  return status_of(cudaGetLastError());
+}
+
+int pf_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* v_cache, const long long* pos,
+               const float* inv_freq, int n_heads, int n_kv_heads, int head_dim, int max_seq, void* stream) {
+  if (!q || !k || !v || !k_cache || !v_cache || !pos || !inv_freq) return PF_ERR_INVALID_ARGUMENT;
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || (head_dim & 1) || head_dim > 2048 || max_seq <= 0)
+    return PF_ERR_SHAPE;
+  if (!al4(q) || !al4(k) || !al4(v) || !al4(k_cache) || !al4(v_cache) || !al4(inv_freq) ||
+      (reinterpret_cast<uintptr_t>(pos) & 7u))
+    return PF_ERR_ALIGNMENT;
+  rope_kv_kernel<<<n_heads + n_kv_heads, head_dim / 2, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, k, v, k_cache, v_cache, pos, inv_freq, n_heads, n_kv_heads, head_dim, max_seq);
+  note_launch();
+  return status_of(cudaGetLastError());
+}
+
+size_t pf_decode_attention_workspace_size(int n_heads, int head_dim, int max_seq) {
+  if (n_heads <= 0 || head_dim <= 0 || max_seq <= 0) return 0;
+  const size_t nchunk = ((size_t)max_seq + kAttnChunk - 1) / kAttnChunk;
+  return (size_t)n_heads * nchunk * (head_dim + 2) * sizeof(float);
+}
+
+int pf_decode_attention(const float* q, const float* k_cache, const float* v_cache, const long long* pos, float* out,
+                        int n_heads, int n_kv_heads, int head_dim, int max_seq, float scale, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !pos || !out || !workspace) return PF_ERR_INVALID_ARGUMENT;
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > kAttnG || head_dim <= 0 ||
+      head_dim > 128 || max_seq <= 0 || max_seq > kDecodeMaxSeq)
+    return PF_ERR_SHAPE;
+  if (!al4(q) || !al4(k_cache) || !al4(v_cache) || !al4(out) || !al4(workspace) ||
+      (reinterpret_cast<uintptr_t>(pos) & 7u))
+    return PF_ERR_ALIGNMENT;
+  if (workspace_bytes < pf_decode_attention_workspace_size(n_heads, head_dim, max_seq)) return PF_ERR_WORKSPACE;
+  const int nchunk = (max_seq + kAttnChunk - 1) / kAttnChunk;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  attn_chunk_kernel<<<dim3(n_kv_heads, nchunk), kAttnThreads, 0, s>>>(q, k_cache, v_cache, pos, part, n_heads,
+                                                                      n_kv_heads, head_dim, max_seq, nchunk, scale);
+  note_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return PF_ERR_CUDA;
+  attn_combine_kernel<<<n_heads, 128, 0, s>>>(part, out, head_dim, nchunk);
+  note_launch();
+  return status_of(cudaGetLastError());
+}
+
+int pf_silu_mul(const float* g, const float* u, float* out, long long n, void* stream) {
+  if (!g || !u || !out || n < 0) return PF_ERR_INVALID_ARGUMENT;
+  if (!al4(g) || !al4(u) || !al4(out)) return PF_ERR_ALIGNMENT;
+  if (n == 0) return PF_OK;
+  const long long blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
+  silu_mul_kernel<<<(int)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, out, n);
+  note_launch();
+  return status_of(cudaGetLastError());
+}

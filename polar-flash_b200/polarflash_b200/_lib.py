@@ -42,6 +42,7 @@ EXPORTS = (
     "pf_qlinear_workspace_size", "pf_qlinear", "pf_qlinear_group_workspace_size", "pf_qlinear_group",
     "pf_dequant", "pf_unpack_codes", "pf_rwht",
     "pf_native_gemv_int4", "pf_native_gemv_int2", "pf_native_gemm_int4", "pf_qlinear_noalloc",
+    "pf_add_rmsnorm", "pf_rope_kv", "pf_decode_attention_workspace_size", "pf_decode_attention", "pf_silu_mul",
 )
 
 
@@ -113,6 +114,17 @@ def load():
         fn.argtypes = [P, P, P, I, I, P, P, SZ, P]
     L.pf_native_gemm_int4.restype = I
     L.pf_native_gemm_int4.argtypes = [P, P, P, I, I, I, P, P, SZ, P]
+    F = ctypes.c_float
+    L.pf_add_rmsnorm.restype = I
+    L.pf_add_rmsnorm.argtypes = [P, P, P, P, I, I, F, P]
+    L.pf_rope_kv.restype = I
+    L.pf_rope_kv.argtypes = [P, P, P, P, P, P, P, I, I, I, I, P]
+    L.pf_decode_attention.restype = I
+    L.pf_decode_attention.argtypes = [P, P, P, P, P, I, I, I, I, F, P, SZ, P]
+    L.pf_decode_attention_workspace_size.restype = SZ
+    L.pf_decode_attention_workspace_size.argtypes = [I, I, I]
+    L.pf_silu_mul.restype = I
+    L.pf_silu_mul.argtypes = [P, P, P, ctypes.c_longlong, P]
     _lib = L
     return L
 

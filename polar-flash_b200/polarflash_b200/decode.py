@@ -14,16 +14,28 @@ RoPE, cache write, attention over the cache, linears, final norm, lm_head)
 can be captured once as a CUDA graph and replayed per token with the token
 id and position read from device tensors.
 
-Attention, norms, RoPE, the embedding lookup and the dense lm_head are torch
-ops (``scaled_dot_product_attention`` for the attention); the packed linears
-are the library's kernels.  There is no CPU path.
+The captured step (fp32 cache) runs the library's decode kernels around the
+packed linears: residual add + RMSNorm (pf_add_rmsnorm), RoPE with the cache
+write (pf_rope_kv), GQA attention over the cache (pf_decode_attention) and
+the SwiGLU gate (pf_silu_mul): about a dozen launches per layer.  The eager
+forward (prompts, any batch of new tokens) uses torch ops for everything but
+the linears (``scaled_dot_product_attention`` for the attention); the
+embedding lookup and the dense lm_head are torch ops in both.  There is no
+CPU path.
 """
+import ctypes
+import math
 from typing import Dict, List, Optional
 
 import torch
 import torch.nn.functional as F
 
+from . import _lib
 from .qweight import QWeight, group_workspace_bytes, qlinear, qlinear_multi
+
+
+def _p(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
 class DecoderLayer:
@@ -82,6 +94,8 @@ class PFlashDecoder:
             need = max(need, group_workspace_bytes([ly.q, ly.k, ly.v], 1), group_workspace_bytes([ly.gate, ly.up], 1),
                        ly.o.workspace_bytes(1), ly.down.workspace_bytes(1))
         self.ws1 = torch.zeros(need, dtype=torch.uint8, device=dev)
+        self.attn_ws = torch.empty(int(_lib.load().pf_decode_attention_workspace_size(self.nh, self.hd, self.max_seq)),
+                                   dtype=torch.uint8, device=dev)
         self._graph = None
 
     # ---- blocks (reference semantics) -------------------------------------
@@ -154,6 +168,39 @@ class PFlashDecoder:
 
     # ---- batch-1 decode step as one CUDA graph -----------------------------
     def _step_body(self):
+        if self.k_cache.dtype != torch.float32:
+            return self._step_body_torch()
+        L = _lib.load()
+        st = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        H, nh, nkv, hd, ms = self.hidden, self.nh, self.nkv, self.hd, self.max_seq
+        scale = 1.0 / math.sqrt(hd)
+        h = self.embed.index_select(0, self._tok).float()  # [1, H]: the residual stream, updated in place
+        n = torch.empty_like(h)
+        delta = None
+        for li, ly in enumerate(self.layers):
+            _lib.check(L.pf_add_rmsnorm(_p(h), _p(delta), _p(ly.input_norm), _p(n), 1, H, self.eps, st),
+                       "pf_add_rmsnorm")
+            q, k, v = qlinear_multi([ly.q, ly.k, ly.v], n, ly.qkv_bias, workspace=self.ws1)
+            _lib.check(L.pf_rope_kv(_p(q), _p(k), _p(v), _p(self.k_cache[li]), _p(self.v_cache[li]), _p(self._pos),
+                                    _p(self.inv_freq), nh, nkv, hd, ms, st), "pf_rope_kv")
+            attn = torch.empty(1, H, dtype=torch.float32, device=self.device)
+            _lib.check(L.pf_decode_attention(_p(q), _p(self.k_cache[li]), _p(self.v_cache[li]), _p(self._pos),
+                                             _p(attn), nh, nkv, hd, ms, scale, _p(self.attn_ws),
+                                             self.attn_ws.numel(), st), "pf_decode_attention")
+            o = qlinear(ly.o, attn, workspace=self.ws1)
+            n2 = torch.empty_like(h)
+            _lib.check(L.pf_add_rmsnorm(_p(h), _p(o), _p(ly.post_norm), _p(n2), 1, H, self.eps, st),
+                       "pf_add_rmsnorm")
+            g, u = qlinear_multi([ly.gate, ly.up], n2, workspace=self.ws1)
+            a = torch.empty_like(g)
+            _lib.check(L.pf_silu_mul(_p(g), _p(u), _p(a), g.numel(), st), "pf_silu_mul")
+            delta = qlinear(ly.down, a, workspace=self.ws1)
+        hn = torch.empty_like(h)
+        _lib.check(L.pf_add_rmsnorm(_p(h), _p(delta), _p(self.final_norm), _p(hn), 1, H, self.eps, st),
+                   "pf_add_rmsnorm")
+        self._logits.copy_(self._head(hn))
+
+    def _step_body_torch(self):
         pos_f = self._pos.float()
         slots = torch.arange(self.max_seq, device=self.device)
         mask = (slots <= self._pos)[None, None, None, :]  # [1, 1, 1, max_seq]
