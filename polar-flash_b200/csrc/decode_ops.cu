@@ -17,6 +17,13 @@ constexpr int kNormThreads = 256;
 constexpr int kAttnThreads = 256;
 constexpr int kDecodeMaxSeq = 32768;  // positions one attention call may cover
 
+// Programmatic dependent launch: every kernel here lets the next launch start
+// and waits for the previous grid to complete before touching its data.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -33,6 +40,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
                                                                    const float* __restrict__ w, float* __restrict__ out,
                                                                    int H, float eps) {
   __shared__ float red[kNormThreads / 32];
+  pdl_enter();
   float* hr = h + (size_t)blockIdx.x * H;
   const float* dr = delta ? delta + (size_t)blockIdx.x * H : nullptr;
   float ss = 0.f;
@@ -54,6 +62,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                                float* __restrict__ kc, float* __restrict__ vc, const long long* __restrict__ pos,
                                const float* __restrict__ inv_freq, int nh, int nkv, int hd, int max_seq) {
+  pdl_enter();
   const long long p = *pos;
   if (p < 0 || p >= max_seq) return;  // rejected on the host when it can see it; never written out of range
   const int half = hd >> 1, i = threadIdx.x;
@@ -102,6 +111,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
   __shared__ float mx[kAttnG], sm[kAttnG];
   __shared__ float po[2][kAttnG][128];
   const int kvh = blockIdx.x, chunk = blockIdx.y, G = nh / nkv;
+  pdl_enter();
   const long long p = *pos;
   const int T = (p < 0) ? 0 : (p >= max_seq ? max_seq : (int)p + 1);
   const int t0 = chunk * kAttnChunk, t1 = min(T, t0 + kAttnChunk), n = t1 - t0;
@@ -196,6 +206,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
 
 __global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out, int hd, int nchunk) {
   const int head = blockIdx.x, rec = hd + 2;
+  pdl_enter();
   const float* base = part + (size_t)head * nchunk * rec;
   float m = -INFINITY;
   for (int c = 0; c < nchunk; ++c) m = fmaxf(m, base[(size_t)c * rec]);
@@ -215,6 +226,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, float* __res
 
 __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
                                 long long n) {
+  pdl_enter();
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const float x = g[i];
     out[i] = x / (1.f + expf(-x)) * u[i];
@@ -222,6 +234,22 @@ __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __rest
 }
 
 int status_of(cudaError_t e) { return e == cudaSuccess ? PF_OK : PF_ERR_CUDA; }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, int threads, cudaStream_t s, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  note_launch();
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
 bool al4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
 }  // namespace
@@ -233,9 +261,8 @@ int pf_add_rmsnorm(float* h, const float* delta, const float* w, float* out, int
   if (!h || !w || !out || rows < 0 || H <= 0 || !(eps >= 0.f)) return PF_ERR_INVALID_ARGUMENT;
   if (!al4(h) || !al4(w) || !al4(out) || (delta && !al4(delta))) return PF_ERR_ALIGNMENT;
   if (rows == 0) return PF_OK;
-  add_rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(h, delta, w, out, H, eps);
-  note_launch();
-  return status_of(cudaGetLastError());
+  return status_of(launch_pdl(add_rmsnorm_kernel, dim3(rows), kNormThreads, static_cast<cudaStream_t>(stream), h, delta,
+                              w, out, H, eps));
 }
 
 int pf_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* v_cache, const long long* pos,
@@ -246,10 +273,9 @@ int pf_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* 
   if (!al4(q) || !al4(k) || !al4(v) || !al4(k_cache) || !al4(v_cache) || !al4(inv_freq) ||
       (reinterpret_cast<uintptr_t>(pos) & 7u))
     return PF_ERR_ALIGNMENT;
-  rope_kv_kernel<<<n_heads + n_kv_heads, head_dim / 2, 0, static_cast<cudaStream_t>(stream)>>>(
-      q, k, v, k_cache, v_cache, pos, inv_freq, n_heads, n_kv_heads, head_dim, max_seq);
-  note_launch();
-  return status_of(cudaGetLastError());
+  return status_of(launch_pdl(rope_kv_kernel, dim3(n_heads + n_kv_heads), head_dim / 2,
+                              static_cast<cudaStream_t>(stream), q, k, v, k_cache, v_cache, pos, inv_freq, n_heads,
+                              n_kv_heads, head_dim, max_seq));
 }
 
 size_t pf_decode_attention_workspace_size(int n_heads, int head_dim, int max_seq) {
@@ -272,14 +298,10 @@ int pf_decode_attention(const float* q, const float* k_cache, const float* v_cac
   const int nchunk = (max_seq + kAttnChunk - 1) / kAttnChunk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
-  attn_chunk_kernel<<<dim3(n_kv_heads, nchunk), kAttnThreads, 0, s>>>(q, k_cache, v_cache, pos, part, n_heads,
-                                                                      n_kv_heads, head_dim, max_seq, nchunk, scale);
-  note_launch();
-  cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_pdl(attn_chunk_kernel, dim3(n_kv_heads, nchunk), kAttnThreads, s, q, k_cache, v_cache,
+                                   pos, part, n_heads, n_kv_heads, head_dim, max_seq, nchunk, scale);
   if (e != cudaSuccess) return PF_ERR_CUDA;
-  attn_combine_kernel<<<n_heads, 128, 0, s>>>(part, out, head_dim, nchunk);
-  note_launch();
-  return status_of(cudaGetLastError());
+  return status_of(launch_pdl(attn_combine_kernel, dim3(n_heads), 128, s, (const float*)part, out, head_dim, nchunk));
 }
 
 int pf_silu_mul(const float* g, const float* u, float* out, long long n, void* stream) {
@@ -287,7 +309,6 @@ int pf_silu_mul(const float* g, const float* u, float* out, long long n, void* s
   if (!al4(g) || !al4(u) || !al4(out)) return PF_ERR_ALIGNMENT;
   if (n == 0) return PF_OK;
   const long long blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
-  silu_mul_kernel<<<(int)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, out, n);
-  note_launch();
-  return status_of(cudaGetLastError());
+  return status_of(launch_pdl(silu_mul_kernel, dim3((unsigned)blocks), 256, static_cast<cudaStream_t>(stream), g, u, out,
+                              n));
 }
