@@ -136,6 +136,7 @@ def decode_rates(copies, xs, outs, ws, stream, dev, layers, tokens=20):
     del graphs, pc, base
     res.update(decode_full_step(copies, stream, dev, layers, tokens=tokens))
     res.update(decode_rates_70b_e8(stream, dev, tokens))
+    res.update(kv_attention_rates(stream, dev, tokens=tokens))
     return res
 
 
@@ -143,8 +144,8 @@ def decode_full_step(copies, stream, dev, layers=32, ctx=512, tokens=20):
     """Tokens/s of a whole batch-1 decode step of the Llama-3-8B shape
     (polarflash_b200.decode.PFlashDecoder, one CUDA graph per token): the
     INT3 g128 linears of `layers` layers (the bench's weights), RMSNorms,
-    RoPE, the fp32 KV cache at `ctx` previous tokens, attention (torch SDPA)
-    and a dense fp16 embedding and lm_head (128256 x 4096, 1.05 GB)."""
+    RoPE, the fp32 KV cache at `ctx` previous tokens, the library's attention
+    kernels and a dense fp16 embedding and lm_head (128256 x 4096, 1.05 GB)."""
     from polarflash_b200.decode import DecoderLayer, PFlashDecoder
 
     H, V = 4096, 128256
@@ -180,6 +181,64 @@ def decode_full_step(copies, stream, dev, layers=32, ctx=512, tokens=20):
     del dec, embed, head
     return {"llama3_8b_int3_full_step_ctx512": {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
                                                 "GB_s": round(nb / ms / 1e6, 1)}}
+
+
+def kv_attention_rates(stream, dev, layers=32, ctx=16384, tokens=20):
+    """Device time of the attention over the KV cache of one batch-1 decode
+    token, Llama-3-8B attention shape (32 query / 8 KV heads of 128), one cache
+    per layer at `ctx` cached positions (every layer's cache resident, the
+    set larger than L2), for the fp32 cache (pf_decode_attention) and the
+    compressed int8 / 2bit / 2bit_asym caches (pf_decode_attention_compressed,
+    codes dequantized inside the kernel).  GB_s counts the cache bytes read
+    (codes, scales, zeros of ctx positions x 8 KV heads, K and V)."""
+    import ctypes
+    import math
+
+    from polarflash_b200 import _lib
+    from polarflash_b200.kv_cache import KV_MODES, kv_row_bytes
+
+    L = _lib.load()
+    nh, nkv, hd, ms = 32, 8, 128, ctx
+    p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    st = ctypes.c_void_p(stream.cuda_stream)
+    q = torch.randn(nh * hd, device=dev)
+    out = torch.empty(nh * hd, device=dev)
+    pos = torch.tensor([ctx - 1], dtype=torch.long, device=dev)
+    aws = torch.empty(int(L.pf_decode_attention_workspace_size(nh, hd, ms)), dtype=torch.uint8, device=dev)
+    res = {}
+    for mode in ("fp32", "int8", "2bit", "2bit_asym"):
+        rb = 4 * hd if mode == "fp32" else kv_row_bytes(mode, hd)
+        asym = mode == "2bit_asym"
+        caches = []
+        for _ in range(layers):
+            kc = torch.zeros(ms, nkv, rb, dtype=torch.uint8, device=dev)
+            vc = torch.zeros(ms, nkv, rb, dtype=torch.uint8, device=dev)
+            sc = None if mode == "fp32" else torch.ones(2, ms, nkv, device=dev)
+            zr = torch.zeros(2, ms, nkv, device=dev) if asym else None
+            caches.append((kc, vc, sc, zr))
+
+        def run():
+            for kc, vc, sc, zr in caches:
+                if mode == "fp32":
+                    _lib.check(L.pf_decode_attention(p(q), p(kc), p(vc), p(pos), p(out), nh, nkv, hd, ms,
+                                                     1.0 / math.sqrt(hd), p(aws), aws.numel(), st))
+                else:
+                    _lib.check(L.pf_decode_attention_compressed(
+                        p(q), p(kc), p(sc[0]), p(zr[0] if asym else None), p(vc), p(sc[1]),
+                        p(zr[1] if asym else None), p(pos), p(out), nh, nkv, hd, ms, KV_MODES[mode],
+                        1.0 / math.sqrt(hd), p(aws), aws.numel(), st))
+
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            run()  # eager set-up outside the capture
+            with torch.cuda.graph(gr, stream=stream):
+                run()
+        ms_tok = time_tokens([gr], stream, tokens)
+        nb = layers * 2 * ctx * nkv * (rb + (0 if mode == "fp32" else 4) + (4 if asym else 0))
+        res[mode] = {"us_per_layer": round(ms_tok * 1e3 / layers, 2), "GB_s": round(nb / ms_tok / 1e6, 1),
+                     "cache_MB_per_layer": round(nb / layers / 1e6, 2)}
+        del gr, caches
+    return {"kv_attention_llama3_8b_ctx16k": res}
 
 
 LINEARS_70B = [("q", 8192, 8192), ("k", 1024, 8192), ("v", 1024, 8192), ("o", 8192, 8192),
@@ -533,8 +592,10 @@ def main():
                           "batch 1 for INT3 / INT2 / polar 1.75, Llama-3-70B shape (80 layers, E8 RVQ2) at batch 1 "
                           "and 32; one resident weight copy per layer, CUDA-graph replays; attention, norms and "
                           "lm_head not included, except llama3_8b_int3_full_step_ctx512: the whole batch-1 step "
-                          "through polarflash_b200.decode (RMSNorms, RoPE, fp32 KV cache at 512 tokens, SDPA "
-                          "attention, fp16 embedding and lm_head), one CUDA graph per token")
+                          "through polarflash_b200.decode (the library's RMSNorm, RoPE + cache write, attention "
+                          "and SiLU kernels, fp32 KV cache at 512 tokens, fp16 embedding and lm_head), one CUDA "
+                          "graph per token; kv_attention_llama3_8b_ctx16k: the attention alone over 32 layers' "
+                          "caches at 16384 tokens, fp32 and compressed (int8, 2bit, 2bit_asym) caches")
 
     # max over ranks
     t = torch.tensor([ms, ms_run, ms_e2e], device=dev, dtype=torch.float64)

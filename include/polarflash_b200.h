@@ -222,6 +222,51 @@ PF_API int pf_decode_attention(const float* q, const float* k_cache, const float
  * PFlashMLPBlock.forward (model_integration.py:160-163). */
 PF_API int pf_silu_mul(const float* g, const float* u, float* out, long long n, void* stream);
 
+/* Compressed KV cache: rows of `dim` values (one token of one KV head)
+ * stored as codes plus a per-row fp32 scale (and zero), as CompressedKVCache
+ * quantizes them (polarflash_rt/kv_cache/compressed_kv.py):
+ *   PF_KV_INT8 (:68-77):  s = max(max|x| / 127, 1e-8), int8 c = clamp(round(x / s), -128, 127),
+ *                         x' = c s; dim bytes per row.
+ *   PF_KV_2BIT (:79-112): s = max(max|x| / 1.75, 1e-8), c = clamp(floor(x / s + 2), 0, 3),
+ *                         x' = (c - 1.5) s; (dim + 3) / 4 bytes per row.
+ *   PF_KV_2BIT_ASYM (:114-150): z = min x, s = max((max x - z) / 3, 1e-8),
+ *                         c = clamp(round((x - z) / s), 0, 3), x' = c s + z.
+ * round is to nearest even; 2-bit codes are packed four per byte, first value
+ * in the top bits (c0 << 6 | c1 << 4 | c2 << 2 | c3), a ragged last byte
+ * padded with zero codes.  Codes, scales and x' are bit-identical to the
+ * reference's fp32 arithmetic for finite inputs.  PF_KV_FP32 names the plain
+ * fp32 cache of pf_rope_kv / pf_decode_attention. */
+typedef enum pf_kv_mode { PF_KV_FP32 = 0, PF_KV_INT8 = 1, PF_KV_2BIT = 2, PF_KV_2BIT_ASYM = 3 } pf_kv_mode;
+/* Bytes of one row of codes (4 * dim for PF_KV_FP32); 0 for a bad mode or dim. */
+PF_API size_t pf_kv_row_bytes(int mode, int dim);
+/* pf_kv_quantize: x [rows][dim] fp32 -> codes [rows][pf_kv_row_bytes],
+ * scales [rows], zeros [rows] (PF_KV_2BIT_ASYM only; may be null otherwise).
+ * The quantize half of CompressedKVCache.update (compressed_kv.py:152-259). */
+PF_API int pf_kv_quantize(const float* x, long long rows, int dim, int mode, void* codes, float* scales,
+                          float* zeros, void* stream);
+/* pf_kv_dequantize: out [rows][dim] fp32 = x' of each row.  The dequantize
+ * half of CompressedKVCache.update (_dequantize_*, compressed_kv.py:75-77,
+ * 101-112, 139-150). */
+PF_API int pf_kv_dequantize(const void* codes, const float* scales, const float* zeros, long long rows, int dim,
+                            int mode, float* out, void* stream);
+/* pf_rope_kv_compressed: as pf_rope_kv, with the rotated k and v quantized
+ * (mode PF_KV_INT8 / PF_KV_2BIT / PF_KV_2BIT_ASYM) into row (*pos, head) of
+ * compressed caches: codes [max_seq][n_kv_heads][pf_kv_row_bytes(mode,
+ * head_dim)], scales and zeros [max_seq][n_kv_heads].  head_dim <= 2048. */
+PF_API int pf_rope_kv_compressed(float* q, const float* k, const float* v, void* k_codes, float* k_scales,
+                                 float* k_zeros, void* v_codes, float* v_scales, float* v_zeros,
+                                 const long long* pos, const float* inv_freq, int n_heads, int n_kv_heads,
+                                 int head_dim, int max_seq, int mode, void* stream);
+/* pf_decode_attention_compressed: pf_decode_attention over compressed caches
+ * laid out as pf_rope_kv_compressed writes them, each K and V value
+ * dequantized inside the attention kernel (the reference dequantizes the
+ * whole cache, compressed_kv.py:173-226, and attends over the result). */
+PF_API int pf_decode_attention_compressed(const float* q, const void* k_codes, const float* k_scales,
+                                          const float* k_zeros, const void* v_codes, const float* v_scales,
+                                          const float* v_zeros, const long long* pos, float* out, int n_heads,
+                                          int n_kv_heads, int head_dim, int max_seq, int mode, float scale,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

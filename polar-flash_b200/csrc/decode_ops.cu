@@ -89,6 +89,173 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
   }
 }
 
+// ---- compressed KV cache ----------------------------------------------------
+// Rows of head_dim values (one token of one KV head) quantized as
+// CompressedKVCache does (polarflash_rt/kv_cache/compressed_kv.py):
+//   int8 (:68-77):      s = max(max|x| / 127, 1e-8), c = clamp(rint(x / s), -128, 127), x' = c s
+//   2bit (:79-112):     s = max(max|x| / 1.75, 1e-8), c = clamp(floor(x / s + 2), 0, 3), x' = (c - 1.5) s
+//   2bit_asym (:114-150): z = min x, s = max((max x - z) / 3, 1e-8), c = clamp(rint((x - z) / s), 0, 3),
+//                       x' = c s + z
+// 2-bit codes are packed four to a byte, first value in the top bits
+// (c0 << 6 | c1 << 4 | c2 << 2 | c3), a ragged last byte padded with zero
+// codes.  Every operation is an explicitly rounded single-precision op (no
+// contraction to fma), so codes, scales and dequantized values are
+// bit-identical to the reference's fp32 arithmetic.
+template <bool kMin>
+__device__ __forceinline__ float block_minmax(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = kMin ? fminf(v, w) : fmaxf(v, w);
+  }
+  __syncthreads();  // red is reused by consecutive reductions
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = kMin ? fminf(r, red[w]) : fmaxf(r, red[w]);
+  return r;
+}
+
+// The whole block (a multiple of 32 threads) quantizes the row x[0..dim).
+template <int MODE>
+__device__ void quantize_row(const float* x, int dim, uint8_t* codes, float* scale_out, float* zero_out, float* red) {
+  const int t = threadIdx.x, nt = blockDim.x;
+  float lo = INFINITY, hi = MODE == PF_KV_2BIT_ASYM ? -INFINITY : 0.f;
+  for (int i = t; i < dim; i += nt) {
+    const float v = x[i];
+    if (MODE == PF_KV_2BIT_ASYM) {
+      lo = fminf(lo, v);
+      hi = fmaxf(hi, v);
+    } else {
+      hi = fmaxf(hi, fabsf(v));
+    }
+  }
+  float z = 0.f, s;
+  hi = block_minmax<false>(hi, red);
+  if (MODE == PF_KV_2BIT_ASYM) z = block_minmax<true>(lo, red);
+  if (MODE == PF_KV_INT8)
+    s = fmaxf(__fdiv_rn(hi, 127.f), 1e-8f);
+  else if (MODE == PF_KV_2BIT)
+    s = fmaxf(__fdiv_rn(hi, 1.75f), 1e-8f);
+  else
+    s = fmaxf(__fdiv_rn(__fsub_rn(hi, z), 3.f), 1e-8f);
+  if (MODE == PF_KV_INT8) {
+    for (int i = t; i < dim; i += nt) {
+      const float r = fminf(fmaxf(rintf(__fdiv_rn(x[i], s)), -128.f), 127.f);
+      reinterpret_cast<int8_t*>(codes)[i] = (int8_t)(int)r;
+    }
+  } else {
+    for (int j = t; j < (dim + 3) >> 2; j += nt) {
+      unsigned byte = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * j + e;
+        if (i < dim) {
+          const float r = MODE == PF_KV_2BIT ? floorf(__fadd_rn(__fdiv_rn(x[i], s), 2.f))
+                                             : rintf(__fdiv_rn(__fsub_rn(x[i], z), s));
+          byte |= (unsigned)fminf(fmaxf(r, 0.f), 3.f) << (6 - 2 * e);
+        }
+      }
+      codes[j] = (uint8_t)byte;
+    }
+  }
+  if (t == 0) {
+    *scale_out = s;
+    if (MODE == PF_KV_2BIT_ASYM) *zero_out = z;
+  }
+}
+
+// Value d of a quantized row (codes of the row, its scale and zero).
+template <int MODE>
+__device__ __forceinline__ float kv_value(const uint8_t* row, int d, float s, float z) {
+  if (MODE == PF_KV_INT8) return __fmul_rn((float)reinterpret_cast<const int8_t*>(row)[d], s);
+  const float c = (float)((row[d >> 2] >> (6 - 2 * (d & 3))) & 3u);
+  if (MODE == PF_KV_2BIT) return __fmul_rn(__fsub_rn(c, 1.5f), s);
+  return __fadd_rn(__fmul_rn(c, s), z);
+}
+
+__host__ __device__ __forceinline__ int kv_row_bytes(int mode, int dim) {
+  return mode == PF_KV_INT8 ? dim : mode == PF_KV_FP32 ? 4 * dim : (dim + 3) / 4;
+}
+
+constexpr int kQuantThreads = 128;
+
+template <int MODE>
+__global__ void __launch_bounds__(kQuantThreads) kv_quantize_kernel(const float* __restrict__ x, int dim,
+                                                                    uint8_t* __restrict__ codes,
+                                                                    float* __restrict__ scales,
+                                                                    float* __restrict__ zeros) {
+  __shared__ float red[kQuantThreads / 32];
+  pdl_enter();
+  const size_t r = blockIdx.x;
+  quantize_row<MODE>(x + r * dim, dim, codes + r * kv_row_bytes(MODE, dim), scales + r, zeros ? zeros + r : nullptr,
+                     red);
+}
+
+template <int MODE>
+__global__ void kv_dequantize_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ scales,
+                                     const float* __restrict__ zeros, long long rows, int dim,
+                                     float* __restrict__ out) {
+  pdl_enter();
+  const long long n = rows * dim;
+  const int rb = kv_row_bytes(MODE, dim);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / dim;
+    const int d = (int)(i - r * dim);
+    out[i] = kv_value<MODE>(codes + r * rb, d, scales[r], MODE == PF_KV_2BIT_ASYM ? zeros[r] : 0.f);
+  }
+}
+
+// As rope_kv_kernel, with the rotated key and the value quantized into the
+// compressed caches' row (*pos, head).  Blocks of the KV heads stage both
+// rows in shared memory and quantize them with the whole block.
+constexpr int kRopeMaxHd = 2048;
+
+struct KvRows {  // one layer's compressed cache: rows [max_seq][n_kv_heads]
+  uint8_t* codes;
+  float* scales;
+  float* zeros;  // 2bit_asym only
+};
+
+template <int MODE>
+__global__ void rope_kvq_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                                KvRows kc, KvRows vc, const long long* __restrict__ pos,
+                                const float* __restrict__ inv_freq, int nh, int nkv, int hd, int max_seq) {
+  __shared__ float xs[2][kRopeMaxHd];
+  __shared__ float red[32];
+  pdl_enter();
+  const long long p = *pos;
+  if (p < 0 || p >= max_seq) return;  // block-uniform
+  const int half = hd >> 1, head = blockIdx.x;
+  if (head < nh) {
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const float f = (float)p * inv_freq[i];
+      const float c = cosf(f), s = sinf(f);
+      float* x = q + (size_t)head * hd;
+      const float x1 = x[i], x2 = x[i + half];
+      x[i] = x1 * c - x2 * s;
+      x[i + half] = x1 * s + x2 * c;
+    }
+    return;  // block-uniform
+  }
+  const int kh = head - nh;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float f = (float)p * inv_freq[i];
+    const float c = cosf(f), s = sinf(f);
+    const float* x = k + (size_t)kh * hd;
+    const float x1 = x[i], x2 = x[i + half];
+    xs[0][i] = x1 * c - x2 * s;
+    xs[0][i + half] = x1 * s + x2 * c;
+    xs[1][i] = v[(size_t)kh * hd + i];
+    xs[1][i + half] = v[(size_t)kh * hd + i + half];
+  }
+  __syncthreads();
+  const size_t r = (size_t)p * nkv + kh;
+  const int rb = kv_row_bytes(MODE, hd);
+  quantize_row<MODE>(xs[0], hd, kc.codes + r * rb, kc.scales + r, kc.zeros ? kc.zeros + r : nullptr, red);
+  quantize_row<MODE>(xs[1], hd, vc.codes + r * rb, vc.scales + r, vc.zeros ? vc.zeros + r : nullptr, red);
+}
+
 // Attention of one new token over positions 0..*pos of the cache, split over
 // chunks of kAttnChunk positions (flash decoding).  attn_chunk_kernel: one
 // block per (KV head, chunk) serves the KV head's G query heads: scores with
@@ -100,9 +267,23 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
 constexpr int kAttnChunk = 64;
 constexpr int kAttnG = 8;  // query heads per KV head handled by one block
 
-__global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* __restrict__ q,
-                                                                  const float* __restrict__ kc,
-                                                                  const float* __restrict__ vc,
+// KV cache rows [max_seq][n_kv_heads]: fp32 values, or codes with a scale
+// (and, for 2bit_asym, a zero) per row.
+struct KvView {
+  const void* codes;
+  const float* scales;
+  const float* zeros;
+};
+
+template <int MODE>
+__device__ __forceinline__ float kv_load(const KvView& c, size_t r, int d, int hd) {
+  if (MODE == PF_KV_FP32) return static_cast<const float*>(c.codes)[r * hd + d];
+  return kv_value<MODE>(static_cast<const uint8_t*>(c.codes) + r * kv_row_bytes(MODE, hd), d, c.scales[r],
+                        MODE == PF_KV_2BIT_ASYM ? c.zeros[r] : 0.f);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* __restrict__ q, KvView kc, KvView vc,
                                                                   const long long* __restrict__ pos,
                                                                   float* __restrict__ part, int nh, int nkv, int hd,
                                                                   int max_seq, int nchunk, float scale) {
@@ -136,7 +317,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int d = lane + 32 * e;
-        kv[u][e] = (j < n && d < hd) ? kc[((size_t)(t0 + j) * nkv + kvh) * hd + d] : 0.f;
+        kv[u][e] = (j < n && d < hd) ? kv_load<MODE>(kc, (size_t)(t0 + j) * nkv + kvh, d, hd) : 0.f;
       }
     }
     for (int g = 0; g < G; ++g) {
@@ -183,7 +364,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
 #pragma unroll
     for (int g = 0; g < kAttnG; ++g) acc[g] = 0.f;
     for (int j = half; j < n; j += 2) {
-      const float val = vc[((size_t)(t0 + j) * nkv + kvh) * hd + d];
+      const float val = kv_load<MODE>(vc, (size_t)(t0 + j) * nkv + kvh, d, hd);
 #pragma unroll
       for (int g = 0; g < kAttnG; ++g)
         if (g < G) acc[g] += sc[g][j] * val;
@@ -284,24 +465,145 @@ size_t pf_decode_attention_workspace_size(int n_heads, int head_dim, int max_seq
   return (size_t)n_heads * nchunk * (head_dim + 2) * sizeof(float);
 }
 
-int pf_decode_attention(const float* q, const float* k_cache, const float* v_cache, const long long* pos, float* out,
-                        int n_heads, int n_kv_heads, int head_dim, int max_seq, float scale, void* workspace,
-                        size_t workspace_bytes, void* stream) {
-  if (!q || !k_cache || !v_cache || !pos || !out || !workspace) return PF_ERR_INVALID_ARGUMENT;
+namespace {
+
+bool kv_mode_ok(int mode) { return mode == PF_KV_INT8 || mode == PF_KV_2BIT || mode == PF_KV_2BIT_ASYM; }
+
+int decode_attention(int mode, const float* q, KvView kc, KvView vc, const long long* pos, float* out, int n_heads,
+                     int n_kv_heads, int head_dim, int max_seq, float scale, void* workspace, size_t workspace_bytes,
+                     void* stream) {
   if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > kAttnG || head_dim <= 0 ||
       head_dim > 128 || max_seq <= 0 || max_seq > kDecodeMaxSeq)
     return PF_ERR_SHAPE;
-  if (!al4(q) || !al4(k_cache) || !al4(v_cache) || !al4(out) || !al4(workspace) ||
-      (reinterpret_cast<uintptr_t>(pos) & 7u))
-    return PF_ERR_ALIGNMENT;
+  if (!al4(q) || !al4(out) || !al4(workspace) || (reinterpret_cast<uintptr_t>(pos) & 7u)) return PF_ERR_ALIGNMENT;
   if (workspace_bytes < pf_decode_attention_workspace_size(n_heads, head_dim, max_seq)) return PF_ERR_WORKSPACE;
   const int nchunk = (max_seq + kAttnChunk - 1) / kAttnChunk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
-  const cudaError_t e = launch_pdl(attn_chunk_kernel, dim3(n_kv_heads, nchunk), kAttnThreads, s, q, k_cache, v_cache,
-                                   pos, part, n_heads, n_kv_heads, head_dim, max_seq, nchunk, scale);
+  const dim3 grid(n_kv_heads, nchunk);
+  cudaError_t e;
+  switch (mode) {
+    case PF_KV_FP32:
+      e = launch_pdl(attn_chunk_kernel<PF_KV_FP32>, grid, kAttnThreads, s, q, kc, vc, pos, part, n_heads, n_kv_heads,
+                     head_dim, max_seq, nchunk, scale);
+      break;
+    case PF_KV_INT8:
+      e = launch_pdl(attn_chunk_kernel<PF_KV_INT8>, grid, kAttnThreads, s, q, kc, vc, pos, part, n_heads, n_kv_heads,
+                     head_dim, max_seq, nchunk, scale);
+      break;
+    case PF_KV_2BIT:
+      e = launch_pdl(attn_chunk_kernel<PF_KV_2BIT>, grid, kAttnThreads, s, q, kc, vc, pos, part, n_heads, n_kv_heads,
+                     head_dim, max_seq, nchunk, scale);
+      break;
+    default:
+      e = launch_pdl(attn_chunk_kernel<PF_KV_2BIT_ASYM>, grid, kAttnThreads, s, q, kc, vc, pos, part, n_heads,
+                     n_kv_heads, head_dim, max_seq, nchunk, scale);
+  }
   if (e != cudaSuccess) return PF_ERR_CUDA;
   return status_of(launch_pdl(attn_combine_kernel, dim3(n_heads), 128, s, (const float*)part, out, head_dim, nchunk));
+}
+
+}  // namespace
+
+int pf_decode_attention(const float* q, const float* k_cache, const float* v_cache, const long long* pos, float* out,
+                        int n_heads, int n_kv_heads, int head_dim, int max_seq, float scale, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !pos || !out || !workspace) return PF_ERR_INVALID_ARGUMENT;
+  if (!al4(k_cache) || !al4(v_cache)) return PF_ERR_ALIGNMENT;
+  return decode_attention(PF_KV_FP32, q, KvView{k_cache, nullptr, nullptr}, KvView{v_cache, nullptr, nullptr}, pos,
+                          out, n_heads, n_kv_heads, head_dim, max_seq, scale, workspace, workspace_bytes, stream);
+}
+
+size_t pf_kv_row_bytes(int mode, int dim) {
+  if (dim <= 0 || (mode != PF_KV_FP32 && !kv_mode_ok(mode))) return 0;
+  return (size_t)kv_row_bytes(mode, dim);
+}
+
+int pf_kv_quantize(const float* x, long long rows, int dim, int mode, void* codes, float* scales, float* zeros,
+                   void* stream) {
+  if (!kv_mode_ok(mode) || !x || !codes || !scales || (mode == PF_KV_2BIT_ASYM && !zeros) || rows < 0)
+    return PF_ERR_INVALID_ARGUMENT;
+  if (dim <= 0 || rows > 0x7fffffffLL) return PF_ERR_SHAPE;
+  if (!al4(x) || !al4(scales) || (zeros && !al4(zeros))) return PF_ERR_ALIGNMENT;
+  if (rows == 0) return PF_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* c = static_cast<uint8_t*>(codes);
+  float* z = mode == PF_KV_2BIT_ASYM ? zeros : nullptr;
+  const dim3 grid((unsigned)rows);
+  cudaError_t e;
+  if (mode == PF_KV_INT8)
+    e = launch_pdl(kv_quantize_kernel<PF_KV_INT8>, grid, kQuantThreads, s, x, dim, c, scales, z);
+  else if (mode == PF_KV_2BIT)
+    e = launch_pdl(kv_quantize_kernel<PF_KV_2BIT>, grid, kQuantThreads, s, x, dim, c, scales, z);
+  else
+    e = launch_pdl(kv_quantize_kernel<PF_KV_2BIT_ASYM>, grid, kQuantThreads, s, x, dim, c, scales, z);
+  return status_of(e);
+}
+
+int pf_kv_dequantize(const void* codes, const float* scales, const float* zeros, long long rows, int dim, int mode,
+                     float* out, void* stream) {
+  if (!kv_mode_ok(mode) || !codes || !scales || !out || (mode == PF_KV_2BIT_ASYM && !zeros) || rows < 0)
+    return PF_ERR_INVALID_ARGUMENT;
+  if (dim <= 0) return PF_ERR_SHAPE;
+  if (!al4(out) || !al4(scales) || (zeros && !al4(zeros))) return PF_ERR_ALIGNMENT;
+  const long long n = rows * dim;
+  if (n == 0) return PF_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* c = static_cast<const uint8_t*>(codes);
+  const long long blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
+  const dim3 grid((unsigned)blocks);
+  cudaError_t e;
+  if (mode == PF_KV_INT8)
+    e = launch_pdl(kv_dequantize_kernel<PF_KV_INT8>, grid, 256, s, c, scales, zeros, rows, dim, out);
+  else if (mode == PF_KV_2BIT)
+    e = launch_pdl(kv_dequantize_kernel<PF_KV_2BIT>, grid, 256, s, c, scales, zeros, rows, dim, out);
+  else
+    e = launch_pdl(kv_dequantize_kernel<PF_KV_2BIT_ASYM>, grid, 256, s, c, scales, zeros, rows, dim, out);
+  return status_of(e);
+}
+
+int pf_rope_kv_compressed(float* q, const float* k, const float* v, void* k_codes, float* k_scales, float* k_zeros,
+                          void* v_codes, float* v_scales, float* v_zeros, const long long* pos, const float* inv_freq,
+                          int n_heads, int n_kv_heads, int head_dim, int max_seq, int mode, void* stream) {
+  if (!kv_mode_ok(mode) || !q || !k || !v || !k_codes || !k_scales || !v_codes || !v_scales || !pos || !inv_freq ||
+      (mode == PF_KV_2BIT_ASYM && (!k_zeros || !v_zeros)))
+    return PF_ERR_INVALID_ARGUMENT;
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || (head_dim & 1) || head_dim > kRopeMaxHd || max_seq <= 0)
+    return PF_ERR_SHAPE;
+  if (!al4(q) || !al4(k) || !al4(v) || !al4(k_scales) || !al4(v_scales) || !al4(inv_freq) ||
+      (k_zeros && !al4(k_zeros)) || (v_zeros && !al4(v_zeros)) || (reinterpret_cast<uintptr_t>(pos) & 7u))
+    return PF_ERR_ALIGNMENT;
+  const bool asym = mode == PF_KV_2BIT_ASYM;
+  const KvRows kc{static_cast<uint8_t*>(k_codes), k_scales, asym ? k_zeros : nullptr};
+  const KvRows vc{static_cast<uint8_t*>(v_codes), v_scales, asym ? v_zeros : nullptr};
+  const int threads = ((head_dim / 2 + 31) / 32) * 32;  // whole warps: the row reductions shuffle over full warps
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(n_heads + n_kv_heads);
+  cudaError_t e;
+  if (mode == PF_KV_INT8)
+    e = launch_pdl(rope_kvq_kernel<PF_KV_INT8>, grid, threads, s, q, k, v, kc, vc, pos, inv_freq, n_heads, n_kv_heads,
+                   head_dim, max_seq);
+  else if (mode == PF_KV_2BIT)
+    e = launch_pdl(rope_kvq_kernel<PF_KV_2BIT>, grid, threads, s, q, k, v, kc, vc, pos, inv_freq, n_heads, n_kv_heads,
+                   head_dim, max_seq);
+  else
+    e = launch_pdl(rope_kvq_kernel<PF_KV_2BIT_ASYM>, grid, threads, s, q, k, v, kc, vc, pos, inv_freq, n_heads,
+                   n_kv_heads, head_dim, max_seq);
+  return status_of(e);
+}
+
+int pf_decode_attention_compressed(const float* q, const void* k_codes, const float* k_scales, const float* k_zeros,
+                                   const void* v_codes, const float* v_scales, const float* v_zeros,
+                                   const long long* pos, float* out, int n_heads, int n_kv_heads, int head_dim,
+                                   int max_seq, int mode, float scale, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  if (!kv_mode_ok(mode) || !q || !k_codes || !k_scales || !v_codes || !v_scales || !pos || !out || !workspace ||
+      (mode == PF_KV_2BIT_ASYM && (!k_zeros || !v_zeros)))
+    return PF_ERR_INVALID_ARGUMENT;
+  if (!al4(k_scales) || !al4(v_scales) || (k_zeros && !al4(k_zeros)) || (v_zeros && !al4(v_zeros)))
+    return PF_ERR_ALIGNMENT;
+  return decode_attention(mode, q, KvView{k_codes, k_scales, k_zeros}, KvView{v_codes, v_scales, v_zeros}, pos, out,
+                          n_heads, n_kv_heads, head_dim, max_seq, scale, workspace, workspace_bytes, stream);
 }
 
 int pf_silu_mul(const float* g, const float* u, float* out, long long n, void* stream) {

@@ -43,6 +43,8 @@ EXPORTS = (
     "pf_dequant", "pf_unpack_codes", "pf_rwht",
     "pf_native_gemv_int4", "pf_native_gemv_int2", "pf_native_gemm_int4", "pf_qlinear_noalloc",
     "pf_add_rmsnorm", "pf_rope_kv", "pf_decode_attention_workspace_size", "pf_decode_attention", "pf_silu_mul",
+    "pf_kv_row_bytes", "pf_kv_quantize", "pf_kv_dequantize", "pf_rope_kv_compressed",
+    "pf_decode_attention_compressed",
 )
 
 
@@ -125,6 +127,17 @@ def load():
     L.pf_decode_attention_workspace_size.argtypes = [I, I, I]
     L.pf_silu_mul.restype = I
     L.pf_silu_mul.argtypes = [P, P, P, ctypes.c_longlong, P]
+    LL = ctypes.c_longlong
+    L.pf_kv_row_bytes.restype = SZ
+    L.pf_kv_row_bytes.argtypes = [I, I]
+    L.pf_kv_quantize.restype = I
+    L.pf_kv_quantize.argtypes = [P, LL, I, I, P, P, P, P]
+    L.pf_kv_dequantize.restype = I
+    L.pf_kv_dequantize.argtypes = [P, P, P, LL, I, I, P, P]
+    L.pf_rope_kv_compressed.restype = I
+    L.pf_rope_kv_compressed.argtypes = [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, P]
+    L.pf_decode_attention_compressed.restype = I
+    L.pf_decode_attention_compressed.argtypes = [P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, P, SZ, P]
     _lib = L
     return L
 

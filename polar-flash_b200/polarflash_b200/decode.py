@@ -31,6 +31,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
+from .kv_cache import KV_MODES, kv_row_bytes
 from .qweight import QWeight, group_workspace_bytes, qlinear, qlinear_multi
 
 
@@ -63,11 +64,16 @@ class PFlashDecoder:
     num_attention_heads.  ``embed`` [vocab, hidden] and ``lm_head`` [vocab,
     hidden] are dense device tensors, ``final_norm`` [hidden].  ``max_seq``
     bounds the cache; ``kv_dtype`` is the cache's dtype (fp32 keeps the
-    reference's arithmetic).
+    reference's arithmetic).  ``kv_mode`` "int8", "2bit" or "2bit_asym"
+    stores the cache compressed as CompressedKVCache quantizes it
+    (polarflash_rt/kv_cache/compressed_kv.py:68-150): each (token, KV head)
+    row as codes plus an fp32 scale (and zero), written by the RoPE kernel and
+    dequantized inside the attention kernel; the eager forward attends over
+    the dequantized rows.
     """
 
     def __init__(self, config: Dict, layers: List[DecoderLayer], embed: torch.Tensor, final_norm: torch.Tensor,
-                 lm_head: torch.Tensor, max_seq: int, kv_dtype: torch.dtype = torch.float32):
+                 lm_head: torch.Tensor, max_seq: int, kv_dtype: torch.dtype = torch.float32, kv_mode: str = "fp32"):
         self.hidden = int(config["hidden_size"])
         self.nh = int(config["num_attention_heads"])
         self.nkv = int(config["num_key_value_heads"])
@@ -82,8 +88,23 @@ class PFlashDecoder:
         self.device = embed.device
         dev = self.device
         L = len(layers)
-        self.k_cache = torch.zeros(L, self.max_seq, self.nkv, self.hd, dtype=kv_dtype, device=dev)
-        self.v_cache = torch.zeros(L, self.max_seq, self.nkv, self.hd, dtype=kv_dtype, device=dev)
+        if kv_mode != "fp32" and kv_mode not in KV_MODES:
+            raise ValueError(f"kv_mode {kv_mode!r}: one of fp32, {', '.join(KV_MODES)}")
+        self.kv_mode = kv_mode
+        if kv_mode == "fp32":
+            self.k_cache = torch.zeros(L, self.max_seq, self.nkv, self.hd, dtype=kv_dtype, device=dev)
+            self.v_cache = torch.zeros(L, self.max_seq, self.nkv, self.hd, dtype=kv_dtype, device=dev)
+        else:
+            # rows [L][max_seq][nkv]: codes, fp32 scales, fp32 zeros (2bit_asym)
+            rb = kv_row_bytes(kv_mode, self.hd)
+            shp = (L, self.max_seq, self.nkv)
+            self.k_cache = torch.zeros(shp + (rb,), dtype=torch.uint8, device=dev)
+            self.v_cache = torch.zeros(shp + (rb,), dtype=torch.uint8, device=dev)
+            self.k_scales = torch.zeros(shp, dtype=torch.float32, device=dev)
+            self.v_scales = torch.zeros(shp, dtype=torch.float32, device=dev)
+            asym = kv_mode == "2bit_asym"
+            self.k_zeros = torch.zeros(shp, dtype=torch.float32, device=dev) if asym else None
+            self.v_zeros = torch.zeros(shp, dtype=torch.float32, device=dev) if asym else None
         half = self.hd // 2
         # reference: 1 / theta ** (arange(0, half) / half), fp32
         self.inv_freq = 1.0 / (self.theta ** (torch.arange(0, half, dtype=torch.float32, device=dev) / half))
@@ -144,10 +165,14 @@ class PFlashDecoder:
         mask = torch.arange(T, device=self.device)[None, :] <= (start + torch.arange(S, device=self.device))[:, None]
 
         def attend(li, q, k, v):
-            self.k_cache[li, start:T] = k.to(self.k_cache.dtype)
-            self.v_cache[li, start:T] = v.to(self.v_cache.dtype)
-            K = self.k_cache[li, :T].float().permute(1, 0, 2)[None]  # [1, nkv, T, hd]
-            V = self.v_cache[li, :T].float().permute(1, 0, 2)[None]
+            if self.kv_mode == "fp32":
+                self.k_cache[li, start:T] = k.to(self.k_cache.dtype)
+                self.v_cache[li, start:T] = v.to(self.v_cache.dtype)
+                K = self.k_cache[li, :T].float().permute(1, 0, 2)[None]  # [1, nkv, T, hd]
+                V = self.v_cache[li, :T].float().permute(1, 0, 2)[None]
+            else:
+                K = self._kv_append(li, 0, k, start, T).permute(1, 0, 2)[None]
+                V = self._kv_append(li, 1, v, start, T).permute(1, 0, 2)[None]
             o = F.scaled_dot_product_attention(q.permute(1, 0, 2)[None], K, V, attn_mask=mask[None, None],
                                                enable_gqa=True)
             return o[0].permute(1, 0, 2).reshape(S, self.hidden)
@@ -160,6 +185,27 @@ class PFlashDecoder:
         self.length = T
         return self._head(self._rmsnorm(h, self.final_norm))
 
+    def _kv_rows(self, li: int, which: int):
+        if which == 0:
+            return self.k_cache[li], self.k_scales[li], None if self.k_zeros is None else self.k_zeros[li]
+        return self.v_cache[li], self.v_scales[li], None if self.v_zeros is None else self.v_zeros[li]
+
+    def _kv_append(self, li: int, which: int, x: torch.Tensor, start: int, T: int) -> torch.Tensor:
+        """Quantize rows x [S, nkv, hd] into cache positions start..T-1 and
+        return the dequantized rows 0..T-1 [T, nkv, hd] (fp32)."""
+        L = _lib.load()
+        st = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        m = KV_MODES[self.kv_mode]
+        codes, sc, zr = self._kv_rows(li, which)
+        x = x.float().contiguous()
+        S = T - start
+        _lib.check(L.pf_kv_quantize(_p(x), S * self.nkv, self.hd, m, _p(codes[start]), _p(sc[start]),
+                                    _p(None if zr is None else zr[start]), st), "pf_kv_quantize")
+        out = torch.empty(T, self.nkv, self.hd, dtype=torch.float32, device=self.device)
+        _lib.check(L.pf_kv_dequantize(_p(codes), _p(sc), _p(zr), T * self.nkv, self.hd, m, _p(out), st),
+                   "pf_kv_dequantize")
+        return out
+
     def _head(self, hn: torch.Tensor) -> torch.Tensor:
         """Dense lm_head in its own dtype, fp32 logits."""
         if self.lm_head.dtype == torch.float32:
@@ -168,7 +214,7 @@ class PFlashDecoder:
 
     # ---- batch-1 decode step as one CUDA graph -----------------------------
     def _step_body(self):
-        if self.k_cache.dtype != torch.float32:
+        if self.kv_mode == "fp32" and self.k_cache.dtype != torch.float32:
             return self._step_body_torch()
         L = _lib.load()
         st = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
@@ -181,12 +227,24 @@ class PFlashDecoder:
             _lib.check(L.pf_add_rmsnorm(_p(h), _p(delta), _p(ly.input_norm), _p(n), 1, H, self.eps, st),
                        "pf_add_rmsnorm")
             q, k, v = qlinear_multi([ly.q, ly.k, ly.v], n, ly.qkv_bias, workspace=self.ws1)
-            _lib.check(L.pf_rope_kv(_p(q), _p(k), _p(v), _p(self.k_cache[li]), _p(self.v_cache[li]), _p(self._pos),
-                                    _p(self.inv_freq), nh, nkv, hd, ms, st), "pf_rope_kv")
             attn = torch.empty(1, H, dtype=torch.float32, device=self.device)
-            _lib.check(L.pf_decode_attention(_p(q), _p(self.k_cache[li]), _p(self.v_cache[li]), _p(self._pos),
-                                             _p(attn), nh, nkv, hd, ms, scale, _p(self.attn_ws),
-                                             self.attn_ws.numel(), st), "pf_decode_attention")
+            if self.kv_mode == "fp32":
+                _lib.check(L.pf_rope_kv(_p(q), _p(k), _p(v), _p(self.k_cache[li]), _p(self.v_cache[li]),
+                                        _p(self._pos), _p(self.inv_freq), nh, nkv, hd, ms, st), "pf_rope_kv")
+                _lib.check(L.pf_decode_attention(_p(q), _p(self.k_cache[li]), _p(self.v_cache[li]), _p(self._pos),
+                                                 _p(attn), nh, nkv, hd, ms, scale, _p(self.attn_ws),
+                                                 self.attn_ws.numel(), st), "pf_decode_attention")
+            else:
+                m = KV_MODES[self.kv_mode]
+                kc, ks, kz = self._kv_rows(li, 0)
+                vc, vs, vz = self._kv_rows(li, 1)
+                _lib.check(L.pf_rope_kv_compressed(_p(q), _p(k), _p(v), _p(kc), _p(ks), _p(kz), _p(vc), _p(vs),
+                                                   _p(vz), _p(self._pos), _p(self.inv_freq), nh, nkv, hd, ms, m, st),
+                           "pf_rope_kv_compressed")
+                _lib.check(L.pf_decode_attention_compressed(_p(q), _p(kc), _p(ks), _p(kz), _p(vc), _p(vs), _p(vz),
+                                                            _p(self._pos), _p(attn), nh, nkv, hd, ms, m, scale,
+                                                            _p(self.attn_ws), self.attn_ws.numel(), st),
+                           "pf_decode_attention_compressed")
             o = qlinear(ly.o, attn, workspace=self.ws1)
             n2 = torch.empty_like(h)
             _lib.check(L.pf_add_rmsnorm(_p(h), _p(o), _p(ly.post_norm), _p(n2), 1, H, self.eps, st),

@@ -52,10 +52,14 @@ def build():
     return out
 
 
-def reference_forward(w, ids, caches, cfg=CFG):
+def reference_forward(w, ids, caches, cfg=CFG, kv_quant=None):
     """fp32 torch restatement of PFlashModelForCausalLM.forward
     (model_integration.py:240-254) on the decoded weights; `caches` is a list
-    of per-layer dicts (k, v: [1, T, heads, hd]) updated in place."""
+    of per-layer dicts (k, v: [1, T, heads, hd]) updated in place.
+    `kv_quant` (rows [..., hd] -> dequantized rows) stands for a compressed
+    KV cache: the new keys (after RoPE) and values pass through it before
+    they are cached, as CompressedKVCache.update quantizes each appended row
+    and attends over the dequantized context."""
     import math
 
     import torch.nn.functional as F
@@ -86,6 +90,8 @@ def reference_forward(w, ids, caches, cfg=CFG):
         c = caches[li]
         off = c["k"].shape[1] if "k" in c else 0
         q, k = rope(q, S, off), rope(k, S, off)
+        if kv_quant is not None:
+            k, v = kv_quant(k), kv_quant(v)
         if "k" in c:
             k, v = torch.cat([c["k"], k], 1), torch.cat([c["v"], v], 1)
         c["k"], c["v"] = k, v

@@ -35,7 +35,7 @@ def test_restatement_matches_reference_logits():
         assert _rel(lg, g["step_logits"][i]) < 1e-5
 
 
-def _decoder(w, max_seq=32):
+def _decoder(w, max_seq=32, kv_mode="fp32"):
     from polarflash_b200.decode import DecoderLayer, PFlashDecoder
     from polarflash_b200.hadamard import column_signs, effective_block
     from polarflash_b200.qweight import QWeight
@@ -52,7 +52,8 @@ def _decoder(w, max_seq=32):
                                effective_block(128, K), column_signs(K, 128, dev))
         layers.append(DecoderLayer(qw["q"], qw["k"], qw["v"], qw["o"], qw["gate"], qw["up"], qw["down"],
                                    t(ly["in_norm"]), t(ly["post_norm"])))
-    return PFlashDecoder(dm.CFG, layers, t(w["embed"]), t(w["final_norm"]), t(w["lm_head"]), max_seq)
+    return PFlashDecoder(dm.CFG, layers, t(w["embed"]), t(w["final_norm"]), t(w["lm_head"]), max_seq,
+                         kv_mode=kv_mode)
 
 
 @pytest.mark.gpu
