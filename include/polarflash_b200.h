@@ -208,8 +208,9 @@ PF_API int pf_rope_kv(float* q, const float* k, const float* v, float* k_cache, 
                       int max_seq, void* stream);
 /* pf_decode_attention: out [n_heads][head_dim] = softmax(q k^T * scale) v over
  * positions 0..*pos of the caches, query head h reading KV head
- * h / (n_heads / n_kv_heads); head_dim <= 128, at most 8 query heads per KV
- * head, max_seq <= 32768.  The positions are split into chunks of 64 whose
+ * h / (n_heads / n_kv_heads); head_dim a multiple of 4 and <= 128, at most
+ * 8 query heads per KV head, max_seq <= 32768; the caches 16-byte aligned
+ * (rows are read as float4).  The positions are split into chunks of 64 whose
  * partial results go to `workspace` (device, at least
  * pf_decode_attention_workspace_size bytes) and are merged by a second
  * launch.  Replaces the GQA attention of PFlashAttentionBlock.forward
@@ -260,7 +261,8 @@ PF_API int pf_rope_kv_compressed(float* q, const float* k, const float* v, void*
 /* pf_decode_attention_compressed: pf_decode_attention over compressed caches
  * laid out as pf_rope_kv_compressed writes them, each K and V value
  * dequantized inside the attention kernel (the reference dequantizes the
- * whole cache, compressed_kv.py:173-226, and attends over the result). */
+ * whole cache, compressed_kv.py:173-226, and attends over the result).
+ * Same shape limits as pf_decode_attention; int8 codes 4-byte aligned. */
 PF_API int pf_decode_attention_compressed(const float* q, const void* k_codes, const float* k_scales,
                                           const float* k_zeros, const void* v_codes, const float* v_scales,
                                           const float* v_zeros, const long long* pos, float* out, int n_heads,

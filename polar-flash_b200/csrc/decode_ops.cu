@@ -56,6 +56,14 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
   for (int i = threadIdx.x; i < H; i += blockDim.x) out[(size_t)blockIdx.x * H + i] = hr[i] * r * w[i];
 }
 
+// The pair (x1, x2) rotated by the angle with cosine c and sine s, each
+// product and sum rounded on its own (as the reference's separate tensor
+// ops round them; no fma contraction, so every kernel rotates alike).
+__device__ __forceinline__ void rope_pair(float x1, float x2, float c, float s, float& o1, float& o2) {
+  o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+  o2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+}
+
 // Blocks 0..nh-1 rotate q's heads in place; blocks nh..nh+nkv-1 rotate k's
 // heads into the key cache at position *pos and copy v's heads into the value
 // cache there.  Thread i handles the pair (i, i + hd/2): angle pos * inv_freq[i].
@@ -72,16 +80,13 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
   const int head = blockIdx.x;
   if (head < nh) {
     float* x = q + (size_t)head * hd;
-    const float x1 = x[i], x2 = x[i + half];
-    x[i] = x1 * c - x2 * s;
-    x[i + half] = x1 * s + x2 * c;
+    rope_pair(x[i], x[i + half], c, s, x[i], x[i + half]);
   } else {
     const int kh = head - nh;
     const float* x = k + (size_t)kh * hd;
     const float x1 = x[i], x2 = x[i + half];
     float* kd = kc + ((size_t)p * nkv + kh) * hd;
-    kd[i] = x1 * c - x2 * s;
-    kd[i + half] = x1 * s + x2 * c;
+    rope_pair(x1, x2, c, s, kd[i], kd[i + half]);
     float* vd = vc + ((size_t)p * nkv + kh) * hd;
     const float* vs = v + (size_t)kh * hd;
     vd[i] = vs[i];
@@ -232,9 +237,7 @@ __global__ void rope_kvq_kernel(float* __restrict__ q, const float* __restrict__
       const float f = (float)p * inv_freq[i];
       const float c = cosf(f), s = sinf(f);
       float* x = q + (size_t)head * hd;
-      const float x1 = x[i], x2 = x[i + half];
-      x[i] = x1 * c - x2 * s;
-      x[i + half] = x1 * s + x2 * c;
+      rope_pair(x[i], x[i + half], c, s, x[i], x[i + half]);
     }
     return;  // block-uniform
   }
@@ -243,9 +246,7 @@ __global__ void rope_kvq_kernel(float* __restrict__ q, const float* __restrict__
     const float f = (float)p * inv_freq[i];
     const float c = cosf(f), s = sinf(f);
     const float* x = k + (size_t)kh * hd;
-    const float x1 = x[i], x2 = x[i + half];
-    xs[0][i] = x1 * c - x2 * s;
-    xs[0][i + half] = x1 * s + x2 * c;
+    rope_pair(x[i], x[i + half], c, s, xs[0][i], xs[0][i + half]);
     xs[1][i] = v[(size_t)kh * hd + i];
     xs[1][i + half] = v[(size_t)kh * hd + i + half];
   }
@@ -258,12 +259,18 @@ __global__ void rope_kvq_kernel(float* __restrict__ q, const float* __restrict__
 
 // Attention of one new token over positions 0..*pos of the cache, split over
 // chunks of kAttnChunk positions (flash decoding).  attn_chunk_kernel: one
-// block per (KV head, chunk) serves the KV head's G query heads: scores with
-// one warp per position (eight positions per warp in flight), the chunk's
-// softmax statistics, and the value sum with threads over head dimensions;
-// it stores per query head (max, sum of exponentials, unnormalised output).
-// Chunks past *pos store an empty entry.  attn_combine_kernel merges a head's
-// chunks: out = sum_c e^(m_c - m) o_c / sum_c e^(m_c - m) l_c.
+// block per (KV head, chunk) serves the KV head's G query heads.  Each cache
+// row (one position of one KV head) is read as vectors, four consecutive
+// head dimensions per thread: a float4 of the fp32 cache, one 32-bit word of
+// int8 codes or one byte of 2-bit codes, with the row's scale (and zero)
+// loaded once.  Scores: one warp per position, eight positions per warp in
+// flight; then the chunk's softmax statistics; then the value sums, thread
+// groups of head_dim / 4 threads over the chunk's positions (all of a
+// thread's positions loaded in one batch), merged across groups in shared
+// memory.  It stores per query head (max, sum of exponentials, unnormalised
+// output); chunks past *pos store an empty entry (never read).
+// attn_combine_kernel merges a head's chunks:
+// out = sum_c e^(m_c - m) o_c / sum_c e^(m_c - m) l_c.
 constexpr int kAttnChunk = 64;
 constexpr int kAttnG = 8;  // query heads per KV head handled by one block
 
@@ -275,22 +282,43 @@ struct KvView {
   const float* zeros;
 };
 
+// Values d0..d0+3 of row r (d0 a multiple of 4, head_dim a multiple of 4).
 template <int MODE>
-__device__ __forceinline__ float kv_load(const KvView& c, size_t r, int d, int hd) {
-  if (MODE == PF_KV_FP32) return static_cast<const float*>(c.codes)[r * hd + d];
-  return kv_value<MODE>(static_cast<const uint8_t*>(c.codes) + r * kv_row_bytes(MODE, hd), d, c.scales[r],
-                        MODE == PF_KV_2BIT_ASYM ? c.zeros[r] : 0.f);
+__device__ __forceinline__ void kv_load4(const KvView& c, size_t r, int d0, int hd, float v[4]) {
+  if (MODE == PF_KV_FP32) {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(c.codes) + r * hd + d0));
+    v[0] = x.x;
+    v[1] = x.y;
+    v[2] = x.z;
+    v[3] = x.w;
+    return;
+  }
+  const uint8_t* row = static_cast<const uint8_t*>(c.codes) + r * kv_row_bytes(MODE, hd);
+  const float s = __ldg(c.scales + r);
+  if (MODE == PF_KV_INT8) {
+    const unsigned w = __ldg(reinterpret_cast<const unsigned*>(row + d0));  // bytes d0..d0+3, d0 lowest
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __fmul_rn((float)(int)(signed char)((w >> (8 * i)) & 0xffu), s);
+    return;
+  }
+  const float z = MODE == PF_KV_2BIT_ASYM ? __ldg(c.zeros + r) : 0.f;
+  const unsigned b = __ldg(row + (d0 >> 2));  // codes of d0..d0+3, d0 in the top bits
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float cv = (float)((b >> (6 - 2 * i)) & 3u);
+    v[i] = MODE == PF_KV_2BIT ? __fmul_rn(__fsub_rn(cv, 1.5f), s) : __fadd_rn(__fmul_rn(cv, s), z);
+  }
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* __restrict__ q, KvView kc, KvView vc,
-                                                                  const long long* __restrict__ pos,
-                                                                  float* __restrict__ part, int nh, int nkv, int hd,
-                                                                  int max_seq, int nchunk, float scale) {
-  __shared__ float qs[kAttnG][128];
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_chunk_kernel(const float* __restrict__ q, KvView kc,
+                                                                     KvView vc, const long long* __restrict__ pos,
+                                                                     float* __restrict__ part, int nh, int nkv,
+                                                                     int hd, int max_seq, int nchunk, float scale) {
+  __shared__ __align__(16) float qs[kAttnG][128];
   __shared__ float sc[kAttnG][kAttnChunk];
   __shared__ float mx[kAttnG], sm[kAttnG];
-  __shared__ float po[2][kAttnG][128];
+  __shared__ float po[kAttnG * 1024];  // [group][g][hd]: groups x head_dim <= 1024
   const int kvh = blockIdx.x, chunk = blockIdx.y, G = nh / nkv;
   pdl_enter();
   const long long p = *pos;
@@ -308,27 +336,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
   for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i / hd][i % hd] = q[(size_t)(kvh * G + i / hd) * hd + i % hd];
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int d0 = 4 * lane;
+  const bool act = d0 < hd;
   // scores: warp w takes positions t0 + w, t0 + w + nw, ... (eight at a time)
   for (int j0 = warp; j0 < n; j0 += 8 * nw) {
     float kv[8][4];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int j = j0 + u * nw;
+      if (act && j < n) {
+        kv_load4<MODE>(kc, (size_t)(t0 + j) * nkv + kvh, d0, hd, kv[u]);
+      } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = lane + 32 * e;
-        kv[u][e] = (j < n && d < hd) ? kv_load<MODE>(kc, (size_t)(t0 + j) * nkv + kvh, d, hd) : 0.f;
+        for (int i = 0; i < 4; ++i) kv[u][i] = 0.f;
       }
     }
     for (int g = 0; g < G; ++g) {
+      const float4 qv = act ? *reinterpret_cast<const float4*>(&qs[g][d0]) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        float dot = 0.f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = lane + 32 * e;
-          if (d < hd) dot += qs[g][d] * kv[u][e];
-        }
+        float dot = qv.x * kv[u][0] + qv.y * kv[u][1] + qv.z * kv[u][2] + qv.w * kv[u][3];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
         const int j = j0 + u * nw;
@@ -357,27 +384,58 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
     }
   }
   __syncthreads();
-  // values: thread (half, d) sums positions of parity `half`, for every query head
-  const int d = threadIdx.x % hd, half = threadIdx.x / hd;
-  if (half < 2) {
-    float acc[kAttnG];
-#pragma unroll
-    for (int g = 0; g < kAttnG; ++g) acc[g] = 0.f;
-    for (int j = half; j < n; j += 2) {
-      const float val = kv_load<MODE>(vc, (size_t)(t0 + j) * nkv + kvh, d, hd);
-#pragma unroll
-      for (int g = 0; g < kAttnG; ++g)
-        if (g < G) acc[g] += sc[g][j] * val;
-    }
+  // values: group gi (head_dim / 4 threads, thread li holds dimensions
+  // 4 li .. 4 li + 3) sums positions gi, gi + ngr, ... for every query head
+  const int tpr = hd >> 2, ngr = blockDim.x / tpr;
+  const int gi = threadIdx.x / tpr, e0 = 4 * (threadIdx.x % tpr);
+  if (gi < ngr) {
+    float acc[kAttnG][4];
 #pragma unroll
     for (int g = 0; g < kAttnG; ++g)
-      if (g < G) po[half][g][d] = acc[g];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[g][i] = 0.f;
+    for (int jb = gi; jb < n; jb += 8 * ngr) {
+      float val[8][4];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = jb + u * ngr;
+        if (j < n) {
+          kv_load4<MODE>(vc, (size_t)(t0 + j) * nkv + kvh, e0, hd, val[u]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) val[u][i] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = jb + u * ngr;
+        if (j < n) {
+#pragma unroll
+          for (int g = 0; g < kAttnG; ++g) {
+            if (g < G) {
+              const float w = sc[g][j];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) acc[g][i] += w * val[u][i];
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kAttnG; ++g) {
+      if (g < G) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) po[(gi * G + g) * hd + e0 + i] = acc[g][i];
+      }
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
     const int g = i / hd, e = i % hd;
+    float o = 0.f;
+    for (int k = 0; k < ngr; ++k) o += po[(k * G + g) * hd + e];
     float* r = part + ((size_t)(kvh * G + g) * nchunk + chunk) * rec;
-    r[2 + e] = po[0][g][e] + po[1][g][e];
+    r[2 + e] = o;
     if (e == 0) {
       r[0] = mx[g];
       r[1] = sm[g];
@@ -385,23 +443,54 @@ __global__ void __launch_bounds__(kAttnThreads) attn_chunk_kernel(const float* _
   }
 }
 
-__global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out, int hd, int nchunk) {
+// Only the chunks that hold positions (all non-empty) are read; warps take
+// chunks in turn (w, w + 8, ...) with lanes over head dimensions, and the
+// eight warp partials are summed in shared memory.
+constexpr int kCombThreads = 256;
+
+__global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const float* __restrict__ part,
+                                                                    const long long* __restrict__ pos,
+                                                                    float* __restrict__ out, int hd, int nchunk,
+                                                                    int max_seq) {
+  __shared__ float so[kCombThreads / 32][128];
+  __shared__ float sl[kCombThreads / 32];
+  __shared__ float red[kCombThreads / 32];
   const int head = blockIdx.x, rec = hd + 2;
   pdl_enter();
+  const long long p = *pos;
+  const int T = (p < 0) ? 0 : (p >= max_seq ? max_seq : (int)p + 1);
+  const int nc = min(nchunk, (T + kAttnChunk - 1) / kAttnChunk);
   const float* base = part + (size_t)head * nchunk * rec;
   float m = -INFINITY;
-  for (int c = 0; c < nchunk; ++c) m = fmaxf(m, base[(size_t)c * rec]);
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float o = 0.f, l = 0.f;
-    for (int c = 0; c < nchunk; ++c) {
-      const float* r = base + (size_t)c * rec;
-      if (r[1] > 0.f) {
-        const float w = expf(r[0] - m);
-        o += w * r[2 + d];
-        l += w * r[1];
-      }
+  for (int c = threadIdx.x; c < nc; c += blockDim.x) m = fmaxf(m, base[(size_t)c * rec]);
+  m = block_minmax<false>(m, red);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float o[4] = {0.f, 0.f, 0.f, 0.f}, l = 0.f;
+#pragma unroll 4
+  for (int c = warp; c < nc; c += nw) {
+    const float* r = base + (size_t)c * rec;
+    const float w = expf(r[0] - m);
+    l += w * r[1];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = lane + 32 * e;
+      if (d < hd) o[e] += w * r[2 + d];
     }
-    out[(size_t)head * hd + d] = l > 0.f ? o / l : 0.f;
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int d = lane + 32 * e;
+    if (d < hd) so[warp][d] = o[e];
+  }
+  if (lane == 0) sl[warp] = l;
+  __syncthreads();
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float a = 0.f, b = 0.f;
+    for (int w = 0; w < nw; ++w) {
+      a += so[w][d];
+      b += sl[w];
+    }
+    out[(size_t)head * hd + d] = b > 0.f ? a / b : 0.f;
   }
 }
 
@@ -473,9 +562,12 @@ int decode_attention(int mode, const float* q, KvView kc, KvView vc, const long 
                      int n_kv_heads, int head_dim, int max_seq, float scale, void* workspace, size_t workspace_bytes,
                      void* stream) {
   if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || n_heads / n_kv_heads > kAttnG || head_dim <= 0 ||
-      head_dim > 128 || max_seq <= 0 || max_seq > kDecodeMaxSeq)
+      head_dim > 128 || (head_dim & 3) || max_seq <= 0 || max_seq > kDecodeMaxSeq)
     return PF_ERR_SHAPE;
   if (!al4(q) || !al4(out) || !al4(workspace) || (reinterpret_cast<uintptr_t>(pos) & 7u)) return PF_ERR_ALIGNMENT;
+  // rows are read as float4 (fp32 cache) or 32-bit words (int8 codes)
+  const uintptr_t need = mode == PF_KV_FP32 ? 15u : mode == PF_KV_INT8 ? 3u : 0u;
+  if ((reinterpret_cast<uintptr_t>(kc.codes) | reinterpret_cast<uintptr_t>(vc.codes)) & need) return PF_ERR_ALIGNMENT;
   if (workspace_bytes < pf_decode_attention_workspace_size(n_heads, head_dim, max_seq)) return PF_ERR_WORKSPACE;
   const int nchunk = (max_seq + kAttnChunk - 1) / kAttnChunk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -500,7 +592,8 @@ int decode_attention(int mode, const float* q, KvView kc, KvView vc, const long 
                      n_kv_heads, head_dim, max_seq, nchunk, scale);
   }
   if (e != cudaSuccess) return PF_ERR_CUDA;
-  return status_of(launch_pdl(attn_combine_kernel, dim3(n_heads), 128, s, (const float*)part, out, head_dim, nchunk));
+  return status_of(launch_pdl(attn_combine_kernel, dim3(n_heads), kCombThreads, s, (const float*)part, pos, out,
+                              head_dim, nchunk, max_seq));
 }
 
 }  // namespace
