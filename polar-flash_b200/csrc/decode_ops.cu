@@ -282,31 +282,56 @@ struct KvView {
   const float* zeros;
 };
 
-// Values d0..d0+3 of row r (d0 a multiple of 4, head_dim a multiple of 4).
+// Values d0..d0+3 of row r (d0 and head_dim multiples of 4) in two steps:
+// kv_fetch issues the loads (a float4 of the fp32 cache; one 32-bit word of
+// int8 codes or one byte of 2-bit codes, with the row's scale and zero),
+// kv_decode does the arithmetic.  Loops fetch all their rows first and decode
+// afterwards, so the loads of every row are in flight together; rows outside
+// the chunk are zero-filled, which decodes to zeros in every mode.
+struct KvRaw {
+  float4 f;    // fp32 values
+  unsigned w;  // int8 codes (d0 in the low byte) or the 2-bit code byte
+  float s, z;  // scale, zero
+};
+
 template <int MODE>
-__device__ __forceinline__ void kv_load4(const KvView& c, size_t r, int d0, int hd, float v[4]) {
+__device__ __forceinline__ void kv_fetch(const KvView& c, size_t r, int d0, int hd, KvRaw& x) {
   if (MODE == PF_KV_FP32) {
-    const float4 x = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(c.codes) + r * hd + d0));
-    v[0] = x.x;
-    v[1] = x.y;
-    v[2] = x.z;
-    v[3] = x.w;
+    x.f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(c.codes) + r * hd + d0));
     return;
   }
   const uint8_t* row = static_cast<const uint8_t*>(c.codes) + r * kv_row_bytes(MODE, hd);
-  const float s = __ldg(c.scales + r);
-  if (MODE == PF_KV_INT8) {
-    const unsigned w = __ldg(reinterpret_cast<const unsigned*>(row + d0));  // bytes d0..d0+3, d0 lowest
+  x.s = __ldg(c.scales + r);
+  if (MODE == PF_KV_2BIT_ASYM) x.z = __ldg(c.zeros + r);
+  if (MODE == PF_KV_INT8)
+    x.w = __ldg(reinterpret_cast<const unsigned*>(row + d0));
+  else
+    x.w = __ldg(row + (d0 >> 2));
+}
+
+__device__ __forceinline__ void kv_zero(KvRaw& x) {
+  x.f = make_float4(0.f, 0.f, 0.f, 0.f);
+  x.w = 0u;
+  x.s = 0.f;
+  x.z = 0.f;
+}
+
+template <int MODE>
+__device__ __forceinline__ void kv_decode(const KvRaw& x, float v[4]) {
+  if (MODE == PF_KV_FP32) {
+    v[0] = x.f.x;
+    v[1] = x.f.y;
+    v[2] = x.f.z;
+    v[3] = x.f.w;
+  } else if (MODE == PF_KV_INT8) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = __fmul_rn((float)(int)(signed char)((w >> (8 * i)) & 0xffu), s);
-    return;
-  }
-  const float z = MODE == PF_KV_2BIT_ASYM ? __ldg(c.zeros + r) : 0.f;
-  const unsigned b = __ldg(row + (d0 >> 2));  // codes of d0..d0+3, d0 in the top bits
+    for (int i = 0; i < 4; ++i) v[i] = __fmul_rn((float)(int)(signed char)((x.w >> (8 * i)) & 0xffu), x.s);
+  } else {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float cv = (float)((b >> (6 - 2 * i)) & 3u);
-    v[i] = MODE == PF_KV_2BIT ? __fmul_rn(__fsub_rn(cv, 1.5f), s) : __fadd_rn(__fmul_rn(cv, s), z);
+    for (int i = 0; i < 4; ++i) {
+      const float cv = (float)((x.w >> (6 - 2 * i)) & 3u);
+      v[i] = MODE == PF_KV_2BIT ? __fmul_rn(__fsub_rn(cv, 1.5f), x.s) : __fadd_rn(__fmul_rn(cv, x.s), x.z);
+    }
   }
 }
 
@@ -341,15 +366,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_chunk_kernel(const float
   // scores: warp w takes positions t0 + w, t0 + w + nw, ... (eight at a time)
   for (int j0 = warp; j0 < n; j0 += 8 * nw) {
     float kv[8][4];
+    {
+      KvRaw raw[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int j = j0 + u * nw;
-      if (act && j < n) {
-        kv_load4<MODE>(kc, (size_t)(t0 + j) * nkv + kvh, d0, hd, kv[u]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) kv[u][i] = 0.f;
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u * nw;
+        kv_zero(raw[u]);
+        if (act && j < n) kv_fetch<MODE>(kc, (size_t)(t0 + j) * nkv + kvh, d0, hd, raw[u]);
       }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) kv_decode<MODE>(raw[u], kv[u]);
     }
     for (int g = 0; g < G; ++g) {
       const float4 qv = act ? *reinterpret_cast<const float4*>(&qs[g][d0]) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -396,15 +422,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_chunk_kernel(const float
       for (int i = 0; i < 4; ++i) acc[g][i] = 0.f;
     for (int jb = gi; jb < n; jb += 8 * ngr) {
       float val[8][4];
+      {
+        KvRaw raw[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = jb + u * ngr;
-        if (j < n) {
-          kv_load4<MODE>(vc, (size_t)(t0 + j) * nkv + kvh, e0, hd, val[u]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) val[u][i] = 0.f;
+        for (int u = 0; u < 8; ++u) {
+          const int j = jb + u * ngr;
+          kv_zero(raw[u]);
+          if (j < n) kv_fetch<MODE>(vc, (size_t)(t0 + j) * nkv + kvh, e0, hd, raw[u]);
         }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) kv_decode<MODE>(raw[u], val[u]);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {

@@ -2,6 +2,13 @@
 used for single-kernel ncu captures of the library's kernels.
 
     python polar-flash_b200/profile_case.py --fmt int3_g128 --M 14336 --K 4096 --N 1 --iters 3
+
+With --attention, the decode attention over a KV cache instead: one new
+token, 32 query / 8 KV heads of 128 (Llama-3-8B), --ctx cached positions of
+random rows, for each listed cache mode (fp32 through pf_decode_attention,
+int8 / 2bit / 2bit_asym through pf_decode_attention_compressed):
+
+    python polar-flash_b200/profile_case.py --attention fp32,int8,2bit --ctx 16384 --iters 1
 """
 import argparse
 import os
@@ -24,7 +31,11 @@ def main():
     ap.add_argument("--time", action="store_true", help="report device time per call (CUDA events)")
     ap.add_argument("--copies", type=int, default=1,
                     help="resident copies of the weight cycled by the timed calls (more than L2 holds: 126 MB)")
+    ap.add_argument("--attention", default=None, help="comma-separated KV cache modes: run decode attention")
+    ap.add_argument("--ctx", type=int, default=16384, help="cached positions (--attention)")
     a = ap.parse_args()
+    if a.attention:
+        return attention_case(a)
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
     W = torch.randn(a.M, a.K, generator=g, device=dev) * 0.02
@@ -55,6 +66,63 @@ def main():
         us = e0.elapsed_time(e1) * 1e3 / reps
         flops = 2.0 * a.M * a.K * a.N
         print(f"time {us:.1f} us  {flops / us / 1e6:.1f} TFLOP/s  {qw.nbytes() / us / 1e3:.1f} GB/s packed")
+
+
+def attention_case(a):
+    import ctypes
+    import math
+
+    from polarflash_b200 import _lib
+    from polarflash_b200.kv_cache import KV_MODES, kv_row_bytes
+
+    L = _lib.load()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    nh, nkv, hd, ms = 32, 8, 128, a.ctx
+    p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    q = torch.randn(nh * hd, generator=g, device=dev)
+    out = torch.empty(nh * hd, device=dev)
+    pos = torch.tensor([ms - 1], dtype=torch.long, device=dev)
+    aws = torch.empty(int(L.pf_decode_attention_workspace_size(nh, hd, ms)), dtype=torch.uint8, device=dev)
+    for mode in a.attention.split(","):
+        rb = 4 * hd if mode == "fp32" else kv_row_bytes(mode, hd)
+
+        def rows():
+            if mode == "fp32":
+                return torch.randn(ms, nkv, hd, generator=g, device=dev).view(torch.uint8)
+            return torch.randint(0, 256, (ms, nkv, rb), generator=g, device=dev, dtype=torch.uint8)
+
+        layers = [(rows(), rows(), torch.rand(2, ms, nkv, generator=g, device=dev) * 0.01,
+                   torch.rand(2, ms, nkv, generator=g, device=dev) if mode == "2bit_asym" else None)
+                  for _ in range(max(1, a.copies))]
+
+        def call(i):
+            kc, vc, sc, zr = layers[i % len(layers)]
+            if mode == "fp32":
+                _lib.check(L.pf_decode_attention(p(q), p(kc), p(vc), p(pos), p(out), nh, nkv, hd, ms,
+                                                 1.0 / math.sqrt(hd), p(aws), aws.numel(), st))
+            else:
+                _lib.check(L.pf_decode_attention_compressed(
+                    p(q), p(kc), p(sc[0]), p(zr[0] if zr is not None else None), p(vc), p(sc[1]),
+                    p(zr[1] if zr is not None else None), p(pos), p(out), nh, nkv, hd, ms, KV_MODES[mode],
+                    1.0 / math.sqrt(hd), p(aws), aws.numel(), st))
+
+        for i in range(a.iters):
+            call(i)
+        torch.cuda.synchronize()
+        print(f"attention {mode} ctx {ms}: out[:4] = {out[:4].tolist()}")
+        if a.time:
+            reps = max(20, a.iters)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(reps):
+                call(i)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            nb = 2 * ms * nkv * (rb + (0 if mode == "fp32" else 4) + (4 if mode == "2bit_asym" else 0))
+            print(f"time {us:.1f} us  {nb / us / 1e3:.1f} GB/s of cache rows")
 
 
 if __name__ == "__main__":
