@@ -71,6 +71,19 @@ def test_mirror_bookkeeping():
     assert okv.window_indices(20, 12, 4) == [0, 1, 2, 3] + list(range(12, 20))
 
 
+def test_no_cpu_path():
+    """The mirror refuses host tensors instead of quantizing on the CPU, and
+    the decoder refuses an unknown cache mode before allocating anything."""
+    from polarflash_b200.decode import PFlashDecoder
+    from polarflash_b200.kv_cache import CompressedKVCache
+
+    c = CompressedKVCache(num_layers=1, num_kv_heads=2, head_dim=8, mode="int8")
+    with pytest.raises(RuntimeError, match="CUDA"):
+        c.update(0, torch.zeros(1, 2, 3, 8), torch.zeros(1, 2, 3, 8))
+    with pytest.raises(ValueError, match="kv_mode"):
+        PFlashDecoder(dm.CFG, [], torch.zeros(4, 256), torch.ones(256), torch.zeros(4, 256), 8, kv_mode="int4")
+
+
 def test_restatement_hook_is_identity_for_fp32():
     """decode_model.reference_forward with an identity KV hook reproduces its
     own uncompressed logits (the hook only touches the cached rows)."""
