@@ -264,11 +264,12 @@ __global__ void rope_kvq_kernel(float* __restrict__ q, const float* __restrict__
 // head dimensions per thread: a float4 of the fp32 cache, one 32-bit word of
 // int8 codes or one byte of 2-bit codes, with the row's scale (and zero)
 // loaded once.  Scores: one warp per position, eight positions per warp in
-// flight; then the chunk's softmax statistics; then the value sums, thread
-// groups of head_dim / 4 threads over the chunk's positions (all of a
-// thread's positions loaded in one batch), merged across groups in shared
-// memory.  It stores per query head (max, sum of exponentials, unnormalised
-// output); chunks past *pos store an empty entry (never read).
+// flight, their dot products reduced over the warp together; then the
+// chunk's softmax statistics; then the value sums, thread groups of
+// head_dim / 4 threads over the chunk's positions (all of a thread's
+// positions loaded in one batch), merged across groups in shared memory.
+// It stores per query head (max, sum of exponentials, unnormalised output);
+// chunks past *pos store an empty entry (never read).
 // attn_combine_kernel merges a head's chunks:
 // out = sum_c e^(m_c - m) o_c / sum_c e^(m_c - m) l_c.
 constexpr int kAttnChunk = 64;
@@ -379,14 +380,36 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_chunk_kernel(const float
     }
     for (int g = 0; g < G; ++g) {
       const float4 qv = act ? *reinterpret_cast<const float4*>(&qs[g][d0]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float a[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float dot = qv.x * kv[u][0] + qv.y * kv[u][1] + qv.z * kv[u][2] + qv.w * kv[u][3];
+      for (int u = 0; u < 8; ++u) a[u] = qv.x * kv[u][0] + qv.y * kv[u][1] + qv.z * kv[u][2] + qv.w * kv[u][3];
+      // Transpose-reduce the eight dot products over the warp (9 shuffles,
+      // not 40): at the xor-16, 8 and 4 steps each lane keeps half of its
+      // partial sums (the upper half when its lane bit is set) and adds the
+      // partner's copy of that half, so lane l ends with a partial sum of
+      // position u = (l >> 2) & 7; the xor-2 and 1 steps complete it.
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        const int j = j0 + u * nw;
-        if (lane == 0 && j < n) sc[g][j] = dot * scale;
+      for (int i = 0; i < 4; ++i) {
+        const bool up = lane & 16;
+        const float send = up ? a[i] : a[i + 4], keep = up ? a[i + 4] : a[i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
       }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const bool up = lane & 8;
+        const float send = up ? a[i] : a[i + 2], keep = up ? a[i + 2] : a[i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      {
+        const bool up = lane & 4;
+        const float send = up ? a[0] : a[1], keep = up ? a[1] : a[0];
+        a[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      float dot = a[0];
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      const int j = j0 + ((lane >> 2) & 7) * nw;
+      if ((lane & 3) == 0 && j < n) sc[g][j] = dot * scale;
     }
   }
   __syncthreads();
