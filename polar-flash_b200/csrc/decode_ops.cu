@@ -337,7 +337,7 @@ __device__ __forceinline__ void kv_decode(const KvRaw& x, float v[4]) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kAttnThreads, 2) attn_chunk_kernel(const float* __restrict__ q, KvView kc,
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_chunk_kernel(const float* __restrict__ q, KvView kc,
                                                                      KvView vc, const long long* __restrict__ pos,
                                                                      float* __restrict__ part, int nh, int nkv,
                                                                      int hd, int max_seq, int nchunk, float scale) {
