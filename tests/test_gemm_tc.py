@@ -4,7 +4,6 @@ double-accumulated matmul, normwise within 1e-3 (the GEMM multiplies fp16
 dequantised weights by fp16 x' scaled per token, accumulating in fp32).
 Cases cover partial 128-row and 128-token tiles, several token chunks,
 rotation blocks 128 and 512, every x dtype, and bias."""
-import numpy as np
 import pytest
 import torch
 

@@ -11,7 +11,6 @@ timeout so that a rank that fails ends the other's collective with an error.
 import os
 import socket
 
-import numpy as np
 import pytest
 import torch
 import torch.multiprocessing as mp
