@@ -587,7 +587,10 @@ def main():
 
     decode = None
     if world == 1 and not args.no_decode and N == 1:
-        decode = decode_rates(copies, xs, outs, ws, stream, dev, layers=32)
+        try:
+            decode = decode_rates(copies, xs, outs, ws, stream, dev, layers=32)
+        except Exception as e:  # the decode extras never cost the headline line
+            decode = {"error": f"{type(e).__name__}: {e}"[:300]}
         decode["what"] = ("linears of one decode step: Llama-3-8B shape (32 layers x q|k|v, o, gate|up, down) at "
                           "batch 1 for INT3 / INT2 / polar 1.75, Llama-3-70B shape (80 layers, E8 RVQ2) at batch 1 "
                           "and 32; one resident weight copy per layer, CUDA-graph replays; attention, norms and "
