@@ -85,3 +85,52 @@ def test_python_status_mapping():
     with pytest.raises(RuntimeError):
         _lib.check(_lib.ERR_CUDA)
     _lib.check(_lib.OK)
+
+
+def test_kv_cache_entry_points_validate_without_gpu():
+    """Compressed KV cache and decode attention: argument errors are answered
+    on the host before any launch.  The addresses are fake, so every call here
+    either fails validation or has no rows to process: none may launch."""
+    L = _lib.load()
+    P = ctypes.c_void_p
+    A = P(0x100000)  # 256-byte aligned stand-in address
+    INT8, TWO, ASYM = 1, 2, 3
+    launches = L.pf_kernel_launches()
+    assert [L.pf_kv_row_bytes(m, d) for m, d in ((1, 128), (2, 130), (3, 8), (0, 16), (4, 8), (1, 0))] == \
+        [128, 33, 2, 64, 0, 0]
+    q = L.pf_kv_quantize
+    assert q(None, 4, 64, INT8, A, A, None, None) == _lib.ERR_INVALID_ARGUMENT
+    assert q(A, 4, 64, 0, A, A, None, None) == _lib.ERR_INVALID_ARGUMENT        # fp32 is not a quantizer mode
+    assert q(A, 4, 64, ASYM, A, A, None, None) == _lib.ERR_INVALID_ARGUMENT     # 2bit_asym needs zeros
+    assert q(A, 4, 0, TWO, A, A, None, None) == _lib.ERR_SHAPE
+    assert q(P(0x100001), 4, 64, INT8, A, A, None, None) == _lib.ERR_ALIGNMENT
+    assert q(A, 0, 64, INT8, A, A, None, None) == _lib.OK                       # nothing to do, nothing launched
+    dq = L.pf_kv_dequantize
+    assert dq(A, A, None, 4, 64, ASYM, A, None) == _lib.ERR_INVALID_ARGUMENT
+    assert dq(A, P(0x100002), None, 4, 64, INT8, A, None) == _lib.ERR_ALIGNMENT
+    assert dq(A, A, None, 0, 64, TWO, A, None) == _lib.OK
+    r = L.pf_rope_kv_compressed
+    args = lambda hd, mode, pos=A: (A, A, A, A, A, A, A, A, A, pos, A, 8, 2, hd, 64, mode, None)  # noqa: E731
+    assert r(*args(128, 9)) == _lib.ERR_INVALID_ARGUMENT
+    assert r(*args(127, INT8)) == _lib.ERR_SHAPE                                # odd head_dim
+    assert r(*args(4096, INT8)) == _lib.ERR_SHAPE
+    assert r(*args(128, INT8, P(0x100004))) == _lib.ERR_ALIGNMENT               # pos is an int64
+    ws = L.pf_decode_attention_workspace_size(8, 128, 64)
+    assert ws == 8 * 1 * 130 * 4
+    att = L.pf_decode_attention_compressed
+
+    def run(nh=8, nkv=2, hd=128, ms=64, mode=INT8, kc=A, wsb=ws):
+        return att(A, kc, A, A, A, A, A, A, A, nh, nkv, hd, ms, mode, 0.1, A, wsb, None)
+
+    assert run(hd=126) == _lib.ERR_SHAPE                                        # head_dim % 4
+    assert run(hd=132) == _lib.ERR_SHAPE                                        # head_dim > 128
+    assert run(nh=9, nkv=1) == _lib.ERR_SHAPE                                   # > 8 query heads per KV head
+    assert run(ms=40000) == _lib.ERR_SHAPE
+    assert run(mode=0) == _lib.ERR_INVALID_ARGUMENT
+    assert run(kc=P(0x100002)) == _lib.ERR_ALIGNMENT                            # int8 rows are read as words
+    assert run(kc=P(0x100002), mode=TWO, wsb=ws - 4) == _lib.ERR_WORKSPACE      # 2-bit codes: byte reads
+    assert run(wsb=ws - 4) == _lib.ERR_WORKSPACE
+    fp = L.pf_decode_attention
+    assert fp(A, P(0x100008), A, A, A, 8, 2, 128, 64, 0.1, A, ws, None) == _lib.ERR_ALIGNMENT  # float4 rows
+    assert fp(A, A, A, A, A, 8, 2, 128, 64, 0.1, A, ws - 1, None) == _lib.ERR_WORKSPACE
+    assert L.pf_kernel_launches() == launches
