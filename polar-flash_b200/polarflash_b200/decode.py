@@ -63,8 +63,9 @@ class PFlashDecoder:
     (default 1e6), rms_norm_eps (default 1e-6); head_dim = hidden_size /
     num_attention_heads.  ``embed`` [vocab, hidden] and ``lm_head`` [vocab,
     hidden] are dense device tensors, ``final_norm`` [hidden].  ``max_seq``
-    bounds the cache; ``kv_dtype`` is the cache's dtype (fp32 keeps the
-    reference's arithmetic).  ``kv_mode`` "int8", "2bit" or "2bit_asym"
+    bounds the cache; ``kv_dtype`` is the uncompressed cache's dtype (fp32
+    keeps the reference's arithmetic; other dtypes run the captured step's
+    attention as torch ops).  ``kv_mode`` "int8", "2bit" or "2bit_asym"
     stores the cache compressed as CompressedKVCache quantizes it
     (polarflash_rt/kv_cache/compressed_kv.py:68-150): each (token, KV head)
     row as codes plus an fp32 scale (and zero), written by the RoPE kernel and
