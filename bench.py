@@ -4,11 +4,14 @@ group-128 asymmetric, block-128 RWHT), batch-1 decode.
 
 One step = one pass over the 7-linear set (q/o 4096x4096, k/v 1024x4096,
 gate/up 14336x4096, down 4096x14336) at INT3 and again at INT2: 14 fused
-GEMVs over 156.7 MB of packed weights, issued as a layer issues them: one
-grouped launch per shared input (q|k|v, o, gate|up, down), 8 launches.  32 resident copies of the packed
-sets (one per layer of the 8B model, 5.0 GB) are cycled so every step reads
-weights untouched for the previous 31 steps (inputs >> the 126 MB L2).  The
-timed region replays CUDA graphs of the steps; inputs are resident in HBM.
+GEMVs over 156.7 MB of packed weights, computed by one pf_qlinear_group call
+(one x' preparation launch for the set's inputs, then one streaming GEMV
+launch per format over its 7 weights).  The same weights issued in layer
+order (one call per shared input: q|k|v, o, gate|up, down) are timed too and
+reported as "layer_order".  32 resident copies of the packed sets (one per
+layer of the 8B model, 5.0 GB) are cycled so every step reads weights
+untouched for the previous 31 steps (inputs >> the 126 MB L2).  The timed
+region replays CUDA graphs of the steps; inputs are resident in HBM.
 
 Metric: effective packed-weight GB/s (algorithmic bytes: packed codes +
 fp16 scales/mins + x + y).  At N GPUs (torchrun) each rank holds a column
@@ -38,6 +41,8 @@ FORMATS = ("int3_g128", "int2_g128")
 # linears sharing one input (q/k/v and gate/up read the same x in a layer): one launch each
 SHARED = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]
 METRIC = "fused dequant-GEMV packed-weight HBM GB/s (Llama-3-8B linear set, INT3+INT2 g128, batch 1)"
+# the GEMV design a recorded ncu traffic capture must be of
+TRAFFIC_DESIGN = "stream-k row-major, in-kernel fixup, x' records from xprep_frag_kernel"
 WORKLOAD = "llama3-8b linear set (q,k,v,o,gate,up,down) INT3 g128 + INT2 g128, RWHT-128, fp16 x, batch 1"
 
 
@@ -419,7 +424,7 @@ def main():
 
     from polarflash_b200 import encoders
     from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
-    from polarflash_b200.qweight import QWeight, group_workspace_bytes, qlinear_multi, workspace
+    from polarflash_b200.qweight import QWeight, group_workspace_bytes, qlinear_group, qlinear_multi, workspace
     from polarflash_b200._lib import kernel_launches
 
     N = args.batch
@@ -462,12 +467,24 @@ def main():
         for name, M, _ in LINEARS:
             outs[(fmt, name)] = y_all[off:off + N * M].view(N, M)
             off += N * M
-    ws_need = max(group_workspace_bytes([base[(fmt, n)] for n in grp], N) for fmt in FORMATS for grp in SHARED)
+    keys = [(fmt, n) for fmt in FORMATS for n, _, _ in LINEARS]
+    grp_of = {n: grp for grp in SHARED for n in grp}
+    set_xs = [xs[grp_of[n]] for _, n in keys]
+    set_outs = [outs[k] for k in keys]
+    ws_need = max([group_workspace_bytes([base[k] for k in keys], N)] +
+                  [group_workspace_bytes([base[(fmt, n)] for n in grp], N) for fmt in FORMATS for grp in SHARED])
     ws = workspace(dev, ws_need)  # zero-filled once; every launch leaves its counters zero
     step_bytes = sum(alg_bytes(qw, N) for qw in base.values())
     packed_bytes = sum(qw.nbytes() for qw in base.values())
 
     def step(cp):
+        """The whole set in one call: one x' preparation launch for the four
+        inputs (per format), then one GEMV launch per format over its 7 weights."""
+        qlinear_group([cp[k] for k in keys], set_xs, workspace=ws, outs=set_outs)
+
+    def step_layer(cp):
+        """As a decoder layer issues them: one call per shared input (q|k|v,
+        o, gate|up, down) and format."""
         for fmt in FORMATS:
             for grp in SHARED:
                 qlinear_multi([cp[(fmt, n)] for n in grp], xs[grp], workspace=ws, outs=[outs[(fmt, n)] for n in grp])
@@ -545,6 +562,27 @@ def main():
         else:
             ms_run = ms / args.steps
 
+        # the same weights issued in layer order (8 calls per step), timed alike
+        layer_graphs = []
+        n0 = kernel_launches()
+        for cp in copies:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                step_layer(cp)
+            layer_graphs.append(gr)
+        layer_launches = (kernel_launches() - n0) // len(copies)
+        for k in range(args.warmup):
+            layer_graphs[k % len(layer_graphs)].replay()
+        torch.cuda.synchronize()
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0.record(stream)
+        for k in range(args.steps):
+            layer_graphs[k % len(layer_graphs)].replay()
+        l1.record(stream)
+        torch.cuda.synchronize()
+        ms_layer = l0.elapsed_time(l1) / args.steps
+        del layer_graphs
+
         # e2e through the public API with host buffers: pinned x in, y out,
         # copies inside the timed region (graph of H2D -> GEMVs -> D2H)
         x_host = {grp: torch.empty(N, xs[grp].shape[1], dtype=torch.float16, pin_memory=True) for grp in xs}
@@ -601,10 +639,10 @@ def main():
                           "caches at 16384 tokens, fp32 and compressed (int8, 2bit, 2bit_asym) caches")
 
     # max over ranks
-    t = torch.tensor([ms, ms_run, ms_e2e], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms, ms_run, ms_e2e, ms_layer], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_run, ms_e2e = (float(v) for v in t.tolist())
+    ms, ms_run, ms_e2e, ms_layer = (float(v) for v in t.tolist())
     ms_step = ms / args.steps
     value = world * step_bytes / (ms_step / 1e3) / 1e9
 
@@ -616,10 +654,15 @@ def main():
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = step_bytes / (ms_run / 1e3) / 1e9
-    traffic = None
+    # DRAM bytes of one step's GEMV launches, from the ncu capture recorded in
+    # profiles/gemv_tma_traffic.json (its "command" reproduces it); used only
+    # while that capture is of the GEMV design this build launches
+    traffic, traffic_src = None, None
     try:
         with open(os.path.join(ROOT, "profiles", "gemv_tma_traffic.json")) as f:
-            traffic = json.load(f).get("bytes_per_step")
+            tj = json.load(f)
+        if tj.get("kernel_design") == TRAFFIC_DESIGN:
+            traffic, traffic_src = tj.get("bytes_per_step"), tj.get("command")
     except Exception:  # noqa: BLE001
         pass
 
@@ -646,15 +689,23 @@ def main():
                              "inputs > 126 MB L2", "parallelism": f"column-shard x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                         "traffic_unit": "DRAM bytes per step (8 GEMV launches, ncu)",
-                         "kernel": "gemv_tma_kernel (8 grouped launches per step: q|k|v, o, gate|up, down at "
-                                   "INT3 and INT2; CUDA events over the timed region)",
+                         "traffic_unit": "DRAM bytes per step (the step's GEMV launches, one ncu capture)",
+                         "traffic_source": traffic_src,
+                         "kernel": "gemv_tma_kernel (one launch per format per step, 7 weights each, after one "
+                                   "xprep_frag_kernel launch); achieved = algorithmic bytes / whole step time "
+                                   "(CUDA events over the timed region, preparation launch included)",
                          "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "of fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": round(world * step_bytes / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "how": "CUDA graph of public-API calls: pinned x H2D, 8 grouped GEMV launches"
+                    "how": "CUDA graph of public-API calls: pinned x H2D, one pf_qlinear_group call over the set"
                            + (", NCCL all-gather of the column shards" if world > 1 else "") + ", y D2H"},
+            "layer_order": {"ms_per_step": round(ms_layer, 5),
+                            "GB_s": round(world * step_bytes / (ms_layer / 1e3) / 1e9, 2),
+                            "frac": round(step_bytes / (ms_layer / 1e3) / 1e9 / hbm_peak, 4),
+                            "launches_per_step": layer_launches,
+                            "how": "the same weights as 8 calls per step, one per shared input (q|k|v, o, "
+                                   "gate|up, down) and format, as a decoder layer issues them"},
             "gpu_launches": launches_per_step * args.steps,
             "decode_tok_s": decode,
             "clocks": clk,

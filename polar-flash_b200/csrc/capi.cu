@@ -203,11 +203,18 @@ size_t ldg_pass_bytes(const pf_qweight* w, int np) {
   return b;
 }
 
+// The streaming GEMV's workspace for one weight: its input's x' records,
+// then its split row blocks' partial sums.
+size_t tma_xq_bytes(const pf_qweight* w, int np) { return round_up((size_t)(w->K / 128) * tma_xrec_bytes(np), 256); }
+size_t tma_member_bytes(const pf_qweight* w, int np) {
+  return tma_xq_bytes(w, np) + tma_partial_bytes(tma_weight(w), np);
+}
+
 // Streaming-GEMV weights also fit the other path (taken for misaligned x).
 size_t pass_bytes(const pf_qweight* w, int np) {
   size_t b = ldg_pass_bytes(w, np);
   if (use_tma(w)) {
-    size_t t = kCounterBytes + tma_partial_bytes(tma_weight(w), np);
+    size_t t = kCounterBytes + tma_member_bytes(w, np);
     if (t > b) b = t;
   }
   return b;
@@ -462,16 +469,97 @@ static int common_args(const pf_qweight* w, int N, void* ws, size_t ws_bytes) {
   return PF_OK;
 }
 
+// Most members one pf_qlinear_group call passes to the streaming GEMV.
+constexpr int kStreamMaxMembers = 1024;
+
+// One streaming-GEMV pass (np <= 16 tokens) over `count` weights: one x'
+// preparation launch for the distinct inputs (an input read by several
+// weights of one format is prepared once), then one GEMV launch per format
+// and scale mode, up to kTmaMaxJobs weights each.  Workspace: counters, then
+// x' records, then partial sums (at most tma_member_bytes per weight).
+static int stream_pass(int count, const pf_qweight* const* ws, const void* const* xs, int x_dtype, int np,
+                       const float* const* biases, float* const* ys, size_t t0, void* workspace, cudaStream_t s) {
+  if (count < 1 || count > kStreamMaxMembers) return PF_ERR_INVALID_ARGUMENT;
+  const size_t xsz = dtype_size(x_dtype);
+  char* cursor = static_cast<char*>(workspace) + kCounterBytes;
+  XPrepJob xj[kXPrepMaxJobs];
+  int nxj = 0;
+  const unsigned char* xq_of[kStreamMaxMembers];
+  cudaError_t e = cudaSuccess;
+  for (int i = 0; i < count; ++i) {
+    const pf_qweight* w = ws[i];
+    const void* x = static_cast<const char*>(xs[i]) + t0 * w->K * xsz;
+    const int8_t* sg = w->had_block ? w->had_signs : nullptr;
+    int found = -1;
+    for (int k = 0; k < nxj; ++k)
+      if (xj[k].x == x && xj[k].fmt == w->format && xj[k].K == w->K && xj[k].had_block == w->had_block &&
+          xj[k].signs == sg)
+        found = k;
+    if (found < 0) {
+      if (nxj == kXPrepMaxJobs) {  // a full preparation launch
+        int st = launch_xprep_frag(xj, nxj, np, x_dtype, s, &e);
+        if (st == PF_ERR_CUDA) return cuda_status(e);
+        if (st) return st;
+        nxj = 0;
+      }
+      XPrepJob& p = xj[nxj];
+      memset(&p, 0, sizeof(p));
+      p.x = x;
+      p.signs = sg;
+      p.xq = reinterpret_cast<unsigned char*>(cursor);
+      p.had_block = w->had_block;
+      p.had_rscale = w->had_block ? 1.f / sqrtf((float)w->had_block) : 1.f;
+      p.K = w->K;
+      p.fmt = w->format;
+      cursor += tma_xq_bytes(w, np);
+      found = nxj++;
+    }
+    xq_of[i] = xj[found].xq;
+  }
+  if (nxj) {
+    int st = launch_xprep_frag(xj, nxj, np, x_dtype, s, &e);
+    if (st == PF_ERR_CUDA) return cuda_status(e);
+    if (st) return st;
+  }
+  // GEMV launches: members of one format and scale mode together
+  bool done[kStreamMaxMembers] = {false};
+  char* part = cursor;
+  for (int i0 = 0; i0 < count; ++i0) {
+    if (done[i0]) continue;
+    TmaWeight tw[kTmaMaxJobs];
+    TmaIO io[kTmaMaxJobs];
+    int n = 0, tiles = 0;
+    char* part0 = part;
+    for (int i = i0; i < count && n < kTmaMaxJobs; ++i) {
+      if (done[i] || ws[i]->format != ws[i0]->format || (ws[i]->scales != nullptr) != (ws[i0]->scales != nullptr))
+        continue;
+      const TmaWeight t = tma_weight(ws[i]);
+      if (n > 0 && (size_t)(tiles + tma_tiles(t)) > kWsStatusSlot) continue;
+      tw[n] = t;
+      io[n].x = nullptr;
+      io[n].bias = biases ? biases[i] : nullptr;
+      io[n].y = ys[i] + t0 * ws[i]->M;
+      io[n].xq = xq_of[i];
+      tiles += tma_tiles(t);
+      part += tma_partial_bytes(t, np);
+      done[i] = true;
+      ++n;
+    }
+    int st = launch_gemv_tma(tw, io, n, np, workspace, part0, s, &e);
+    if (st == PF_ERR_CUDA) return cuda_status(e);
+    if (st) return st;
+  }
+  return PF_OK;
+}
+
 // One pass (N <= 16 tokens) of pf_qlinear.
 static int qlinear_pass(const pf_qweight* w, const HadPlan& plan, const void* x, int x_dtype, int np,
                         const float* bias, float* y, void* ws, cudaStream_t s) {
   if (use_tma(w) && x_tma_aligned(x, x_dtype)) {
-    TmaWeight tw = tma_weight(w);
-    TmaIO io = {x, bias, y};
-    cudaError_t e = cudaSuccess;
-    int st = launch_gemv_tma(&tw, &io, 1, np, x_dtype, ws, s, &e);
-    if (st == PF_ERR_CUDA) return cuda_status(e);
-    return st;
+    const void* xs[1] = {x};
+    const float* bs[1] = {bias};
+    float* yv[1] = {y};
+    return stream_pass(1, &w, xs, x_dtype, np, bs, yv, 0, ws, s);
   }
   int st = do_prepare(w, plan, x, x_dtype, np, ws, s);
   if (st) return st;
@@ -600,16 +688,13 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
   return PF_OK;
 }
 
-// ---- grouped linears: members [c, c + 4) of a group share one launch when
-// every member takes the streaming GEMV with one format and scale mode.
+// ---- grouped linears: every member that takes the streaming GEMV (any INT
+// format it serves) shares one x' preparation launch and one GEMV launch per
+// format, up to kTmaMaxJobs members each.
 static bool group_streams(int count, const pf_qweight* const* ws) {
-  if (count < 1) return false;
-  for (int i = 0; i < count; ++i) {
+  if (count < 1 || count > kStreamMaxMembers) return false;
+  for (int i = 0; i < count; ++i)
     if (!use_tma(ws[i])) return false;
-    if (ws[i]->format != ws[0]->format) return false;
-    if (!is_group_int_format(ws[0]->format) && ((ws[i]->scales != nullptr) != (ws[0]->scales != nullptr)))
-      return false;
-  }
   return true;
 }
 
@@ -637,20 +722,18 @@ static size_t group_bytes(int count, const pf_qweight* const* ws, int N) {
     if (t > b) b = t;
   }
   if (const int kind = group_lut_kind(count, ws, N)) {
-    for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
+    for (int c0 = 0; c0 < count; c0 += kLutGroupJobs) {
       size_t t = kCounterBytes;
-      for (int i = c0; i < count && i < c0 + kTmaMaxJobs; ++i)
+      for (int i = c0; i < count && i < c0 + kLutGroupJobs; ++i)
         t += kind == 1 ? e8_lut_partial_bytes(ws[i]->M, ws[i]->K) : polar8_lut_partial_bytes(ws[i]->M, ws[i]->K);
       if (t > b) b = t;
     }
   }
   if (N <= kMaxGemvTokens && group_streams(count, ws)) {
-    int np = tokens_per_pass(N < 1 ? 1 : N);
-    for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
-      size_t t = kCounterBytes;
-      for (int i = c0; i < count && i < c0 + kTmaMaxJobs; ++i) t += tma_partial_bytes(tma_weight(ws[i]), np);
-      if (t > b) b = t;
-    }
+    const int np = tokens_per_pass(N < 1 ? 1 : N);
+    size_t t = kCounterBytes;
+    for (int i = 0; i < count; ++i) t += tma_member_bytes(ws[i], np);
+    if (t > b) b = t;
   }
   return b;
 }
@@ -687,17 +770,17 @@ int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* const* 
     bool ok = make_plan(ws[0]->K, ws[0]->had_block, &plan) == PF_OK &&
               (kind == 1 ? use_e8_lut(ws[0], 1, plan, xs[0], x_dtype) : use_polar_lut(ws[0], 1, plan, xs[0], x_dtype));
     for (int i = 1; i < count && ok; ++i) ok = xs[i] == xs[0];
-    for (int c0 = 0; ok && c0 < count; c0 += kTmaMaxJobs) {
-      const int n = count - c0 < kTmaMaxJobs ? count - c0 : kTmaMaxJobs;
+    for (int c0 = 0; ok && c0 < count; c0 += kLutGroupJobs) {
+      const int n = count - c0 < kLutGroupJobs ? count - c0 : kLutGroupJobs;
       cudaError_t e = cudaSuccess;
       int st;
       if (kind == 1) {
-        E8In in[kTmaMaxJobs];
+        E8In in[kLutGroupJobs];
         for (int k = 0; k < n; ++k)
           in[k] = e8_in(ws[c0 + k], plan, xs[0], x_dtype, biases ? biases[c0 + k] : nullptr, ys[c0 + k]);
         st = launch_e8_lut(in, n, workspace, s, &e);
       } else {
-        Polar8In in[kTmaMaxJobs];
+        Polar8In in[kLutGroupJobs];
         for (int k = 0; k < n; ++k)
           in[k] = polar8_in(ws[c0 + k], plan, xs[0], x_dtype, biases ? biases[c0 + k] : nullptr, ys[c0 + k]);
         st = launch_polar8_lut(in, n, workspace, s, &e);
@@ -709,7 +792,6 @@ int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* const* 
   }
   bool grouped = N <= kMaxGemvTokens && group_streams(count, ws);
   for (int i = 0; i < count && grouped; ++i) grouped = x_tma_aligned(xs[i], x_dtype);
-  const size_t xsz = dtype_size(x_dtype);
   if (!grouped) {
     for (int i = 0; i < count; ++i) {
       int st = pf_qlinear(ws[i], xs[i], x_dtype, N, biases ? biases[i] : nullptr, ys[i], workspace, ws_bytes,
@@ -720,22 +802,8 @@ int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* const* 
   }
   for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {
     const int np = N - t0 < kMaxGemvTokens ? N - t0 : kMaxGemvTokens;
-    for (int c0 = 0; c0 < count; c0 += kTmaMaxJobs) {
-      const int n = count - c0 < kTmaMaxJobs ? count - c0 : kTmaMaxJobs;
-      TmaWeight tw[kTmaMaxJobs];
-      TmaIO io[kTmaMaxJobs];
-      for (int k = 0; k < n; ++k) {
-        const pf_qweight* w = ws[c0 + k];
-        tw[k] = tma_weight(w);
-        io[k].x = static_cast<const char*>(xs[c0 + k]) + (size_t)t0 * w->K * xsz;
-        io[k].bias = biases ? biases[c0 + k] : nullptr;
-        io[k].y = ys[c0 + k] + (size_t)t0 * w->M;
-      }
-      cudaError_t e = cudaSuccess;
-      int st = launch_gemv_tma(tw, io, n, np, x_dtype, workspace, s, &e);
-      if (st == PF_ERR_CUDA) return cuda_status(e);
-      if (st) return st;
-    }
+    int st = stream_pass(count, ws, xs, x_dtype, np, biases, ys, (size_t)t0, workspace, s);
+    if (st) return st;
   }
   return PF_OK;
 }

@@ -66,30 +66,32 @@ struct GemvCCArgs {
 cudaError_t launch_gemv_cc(const GemvCCArgs& a, cudaStream_t s);
 
 // ---- streaming integer GEMV (gemv_tma.cu): up to kTmaMaxJobs weights of one
-// format per launch, x' computed inside the kernel.
-constexpr int kTmaMaxJobs = 4;
+// format per launch, each with its own input.  The forward RWHT of every
+// input is prepared once, by launch_xprep_frag, as tensor-core B-fragment
+// records in the workspace; the GEMV streams them with the weights.
+constexpr int kTmaMaxJobs = 16;
+constexpr int kLutGroupJobs = 4;  // weights per table-GEMV launch (gemv_lut.cu)
 
 struct TmaJob {  // device view of one weight of a launch
-  const void* scales;   // fp16 [M][G] (group) or fp32 [M] (row)
-  const __half* mins;   // fp16 [M][G] (group)
-  const void* x;        // [N][K] activations (x_dtype)
-  const int8_t* signs;  // RWHT column signs, or nullptr
+  const void* scales;         // fp16 [M][G] (group) or fp32 [M] (row)
+  const __half* mins;         // fp16 [M][G] (group)
+  const unsigned char* xq;    // x' records of the job's input, [G][record bytes]
   const float* bias;
-  float* y;             // [N][M] fp32
-  float* partials;      // [n_rb][spb][128][N] stage partial sums (spb > 1)
+  float* y;                   // [N][M] fp32
+  float* partials;            // [n_rb][spb][128][N] partial sums of split row blocks (spb > 1)
   float tensor_scale;
-  float had_rscale;     // 1/sqrt(had_block), 1 when not rotated
-  int had_block;        // 0 or a power of two <= 512 dividing K
   int M, K, G, n_rb, spb;
-  int unit0, run0;      // first unit and first (job, stage) run of the job
+  int unit0;                  // first unit of the job
+  int tile0;                  // first 16-row arrival counter of the job
 };
 
 struct TmaArgs {
   TmaJob job[kTmaMaxJobs];
+  unsigned* counters;   // workspace head: 16-row arrival counters (zero, left zero)
   unsigned* status;     // workspace status word
-  int n_jobs, n_units, N, x_dtype;
-  int NS, XS;           // ring stages, resident x' stage slots
-  int chunk_max;        // largest x-prep chunk (columns)
+  int n_jobs, n_units, N;
+  int NS, XS;           // weight ring stages per warp, x' ring stages per CTA
+  unsigned xstage;      // bytes of one stage of x' records (a multiple of 128)
 };
 
 struct TmaWeight {  // host view of one weight
@@ -104,18 +106,41 @@ struct TmaIO {
   const void* x;
   const float* bias;
   float* y;
+  const unsigned char* xq;  // the job's x' records (from launch_xprep_frag)
 };
 
+// One input of launch_xprep_frag: x' records of x [N][K] for weights of
+// format `fmt` rotated with `had_block` (0: none) and `signs`.
+struct XPrepJob {
+  const void* x;
+  const int8_t* signs;
+  unsigned char* xq;  // out: [K/128][tma_xrec_bytes(N)]
+  float had_rscale;
+  int had_block;
+  int K;
+  int fmt;
+  int blk0;           // first prep block of this input (set by launch_xprep_frag)
+};
+constexpr int kXPrepMaxJobs = 2 * kTmaMaxJobs;
+
 bool tma_eligible(const TmaWeight& w);
+// Bytes of one 128-column group of x' records for N tokens.
+size_t tma_xrec_bytes(int N);
+// Workspace bytes of a job's split row-block partial sums.
 size_t tma_partial_bytes(const TmaWeight& w, int N);
+// 16-row arrival counters one weight uses.
+int tma_tiles(const TmaWeight& w);
 int tma_block_rows();
 int tma_stage_groups(int fmt);
 int row_words_of_tma(int fmt, int K);
-// One GEMV launch for `count` weights (same format) and N <= 16 tokens, then
-// (when K spans more than one column stage) one combine launch; the workspace
-// holds the status word (in its first kWsCounterBytes) followed by every
-// job's stage partial sums.  Returns a pf_status; *err receives a CUDA error.
-int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int x_dtype, void* workspace,
+// x' records of `count` inputs (any streaming formats) in one launch.
+int launch_xprep_frag(XPrepJob* xj, int count, int N, int x_dtype, cudaStream_t s, cudaError_t* err);
+// One GEMV launch for `count` weights (same format, each with its x' records
+// in io[k].xq) and N <= 16 tokens; split row blocks are reduced inside the
+// launch.  `workspace` holds the counter/status head; every job's partial
+// sums follow one another from `partials` (tma_partial_bytes each, in job
+// order).  Returns a pf_status; *err receives a CUDA error.
+int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void* workspace, char* partials,
                     cudaStream_t s, cudaError_t* err);
 
 // ---- streaming lookup-table GEMVs at batch 1 (gemv_lut.cu): E8 RVQ2, and

@@ -1,32 +1,37 @@
 // Streaming fused dequant-GEMV for the INT formats (N <= 16 tokens): one
-// launch computes y = x W^T for up to four weights ("jobs") of one format.
+// launch computes y_j = x_j W_j^T for up to sixteen weights ("jobs") of one
+// format, each with its own input, e.g. every linear of a model layer.
 //
-// Work unit = (job, 128-row block, stage of S groups of 128 columns), dealt to
-// the CTAs stream-K style in stage-major order: a CTA's consecutive units
-// share a column stage, so it transforms only the one or two stages of x it
-// needs (x' = forward block RWHT of x, scaled and split for the tensor cores)
-// straight into shared memory; there is no separate x-prep launch.
+// x' (the forward block RWHT of x, scaled and split into the tensor cores'
+// B fragments) is made once per input by xprep_frag_kernel into the
+// workspace: one 576-byte record per 128-column group at N = 1.
+//
+// GEMV work unit = (job, 128-row block, stage of S groups of 128 columns).
+// The units are dealt to the CTAs stream-K style, each CTA taking an equal
+// contiguous range in row-block-major order, so a CTA walks all stages of
+// its row blocks and keeps their sums in registers: only the (at most two)
+// row blocks a CTA shares with its neighbours are reduced through memory,
+// by the last of their warps to arrive (arrival counter per 16 rows, parts
+// added in stage order, so the result does not depend on timing).  There is
+// no separate combine launch.
 //
 // CTA = 8 warps, two CTAs per SM.  Every warp owns 16 rows of each unit and
 // streams them itself through a private ring of shared-memory slots: lane 0
 // issues the 2-D TMA copy of its 16 x (S groups) tile of packed codes (L2
 // evict-first), all lanes copy the tile's fp16 scales / zero points with
-// cp.async, and the copies themselves arrive on the slot's mbarrier.  A warp
-// refills a slot it has just consumed, so warps never wait for each other
-// except at the x' preparation barrier, and the weights of the first slots
-// are requested before the kernel waits for the preceding grid
-// (programmatic dependent launch; packed weights and scales are never written
-// by a kernel that precedes a GEMV in this library).
+// cp.async, and the copies themselves arrive on the slot's mbarrier.  The
+// x' records of each unit's stage come from the workspace (L2) into a small
+// CTA-wide ring by one bulk copy; the last warp done with a stage's records
+// refills that slot.  Weights are requested before the kernel waits for the
+// preceding grid (programmatic dependent launch: packed weights and scales
+// are never written by a kernel that precedes a GEMV in this library).
 //
 // Compute: the unit's code words are read into registers, every code pair
 // becomes one AND (exact subnormal fp16 q 2^(p-24)), and mma.sync m16n8k16
 // multiplies two groups at a time against the B fragments of x' (fp16 hi / lo
 // halves of x' in the two columns of each token).
 // Per 128-column group:  sum w x' = s 2^E Q + m Sx  with  Q = sum q x'/2^E.
-// Each unit's 16 x N partial sums per warp go to the workspace (plain
-// stores); combine_kernel, launched next as a programmatic dependent, adds a
-// row block's stage partials in a fixed order (deterministic) and writes y.
-// Every wait is bounded (2 s, %globaltimer): on expiry the kernel records
+// Every wait is bounded (%globaltimer): on expiry the kernel records
 // PF_ERR_TIMEOUT in the workspace status word, skips every later wait and
 // finishes.
 #include <cuda.h>
@@ -49,7 +54,7 @@ constexpr int kThreadsT = kWarps * 32;
 constexpr int kWarpRows = 16;              // rows per warp and unit (one MMA row tile)
 constexpr int kRowsBlk = kWarpRows * kWarps;  // rows per unit
 constexpr int kMaxStages = 8;
-constexpr int kMaxXSlots = 3;
+constexpr int kMaxXSlots = 4;
 
 // Dynamic shared memory per CTA: two CTAs share an SM's 228 KB.
 int smem_budget(int ctas_per_sm) { return ctas_per_sm >= 2 ? 110 * 1024 : 200 * 1024; }
@@ -211,18 +216,6 @@ __device__ __forceinline__ void load_words(const unsigned char* stg, int r, int 
   }
 }
 
-__device__ __forceinline__ const TmaJob& job_ref(const TmaArgs& a, int j) {
-  return j == 0 ? a.job[0] : j == 1 ? a.job[1] : j == 2 ? a.job[2] : a.job[3];
-}
-
-// Job holding global unit u.
-__device__ __forceinline__ int job_of(const TmaArgs& a, int u) {
-  int j = 0;
-#pragma unroll
-  for (int k = 1; k < kTmaMaxJobs; ++k)
-    if (k < a.n_jobs && u >= a.job[k].unit0) j = k;
-  return j;
-}
 
 // Group-relative columns (lo0, hi0, lo1, hi1) of a lane's B fragment and the
 // mantissa positions of its two code pairs.
@@ -241,11 +234,13 @@ __device__ __forceinline__ float pow2f(int e) {
 // block RWHT of x (signs, Walsh-Hadamard butterflies in registers and across
 // lanes, 1/sqrt(b)), then for every group of the chunk inside [g_lo, g_hi):
 // the group's power-of-two normaliser E (|x'| < 2^E), the tensor-core B
-// fragments of x' 2^(14 - p - E) split into fp16 hi + lo, and {Sx, 1024 2^E}.
+// fragments of x' 2^(14 - p - E) split into fp16 hi + lo, and {Sx, 1024 2^E},
+// written to the records at `recs` (the record of group g_lo first).
 // Tokens t >= N write zeros.  Every global load is issued before any is used.
 template <int NT, int LP, int E, int TPT>
-__device__ __forceinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype, int col0, int g_lo, int g_hi, int t,
-                                           unsigned char* xslot, float* scratch, int lane, const LaneCols& lc) {
+__device__ __forceinline__ void prep_chunk(const XPrepJob& jb, int N, int x_dtype, int col0, int g_lo, int g_hi,
+                                           int t, unsigned char* recs, float* scratch, int lane,
+                                           const LaneCols& lc) {
   constexpr int C = 32 * E;
   constexpr int LG = 128 / E;  // lanes per 128-column group
   const int b = jb.had_block;
@@ -345,10 +340,10 @@ __device__ __forceinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype,
     *reinterpret_cast<float4*>(scratch + E * lane + 4 * q) =
         make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   __syncwarp();
-  const int j8 = lane >> 2, c = lane & 3;
+  const int j8 = lane >> 2;
   // B-fragment lane of the token's column: hi at column 2 (t % 4), lo next to
   // it, or the token's own column t % 8
-  const int fl = TPT == 4 ? 8 * (t & 3) + c : 4 * (t & 7) + c;
+  const int fl = TPT == 4 ? 8 * (t & 3) + (lane & 3) : 4 * (t & 7) + (lane & 3);
   const int tile = TPT == 4 ? t >> 2 : t >> 3;
 #pragma unroll
   for (int gi = 0; gi < C / 128; ++gi) {
@@ -369,7 +364,7 @@ __device__ __forceinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype,
       lw[k] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
     using XR = XRec<NT, LP, TPT>;
-    unsigned char* rec = xslot + (size_t)(g - g_lo) * XR::R;
+    unsigned char* rec = recs + (size_t)(g - g_lo) * XR::R;
     unsigned char* fr = rec + (tile * 4 + (j8 >> 1)) * LP * 16 + (j8 & 1) * 8;
     *reinterpret_cast<uint2*>(fr + fl * 16) = make_uint2(hw[0], hw[1]);
     if (TPT == 4) *reinterpret_cast<uint2*>(fr + (fl + 4) * 16) = make_uint2(lw[0], lw[1]);
@@ -378,11 +373,81 @@ __device__ __forceinline__ void prep_chunk(const TmaJob& jb, int N, int x_dtype,
   __syncwarp();
 }
 
+// Inputs of one x' preparation launch.
+struct XPrepArgs {
+  XPrepJob xj[kXPrepMaxJobs];
+  int n_xj, N, x_dtype;
+};
+constexpr int kPrepCols = 512;  // columns of one prep block
+
+// One block per (input, 512 columns): the four groups' records of every
+// token slot.  Launched as a programmatic dependent (x may come from the
+// preceding grid).
+template <int NT, int LP, int TPT>
+__global__ void __launch_bounds__(kThreadsT) xprep_frag_kernel(const __grid_constant__ XPrepArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  __shared__ __align__(16) float scratch[kWarps][kPrepCols];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int k = 0;
+  for (int i = 1; i < a.n_xj; ++i)
+    if ((int)blockIdx.x >= a.xj[i].blk0) k = i;
+  const XPrepJob& jb = a.xj[k];
+  const int region = (int)blockIdx.x - jb.blk0;
+  const int g_lo = region * (kPrepCols / 128), g_hi = g_lo + kPrepCols / 128;
+  LaneCols lc;
+  {
+    const int c = lane & 3, rq = lane >> 2;
+    int lo, hi, p;
+    frag_cols2(jb.fmt, c, 2 * rq, lo, hi, p);
+    lc.col[0] = lo; lc.col[1] = hi; lc.p[0] = p;
+    frag_cols2(jb.fmt, c, 2 * rq + 1, lo, hi, p);
+    lc.col[2] = lo; lc.col[3] = hi; lc.p[1] = p;
+  }
+  using XR = XRec<NT, LP, TPT>;
+  unsigned char* recs = jb.xq + (size_t)g_lo * XR::R;
+  const int b = jb.had_block;
+  const int E = b > 256 ? 16 : (b > 128 ? 8 : 4);
+  const int Cc = 32 * E;
+  const int tslots = LP == 8 ? 1 : TPT * NT;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  int task = 0;
+  for (int ci = 0; ci < kPrepCols / Cc; ++ci)
+    for (int t = 0; t < tslots; ++t, ++task) {
+      if (task % kWarps != warp) continue;
+      const int col0 = region * kPrepCols + ci * Cc;
+      if (E == 4)
+        prep_chunk<NT, LP, 4, TPT>(jb, a.N, a.x_dtype, col0, g_lo, g_hi, t, recs, scratch[warp], lane, lc);
+      else if (E == 8)
+        prep_chunk<NT, LP, 8, TPT>(jb, a.N, a.x_dtype, col0, g_lo, g_hi, t, recs, scratch[warp], lane, lc);
+      else
+        prep_chunk<NT, LP, 16, TPT>(jb, a.N, a.x_dtype, col0, g_lo, g_hi, t, recs, scratch[warp], lane, lc);
+    }
+}
+
+struct TmaMaps {
+  CUtensorMap m[kTmaMaxJobs];
+};
+
+// Job holding global unit u.
+__device__ __forceinline__ int job_of(const TmaArgs& a, int u) {
+  int j = 0;
+#pragma unroll
+  for (int k = 1; k < kTmaMaxJobs; ++k)
+    if (k < a.n_jobs && u >= a.job[k].unit0) j = k;
+  return j;
+}
+
+// Stream-K partition: CTA c of P takes units [c U / P, (c + 1) U / P).
+__device__ __forceinline__ int cta_first_unit(unsigned c, unsigned U, unsigned P) {
+  return (int)(((unsigned long long)c * U) / P);
+}
+__device__ __forceinline__ int cta_of_unit(unsigned u, unsigned U, unsigned P) {
+  return (int)((((unsigned long long)u + 1) * P - 1) / U);
+}
+
 template <int FMT, int NT, int LP, int SMODE, int TPT>
 __global__ void __launch_bounds__(kThreadsT, 2)
-    gemv_tma_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
-                    const __grid_constant__ CUtensorMap map2, const __grid_constant__ CUtensorMap map3,
-                    const __grid_constant__ TmaArgs a) {
+    gemv_tma_kernel(const __grid_constant__ TmaMaps maps, const __grid_constant__ TmaArgs a) {
   using F = TmaFmt<FMT>;
   using L = WarpSlot<FMT, SMODE>;
   using XR = XRec<NT, LP, TPT>;
@@ -399,52 +464,59 @@ __global__ void __launch_bounds__(kThreadsT, 2)
     const uint32_t w = reinterpret_cast<const uint32_t*>(&a)[i];
     asm volatile("" ::"r"(w));
   }
-  if (threadIdx.x >= 32 && threadIdx.x < 32 + kTmaMaxJobs) {
-    const int k = threadIdx.x - 32;
-    const CUtensorMap* m = k == 0 ? &map0 : k == 1 ? &map1 : k == 2 ? &map2 : &map3;
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
-  }
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ int abort_flag;
+  __shared__ unsigned xcnt[kMaxXSlots];  // warps done with each x' slot
+  __shared__ int xlast;                  // last unit whose x' records were requested
   unsigned char* const base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int NS = a.NS, XS = a.XS;
-  constexpr uint32_t X = S * XR::R;
+  const uint32_t XB = a.xstage;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  unsigned char* const ring = base + (size_t)warp * NS * L::BYTES;  // this warp's slots
-  unsigned char* const xarea = base + (size_t)kWarps * NS * L::BYTES;
-  float* const scratch = reinterpret_cast<float*>(xarea + XS * X) + warp * a.chunk_max;
-  const uint32_t full0 = smem_u32(reinterpret_cast<float*>(xarea + XS * X) + kWarps * a.chunk_max) + warp * NS * 8;
-
-  if (threadIdx.x == 0) abort_flag = 0;
-  if (lane == 0) {
-    for (int s = 0; s < NS; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full0 + 8 * s), "r"(33));
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
+  unsigned char* const ring = base + (size_t)warp * NS * L::BYTES;  // this warp's weight slots
+  unsigned char* const xring = base + (size_t)kWarps * NS * L::BYTES;
+  const uint32_t bars = smem_u32(xring + (size_t)XS * XB);
+  const uint32_t full0 = bars + warp * NS * 8;     // this warp's weight slots
+  const uint32_t xfull0 = bars + kWarps * NS * 8;  // the x' slots
 
   const unsigned U = (unsigned)a.n_units, P = gridDim.x, cta = blockIdx.x;
-  const int u0 = (int)(cta * U / P), u1 = (int)((cta + 1) * U / P);  // U * P < 2^32 (host-checked)
+  const int u0 = cta_first_unit(cta, U, P), u1 = cta_first_unit(cta + 1, U, P);  // U * P < 2^32 (host-checked)
   const int nunits = u1 - u0;
+
+  if (threadIdx.x >= 32 && threadIdx.x < 32 + kTmaMaxJobs && nunits > 0) {
+    const int k = threadIdx.x - 32;
+    if (k >= job_of(a, u0) && k <= job_of(a, u1 - 1))
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.m[k])) : "memory");
+  }
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    xlast = -1;
+    for (int s = 0; s < XS; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(xfull0 + 8 * s), "r"(1));
+  }
+  if (threadIdx.x < kMaxXSlots) xcnt[threadIdx.x] = 0u;
+  if (lane == 0)
+    for (int s = 0; s < NS; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full0 + 8 * s), "r"(33));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncthreads();
   if (nunits <= 0) return;
   const int N = a.N;
   const int c = lane & 3, rq = lane >> 2;
 
-  // ---- load side: this warp's next unit to request (job, stage, row block)
-  int fj = job_of(a, u0), fst, frb;
+  // ---- load side: this warp's next unit to request (job, row block, stage)
+  int fj = job_of(a, u0), frb, fst;
   {
-    const TmaJob& jb = job_ref(a, fj);
+    const TmaJob& jb = a.job[fj];
     const int v = u0 - jb.unit0;
-    fst = v / jb.n_rb;
-    frb = v - fst * jb.n_rb;
+    frb = v / jb.spb;
+    fst = v - frb * jb.spb;
   }
   const CUtensorMap* fmap = nullptr;
   const __half* fsc = nullptr;
   const __half* fmn = nullptr;
   int fM = 0, fG = 0, fnrb = 1, fspb = 1;
   auto load_fjob = [&]() {
-    const TmaJob& jb = job_ref(a, fj);
-    fmap = fj == 0 ? &map0 : fj == 1 ? &map1 : fj == 2 ? &map2 : &map3;
+    const TmaJob& jb = a.job[fj];
+    fmap = &maps.m[fj];
     fsc = static_cast<const __half*>(jb.scales);
     fmn = jb.mins;
     fM = jb.M;
@@ -482,98 +554,54 @@ __global__ void __launch_bounds__(kThreadsT, 2)
         cp_async4(sb + L::W + lane * 4, reinterpret_cast<const float*>(fsc) + (ok ? grow : 0), ok ? 4u : 0u);
     }
     cp_async_arrive(bar);
-    if (++frb == fnrb) {
-      frb = 0;
-      if (++fst == fspb) {
-        fst = 0;
-        ++fj;
-        if (fj < a.n_jobs) load_fjob();
+    if (++fst == fspb) {
+      fst = 0;
+      if (++frb == fnrb) {
+        frb = 0;
+        if (++fj < a.n_jobs) load_fjob();
       }
     }
   };
-  // the first two units (weights and scales never come from the preceding
-  // grid); the rest of the ring is requested after the x' preparation, when
-  // the copy engine's queue has drained
+  // the weights of the first ring slots never come from the preceding grid
   int requested = 0;
-  for (; requested < 2 && requested < NS && requested < nunits; ++requested) request(requested);
+  for (; requested < NS && requested < nunits; ++requested) request(requested);
 
-  // ---- compute side: unit walk (job, stage, row block) and its x' runs
-  int j = job_of(a, u0), st, rb;
-  {
-    const TmaJob& jb = job_ref(a, j);
-    const int v = u0 - jb.unit0;
-    st = v / jb.n_rb;
-    rb = v - st * jb.n_rb;
+  // x' records of unit u (its job's input, its stage) into x' slot `xs`
+  auto xload = [&](int xs, int u) {
+    const TmaJob& jb = a.job[job_of(a, u)];
+    const int st = (u - jb.unit0) % jb.spb;
+    const uint32_t bar = xfull0 + 8 * xs;
+    mbar_expect(bar, XB);
+    bulk_g2s(smem_u32(xring + (size_t)xs * XB), jb.xq + (size_t)st * XB, XB, bar);
+  };
+
+  // x' records, y, partial sums and counters may be written by the preceding grid
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) {
+    int k = 0;
+    for (; k < XS && k < nunits; ++k) xload(k, u0 + k);
+    xlast = u0 + k - 1;
   }
-  int rl[2];  // the thread's two rows within the warp's 16
+
+  // ---- compute side: unit walk (job, row block, stage)
+  int j = job_of(a, u0), rb, st;
+  {
+    const TmaJob& jb = a.job[j];
+    const int v = u0 - jb.unit0;
+    rb = v / jb.spb;
+    st = v - rb * jb.spb;
+  }
+  int seg0 = st;  // first stage of this CTA's part of the current row block
+  int rl[2];      // the thread's two rows within the warp's 16
   rl[0] = row_perm<FMT>(rq);
   rl[1] = rl[0] + 8;
-  LaneCols lc;
-  {
-    int lo, hi, p;
-    frag_cols2(FMT, c, 2 * rq, lo, hi, p);
-    lc.col[0] = lo; lc.col[1] = hi; lc.p[0] = p;
-    frag_cols2(FMT, c, 2 * rq + 1, lo, hi, p);
-    lc.col[2] = lo; lc.col[3] = hi; lc.p[1] = p;
-  }
   const uint32_t blane = (uint32_t)(lane & (LP - 1)) * 16;
 
-  // x' windows over the CTA's runs (consecutive units with one job and stage);
-  // XS runs are resident, run r in slot r % XS
-  int nruns;
-  {
-    const int jl = job_of(a, u1 - 1);
-    const TmaJob& jf = job_ref(a, j);
-    const TmaJob& jL = job_ref(a, jl);
-    nruns = (jL.run0 + (u1 - 1 - jL.unit0) / jL.n_rb) - (jf.run0 + (u0 - jf.unit0) / jf.n_rb) + 1;
-  }
-  int pj = j, pst = st;  // (job, stage) of the next run to prepare
-  int win_end = 0;
-  auto prep_window = [&](int r0) {
-    const int r1 = (r0 + XS < nruns) ? r0 + XS : nruns;
-    const int tslots = LP == 8 ? 1 : TPT * NT;
-    int task = 0;
-    for (int r = r0; r < r1; ++r) {
-      const TmaJob& jb = job_ref(a, pj);
-      const int b = jb.had_block;
-      const int E = b > 256 ? 16 : (b > 128 ? 8 : 4);
-      const int Cc = 32 * E;
-      const int g_lo = pst * S, g_hi = g_lo + S;
-      const int nchunk = (S * 128) / Cc > 0 ? (S * 128) / Cc : 1;
-      const int cbase = ((g_lo * 128) / Cc) * Cc;
-      unsigned char* xslot = xarea + (size_t)(r % XS) * X;
-      for (int ci = 0; ci < nchunk; ++ci)
-        for (int t = 0; t < tslots; ++t, ++task) {
-          if (task % kWarps != warp) continue;
-          const int col0 = cbase + ci * Cc;
-          if (E == 4)
-            prep_chunk<NT, LP, 4, TPT>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
-          else if (E == 8)
-            prep_chunk<NT, LP, 8, TPT>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
-          else
-            prep_chunk<NT, LP, 16, TPT>(jb, N, a.x_dtype, col0, g_lo, g_hi, t, xslot, scratch, lane, lc);
-        }
-      if (++pst == jb.spb) {
-        pst = 0;
-        ++pj;
-      }
-    }
-    win_end = r1;
-  };
-
-  // x may be written by the preceding grid, and so may the workspace and y
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  prep_window(0);
-  for (; requested < NS && requested < nunits; ++requested) request(requested);
-  __syncthreads();
-
   // the current job's fields, reloaded when the walk enters the next job
-  float* jpart = nullptr;
   float jts = 0.f;
   int jM = 0, jnrb = 1, jspb = 1;
   auto load_job = [&]() {
-    const TmaJob& jb = job_ref(a, j);
-    jpart = jb.partials;
+    const TmaJob& jb = a.job[j];
     jts = jb.tensor_scale;
     jM = jb.M;
     jnrb = jb.n_rb;
@@ -581,18 +609,84 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   };
   load_job();
 
-  int run = 0, xslot = 0, slot = 0;
-  uint32_t phase = 0;
+  float y[NT][2][YT];
+#pragma unroll
+  for (int i = 0; i < NT; ++i)
+#pragma unroll
+    for (int u = 0; u < YT; ++u) y[i][0][u] = y[i][1][u] = 0.f;
+
+  // a token held by this thread: accumulator columns 2c, 2c + 1 are one token
+  // as hi + lo (TPT 4) or two tokens (TPT 8)
+  auto tok = [&](int i, int u) { return TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u; };
+  auto holds = [&](int t) { return t < N && (LP == 32 || c == 0); };
+
+  // End of this CTA's part of row block rb (stages seg0..st): y when the
+  // part is the whole row block; else the part's sums go to the workspace
+  // and the warp whose arrival completes the row block adds every part in
+  // stage order and writes y.
+  auto finish = [&]() {
+    const TmaJob& jb = a.job[j];
+    if (!(seg0 == 0 && st == jspb - 1)) {
+      const size_t rstride = (size_t)kRowsBlk * N;
+      float* const pbase = jb.partials + ((size_t)rb * jspb * kRowsBlk + warp * kWarpRows) * N;
+      float* const part = pbase + (size_t)seg0 * rstride;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int i = 0; i < NT; ++i)
+#pragma unroll
+          for (int u = 0; u < YT; ++u)
+            if (holds(tok(i, u))) __stcg(part + (size_t)rl[hh] * N + tok(i, u), y[i][hh][u]);
+      __threadfence();
+      __syncwarp();
+      const unsigned R0 = (unsigned)(jb.unit0 + rb * jspb);
+      const int cf = cta_of_unit(R0, U, P), cl = cta_of_unit(R0 + jspb - 1, U, P);
+      unsigned last = 0;
+      if (lane == 0) {
+        unsigned* cnt = a.counters + jb.tile0 + rb * kWarps + warp;
+        last = atomicAdd(cnt, 1u) == (unsigned)(cl - cf);
+        if (last) atomicExch(cnt, 0u);
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) return;
+      __threadfence();
+#pragma unroll
+      for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int u = 0; u < YT; ++u) y[i][0][u] = y[i][1][u] = 0.f;
+      for (int cc = cf; cc <= cl; ++cc) {
+        const int s0 = max(cta_first_unit(cc, U, P), (int)R0) - (int)R0;
+        const float* p = pbase + (size_t)s0 * rstride;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int i = 0; i < NT; ++i)
+#pragma unroll
+            for (int u = 0; u < YT; ++u)
+              if (holds(tok(i, u))) y[i][hh][u] += __ldcg(p + (size_t)rl[hh] * N + tok(i, u));
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int grow = rb * kRowsBlk + warp * kWarpRows + rl[hh];
+      if (grow >= jM) continue;
+      const float bv = jb.bias ? jb.bias[grow] : 0.f;
+#pragma unroll
+      for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int u = 0; u < YT; ++u)
+          if (holds(tok(i, u))) jb.y[(size_t)tok(i, u) * jM + grow] = y[i][hh][u] + bv;
+    }
+  };
+
+  int slot = 0, xslot = 0;
+  uint32_t phase = 0, xphase = 0;
   bool live = true;
   for (int it = 0; it < nunits; ++it) {
-    if (run >= win_end) {  // same decision in every warp of the CTA
-      __syncthreads();
-      prep_window(win_end);
-      __syncthreads();
-    }
     const unsigned char* stg = ring + slot * L::BYTES;
-    const unsigned char* xs = xarea + xslot * X;
-    if (live && !mbar_wait(full0 + 8 * slot, phase, &abort_flag)) {
+    const unsigned char* xs = xring + (size_t)xslot * XB;
+    if (live && !(mbar_wait(full0 + 8 * slot, phase, &abort_flag) &&
+                  mbar_wait(xfull0 + 8 * xslot, xphase, &abort_flag))) {
       live = false;
       if (lane == 0) {
         abort_flag = 1;
@@ -600,11 +694,6 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       }
     }
     if (live) {
-      float y[NT][2][YT];
-#pragma unroll
-      for (int i = 0; i < NT; ++i)
-#pragma unroll
-        for (int u = 0; u < YT; ++u) y[i][0][u] = y[i][1][u] = 0.f;
 #pragma unroll
       for (int pp = 0; pp < S / 2; ++pp) {
         // scales / zero points of the pair's two groups, then their code words
@@ -659,8 +748,7 @@ __global__ void __launch_bounds__(kThreadsT, 2)
           for (int i = 0; i < NT; ++i) {
 #pragma unroll
             for (int u = 0; u < YT; ++u) {
-              // token of accumulator columns 2c, 2c + 1: one token as hi + lo, or two tokens
-              const int t = LP == 8 ? 0 : (TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u);
+              const int t = LP == 8 ? 0 : tok(i, u);
               const float2 gs = lds<float2>(xs + g * XR::R + XR::FRAG + t * 16);
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh) {
@@ -679,54 +767,49 @@ __global__ void __launch_bounds__(kThreadsT, 2)
           }
         }
       }
-
-      if (jspb == 1) {
-        const TmaJob& jb = job_ref(a, j);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int grow = rb * kRowsBlk + warp * kWarpRows + rl[hh];
-          if (grow >= jM) continue;
-          const float bv = jb.bias ? jb.bias[grow] : 0.f;
-#pragma unroll
-          for (int i = 0; i < NT; ++i)
-#pragma unroll
-            for (int u = 0; u < YT; ++u) {
-              const int t = TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u;
-              if (t < N && (LP == 32 || c == 0)) jb.y[(size_t)t * jM + grow] = y[i][hh][u] + bv;
-            }
+      // done with this unit's x' records: the last warp refills the slot
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&xcnt[xslot], 1u) == (unsigned)(kWarps - 1)) {
+          atomicExch(&xcnt[xslot], 0u);
+          __threadfence_block();
+          if (it + XS < nunits) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            xload(xslot, u0 + it + XS);
+            atomicMax(&xlast, u0 + it + XS);
+          }
         }
-      } else {
-        // the stage partial sums; the combine kernel adds them in stage order
-        float* part = jpart + (((size_t)rb * jspb + st) * kRowsBlk + warp * kWarpRows) * N;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-          for (int i = 0; i < NT; ++i)
-#pragma unroll
-            for (int u = 0; u < YT; ++u) {
-              const int t = TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u;
-              if (t < N && (LP == 32 || c == 0)) __stcg(part + (size_t)rl[hh] * N + t, y[i][hh][u]);
-            }
       }
-    }
-    if (live && requested < nunits) {  // refill the slot just consumed
-      request(slot);
-      ++requested;
+      if (requested < nunits) {  // refill the weight slot just consumed
+        request(slot);
+        ++requested;
+      }
     }
     if (++slot == NS) {
       slot = 0;
       phase ^= 1u;
     }
-    if (++rb == jnrb) {
-      rb = 0;
-      ++run;
-      if (++xslot == XS) xslot = 0;
-      if (++st == jspb) {
-        st = 0;
-        ++j;
-        if (j < a.n_jobs) load_job();
+    if (++xslot == XS) {
+      xslot = 0;
+      xphase ^= 1u;
+    }
+    const bool row_end = st == jspb - 1;
+    if (row_end || it == nunits - 1) {
+      if (live) finish();
+#pragma unroll
+      for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int u = 0; u < YT; ++u) y[i][0][u] = y[i][1][u] = 0.f;
+    }
+    if (++st == jspb) {
+      st = 0;
+      if (++rb == jnrb) {
+        rb = 0;
+        if (++j < a.n_jobs) load_job();
       }
     }
+    if (row_end) seg0 = 0;
   }
   if (!live && lane == 0) {
     // after a timeout: bounded waits on this warp's tiles that may still be in flight
@@ -735,56 +818,14 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       mbar_wait(full0 + 8 * (k % NS), (k / NS) & 1, &keep_waiting);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-}
-
-// y = the sum of a job's stage partial sums (+ bias).  A block covers 32
-// consecutive (row, token) elements of one job; warp w adds stages w, w + 8,
-// ... (all its loads in flight at once) and warp 0 adds the eight warp sums
-// in warp order, so the result is the same on every run.  Launched after the
-// GEMV as a programmatic dependent: it lets its own dependents start at once
-// and waits for the GEMV's partial sums.
-constexpr int kCombineWarps = 8;
-
-__global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(const __grid_constant__ TmaArgs a) {
-  asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  __shared__ float red[kCombineWarps][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int N = a.N;
-  int blk = blockIdx.x, j = 0;
-  for (; j < a.n_jobs; ++j) {
-    const int nb = (((a.job[j].M + kRowsBlk - 1) / kRowsBlk) * kRowsBlk * N + 31) / 32;
-    if (blk < nb) break;
-    blk -= nb;
-  }
-  if (j >= a.n_jobs) return;
-  const TmaJob& jb = a.job[j];
-  if (jb.spb <= 1) return;
-  const int e = blk * 32 + lane;  // element row * N + t of the job
-  const int row = e / N, t = e - row * N;
-  const bool valid = row < jb.M;
-  float acc = 0.f;
-  if (valid) {
-    const int rb = row / kRowsBlk, r = row - rb * kRowsBlk;
-    const float* p = jb.partials + (size_t)rb * jb.spb * kRowsBlk * N + (size_t)r * N + t;
-    const size_t stride = (size_t)kRowsBlk * N;
-    float v[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int st = warp + k * kCombineWarps;
-      v[k] = st < jb.spb ? __ldcg(p + st * stride) : 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc += v[k];
-    for (int st = warp + 8 * kCombineWarps; st < jb.spb; st += kCombineWarps) acc += __ldcg(p + st * stride);
-  }
-  red[warp][lane] = acc;
   __syncthreads();
-  if (warp == 0 && valid) {
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < kCombineWarps; ++w) s += red[w][lane];
-    jb.y[(size_t)t * jb.M + row] = s + (jb.bias ? jb.bias[row] : 0.f);
+  if (abort_flag && threadIdx.x == 0) {
+    // and on the x' records still in flight
+    volatile int keep_waiting = 0;
+    for (int k = max(xlast - XS + 1, u0); k <= xlast; ++k) {
+      const int i = k - u0;
+      mbar_wait(xfull0 + 8 * (i % XS), (i / XS) & 1, &keep_waiting);
+    }
   }
 }
 
@@ -827,15 +868,37 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 int stage_groups(int fmt) { return is_int4(fmt) ? 2 : 4; }
 
-// Prep chunk (columns) of a rotation block size.
-int chunk_cols(int had_block) { return had_block > 256 ? 512 : (had_block > 128 ? 256 : 128); }
+// The shared-memory opt-in of a kernel, once per device.
+template <class K>
+cudaError_t opt_in_smem(K kern, int bytes) {
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64 || !done[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) done[dev] = true;
+  }
+  return cudaSuccess;
+}
 
-// Global run index (job, stage) of unit u.
-int run_of(const TmaArgs& a, int u) {
-  int j = 0;
-  for (int k = 1; k < a.n_jobs; ++k)
-    if (u >= a.job[k].unit0) j = k;
-  return a.job[j].run0 + (u - a.job[j].unit0) / a.job[j].n_rb;
+// A launch that may begin while the preceding kernel of the stream finishes
+// (programmatic dependent launch; the kernel waits with griddepcontrol.wait).
+cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 template <int FMT, int NT, int LP, int SMODE, int TPT>
@@ -845,71 +908,49 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   using XR = XRec<NT, LP, TPT>;
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
-  CUtensorMap maps[kTmaMaxJobs];
+  TmaMaps maps;
   for (int k = 0; k < a.n_jobs; ++k) {
     cuuint64_t dims[2] = {(cuuint64_t)row_words[k], (cuuint64_t)a.job[k].M};
     cuuint64_t strides[1] = {(cuuint64_t)row_words[k] * 4};
     cuuint32_t box[2] = {(cuuint32_t)(F::S * F::WPG), (cuuint32_t)kWarpRows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(&maps[k], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes[k]), dims, strides, box,
+    CUresult r = fn(&maps.m[k], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes[k]), dims, strides, box,
                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     F::SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   }
-  for (int k = a.n_jobs; k < kTmaMaxJobs; ++k) maps[k] = maps[0];
+  for (int k = a.n_jobs; k < kTmaMaxJobs; ++k) maps.m[k] = maps.m[0];
 
   const int cps = ctas_per_sm();
   int P = sm_count() * cps;
   if (P > a.n_units) P = a.n_units;
   if (P < 1) P = 1;
-  int max_runs = 1;
-  for (int cta = 0; cta < P; ++cta) {
-    const int u0 = (int)((long long)cta * a.n_units / P), u1 = (int)((long long)(cta + 1) * a.n_units / P);
-    if (u1 <= u0) continue;
-    const int r = run_of(a, u1 - 1) - run_of(a, u0) + 1;
-    if (r > max_runs) max_runs = r;
-  }
+  const int most_units = (a.n_units + P - 1) / P;
   const int budget = smem_budget(cps);
-  const uint32_t X = F::S * XR::R;
-  const uint32_t fixed = (uint32_t)kWarps * a.chunk_max * 4 + 1024;
+  const uint32_t XB = (uint32_t)F::S * XR::R;  // a multiple of 128 for every layout
+  static_assert((F::S * XR::R) % 128 == 0, "x' stage must keep the ring slots 128-byte aligned");
+  a.xstage = XB;
+  const uint32_t fixed = 1024;
   const uint32_t per_stage = (uint32_t)kWarps * (L::BYTES + 8);
-  int XS = max_runs < kMaxXSlots ? max_runs : kMaxXSlots;
-  while (XS > 1 && fixed + XS * X + 3 * per_stage > (uint32_t)budget) --XS;
-  int NS = (int)(((uint32_t)budget - fixed - XS * X) / per_stage);
+  auto ns_for = [&](int xs) { return (int)(((uint32_t)budget - fixed - xs * (XB + 8)) / per_stage); };
+  // three x' slots and three weight slots per warp where they fit, else fewer
+  int XS = most_units < 3 ? most_units : 3;
+  while (XS > 2 && ns_for(XS) < 3) --XS;
+  while (XS > 1 && ns_for(XS) < 2) --XS;
+  int NS = ns_for(XS);
   if (NS > kMaxStages) NS = kMaxStages;
-  if (NS < 2) return cudaErrorInvalidConfiguration;
+  if (XS < 1 || NS < 2) return cudaErrorInvalidConfiguration;
   a.NS = NS;
   a.XS = XS;
-  const size_t smem = (size_t)1024 + (size_t)kWarps * NS * L::BYTES + (size_t)XS * X +
-                      (size_t)kWarps * a.chunk_max * 4 + (size_t)kWarps * NS * 8;
+  const size_t smem = (size_t)fixed + (size_t)kWarps * NS * L::BYTES + (size_t)XS * XB + (size_t)kWarps * NS * 8 +
+                      (size_t)XS * 8;
 
   auto kern = gemv_tma_kernel<FMT, NT, LP, SMODE, TPT>;
-  {
-    // the shared-memory opt-in is per device
-    static std::mutex mu;
-    static bool done[64] = {false};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev < 0 || dev >= 64 || !done[dev]) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_budget(1) + 1024);
-      if (e != cudaSuccess) return e;
-      if (dev >= 0 && dev < 64) done[dev] = true;
-    }
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(P);
-  cfg.blockDim = dim3(kThreadsT);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], (const TmaArgs)a);
+  cudaError_t e = opt_in_smem(kern, smem_budget(1) + 1024);
+  if (e != cudaSuccess) return e;
+  void* args[2] = {&maps, &a};
+  e = launch_pdl(reinterpret_cast<const void*>(kern), dim3(P), dim3(kThreadsT), smem, s, args);
   if (e == cudaSuccess) note_launch();
   return e;
 }
@@ -924,14 +965,24 @@ cudaError_t launch_sm(TmaArgs& a, int smode, const void* const* codes, const int
   }
 }
 
+// Up to 4 tokens: fp16 hi / lo halves of x' (4 tokens per MMA tile); more:
+// one fp16 per token (8 per tile), half the MMAs and x' reads per token.
+// The x' record layout follows the same choice (tma_xrec_bytes).
 template <int FMT>
 cudaError_t launch_fmt(TmaArgs& a, int smode, const void* const* codes, const int* rw, cudaStream_t s) {
-  // up to 4 tokens: fp16 hi / lo halves of x' (4 tokens per MMA tile); more:
-  // one fp16 per token (8 per tile), half the MMAs and x' reads per token
   if (a.N == 1) return launch_sm<FMT, 1, 8, 4>(a, smode, codes, rw, s);
   if (a.N <= 4) return launch_sm<FMT, 1, 32, 4>(a, smode, codes, rw, s);
   if (a.N <= 8) return launch_sm<FMT, 1, 32, 8>(a, smode, codes, rw, s);
   return launch_sm<FMT, 2, 32, 8>(a, smode, codes, rw, s);
+}
+
+template <int NT, int LP, int TPT>
+cudaError_t launch_prep_frag(XPrepArgs& a, int blocks, cudaStream_t s) {
+  void* args[1] = {&a};
+  cudaError_t e = launch_pdl(reinterpret_cast<const void*>(xprep_frag_kernel<NT, LP, TPT>), dim3(blocks),
+                             dim3(kThreadsT), 0, s, args);
+  if (e == cudaSuccess) note_launch();
+  return e;
 }
 
 }  // namespace
@@ -951,6 +1002,13 @@ int row_words_of_tma(int fmt, int K) {
 }
 int tma_stage_groups(int fmt) { return stage_groups(fmt); }
 
+size_t tma_xrec_bytes(int N) {
+  if (N <= 1) return XRec<1, 8, 4>::R;
+  if (N <= 4) return XRec<1, 32, 4>::R;
+  if (N <= 8) return XRec<1, 32, 8>::R;
+  return XRec<2, 32, 8>::R;
+}
+
 bool tma_eligible(const TmaWeight& w) {
   const int f = w.format;
   if (!(f == PF_FMT_INT4_G128 || f == PF_FMT_INT3_G128 || f == PF_FMT_INT2_G128 || f == PF_FMT_INT4 ||
@@ -968,6 +1026,8 @@ bool tma_eligible(const TmaWeight& w) {
   return encode_fn() != nullptr;
 }
 
+int tma_tiles(const TmaWeight& w) { return ((w.M + kRowsBlk - 1) / kRowsBlk) * kWarps; }
+
 size_t tma_partial_bytes(const TmaWeight& w, int N) {
   const size_t n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
   const size_t spb = (size_t)(w.K / 128) / stage_groups(w.format);
@@ -976,7 +1036,38 @@ size_t tma_partial_bytes(const TmaWeight& w, int N) {
   return (b + 255) / 256 * 256;
 }
 
-int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int x_dtype, void* workspace,
+int launch_xprep_frag(XPrepJob* xj, int count, int N, int x_dtype, cudaStream_t s, cudaError_t* err) {
+  *err = cudaSuccess;
+  if (count < 1 || count > kXPrepMaxJobs || N < 1 || N > kMaxGemvTokens) return PF_ERR_INVALID_ARGUMENT;
+  XPrepArgs a;
+  memset(&a, 0, sizeof(a));
+  int blocks = 0;
+  for (int k = 0; k < count; ++k) {
+    if (xj[k].K <= 0 || xj[k].K % kPrepCols) return PF_ERR_SHAPE;
+    xj[k].blk0 = blocks;
+    blocks += xj[k].K / kPrepCols;
+    a.xj[k] = xj[k];
+  }
+  a.n_xj = count;
+  a.N = N;
+  a.x_dtype = x_dtype;
+  cudaError_t e;
+  if (N == 1)
+    e = launch_prep_frag<1, 8, 4>(a, blocks, s);
+  else if (N <= 4)
+    e = launch_prep_frag<1, 32, 4>(a, blocks, s);
+  else if (N <= 8)
+    e = launch_prep_frag<1, 32, 8>(a, blocks, s);
+  else
+    e = launch_prep_frag<2, 32, 8>(a, blocks, s);
+  if (e != cudaSuccess) {
+    *err = e;
+    return PF_ERR_CUDA;
+  }
+  return PF_OK;
+}
+
+int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void* workspace, char* partials,
                     cudaStream_t s, cudaError_t* err) {
   *err = cudaSuccess;
   if (count < 1 || count > kTmaMaxJobs || N < 1 || N > kMaxGemvTokens) return PF_ERR_INVALID_ARGUMENT;
@@ -985,21 +1076,18 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
   const void* codes[kTmaMaxJobs];
   int rw[kTmaMaxJobs];
   unsigned* counters = static_cast<unsigned*>(workspace);
-  char* part = static_cast<char*>(workspace) + kWsCounterBytes;
-  int unit0 = 0, run0 = 0, chunk = 128;
+  char* part = partials;
+  int unit0 = 0, tile0 = 0;
   const int fmt = ws[0].format;
   const int S = stage_groups(fmt);
   for (int k = 0; k < count; ++k) {
     const TmaWeight& w = ws[k];
     TmaJob& jb = a.job[k];
-    if (w.format != fmt) return PF_ERR_INVALID_ARGUMENT;
+    if (w.format != fmt || !io[k].xq) return PF_ERR_INVALID_ARGUMENT;
     jb.scales = w.scales;
     jb.mins = static_cast<const __half*>(w.mins);
+    jb.xq = io[k].xq;
     jb.tensor_scale = w.tensor_scale;
-    jb.x = io[k].x;
-    jb.signs = w.had_block ? w.signs : nullptr;
-    jb.had_block = w.had_block;
-    jb.had_rscale = w.had_block ? 1.f / sqrtf((float)w.had_block) : 1.f;
     jb.bias = io[k].bias;
     jb.y = io[k].y;
     jb.M = w.M;
@@ -1008,23 +1096,21 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
     jb.n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
     jb.spb = jb.G / S;
     jb.unit0 = unit0;
-    jb.run0 = run0;
+    jb.tile0 = tile0;
     jb.partials = reinterpret_cast<float*>(part);
     part += tma_partial_bytes(w, N);
     unit0 += jb.n_rb * jb.spb;
-    run0 += jb.spb;
-    const int cc = chunk_cols(w.had_block);
-    if (cc > chunk) chunk = cc;
+    tile0 += tma_tiles(w);
     codes[k] = w.codes;
     rw[k] = row_words_of_tma(fmt, w.K);
   }
   if ((unsigned long long)unit0 * (unsigned long long)(sm_count() * ctas_per_sm() + 1) >= (1ull << 32))
     return PF_ERR_SHAPE;
+  if ((size_t)tile0 > kWsStatusSlot) return PF_ERR_SHAPE;
   a.n_jobs = count;
   a.n_units = unit0;
   a.N = N;
-  a.x_dtype = x_dtype;
-  a.chunk_max = chunk;
+  a.counters = counters;
   a.status = counters + kWsStatusSlot;
   cudaError_t e;
   switch (fmt) {
@@ -1042,28 +1128,6 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, int 
   if (e != cudaSuccess) {
     *err = e;
     return PF_ERR_CUDA;
-  }
-  int blocks = 0, split = 0;
-  for (int k = 0; k < count; ++k) {
-    blocks += (((a.job[k].M + kRowsBlk - 1) / kRowsBlk) * kRowsBlk * N + 31) / 32;
-    split |= a.job[k].spb > 1;
-  }
-  if (split) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(kCombineWarps * 32);
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, combine_kernel, (const TmaArgs)a);
-    if (e == cudaSuccess) note_launch();
-    if (e != cudaSuccess) {
-      *err = e;
-      return PF_ERR_CUDA;
-    }
   }
   return PF_OK;
 }

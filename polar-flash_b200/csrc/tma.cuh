@@ -24,9 +24,10 @@ __device__ __forceinline__ unsigned long long now_ns() {
   return t;
 }
 
-// Bounded wait on an mbarrier phase; false when it gave up (or another warp
-// of the CTA already did).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const volatile int* abort_flag) {
+// Bounded wait on an mbarrier phase; false when it gave up after `limit_ns`
+// (or another warp of the CTA already did).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const volatile int* abort_flag,
+                                          unsigned long long limit_ns = kWaitNs) {
   unsigned long long t0 = 0;
   for (unsigned it = 0;; ++it) {
     uint32_t done;
@@ -41,7 +42,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const v
       const unsigned long long t = now_ns();
       if (t0 == 0)
         t0 = t;
-      else if (t - t0 > kWaitNs)
+      else if (t - t0 > limit_ns)
         return false;
     }
   }
@@ -57,6 +58,13 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int
       " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
       : "memory");
+}
+// Bulk copy (no tensor map) of `bytes` (a multiple of 16; both addresses
+// 16-byte aligned) from global memory into this CTA's shared memory.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
 }
 // cp.async of 4 / 8 bytes (src_bytes = 0: zero fill, nothing read)
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {

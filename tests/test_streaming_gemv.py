@@ -1,11 +1,9 @@
 """GPU parity of the streaming GEMV (the INT formats' decode path, K % 512 == 0):
-grouped launches, rotation-block variants, CTAs whose units span more column
-stages than stay resident, and the fall back for misaligned inputs.
+grouped and mixed-format launches, rotation-block variants, row blocks split
+over many CTAs, and the fall back for misaligned inputs.
 
 Tolerance as in test_gpu_parity: y within 1e-3 normwise of the oracle's fp32
-decode + double-accumulated matvec.  A grouped launch computes every unit and
-every partial-sum combine exactly as a single launch does, so its outputs
-must be bit-identical to the single-weight calls'.
+decode + double-accumulated matvec.
 """
 import numpy as np
 import pytest
@@ -30,9 +28,12 @@ META = {"hadamard_rotation": True, "hadamard_block_size": 128}
 
 @pytest.mark.parametrize("bits", [4, 3, 2])
 @pytest.mark.parametrize("N", [1, 3, 16])
-def test_group_launch_bit_identical_to_single(bits, N):
-    """q/k/v-like group (three M, one K) plus a fifth weight (two launches of
-    at most four), each weight with its own x and bias."""
+def test_group_launch_matches_single(bits, N):
+    """q/k/v-like group (three M, one K) plus two weights with other shapes,
+    each with its own x and bias, in one launch.  The launch deals its units
+    over the CTAs differently from a single-weight launch, so the order of the
+    fp32 stage additions differs: agreement within 1e-5 normwise, and the
+    same call twice gives the same bits."""
     from polarflash_b200 import qlinear
     from polarflash_b200.qweight import qlinear_group
 
@@ -45,12 +46,49 @@ def test_group_launch_bit_identical_to_single(bits, N):
         xs.append(_x(N, K, 50 + i).cuda())
         bs.append((torch.randn(M, generator=torch.Generator().manual_seed(i)) * 0.1).cuda())
     ys = qlinear_group(qws, xs, bs)
+    ys2 = qlinear_group(qws, xs, bs)
     for i, (M, K) in enumerate(shapes):
+        assert torch.equal(ys[i], ys2[i]), f"weight {i}: repeated call differs"
         y1 = qlinear(qws[i], xs[i], bs[i])
-        assert torch.equal(ys[i], y1), f"weight {i}"
+        assert_rel(ys[i].cpu().numpy(), y1.cpu().numpy(), rel=1e-5)
         ref = oracle.linear(f"int{bits}_g128", pays[i], M, K, META, xs[i].float().cpu().numpy(),
                             bs[i].cpu().numpy())
         assert_rel(ys[i].cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("N", [1, 4])
+def test_mixed_format_set_in_one_call(N):
+    """A Llama-like linear set at INT3 and INT2 (and one INT4 weight) in ONE
+    pf_qlinear_group call: one x' preparation launch, one GEMV launch per
+    format; inputs shared by several weights are prepared once.  Every output
+    against the oracle."""
+    from polarflash_b200._lib import kernel_launches
+    from polarflash_b200.qweight import qlinear_group
+
+    shapes = [("q", 512, 1024), ("k", 128, 1024), ("v", 128, 1024), ("o", 512, 512), ("up", 1536, 1024),
+              ("down", 1024, 1536)]
+    xin = {K: _x(N, K, K).cuda() for K in (512, 1024, 1536)}
+    qws, pays, fmts, xs = [], [], [], []
+    for bits in (3, 2):
+        for i, (_, M, K) in enumerate(shapes):
+            qw, pay, _ = _g128_qweight(_w(M, K, 100 * bits + i), bits)
+            qws.append(qw)
+            pays.append(pay)
+            fmts.append(f"int{bits}_g128")
+            xs.append(xin[K])
+    qw4, pay4, _ = _g128_qweight(_w(256, 1024, 77), 4)
+    qws.append(qw4)
+    pays.append(pay4)
+    fmts.append("int4_g128")
+    xs.append(xin[1024])
+    qlinear_group(qws, xs)  # first call: one-time set-up
+    torch.cuda.synchronize()
+    n0 = kernel_launches()
+    ys = qlinear_group(qws, xs)
+    assert kernel_launches() - n0 == 4  # x' preparation + INT3, INT2 and INT4 GEMVs
+    for y, qw, pay, fmt, x in zip(ys, qws, pays, fmts, xs):
+        ref = oracle.linear(fmt, pay, qw.M, qw.K, META, x.float().cpu().numpy())
+        assert_rel(y.cpu().numpy(), ref)
 
 
 @pytest.mark.parametrize("bits", [4, 3, 2])
@@ -71,8 +109,9 @@ def test_rotation_blocks(bits, hb, N, xdt):
 
 @pytest.mark.parametrize("bits,N", [(2, 1), (3, 1), (4, 1), (3, 4)])
 def test_cta_spanning_many_stages(bits, N):
-    """One 128-row block and a very long K: every CTA streams several column
-    stages, more than its resident x' slots, so it re-prepares x' mid-run."""
+    """One 128-row block and a very long K: the row block is split over every
+    CTA of the launch, each streaming many column stages through its x' ring,
+    and the last warp to arrive adds all the parts."""
     from polarflash_b200 import qlinear
 
     M, K = 128, 512 * 640
