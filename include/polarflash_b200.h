@@ -154,13 +154,38 @@ PF_API int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* 
  * Same inputs, outputs and semantics as pf_qlinear, but the scratch space
  * comes from a fixed 8 MiB array inside the library's device image, reserved
  * on every GPU that loads the library until the process exits; no device
- * memory is allocated.  Requests whose pf_qlinear_workspace_size exceeds
- * 8 MiB return PF_ERR_WORKSPACE.  The first call on a device looks up the
- * array's address and zeroes its counters (synchronous), so make it before
- * any stream capture.  All calls on a device share the array: calls that
- * overlap on the GPU (unordered streams) race on it. */
+ * memory is allocated.  A request is refused with PF_ERR_WORKSPACE when even
+ * the least workspace pf_qlinear accepts for it (smaller than
+ * pf_qlinear_workspace_size for batches above 16 tokens) exceeds 8 MiB;
+ * batches above 16 tokens then run the tensor-core GEMM without its stream-K
+ * partial tiles.  The first call on a device looks up the array's address,
+ * zeroes its counters and waits for the device, so make it before any stream
+ * capture.  All calls on a device share the array: calls that overlap on the
+ * GPU (unordered streams) race on it. */
 PF_API int pf_qlinear_noalloc(const pf_qweight* w, const void* x, int x_dtype, int N, const float* bias,
                               float* y, void* stream);
+
+/* Device status after the work queued on `stream` (the call synchronises
+ * the stream).  Every device wait of this library's kernels is bounded: a
+ * wait that runs out records PF_ERR_TIMEOUT in the workspace's status word
+ * and the kernel finishes early with incomplete outputs, after its launch
+ * already returned PF_OK.  *status receives PF_OK or the recorded PF_ERR_*;
+ * *busy_counters (may be NULL) the number of split-K arrival counters not
+ * back at zero (0 after every completed call); `reset` non-zero zeroes the
+ * status word and the counters again so the workspace can be reused.  The
+ * reference surfaces driver failures as RuntimeError
+ * (polarflash_rt/cuda/native_kernels.py:396-410); the Python layer raises it
+ * from this status.  pf_qlinear_noalloc_status does the same for the
+ * library-held scratch array of pf_qlinear_noalloc on the current device. */
+PF_API int pf_workspace_status(void* workspace, int reset, int* status, int* busy_counters, void* stream);
+PF_API int pf_qlinear_noalloc_status(int reset, int* status, int* busy_counters, void* stream);
+/* Runs the library's bounded device wait (the loop every streaming kernel
+ * uses) on a barrier that no thread completes, with a limit of `wait_ns`
+ * (0 < wait_ns <= 2e9): the wait runs out and records PF_ERR_TIMEOUT in the
+ * workspace's status word, as a kernel that timed out does.  A diagnostic of
+ * the timeout path for tests and deployment checks; no counterpart in the
+ * reference. */
+PF_API int pf_wait_selftest(void* workspace, unsigned long long wait_ns, void* stream);
 
 /* W_hat[M][K] (fp32) = decoded weight, followed by the inverse block RWHT
  * when `inverse_rwht` is non-zero and the weight is rotated.  Replaces

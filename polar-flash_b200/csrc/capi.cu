@@ -423,6 +423,7 @@ int do_run(const pf_qweight* w, int N, const float* bias, float* y, void* ws, cu
 }  // namespace
 
 size_t pfb::min_workspace_bytes(const pf_qweight* w, int N) { return workspace_bytes(w, N, false); }
+int pfb::report_cuda(cudaError_t e) { return cuda_status(e); }
 
 static std::atomic<unsigned long long> g_launches{0};
 void pfb::note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }

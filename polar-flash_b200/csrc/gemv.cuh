@@ -8,6 +8,12 @@ namespace pfb {
 // Adds one to the library's count of kernel launches (read by
 // pf_kernel_launches); called after every launch this library makes.
 void note_launch();
+// PF_OK, or PF_ERR_CUDA with `e` kept for pf_last_cuda_error.
+int report_cuda(cudaError_t e);
+// The workspace head after the stream's work: the status word (PF_OK or the
+// PF_ERR_* a kernel recorded), optionally the number of non-zero arrival
+// counters, then optionally zeroed again (pf_workspace_status).
+int read_workspace_head(void* ws, int reset, int* status, int* busy_counters, cudaStream_t s);
 
 // The least workspace pf_qlinear accepts for (w, N) (pf_qlinear_workspace_size
 // reports the size for the fastest paths, which can be larger).

@@ -13,10 +13,16 @@
 //
 // Host code may not use the array's name as a device address (on the host it
 // names a shadow symbol), so the first call on each device, with that device
-// current, looks up the real device address with cudaGetSymbolAddress and
-// zero-fills the split-K arrival counters at the start of the array with a
-// synchronous cudaMemset.  That first call must therefore happen before any
-// stream capture on the device.  Later calls reuse the cached address.
+// current, looks up the real device address with cudaGetSymbolAddress,
+// zero-fills the split-K arrival counters and the status word at the start
+// of the array and waits for the device to finish that fill.  That first call
+// must therefore happen before any stream capture on the device.  Later
+// calls reuse the cached address.
+//
+// A kernel whose bounded wait runs out records PF_ERR_TIMEOUT in the array's
+// status word and may leave arrival counters set; the call has returned
+// PF_OK by then.  pf_qlinear_noalloc_status reads that word (and counts the
+// counters left set) after the stream's work and can zero them again.
 //
 // All calls on a device share the one array and leave their contents in it
 // (the counters end every call at zero again).  Calls whose kernels overlap
@@ -49,6 +55,7 @@ int noalloc_scratch(void** out) {
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) return PF_ERR_CUDA;
     e = cudaMemset(p, 0, kNoAllocCounterBytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();  // ordered before work on any stream
     if (e != cudaSuccess) return PF_ERR_CUDA;
     g_noalloc_ptr[dev] = p;
   }
@@ -72,4 +79,12 @@ extern "C" int pf_qlinear_noalloc(const pf_qweight* w, const void* x, int x_dtyp
   st = noalloc_scratch(&scratch);
   if (st) return st;
   return pf_qlinear(w, x, x_dtype, N, bias, y, scratch, kNoAllocScratchBytes, stream);
+}
+
+extern "C" int pf_qlinear_noalloc_status(int reset, int* status, int* busy_counters, void* stream) {
+  if (!status) return PF_ERR_INVALID_ARGUMENT;
+  void* scratch = nullptr;
+  int st = noalloc_scratch(&scratch);
+  if (st) return st;
+  return pfb::read_workspace_head(scratch, reset, status, busy_counters, static_cast<cudaStream_t>(stream));
 }

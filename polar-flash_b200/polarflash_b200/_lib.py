@@ -44,7 +44,7 @@ EXPORTS = (
     "pf_native_gemv_int4", "pf_native_gemv_int2", "pf_native_gemm_int4", "pf_qlinear_noalloc",
     "pf_add_rmsnorm", "pf_rope_kv", "pf_decode_attention_workspace_size", "pf_decode_attention", "pf_silu_mul",
     "pf_kv_row_bytes", "pf_kv_quantize", "pf_kv_dequantize", "pf_rope_kv_compressed",
-    "pf_decode_attention_compressed",
+    "pf_decode_attention_compressed", "pf_workspace_status", "pf_qlinear_noalloc_status", "pf_wait_selftest",
 )
 
 
@@ -138,6 +138,13 @@ def load():
     L.pf_rope_kv_compressed.argtypes = [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, P]
     L.pf_decode_attention_compressed.restype = I
     L.pf_decode_attention_compressed.argtypes = [P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, P, SZ, P]
+    IP = ctypes.POINTER(I)
+    L.pf_workspace_status.restype = I
+    L.pf_workspace_status.argtypes = [P, I, IP, IP, P]
+    L.pf_qlinear_noalloc_status.restype = I
+    L.pf_qlinear_noalloc_status.argtypes = [I, IP, IP, P]
+    L.pf_wait_selftest.restype = I
+    L.pf_wait_selftest.argtypes = [P, ctypes.c_ulonglong, P]
     _lib = L
     return L
 

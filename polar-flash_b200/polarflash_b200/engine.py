@@ -14,6 +14,7 @@ import torch
 
 from .linear import PolarLinearLayer
 from .pflash import PFlashReader
+from .qweight import check_device_status
 
 try:
     import psutil
@@ -86,6 +87,9 @@ class PFlashCUDAEngine:
         with torch.cuda.stream(self.stream):
             out = layer(x_dev)
         self.stream.synchronize()
+        # a device wait that ran out leaves `out` incomplete: raise as the
+        # reference does for a driver failure
+        check_device_status(self.device, self.stream)
         if not self.keep_cached:
             layer.clear_cache()
         return out

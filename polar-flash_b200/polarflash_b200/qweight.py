@@ -208,6 +208,36 @@ def workspace(device, nbytes: int, stream=None) -> torch.Tensor:
     return ws
 
 
+def workspace_status(ws: torch.Tensor, reset: bool = False, counters: bool = False, stream=None):
+    """(status, busy_counters) of a workspace after the work queued on
+    `stream`: status is OK or the pf_status a device wait recorded
+    (ERR_TIMEOUT); busy_counters (when `counters`) the split-K arrival
+    counters left non-zero.  `reset` zeroes both so the workspace is usable
+    again.  Synchronises the stream."""
+    s = stream if stream is not None else torch.cuda.current_stream(ws.device)
+    st, busy = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.load().pf_workspace_status(_ptr(ws), 1 if reset else 0, ctypes.byref(st),
+                                               ctypes.byref(busy) if counters else None,
+                                               ctypes.c_void_p(s.cuda_stream)), "pf_workspace_status")
+    return int(st.value), (int(busy.value) if counters else None)
+
+
+def check_device_status(device, stream=None) -> None:
+    """Raises RuntimeError (as the reference does for driver failures,
+    native_kernels.py:396-410) when a kernel on `stream`'s cached workspace
+    recorded a timed-out device wait; the workspace is reset first, so later
+    calls can run."""
+    device = torch.device(device)
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    ws = _ws_cache.get((device.index, s.cuda_stream))
+    if ws is None:
+        return
+    st, _ = workspace_status(ws, stream=s)
+    if st != _lib.OK:
+        workspace_status(ws, reset=True, stream=s)
+        _lib.check(st, "device kernel")
+
+
 def _x2(qw: QWeight, x: torch.Tensor):
     if x.device.type != "cuda":
         raise ValueError("polarflash_b200.qlinear needs CUDA input tensors (no CPU path)")

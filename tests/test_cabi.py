@@ -134,3 +134,18 @@ def test_kv_cache_entry_points_validate_without_gpu():
     assert fp(A, P(0x100008), A, A, A, 8, 2, 128, 64, 0.1, A, ws, None) == _lib.ERR_ALIGNMENT  # float4 rows
     assert fp(A, A, A, A, A, 8, 2, 128, 64, 0.1, A, ws - 1, None) == _lib.ERR_WORKSPACE
     assert L.pf_kernel_launches() == launches
+
+
+def test_status_entry_points_validate_on_the_host():
+    """pf_wait_selftest and pf_workspace_status refuse bad arguments before
+    touching the device."""
+    L = _lib.load()
+    st = ctypes.c_int(0)
+    assert L.pf_workspace_status(None, 0, ctypes.byref(st), None, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.pf_workspace_status(0x10000, 0, None, None, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.pf_workspace_status(0x10010, 0, ctypes.byref(st), None, None) == _lib.ERR_ALIGNMENT
+    assert L.pf_wait_selftest(None, 1000, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.pf_wait_selftest(0x10000, 0, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.pf_wait_selftest(0x10000, 3_000_000_000, None) == _lib.ERR_INVALID_ARGUMENT  # above the 2 s limit
+    assert L.pf_wait_selftest(0x10010, 1000, None) == _lib.ERR_ALIGNMENT
+    assert L.pf_qlinear_noalloc_status(0, None, None, None) == _lib.ERR_INVALID_ARGUMENT

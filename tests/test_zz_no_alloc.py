@@ -26,6 +26,9 @@ def _lib():
     L.pf_qlinear_noalloc.restype = ctypes.c_int
     L.pf_qlinear_noalloc.argtypes = [ctypes.POINTER(_lib.PFQWeight), ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    L.pf_qlinear_noalloc_status.restype = ctypes.c_int
+    L.pf_qlinear_noalloc_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                            ctypes.c_void_p]
     return L
 
 
@@ -61,6 +64,69 @@ def test_noalloc_matches_workspace_entry_point_twice(fmt, M, K, N):
         ref = qlinear(qw, x, bias)
         torch.cuda.synchronize()
         _close(y, ref)
+    assert _noalloc_status() == (0, 0)  # status word clear, every arrival counter back at zero
+
+
+def _noalloc_status():
+    L = _lib()
+    st, busy = ctypes.c_int(-1), ctypes.c_int(-1)
+    rc = L.pf_qlinear_noalloc_status(0, ctypes.byref(st), ctypes.byref(busy),
+                                     ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, L.pf_status_string(rc)
+    return st.value, busy.value
+
+
+def _call(L, qw, x, N, bias, y):
+    stream = torch.cuda.current_stream()
+    return L.pf_qlinear_noalloc(ctypes.byref(qw.descriptor()), ctypes.c_void_p(x.data_ptr()), 1, N,
+                                ctypes.c_void_p(bias.data_ptr()) if bias is not None else None,
+                                ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(stream.cuda_stream))
+
+
+# The paths whose scratch use differs from the INT streaming GEMV: the E8
+# table GEMV (batch 1) and tensor-core GEMM (batch 3), the block-8 polar
+# table GEMV, and an INT3 input only 2-byte aligned, which takes the
+# register-prefetch GEMV and its split-K arrival counters.
+@pytest.mark.parametrize("case", ["e8_n1", "e8_n3", "polar8_n1", "int3_misaligned"])
+def test_noalloc_other_paths_twice_and_counters_clear(case):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from polarflash_b200 import encoders, qlinear
+    from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
+    from polarflash_b200.qweight import QWeight
+    from polarflash_b200 import UnifiedQuantizer
+
+    L = _lib()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(17)
+    M, K = 1536, 2048
+    W = torch.randn(M, K, generator=g, device=dev) * 0.02
+    N = 3 if case == "e8_n3" else 1
+    if case.startswith("e8"):
+        idx, sc = encoders.e8_encode(BlockHadamardTransform(K, 128, device=dev).forward(W))
+        qw = QWeight(7, M, K, idx.reshape(-1), sc, None, effective_block(128, K), column_signs(K, 128, dev))
+    elif case == "polar8_n1":
+        payload, meta = encoders.polar_encode(BlockHadamardTransform(K, 128, device=dev).forward(W), 8, 1.75)
+        qw = QWeight(8, M, K, payload, None, None, effective_block(128, K), column_signs(K, 128, dev),
+                     meta["r_scale"], [8] + meta["alloc"])
+    else:
+        qw, _ = UnifiedQuantizer(backend="int3_g128", hadamard_block_size=128).quantize_to_qweight(W)
+    for call in range(2):
+        x = torch.randn(N, K, generator=g, device=dev).half()
+        if case == "int3_misaligned":
+            buf = torch.zeros(N * K + 1, dtype=torch.float16, device=dev)
+            xm = buf[1:].view(N, K)
+            xm.copy_(x)
+            assert xm.data_ptr() % 8 != 0
+            x = xm
+        bias = torch.randn(M, generator=g, device=dev)
+        y = torch.empty(N, M, dtype=torch.float32, device=dev)
+        st = _call(L, qw, x, N, bias, y)
+        assert st == 0, L.pf_status_string(st)
+        ref = qlinear(qw, x, bias)
+        torch.cuda.synchronize()
+        _close(y, ref)
+        assert _noalloc_status() == (0, 0)
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
