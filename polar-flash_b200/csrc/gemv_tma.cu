@@ -868,11 +868,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 int stage_groups(int fmt) { return is_int4(fmt) ? 2 : 4; }
 
-// The shared-memory opt-in of a kernel, once per device.
-template <class K>
-cudaError_t opt_in_smem(K kern, int bytes) {
+// The shared-memory opt-in of kernel `kern`, once per device; `done` is the
+// kernel's own per-device flags.
+cudaError_t opt_in_smem(const void* kern, int bytes, bool (&done)[64]) {
   static std::mutex mu;
-  static bool done[64] = {false};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -947,7 +946,8 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
                       (size_t)XS * 8;
 
   auto kern = gemv_tma_kernel<FMT, NT, LP, SMODE, TPT>;
-  cudaError_t e = opt_in_smem(kern, smem_budget(1) + 1024);
+  static bool opted[64] = {false};  // this instantiation's opt-in, per device
+  cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(kern), smem_budget(1) + 1024, opted);
   if (e != cudaSuccess) return e;
   void* args[2] = {&maps, &a};
   e = launch_pdl(reinterpret_cast<const void*>(kern), dim3(P), dim3(kThreadsT), smem, s, args);
