@@ -3,6 +3,13 @@ used for single-kernel ncu captures of the library's kernels.
 
     python polar-flash_b200/profile_case.py --fmt int3_g128 --M 14336 --K 4096 --N 1 --iters 3
 
+With --set, the Llama-3-8B linear set (q/k/v/o/gate/up/down at INT3 and INT2
+group-128, RWHT 128, batch --N) as ONE pf_qlinear_group call, as bench.py
+issues it (--layer-order: one call per shared input and format instead),
+cycling --copies resident copies of the set:
+
+    python polar-flash_b200/profile_case.py --set --copies 4 --iters 6 --time
+
 With --attention, the decode attention over a KV cache instead: one new
 token, 32 query / 8 KV heads of 128 (Llama-3-8B), --ctx cached positions of
 random rows, for each listed cache mode (fp32 through pf_decode_attention,
@@ -33,9 +40,13 @@ def main():
                     help="resident copies of the weight cycled by the timed calls (more than L2 holds: 126 MB)")
     ap.add_argument("--attention", default=None, help="comma-separated KV cache modes: run decode attention")
     ap.add_argument("--ctx", type=int, default=16384, help="cached positions (--attention)")
+    ap.add_argument("--set", action="store_true", help="the Llama-3-8B linear set at INT3 + INT2 in one call")
+    ap.add_argument("--layer-order", action="store_true", help="with --set: one call per shared input")
     a = ap.parse_args()
     if a.attention:
         return attention_case(a)
+    if a.set:
+        return set_case(a)
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
     W = torch.randn(a.M, a.K, generator=g, device=dev) * 0.02
@@ -66,6 +77,57 @@ def main():
         us = e0.elapsed_time(e1) * 1e3 / reps
         flops = 2.0 * a.M * a.K * a.N
         print(f"time {us:.1f} us  {flops / us / 1e6:.1f} TFLOP/s  {qw.nbytes() / us / 1e3:.1f} GB/s packed")
+
+
+LINEARS = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+           ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
+SHARED = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]
+
+
+def set_case(a):
+    from polarflash_b200.qweight import QWeight, qlinear_group
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    base = {}
+    for fmt in ("int3_g128", "int2_g128"):
+        for name, M, K in LINEARS:
+            W = torch.randn(M, K, generator=g, device=dev) * 0.02
+            base[(fmt, name)], _ = UnifiedQuantizer(backend=fmt, hadamard_block_size=128).quantize_to_qweight(W)
+            del W
+    copies = [base] + [{k: QWeight(q.format, q.M, q.K, q.codes.clone(), q.scales.clone(), q.mins.clone(),
+                                   q.had_block, q.had_signs) for k, q in base.items()} for _ in range(a.copies - 1)]
+    kdim = {n: K for n, _, K in LINEARS}
+    xs = {grp: torch.randn(a.N, kdim[grp[0]], generator=g, device=dev).half() for grp in SHARED}
+    keys = list(base.keys())
+    xl = [xs[next(gp for gp in SHARED if n in gp)] for _, n in keys]
+    outs = [torch.empty(a.N, base[k].M, device=dev) for k in keys]
+
+    def call(i):
+        cp = copies[i % len(copies)]
+        if not a.layer_order:
+            qlinear_group([cp[k] for k in keys], xl, outs=outs)
+            return
+        for fmt in ("int3_g128", "int2_g128"):
+            for grp in SHARED:
+                idx = [keys.index((fmt, n)) for n in grp]
+                qlinear_group([cp[keys[i]] for i in idx], [xl[i] for i in idx], outs=[outs[i] for i in idx])
+
+    for i in range(a.iters):
+        call(i)
+    torch.cuda.synchronize()
+    nbytes = sum(q.nbytes() + a.N * q.K * 2 + a.N * q.M * 4 for q in base.values())
+    print(f"linear set N={a.N}: {nbytes} algorithmic bytes per call, y[0][0,:4] = {outs[0][0, :4].tolist()}")
+    if a.time:
+        reps = max(5, a.iters)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            call(i)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        print(f"time {us:.1f} us per set call  {nbytes / us / 1e3:.1f} GB/s")
 
 
 def attention_case(a):
