@@ -75,24 +75,24 @@ __device__ __forceinline__ unsigned long long gtime() {
   return t;
 }
 
+// The waiting thread may be suspended in try_wait until the phase completes
+// (or 100 us pass) instead of spinning.
 __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, const volatile int* abort_flag) {
   unsigned long long t0 = 0;
-  for (unsigned it = 0;; ++it) {
+  for (;;) {
     uint32_t done;
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
         : "=r"(done)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(100000u)
         : "memory");
     if (done) return true;
-    if ((it & 63) == 63) {
-      if (*abort_flag) return false;
-      const unsigned long long t = gtime();
-      if (t0 == 0)
-        t0 = t;
-      else if (t - t0 > kGemmWaitNs)
-        return false;
-    }
+    if (*abort_flag) return false;
+    const unsigned long long t = gtime();
+    if (t0 == 0)
+      t0 = t;
+    else if (t - t0 > kGemmWaitNs)
+      return false;
   }
 }
 

@@ -54,7 +54,7 @@ constexpr int kThreadsT = kWarps * 32;
 constexpr int kWarpRows = 16;              // rows per warp and unit (one MMA row tile)
 constexpr int kRowsBlk = kWarpRows * kWarps;  // rows per unit
 constexpr int kMaxStages = 8;
-constexpr int kMaxXSlots = 4;
+constexpr int kMaxXSlots = 8;
 
 // Dynamic shared memory per CTA: two CTAs share an SM's 228 KB.
 int smem_budget(int ctas_per_sm) { return ctas_per_sm >= 2 ? 110 * 1024 : 200 * 1024; }
@@ -853,6 +853,13 @@ int ctas_per_sm() {
   return v;
 }
 
+// Ring depth set by an environment variable (tuning sweeps), else `dflt`.
+int ring_knob(const char* name, int dflt, int most) {
+  const char* e = getenv(name);
+  const int v = e ? atoi(e) : dflt;
+  return v < 1 ? 1 : (v > most ? most : v);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -933,12 +940,14 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   const uint32_t fixed = 1024;
   const uint32_t per_stage = (uint32_t)kWarps * (L::BYTES + 8);
   auto ns_for = [&](int xs) { return (int)(((uint32_t)budget - fixed - xs * (XB + 8)) / per_stage); };
-  // three x' slots and three weight slots per warp where they fit, else fewer
-  int XS = most_units < 3 ? most_units : 3;
+  // x' slots (PF_TMA_XS, default 3) and weight slots per warp (PF_TMA_NS, default
+  // as many as fit), fewer x' slots where three weight slots would not fit
+  const int xs_want = ring_knob("PF_TMA_XS", 3, kMaxXSlots), ns_want = ring_knob("PF_TMA_NS", kMaxStages, kMaxStages);
+  int XS = most_units < xs_want ? most_units : xs_want;
   while (XS > 2 && ns_for(XS) < 3) --XS;
   while (XS > 1 && ns_for(XS) < 2) --XS;
   int NS = ns_for(XS);
-  if (NS > kMaxStages) NS = kMaxStages;
+  if (NS > ns_want) NS = ns_want;
   if (XS < 1 || NS < 2) return cudaErrorInvalidConfiguration;
   a.NS = NS;
   a.XS = XS;

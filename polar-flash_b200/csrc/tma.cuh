@@ -24,27 +24,30 @@ __device__ __forceinline__ unsigned long long now_ns() {
   return t;
 }
 
+// A thread waiting in mbarrier.try_wait may be suspended by the hardware
+// until the phase completes or this many nanoseconds pass, instead of
+// spinning (spinning warps take issue slots from the warps that compute).
+constexpr uint32_t kSuspendHintNs = 100000;
+
 // Bounded wait on an mbarrier phase; false when it gave up after `limit_ns`
 // (or another warp of the CTA already did).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const volatile int* abort_flag,
                                           unsigned long long limit_ns = kWaitNs) {
   unsigned long long t0 = 0;
-  for (unsigned it = 0;; ++it) {
+  for (;;) {
     uint32_t done;
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
         : "=r"(done)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     if (done) return true;
-    if ((it & 63) == 63) {
-      if (*abort_flag) return false;
-      const unsigned long long t = now_ns();
-      if (t0 == 0)
-        t0 = t;
-      else if (t - t0 > limit_ns)
-        return false;
-    }
+    if (*abort_flag) return false;
+    const unsigned long long t = now_ns();
+    if (t0 == 0)
+      t0 = t;
+    else if (t - t0 > limit_ns)
+      return false;
   }
 }
 
