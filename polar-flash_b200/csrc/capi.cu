@@ -476,7 +476,8 @@ constexpr int kStreamMaxMembers = 1024;
 // One streaming-GEMV pass (np <= 16 tokens) over `count` weights: one x'
 // preparation launch for the distinct inputs (an input read by several
 // weights of one format is prepared once), then one GEMV launch per format
-// and scale mode, up to kTmaMaxJobs weights each.  Workspace: counters, then
+// and scale mode (INT3 and INT2 group-128 share one), up to kTmaMaxJobs
+// weights each.  Workspace: counters, then
 // x' records, then partial sums (at most tma_member_bytes per weight).
 static int stream_pass(int count, const pf_qweight* const* ws, const void* const* xs, int x_dtype, int np,
                        const float* const* biases, float* const* ys, size_t t0, void* workspace, cudaStream_t s) {
@@ -522,7 +523,12 @@ static int stream_pass(int count, const pf_qweight* const* ws, const void* const
     if (st == PF_ERR_CUDA) return cuda_status(e);
     if (st) return st;
   }
-  // GEMV launches: members of one format and scale mode together
+  // GEMV launches: members of one format and scale mode together, and the
+  // group-128 INT3 and INT2 members in one launch
+  auto joins = [&](int f, int g) {
+    const bool pair = (f == PF_FMT_INT3_G128 || f == PF_FMT_INT2_G128) && (g == PF_FMT_INT3_G128 || g == PF_FMT_INT2_G128);
+    return f == g || pair;
+  };
   bool done[kStreamMaxMembers] = {false};
   char* part = cursor;
   for (int i0 = 0; i0 < count; ++i0) {
@@ -532,7 +538,7 @@ static int stream_pass(int count, const pf_qweight* const* ws, const void* const
     int n = 0, tiles = 0;
     char* part0 = part;
     for (int i = i0; i < count && n < kTmaMaxJobs; ++i) {
-      if (done[i] || ws[i]->format != ws[i0]->format || (ws[i]->scales != nullptr) != (ws[i0]->scales != nullptr))
+      if (done[i] || !joins(ws[i]->format, ws[i0]->format) || (ws[i]->scales != nullptr) != (ws[i0]->scales != nullptr))
         continue;
       const TmaWeight t = tma_weight(ws[i]);
       if (n > 0 && (size_t)(tiles + tma_tiles(t)) > kWsStatusSlot) continue;

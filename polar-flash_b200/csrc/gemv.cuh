@@ -89,6 +89,7 @@ struct TmaJob {  // device view of one weight of a launch
   int M, K, G, n_rb, spb;
   int unit0;                  // first unit of the job
   int tile0;                  // first 16-row arrival counter of the job
+  int fsel;                   // 0: the launch's first format, 1: its second
 };
 
 struct TmaArgs {
@@ -96,7 +97,7 @@ struct TmaArgs {
   unsigned* counters;   // workspace head: 16-row arrival counters (zero, left zero)
   unsigned* status;     // workspace status word
   int n_jobs, n_units, N;
-  int NS, XS;           // weight ring stages per warp, x' ring stages per CTA
+  int NS, XS;           // ring stages of the CTA (XS unused)
   unsigned xstage;      // bytes of one stage of x' records (a multiple of 128)
 };
 
@@ -141,9 +142,9 @@ int tma_stage_groups(int fmt);
 int row_words_of_tma(int fmt, int K);
 // x' records of `count` inputs (any streaming formats) in one launch.
 int launch_xprep_frag(XPrepJob* xj, int count, int N, int x_dtype, cudaStream_t s, cudaError_t* err);
-// One GEMV launch for `count` weights (same format, each with its x' records
-// in io[k].xq) and N <= 16 tokens; split row blocks are reduced inside the
-// launch.  `workspace` holds the counter/status head; every job's partial
+// One GEMV launch for `count` weights (of one format, or of INT3 and INT2
+// group-128 together; each with its x' records in io[k].xq) and N <= 16
+// tokens; split row blocks are reduced inside the launch.  `workspace` holds the counter/status head; every job's partial
 // sums follow one another from `partials` (tma_partial_bytes each, in job
 // order).  Returns a pf_status; *err receives a CUDA error.
 int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void* workspace, char* partials,

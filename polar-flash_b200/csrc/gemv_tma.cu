@@ -445,14 +445,126 @@ __device__ __forceinline__ int cta_of_unit(unsigned u, unsigned U, unsigned P) {
   return (int)((((unsigned long long)u + 1) * P - 1) / U);
 }
 
+// One stage of a CTA's ring for format FMT: the 128-row code tile (one TMA
+// box), the rows' scales / zero points, then the stage's x' records.  Tiles
+// under the 128B swizzle start on a 1024-byte boundary.
+template <int FMT, int SMODE, int XB>
+struct CtaSlot {
+  static constexpr int S = TmaFmt<FMT>::S;
+  static constexpr uint32_t ROW = S * TmaFmt<FMT>::WPG * 4;  // code bytes per row
+  static constexpr uint32_t CW = kRowsBlk * ROW;
+  static constexpr uint32_t SROW = SMODE == kScaleGroup ? S * 4 : (SMODE == kScaleRow ? 4 : 0);
+  static constexpr uint32_t XOFF = (CW + kRowsBlk * SROW + 127) & ~127u;
+  static constexpr uint32_t ALIGN = TmaFmt<FMT>::SW128 ? 1024u : 128u;
+  static constexpr uint32_t BYTES = (XOFF + XB + ALIGN - 1) & ~(ALIGN - 1);
+};
+template <int FA, int FB, int SMODE, int XB>
+struct MixSlot {
+  using A = CtaSlot<FA, SMODE, XB>;
+  using B = CtaSlot<FB, SMODE, XB>;
+  static constexpr uint32_t ALIGN = A::ALIGN > B::ALIGN ? A::ALIGN : B::ALIGN;
+  static constexpr uint32_t RAW = A::BYTES > B::BYTES ? A::BYTES : B::BYTES;
+  static constexpr uint32_t BYTES = (RAW + ALIGN - 1) & ~(ALIGN - 1);
+};
+
+// One unit of format FMT (this warp's 16 rows x S groups) accumulated into
+// y: code words read into registers, decoded by one AND per code pair,
+// mma.sync against the x' B fragments, per-group scale and zero point.
+// codes: the warp's 16-row code tile; sc: its rows' scales; xs: the x' records.
 template <int FMT, int NT, int LP, int SMODE, int TPT>
+__device__ __forceinline__ void unit_body(const unsigned char* codes, const unsigned char* sc, const unsigned char* xs,
+                                          const int (&rl)[2], int c, uint32_t blane, float jts,
+                                          float (&y)[NT][2][TPT / 4]) {
+  using XR = XRec<NT, LP, TPT>;
+  constexpr int S = TmaFmt<FMT>::S;
+  constexpr int kOffset = IntFmt<FMT>::kOffset;
+  constexpr int YT = TPT / 4;
+  constexpr uint32_t SROW = SMODE == kScaleGroup ? S * 4 : (SMODE == kScaleRow ? 4 : 0);
+#pragma unroll
+  for (int pp = 0; pp < S / 2; ++pp) {
+    // scales / zero points of the pair's two groups, then their code words
+    uint32_t sv2[2], mv2[2];
+    float frow[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const unsigned char* sp = sc + rl[hh] * SROW;
+      if constexpr (SMODE == kScaleGroup) {
+        sv2[hh] = lds<uint32_t>(sp + 4 * pp);
+        mv2[hh] = lds<uint32_t>(sp + 2 * S + 4 * pp);
+        frow[hh] = 0.f;
+      } else if constexpr (SMODE == kScaleRow) {
+        frow[hh] = lds<float>(sp);
+        sv2[hh] = mv2[hh] = 0u;
+      } else {
+        frow[hh] = jts;
+        sv2[hh] = mv2[hh] = 0u;
+      }
+    }
+    RowCodes<FMT> rc[2][2];
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t raw[4];
+        load_words<FMT>(codes, rl[hh], 2 * pp + gg, c, raw);
+        rc[gg][hh].set(raw, c);
+      }
+    float acc[2][NT][4];
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+      for (int i = 0; i < NT; ++i) acc[gg][i][0] = acc[gg][i][1] = acc[gg][i][2] = acc[gg][i][3] = 0.f;
+#pragma unroll
+    for (int jp = 0; jp < 4; ++jp)
+#pragma unroll
+      for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int gg = 0; gg < 2; ++gg) {
+          const uint4 bq = lds<uint4>(xs + (2 * pp + gg) * XR::R + (i * 4 + jp) * LP * 16 + blane);
+          const RowCodes<FMT>& r0 = rc[gg][0];
+          const RowCodes<FMT>& r1 = rc[gg][1];
+          mma16816(acc[gg][i], r0.h(4 * jp), r1.h(4 * jp), r0.h(4 * jp + 1), r1.h(4 * jp + 1), bq.x, bq.y);
+          mma16816(acc[gg][i], r0.h(4 * jp + 2), r1.h(4 * jp + 2), r0.h(4 * jp + 3), r1.h(4 * jp + 3), bq.z, bq.w);
+        }
+#pragma unroll
+    for (int gg = 0; gg < 2; ++gg) {
+      const int g = 2 * pp + gg;
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+#pragma unroll
+        for (int u = 0; u < YT; ++u) {
+          // token of accumulator columns 2c, 2c + 1: one token as hi + lo, or two tokens
+          const int t = LP == 8 ? 0 : (TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u);
+          const float2 gs = lds<float2>(xs + g * XR::R + XR::FRAG + t * 16);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            float sv, mv;
+            if constexpr (SMODE == kScaleGroup) {
+              sv = __half2float(__ushort_as_half((unsigned short)(gg ? (sv2[hh] >> 16) : (sv2[hh] & 0xFFFFu))));
+              mv = __half2float(__ushort_as_half((unsigned short)(gg ? (mv2[hh] >> 16) : (mv2[hh] & 0xFFFFu))));
+            } else {
+              sv = frow[hh];
+              mv = -(float)kOffset * sv;
+            }
+            const float q = TPT == 4 ? acc[gg][i][2 * hh] + acc[gg][i][2 * hh + 1] : acc[gg][i][2 * hh + u];
+            y[i][hh][u] += (sv * gs.y) * q + mv * gs.x;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int FA, int FB, int NT, int LP, int SMODE, int TPT>
 __global__ void __launch_bounds__(kThreadsT, 2)
     gemv_tma_kernel(const __grid_constant__ TmaMaps maps, const __grid_constant__ TmaArgs a) {
-  using F = TmaFmt<FMT>;
-  using L = WarpSlot<FMT, SMODE>;
   using XR = XRec<NT, LP, TPT>;
-  constexpr int S = F::S;
-  constexpr int kOffset = IntFmt<FMT>::kOffset;
+  constexpr int S = TmaFmt<FA>::S;
+  static_assert(TmaFmt<FB>::S == S, "formats of one launch share the stage width");
+  constexpr int XB = S * XR::R;  // x' bytes of one stage (a multiple of 128)
+  using SA = CtaSlot<FA, SMODE, XB>;
+  using SB = CtaSlot<FB, SMODE, XB>;
+  constexpr uint32_t SLOT = MixSlot<FA, FB, SMODE, XB>::BYTES;
   constexpr int YT = TPT / 4;  // tokens of a thread per tile
 
   asm volatile("griddepcontrol.launch_dependents;");
@@ -467,17 +579,13 @@ __global__ void __launch_bounds__(kThreadsT, 2)
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ int abort_flag;
-  __shared__ unsigned xcnt[kMaxXSlots];  // warps done with each x' slot
-  __shared__ int xlast;                  // last unit whose x' records were requested
+  __shared__ unsigned scnt[kMaxStages];  // warps done with each ring stage
+  __shared__ int flast;                  // CTA unit ordinal of the last stage fill issued
   unsigned char* const base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  const int NS = a.NS, XS = a.XS;
-  const uint32_t XB = a.xstage;
+  const int NS = a.NS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  unsigned char* const ring = base + (size_t)warp * NS * L::BYTES;  // this warp's weight slots
-  unsigned char* const xring = base + (size_t)kWarps * NS * L::BYTES;
-  const uint32_t bars = smem_u32(xring + (size_t)XS * XB);
-  const uint32_t full0 = bars + warp * NS * 8;     // this warp's weight slots
-  const uint32_t xfull0 = bars + kWarps * NS * 8;  // the x' slots
+  const uint32_t ring_s = smem_u32(base);
+  const uint32_t full0 = ring_s + NS * SLOT;  // NS mbarriers after the stages
 
   const unsigned U = (unsigned)a.n_units, P = gridDim.x, cta = blockIdx.x;
   const int u0 = cta_first_unit(cta, U, P), u1 = cta_first_unit(cta + 1, U, P);  // U * P < 2^32 (host-checked)
@@ -490,100 +598,84 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   }
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    xlast = -1;
-    for (int s = 0; s < XS; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(xfull0 + 8 * s), "r"(1));
-  }
-  if (threadIdx.x < kMaxXSlots) xcnt[threadIdx.x] = 0u;
-  if (lane == 0)
+    flast = -1;
     for (int s = 0; s < NS; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full0 + 8 * s), "r"(33));
+  }
+  if (threadIdx.x < kMaxStages) scnt[threadIdx.x] = 0u;
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   __syncthreads();
   if (nunits <= 0) return;
   const int N = a.N;
   const int c = lane & 3, rq = lane >> 2;
-
-  // ---- load side: this warp's next unit to request (job, row block, stage)
-  int fj = job_of(a, u0), frb, fst;
-  {
-    const TmaJob& jb = a.job[fj];
-    const int v = u0 - jb.unit0;
-    frb = v / jb.spb;
-    fst = v - frb * jb.spb;
-  }
-  const CUtensorMap* fmap = nullptr;
-  const __half* fsc = nullptr;
-  const __half* fmn = nullptr;
-  int fM = 0, fG = 0, fnrb = 1, fspb = 1;
-  auto load_fjob = [&]() {
-    const TmaJob& jb = a.job[fj];
-    fmap = &maps.m[fj];
-    fsc = static_cast<const __half*>(jb.scales);
-    fmn = jb.mins;
-    fM = jb.M;
-    fG = jb.G;
-    fnrb = jb.n_rb;
-    fspb = jb.spb;
-  };
-  load_fjob();
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-  const uint32_t ring_s = smem_u32(ring);
-  // request the next unit into `slot` (which this warp no longer reads)
-  auto request = [&](int slot) {
-    const uint32_t sb = ring_s + slot * L::BYTES, bar = full0 + 8 * slot;
-    const int row0 = frb * kRowsBlk + warp * kWarpRows;
+
+  // Fill ring stage `slot` with the CTA's unit ordinal `i` (called by a whole
+  // warp): lane 0 announces the bytes and issues the TMA of the 128-row code
+  // tile (and, unless `weights_only`, the bulk copy of the stage's x'
+  // records), every lane copies its share of the rows' scales / zero points
+  // with cp.async and arrives on the stage's barrier when they land.
+  auto fill = [&](int slot, int i, bool weights_only) {
+    const int u = u0 + i;
+    const int jj = job_of(a, u);
+    const TmaJob& jb = a.job[jj];
+    const int v = u - jb.unit0, rb = v / jb.spb, st = v - rb * jb.spb;
+    const bool fs = FA != FB && jb.fsel;
+    const uint32_t sb = ring_s + slot * SLOT, bar = full0 + 8 * slot;
+    const uint32_t cw = fs ? SB::CW : SA::CW, xoff = fs ? SB::XOFF : SA::XOFF;
+    const int wpg = fs ? TmaFmt<FB>::WPG : TmaFmt<FA>::WPG;
     __syncwarp();
     if (lane == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_expect(bar, L::W);
-      tma_2d(sb, fmap, fst * S * F::WPG, row0, bar, policy);
+      mbar_expect(bar, cw + XB);
+      tma_2d(sb, &maps.m[jj], st * S * wpg, rb * kRowsBlk, bar, policy);
+      if (!weights_only) bulk_g2s(sb + xoff, jb.xq + (size_t)st * XB, XB, bar);
     }
     if constexpr (SMODE == kScaleGroup) {
-      const int row = lane & 15, which = lane >> 4, grow = row0 + row;
-      const bool ok = grow < fM;
-      const __half* src = (which ? fmn : fsc) + (ok ? (size_t)grow * fG + (size_t)fst * S : 0);
-      const uint32_t d = sb + L::W + row * L::SROW + which * (S * 2);
-      if constexpr (S == 4)
-        cp_async8(d, src, ok ? 8u : 0u);
-      else
-        cp_async4(d, src, ok ? 4u : 0u);
+      const __half* const sc0 = static_cast<const __half*>(jb.scales);
+      const __half* const mn0 = jb.mins;
+      const int M = jb.M, G = jb.G;
+#pragma unroll
+      for (int q = 0; q < 2 * kRowsBlk / 32; ++q) {
+        const int idx = q * 32 + lane, row = idx & (kRowsBlk - 1), which = idx / kRowsBlk;
+        const int grow = rb * kRowsBlk + row;
+        const bool ok = grow < M;
+        const __half* src = (which ? mn0 : sc0) + (ok ? (size_t)grow * G + (size_t)st * S : 0);
+        const uint32_t d = sb + cw + row * SA::SROW + which * (S * 2);
+        if constexpr (S == 4)
+          cp_async8(d, src, ok ? 8u : 0u);
+        else
+          cp_async4(d, src, ok ? 4u : 0u);
+      }
     } else if constexpr (SMODE == kScaleRow) {
-      const int grow = row0 + (lane & 15);
-      const bool ok = lane < 16 && grow < fM;
-      if (lane < 16)
-        cp_async4(sb + L::W + lane * 4, reinterpret_cast<const float*>(fsc) + (ok ? grow : 0), ok ? 4u : 0u);
-    }
-    cp_async_arrive(bar);
-    if (++fst == fspb) {
-      fst = 0;
-      if (++frb == fnrb) {
-        frb = 0;
-        if (++fj < a.n_jobs) load_fjob();
+#pragma unroll
+      for (int q = 0; q < kRowsBlk / 32; ++q) {
+        const int row = q * 32 + lane, grow = rb * kRowsBlk + row;
+        const bool ok = grow < jb.M;
+        cp_async4(sb + cw + row * 4, static_cast<const float*>(jb.scales) + (ok ? grow : 0), ok ? 4u : 0u);
       }
     }
+    cp_async_arrive(bar);
   };
-  // the weights of the first ring slots never come from the preceding grid
-  int requested = 0;
-  for (; requested < NS && requested < nunits; ++requested) request(requested);
-
-  // x' records of unit u (its job's input, its stage) into x' slot `xs`
-  auto xload = [&](int xs, int u) {
+  // x' records of the CTA's unit ordinal i into stage `slot` (after the
+  // preceding grid: they come from the x' preparation launch)
+  auto fill_x = [&](int slot, int i) {
+    const int u = u0 + i;
     const TmaJob& jb = a.job[job_of(a, u)];
     const int st = (u - jb.unit0) % jb.spb;
-    const uint32_t bar = xfull0 + 8 * xs;
-    mbar_expect(bar, XB);
-    bulk_g2s(smem_u32(xring + (size_t)xs * XB), jb.xq + (size_t)st * XB, XB, bar);
+    const bool fs = FA != FB && jb.fsel;
+    bulk_g2s(ring_s + slot * SLOT + (fs ? SB::XOFF : SA::XOFF), jb.xq + (size_t)st * XB, XB, full0 + 8 * slot);
   };
 
+  // the first stages' weights (never written by the preceding grid), one warp per stage
+  const int first = nunits < NS ? nunits : NS;
+  if (warp < first) fill(warp, warp, true);
   // x' records, y, partial sums and counters may be written by the preceding grid
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (threadIdx.x == 0) {
-    int k = 0;
-    for (; k < XS && k < nunits; ++k) xload(k, u0 + k);
-    xlast = u0 + k - 1;
-  }
+  if (warp < first && lane == 0) fill_x(warp, warp);
+  if (threadIdx.x == 0) flast = first - 1;
 
-  // ---- compute side: unit walk (job, row block, stage)
+  // ---- unit walk (job, row block, stage)
   int j = job_of(a, u0), rb, st;
   {
     const TmaJob& jb = a.job[j];
@@ -592,20 +684,20 @@ __global__ void __launch_bounds__(kThreadsT, 2)
     st = v - rb * jb.spb;
   }
   int seg0 = st;  // first stage of this CTA's part of the current row block
-  int rl[2];      // the thread's two rows within the warp's 16
-  rl[0] = row_perm<FMT>(rq);
-  rl[1] = rl[0] + 8;
+  int rl[2];      // the thread's two rows within the warp's 16 (the order depends on the format)
   const uint32_t blane = (uint32_t)(lane & (LP - 1)) * 16;
-
-  // the current job's fields, reloaded when the walk enters the next job
   float jts = 0.f;
   int jM = 0, jnrb = 1, jspb = 1;
+  bool jfs = false;
   auto load_job = [&]() {
     const TmaJob& jb = a.job[j];
     jts = jb.tensor_scale;
     jM = jb.M;
     jnrb = jb.n_rb;
     jspb = jb.spb;
+    jfs = FA != FB && jb.fsel;
+    rl[0] = jfs ? row_perm<FB>(rq) : row_perm<FA>(rq);
+    rl[1] = rl[0] + 8;
   };
   load_job();
 
@@ -614,9 +706,6 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   for (int i = 0; i < NT; ++i)
 #pragma unroll
     for (int u = 0; u < YT; ++u) y[i][0][u] = y[i][1][u] = 0.f;
-
-  // a token held by this thread: accumulator columns 2c, 2c + 1 are one token
-  // as hi + lo (TPT 4) or two tokens (TPT 8)
   auto tok = [&](int i, int u) { return TPT == 4 ? 4 * i + c : 8 * i + 2 * c + u; };
   auto holds = [&](int t) { return t < N && (LP == 32 || c == 0); };
 
@@ -679,14 +768,11 @@ __global__ void __launch_bounds__(kThreadsT, 2)
     }
   };
 
-  int slot = 0, xslot = 0;
-  uint32_t phase = 0, xphase = 0;
+  int slot = 0;
+  uint32_t phase = 0;
   bool live = true;
   for (int it = 0; it < nunits; ++it) {
-    const unsigned char* stg = ring + slot * L::BYTES;
-    const unsigned char* xs = xring + (size_t)xslot * XB;
-    if (live && !(mbar_wait(full0 + 8 * slot, phase, &abort_flag) &&
-                  mbar_wait(xfull0 + 8 * xslot, xphase, &abort_flag))) {
+    if (live && !mbar_wait(full0 + 8 * slot, phase, &abort_flag)) {
       live = false;
       if (lane == 0) {
         abort_flag = 1;
@@ -694,105 +780,33 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       }
     }
     if (live) {
-#pragma unroll
-      for (int pp = 0; pp < S / 2; ++pp) {
-        // scales / zero points of the pair's two groups, then their code words
-        uint32_t sv2[2], mv2[2];
-        float frow[2];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const unsigned char* sp = stg + L::W + rl[hh] * L::SROW;
-          if constexpr (SMODE == kScaleGroup) {
-            sv2[hh] = lds<uint32_t>(sp + 4 * pp);
-            mv2[hh] = lds<uint32_t>(sp + 2 * S + 4 * pp);
-            frow[hh] = 0.f;
-          } else if constexpr (SMODE == kScaleRow) {
-            frow[hh] = lds<float>(sp);
-            sv2[hh] = mv2[hh] = 0u;
-          } else {
-            frow[hh] = jts;
-            sv2[hh] = mv2[hh] = 0u;
-          }
-        }
-        RowCodes<FMT> rc[2][2];
-#pragma unroll
-        for (int gg = 0; gg < 2; ++gg)
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t raw[4];
-            load_words<FMT>(stg, rl[hh], 2 * pp + gg, c, raw);
-            rc[gg][hh].set(raw, c);
-          }
-        float acc[2][NT][4];
-#pragma unroll
-        for (int gg = 0; gg < 2; ++gg)
-#pragma unroll
-          for (int i = 0; i < NT; ++i) acc[gg][i][0] = acc[gg][i][1] = acc[gg][i][2] = acc[gg][i][3] = 0.f;
-#pragma unroll
-        for (int jp = 0; jp < 4; ++jp)
-#pragma unroll
-          for (int i = 0; i < NT; ++i)
-#pragma unroll
-            for (int gg = 0; gg < 2; ++gg) {
-              const uint4 bq = lds<uint4>(xs + (2 * pp + gg) * XR::R + (i * 4 + jp) * LP * 16 + blane);
-              const RowCodes<FMT>& r0 = rc[gg][0];
-              const RowCodes<FMT>& r1 = rc[gg][1];
-              mma16816(acc[gg][i], r0.h(4 * jp), r1.h(4 * jp), r0.h(4 * jp + 1), r1.h(4 * jp + 1), bq.x, bq.y);
-              mma16816(acc[gg][i], r0.h(4 * jp + 2), r1.h(4 * jp + 2), r0.h(4 * jp + 3), r1.h(4 * jp + 3), bq.z,
-                       bq.w);
-            }
-#pragma unroll
-        for (int gg = 0; gg < 2; ++gg) {
-          const int g = 2 * pp + gg;
-#pragma unroll
-          for (int i = 0; i < NT; ++i) {
-#pragma unroll
-            for (int u = 0; u < YT; ++u) {
-              const int t = LP == 8 ? 0 : tok(i, u);
-              const float2 gs = lds<float2>(xs + g * XR::R + XR::FRAG + t * 16);
-#pragma unroll
-              for (int hh = 0; hh < 2; ++hh) {
-                float sv, mv;
-                if constexpr (SMODE == kScaleGroup) {
-                  sv = __half2float(__ushort_as_half((unsigned short)(gg ? (sv2[hh] >> 16) : (sv2[hh] & 0xFFFFu))));
-                  mv = __half2float(__ushort_as_half((unsigned short)(gg ? (mv2[hh] >> 16) : (mv2[hh] & 0xFFFFu))));
-                } else {
-                  sv = frow[hh];
-                  mv = -(float)kOffset * sv;
-                }
-                const float q = TPT == 4 ? acc[gg][i][2 * hh] + acc[gg][i][2 * hh + 1] : acc[gg][i][2 * hh + u];
-                y[i][hh][u] += (sv * gs.y) * q + mv * gs.x;
-              }
-            }
-          }
-        }
-      }
-      // done with this unit's x' records: the last warp refills the slot
+      const unsigned char* stg = base + (size_t)slot * SLOT;
+      if (jfs)
+        unit_body<FB, NT, LP, SMODE, TPT>(stg + warp * kWarpRows * SB::ROW, stg + SB::CW + warp * kWarpRows * SB::SROW,
+                                          stg + SB::XOFF, rl, c, blane, jts, y);
+      else
+        unit_body<FA, NT, LP, SMODE, TPT>(stg + warp * kWarpRows * SA::ROW, stg + SA::CW + warp * kWarpRows * SA::SROW,
+                                          stg + SA::XOFF, rl, c, blane, jts, y);
+      // done with this stage: the last warp to finish it refills it
       __syncwarp();
+      unsigned last = 0;
       if (lane == 0) {
         __threadfence_block();
-        if (atomicAdd(&xcnt[xslot], 1u) == (unsigned)(kWarps - 1)) {
-          atomicExch(&xcnt[xslot], 0u);
+        last = atomicAdd(&scnt[slot], 1u) == (unsigned)(kWarps - 1);
+        if (last) {
+          atomicExch(&scnt[slot], 0u);
           __threadfence_block();
-          if (it + XS < nunits) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            xload(xslot, u0 + it + XS);
-            atomicMax(&xlast, u0 + it + XS);
-          }
         }
       }
-      if (requested < nunits) {  // refill the weight slot just consumed
-        request(slot);
-        ++requested;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last && it + NS < nunits) {
+        fill(slot, it + NS, false);
+        if (lane == 0) atomicMax(&flast, it + NS);
       }
     }
     if (++slot == NS) {
       slot = 0;
       phase ^= 1u;
-    }
-    if (++xslot == XS) {
-      xslot = 0;
-      xphase ^= 1u;
     }
     const bool row_end = st == jspb - 1;
     if (row_end || it == nunits - 1) {
@@ -811,21 +825,12 @@ __global__ void __launch_bounds__(kThreadsT, 2)
     }
     if (row_end) seg0 = 0;
   }
-  if (!live && lane == 0) {
-    // after a timeout: bounded waits on this warp's tiles that may still be in flight
-    volatile int keep_waiting = 0;
-    for (int k = requested > NS ? requested - NS : 0; k < requested; ++k)
-      mbar_wait(full0 + 8 * (k % NS), (k / NS) & 1, &keep_waiting);
-  }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   if (abort_flag && threadIdx.x == 0) {
-    // and on the x' records still in flight
+    // after a timeout: bounded waits on the stages still being filled
     volatile int keep_waiting = 0;
-    for (int k = max(xlast - XS + 1, u0); k <= xlast; ++k) {
-      const int i = k - u0;
-      mbar_wait(xfull0 + 8 * (i % XS), (i / XS) & 1, &keep_waiting);
-    }
+    for (int k = max(flast - NS + 1, 0); k <= flast; ++k) mbar_wait(full0 + 8 * (k % NS), (k / NS) & 1, &keep_waiting);
   }
 }
 
@@ -907,23 +912,31 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
   return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-template <int FMT, int NT, int LP, int SMODE, int TPT>
-cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_words, cudaStream_t s) {
+// Tensor map of one job's packed rows: boxes of one row block (128 rows) x one stage.
+template <int FMT>
+CUresult encode_rows(CUtensorMap* m, const void* codes, int row_words, int M) {
   using F = TmaFmt<FMT>;
-  using L = WarpSlot<FMT, SMODE>;
+  cuuint64_t dims[2] = {(cuuint64_t)row_words, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)row_words * 4};
+  cuuint32_t box[2] = {(cuuint32_t)(F::S * F::WPG), (cuuint32_t)kRowsBlk};
+  cuuint32_t estr[2] = {1, 1};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, F::SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int FA, int FB, int NT, int LP, int SMODE, int TPT>
+cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_words, cudaStream_t s) {
   using XR = XRec<NT, LP, TPT>;
-  auto fn = encode_fn();
-  if (!fn) return cudaErrorNotSupported;
+  constexpr int S = TmaFmt<FA>::S;
+  constexpr int XB = S * XR::R;
+  static_assert(XB % 128 == 0, "x' stage must keep the ring stages 128-byte aligned");
+  constexpr uint32_t SLOT = MixSlot<FA, FB, SMODE, XB>::BYTES;
+  if (!encode_fn()) return cudaErrorNotSupported;
   TmaMaps maps;
   for (int k = 0; k < a.n_jobs; ++k) {
-    cuuint64_t dims[2] = {(cuuint64_t)row_words[k], (cuuint64_t)a.job[k].M};
-    cuuint64_t strides[1] = {(cuuint64_t)row_words[k] * 4};
-    cuuint32_t box[2] = {(cuuint32_t)(F::S * F::WPG), (cuuint32_t)kWarpRows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(&maps.m[k], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes[k]), dims, strides, box,
-                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    F::SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = a.job[k].fsel ? encode_rows<FB>(&maps.m[k], codes[k], row_words[k], a.job[k].M)
+                                     : encode_rows<FA>(&maps.m[k], codes[k], row_words[k], a.job[k].M);
     if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   }
   for (int k = a.n_jobs; k < kTmaMaxJobs; ++k) maps.m[k] = maps.m[0];
@@ -932,29 +945,19 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   int P = sm_count() * cps;
   if (P > a.n_units) P = a.n_units;
   if (P < 1) P = 1;
-  const int most_units = (a.n_units + P - 1) / P;
   const int budget = smem_budget(cps);
-  const uint32_t XB = (uint32_t)F::S * XR::R;  // a multiple of 128 for every layout
-  static_assert((F::S * XR::R) % 128 == 0, "x' stage must keep the ring slots 128-byte aligned");
   a.xstage = XB;
-  const uint32_t fixed = 1024;
-  const uint32_t per_stage = (uint32_t)kWarps * (L::BYTES + 8);
-  auto ns_for = [&](int xs) { return (int)(((uint32_t)budget - fixed - xs * (XB + 8)) / per_stage); };
-  // x' slots (PF_TMA_XS, default 3) and weight slots per warp (PF_TMA_NS, default
-  // as many as fit), fewer x' slots where three weight slots would not fit
-  const int xs_want = ring_knob("PF_TMA_XS", 3, kMaxXSlots), ns_want = ring_knob("PF_TMA_NS", kMaxStages, kMaxStages);
-  int XS = most_units < xs_want ? most_units : xs_want;
-  while (XS > 2 && ns_for(XS) < 3) --XS;
-  while (XS > 1 && ns_for(XS) < 2) --XS;
-  int NS = ns_for(XS);
+  // ring stages per CTA (PF_TMA_NS, default as many as fit)
+  int NS = (int)(((uint32_t)budget - 1024u) / (SLOT + 8u));
+  const int ns_want = ring_knob("PF_TMA_NS", kMaxStages, kMaxStages);
   if (NS > ns_want) NS = ns_want;
-  if (XS < 1 || NS < 2) return cudaErrorInvalidConfiguration;
+  if (NS > kMaxStages) NS = kMaxStages;
+  if (NS < 2) return cudaErrorInvalidConfiguration;
   a.NS = NS;
-  a.XS = XS;
-  const size_t smem = (size_t)fixed + (size_t)kWarps * NS * L::BYTES + (size_t)XS * XB + (size_t)kWarps * NS * 8 +
-                      (size_t)XS * 8;
+  a.XS = 0;
+  const size_t smem = 1024 + (size_t)NS * SLOT + (size_t)NS * 8;
 
-  auto kern = gemv_tma_kernel<FMT, NT, LP, SMODE, TPT>;
+  auto kern = gemv_tma_kernel<FA, FB, NT, LP, SMODE, TPT>;
   static bool opted[64] = {false};  // this instantiation's opt-in, per device
   cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(kern), smem_budget(1) + 1024, opted);
   if (e != cudaSuccess) return e;
@@ -964,25 +967,25 @@ cudaError_t launch_one(TmaArgs& a, const void* const* codes, const int* row_word
   return e;
 }
 
-template <int FMT, int NT, int LP, int TPT>
+template <int FA, int FB, int NT, int LP, int TPT>
 cudaError_t launch_sm(TmaArgs& a, int smode, const void* const* codes, const int* rw, cudaStream_t s) {
-  if constexpr (FMT == PF_FMT_INT4 || FMT == PF_FMT_INT2) {
-    if (smode == kScaleRow) return launch_one<FMT, NT, LP, kScaleRow, TPT>(a, codes, rw, s);
-    return launch_one<FMT, NT, LP, kScaleTensor, TPT>(a, codes, rw, s);
+  if constexpr (FA == PF_FMT_INT4 || FA == PF_FMT_INT2) {
+    if (smode == kScaleRow) return launch_one<FA, FB, NT, LP, kScaleRow, TPT>(a, codes, rw, s);
+    return launch_one<FA, FB, NT, LP, kScaleTensor, TPT>(a, codes, rw, s);
   } else {
-    return launch_one<FMT, NT, LP, kScaleGroup, TPT>(a, codes, rw, s);
+    return launch_one<FA, FB, NT, LP, kScaleGroup, TPT>(a, codes, rw, s);
   }
 }
 
 // Up to 4 tokens: fp16 hi / lo halves of x' (4 tokens per MMA tile); more:
 // one fp16 per token (8 per tile), half the MMAs and x' reads per token.
 // The x' record layout follows the same choice (tma_xrec_bytes).
-template <int FMT>
+template <int FA, int FB = FA>
 cudaError_t launch_fmt(TmaArgs& a, int smode, const void* const* codes, const int* rw, cudaStream_t s) {
-  if (a.N == 1) return launch_sm<FMT, 1, 8, 4>(a, smode, codes, rw, s);
-  if (a.N <= 4) return launch_sm<FMT, 1, 32, 4>(a, smode, codes, rw, s);
-  if (a.N <= 8) return launch_sm<FMT, 1, 32, 8>(a, smode, codes, rw, s);
-  return launch_sm<FMT, 2, 32, 8>(a, smode, codes, rw, s);
+  if (a.N == 1) return launch_sm<FA, FB, 1, 8, 4>(a, smode, codes, rw, s);
+  if (a.N <= 4) return launch_sm<FA, FB, 1, 32, 4>(a, smode, codes, rw, s);
+  if (a.N <= 8) return launch_sm<FA, FB, 1, 32, 8>(a, smode, codes, rw, s);
+  return launch_sm<FA, FB, 2, 32, 8>(a, smode, codes, rw, s);
 }
 
 template <int NT, int LP, int TPT>
@@ -1080,6 +1083,14 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void
                     cudaStream_t s, cudaError_t* err) {
   *err = cudaSuccess;
   if (count < 1 || count > kTmaMaxJobs || N < 1 || N > kMaxGemvTokens) return PF_ERR_INVALID_ARGUMENT;
+  // one format, or the group-128 INT3 and INT2 pair (same stage width)
+  const int fa = ws[0].format;
+  int fb = fa;
+  for (int k = 1; k < count; ++k)
+    if (ws[k].format != fa) fb = ws[k].format;
+  const bool mixed = fb != fa;
+  if (mixed && !((fa == PF_FMT_INT3_G128 && fb == PF_FMT_INT2_G128) || (fa == PF_FMT_INT2_G128 && fb == PF_FMT_INT3_G128)))
+    return PF_ERR_INVALID_ARGUMENT;
   TmaArgs a;
   memset(&a, 0, sizeof(a));
   const void* codes[kTmaMaxJobs];
@@ -1087,12 +1098,10 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void
   unsigned* counters = static_cast<unsigned*>(workspace);
   char* part = partials;
   int unit0 = 0, tile0 = 0;
-  const int fmt = ws[0].format;
-  const int S = stage_groups(fmt);
   for (int k = 0; k < count; ++k) {
     const TmaWeight& w = ws[k];
     TmaJob& jb = a.job[k];
-    if (w.format != fmt || !io[k].xq) return PF_ERR_INVALID_ARGUMENT;
+    if ((w.format != fa && w.format != fb) || !io[k].xq) return PF_ERR_INVALID_ARGUMENT;
     jb.scales = w.scales;
     jb.mins = static_cast<const __half*>(w.mins);
     jb.xq = io[k].xq;
@@ -1103,15 +1112,17 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void
     jb.K = w.K;
     jb.G = w.K / 128;
     jb.n_rb = (w.M + kRowsBlk - 1) / kRowsBlk;
-    jb.spb = jb.G / S;
+    jb.spb = jb.G / stage_groups(w.format);
     jb.unit0 = unit0;
     jb.tile0 = tile0;
+    // INT3 is always the launch's first format when mixed
+    jb.fsel = mixed ? (w.format == PF_FMT_INT2_G128 ? 1 : 0) : 0;
     jb.partials = reinterpret_cast<float*>(part);
     part += tma_partial_bytes(w, N);
     unit0 += jb.n_rb * jb.spb;
     tile0 += tma_tiles(w);
     codes[k] = w.codes;
-    rw[k] = row_words_of_tma(fmt, w.K);
+    rw[k] = row_words_of_tma(w.format, w.K);
   }
   if ((unsigned long long)unit0 * (unsigned long long)(sm_count() * ctas_per_sm() + 1) >= (1ull << 32))
     return PF_ERR_SHAPE;
@@ -1122,17 +1133,21 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void
   a.counters = counters;
   a.status = counters + kWsStatusSlot;
   cudaError_t e;
-  switch (fmt) {
-    case PF_FMT_INT4_G128: e = launch_fmt<PF_FMT_INT4_G128>(a, kScaleGroup, codes, rw, s); break;
-    case PF_FMT_INT3_G128: e = launch_fmt<PF_FMT_INT3_G128>(a, kScaleGroup, codes, rw, s); break;
-    case PF_FMT_INT2_G128: e = launch_fmt<PF_FMT_INT2_G128>(a, kScaleGroup, codes, rw, s); break;
-    case PF_FMT_INT4:
-      e = launch_fmt<PF_FMT_INT4>(a, ws[0].scales ? kScaleRow : kScaleTensor, codes, rw, s);
-      break;
-    case PF_FMT_INT2:
-      e = launch_fmt<PF_FMT_INT2>(a, ws[0].scales ? kScaleRow : kScaleTensor, codes, rw, s);
-      break;
-    default: return PF_ERR_UNSUPPORTED;
+  if (mixed) {
+    e = launch_fmt<PF_FMT_INT3_G128, PF_FMT_INT2_G128>(a, kScaleGroup, codes, rw, s);
+  } else {
+    switch (fa) {
+      case PF_FMT_INT4_G128: e = launch_fmt<PF_FMT_INT4_G128>(a, kScaleGroup, codes, rw, s); break;
+      case PF_FMT_INT3_G128: e = launch_fmt<PF_FMT_INT3_G128>(a, kScaleGroup, codes, rw, s); break;
+      case PF_FMT_INT2_G128: e = launch_fmt<PF_FMT_INT2_G128>(a, kScaleGroup, codes, rw, s); break;
+      case PF_FMT_INT4:
+        e = launch_fmt<PF_FMT_INT4>(a, ws[0].scales ? kScaleRow : kScaleTensor, codes, rw, s);
+        break;
+      case PF_FMT_INT2:
+        e = launch_fmt<PF_FMT_INT2>(a, ws[0].scales ? kScaleRow : kScaleTensor, codes, rw, s);
+        break;
+      default: return PF_ERR_UNSUPPORTED;
+    }
   }
   if (e != cudaSuccess) {
     *err = e;
