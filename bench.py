@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--copies", type=int, default=32)
+    ap.add_argument("--graph-steps", type=int, default=8, help="steps captured per CUDA graph (layers of a decode graph)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode tokens/s figures")
     return ap.parse_args()
@@ -495,7 +496,14 @@ def main():
     torch.cuda.synchronize()
 
     stream = torch.cuda.Stream(device=dev)
-    graphs = []
+    # one CUDA graph per step (per resident copy), and graphs of G consecutive
+    # steps on G different copies, as a decoder captures several layers in one
+    # graph: consecutive launches then overlap through programmatic dependent
+    # launch (a step's weights stream in while the previous step's last CTAs
+    # finish).  The timed region replays K steps as K // G group graphs and
+    # K % G single-step graphs.
+    G = max(1, min(args.graph_steps, len(copies)))
+    graphs, ggraphs = [], []
     launches_per_step = None
     with torch.cuda.stream(stream):
         for cp in copies:
@@ -504,15 +512,34 @@ def main():
             with torch.cuda.graph(gr, stream=stream):
                 step(cp)
             # the library's own count of the kernels one step's graph holds
-            # (every grouped GEMV launch plus its partial-sum combine)
+            # (one x' preparation and one GEMV launch)
             launches_per_step = kernel_launches() - n0
             graphs.append(gr)
+        for g0 in range(0, len(copies) - G + 1, G):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for cp in copies[g0:g0 + G]:
+                    step(cp)
+            ggraphs.append(gr)
     torch.cuda.synchronize()
 
     def replay(k, gl):
         gl[k % len(gl)].replay()
         if world > 1:
             dist.all_gather_into_tensor(gather_buf, y_all)
+
+    def replay_steps(n, gather=True):
+        """n steps: n // G group graphs, then n % G single-step graphs (each
+        step followed by the all-gather of its outputs at N GPUs)."""
+        for i in range(n // G):
+            ggraphs[i % len(ggraphs)].replay()
+            if world > 1 and gather:
+                for _ in range(G):
+                    dist.all_gather_into_tensor(gather_buf, y_all)
+        for i in range(n % G):
+            graphs[i % len(graphs)].replay()
+            if world > 1 and gather:
+                dist.all_gather_into_tensor(gather_buf, y_all)
 
     if world > 1:
         gather_buf = torch.empty(world * y_all.numel(), dtype=torch.float32, device=dev)
@@ -530,8 +557,7 @@ def main():
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(stream)
-        for k in range(args.steps):
-            replay(k, graphs)
+        replay_steps(args.steps)
         e1.record(stream)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
@@ -554,8 +580,7 @@ def main():
         if world > 1:
             r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             r0.record(stream)
-            for k in range(args.steps):
-                graphs[k % len(graphs)].replay()
+            replay_steps(args.steps, gather=False)
             r1.record(stream)
             torch.cuda.synchronize()
             ms_run = r0.elapsed_time(r1) / args.steps
@@ -563,24 +588,27 @@ def main():
             ms_run = ms / args.steps
 
         # the same weights issued in layer order (8 calls per step), timed alike
+        # (G steps per graph as above; the step count rounded up to whole graphs)
         layer_graphs = []
         n0 = kernel_launches()
-        for cp in copies:
+        for g0 in range(0, len(copies) - G + 1, G):
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr, stream=stream):
-                step_layer(cp)
+                for cp in copies[g0:g0 + G]:
+                    step_layer(cp)
             layer_graphs.append(gr)
-        layer_launches = (kernel_launches() - n0) // len(copies)
-        for k in range(args.warmup):
+        layer_launches = (kernel_launches() - n0) // (len(layer_graphs) * G)
+        for k in range(max(1, args.warmup // G)):
             layer_graphs[k % len(layer_graphs)].replay()
         torch.cuda.synchronize()
+        n_lg = max(1, (args.steps + G - 1) // G)
         l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         l0.record(stream)
-        for k in range(args.steps):
+        for k in range(n_lg):
             layer_graphs[k % len(layer_graphs)].replay()
         l1.record(stream)
         torch.cuda.synchronize()
-        ms_layer = l0.elapsed_time(l1) / args.steps
+        ms_layer = l0.elapsed_time(l1) / (n_lg * G)
         del layer_graphs
 
         # e2e through the public API with host buffers: pinned x in, y out,
@@ -686,7 +714,8 @@ def main():
             "config": {"workload": WORKLOAD, "batch": N, "copies": args.copies,
                        "packed_bytes_per_step": packed_bytes, "alg_bytes_per_step": step_bytes,
                        "l2": f"{args.copies} resident copies ({args.copies * packed_bytes / 1e9:.2f} GB) cycled; "
-                             "inputs > 126 MB L2", "parallelism": f"column-shard x{world}"},
+                             "inputs > 126 MB L2", "parallelism": f"column-shard x{world}",
+                       "graph_steps": G},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                          "traffic_unit": "DRAM bytes per step (the step's GEMV launches, one ncu capture)",
