@@ -14,9 +14,12 @@ untouched for the previous 31 steps (inputs >> the 126 MB L2).  The timed
 region replays CUDA graphs of the steps; inputs are resident in HBM.
 
 Metric: effective packed-weight GB/s (algorithmic bytes: packed codes +
-fp16 scales/mins + x + y).  At N GPUs (torchrun) each rank holds a column
-shard of an N-times-wider set (weak scaling: per-rank work is fixed) and the
-step ends with one NCCL all-gather of the step's outputs.
+fp16 scales/mins + x + y).  At N GPUs (torchrun) the same fixed set is
+column-sharded: rank r holds rows [r M / N, (r + 1) M / N) of every linear
+(strong scaling), and every step ends with one NCCL all-gather of the step's
+outputs, captured in the CUDA graphs; the all-gather's time per step is
+reported beside the kernel-only figure (`--scaling weak`: each rank a full
+set of its own).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -55,6 +58,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--copies", type=int, default=32)
     ap.add_argument("--graph-steps", type=int, default=8, help="steps captured per CUDA graph (layers of a decode graph)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="at N GPUs: strong = one fixed set, each rank a row shard of every linear; "
+                         "weak = each rank a full set of its own")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode tokens/s figures")
     return ap.parse_args()
@@ -360,6 +366,18 @@ def cpu_reference_leg(fmt_sets, samples, threads=None):
     return b_total / t_total / 1e9, t_total, cores
 
 
+def cpu_model():
+    """The host CPU's model string (/proc/cpuinfo), for the CPU baseline records."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def host_payload(qw):
     return {"words": qw.codes.cpu().numpy().view(np.uint32).reshape(qw.M, -1),
             "s": qw.scales.cpu().numpy(), "m": qw.mins.cpu().numpy()}
@@ -374,6 +392,9 @@ def run_reference(args, rank, world):
     from polarflash_b200.quantizer import rwht_cpu
     from polarflash_b200 import encoders
 
+    # every host core, whatever OMP_NUM_THREADS the launcher set (torchrun sets 1)
+    oracle.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(os.cpu_count() or 1)
     samples = []
     for fmt in FORMATS:
         bits = int(fmt[3])
@@ -396,9 +417,11 @@ def run_reference(args, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "higher_is_better": True, "scaling": args.scaling if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "batch": args.batch, "step": "one linear of the set, cycled"},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "cpu_model": cpu_model(),
                          "sample": f"{args.steps} linears of the set (cycled), decode + inverse RWHT + fp32 matvec"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -429,19 +452,30 @@ def main():
     from polarflash_b200._lib import kernel_launches
 
     N = args.batch
-    # --- encode one set per format (this rank's column shard of the N-times-wider
-    # set), then replicate the packed buffers into `copies` resident copies
+    from polarflash_b200.parallel import shard_bounds
+
+    strong = world > 1 and args.scaling == "strong"
+    # --- encode one set per format, then replicate the packed buffers into
+    # `copies` resident copies.  Strong scaling: every rank encodes the same
+    # set and keeps rows [r M / N, (r + 1) M / N) of every linear (column
+    # parallel; row shards slice without re-encoding).  Weak: each rank
+    # encodes a full set of its own.
     base = {}
     for fmt in FORMATS:
         bits = int(fmt[3])
         for i, (name, M, K) in enumerate(LINEARS):
-            W = synth_weight(M, K, 1000 + 97 * rank + i, dev)
+            seed = 1000 + i if (strong or world == 1) else 1000 + 97 * rank + i
+            W = synth_weight(M, K, seed, dev)
             Wr = BlockHadamardTransform(K, 128, device=dev).forward(W)
             q, s, m = encoders.quant_g128_asym(Wr, bits)
             words = encoders.pack_g128(q, bits)
             fmt_id = {3: 2, 2: 3}[bits]
-            base[(fmt, name)] = QWeight(fmt_id, M, K, words.view(torch.uint8).flatten(), s, m,
-                                        effective_block(128, K), column_signs(K, 128, dev))
+            qw = QWeight(fmt_id, M, K, words.view(torch.uint8).flatten(), s, m, effective_block(128, K),
+                         column_signs(K, 128, dev))
+            if strong:
+                r0, r1 = shard_bounds(M, world, rank)
+                qw = qw.shard_rows(r0, r1)
+            base[(fmt, name)] = qw
             del W, Wr, q
     copies = []
     for c in range(args.copies):
@@ -460,12 +494,13 @@ def main():
     xs = {grp: torch.randn(N, kdim[grp[0]], generator=g).half().to(dev) for grp in SHARED}
     # every linear's y [N, M] is a contiguous block of one flat buffer, which is
     # also the all-gather buffer at N GPUs and the D2H source of the e2e leg
-    y_total = sum(M for _, M, _ in LINEARS) * len(FORMATS)
+    y_total = sum(base[(fmt, name)].M for fmt in FORMATS for name, _, _ in LINEARS)
     y_all = torch.empty(N * y_total, dtype=torch.float32, device=dev)
     outs = {}
     off = 0
     for fmt in FORMATS:
-        for name, M, _ in LINEARS:
+        for name, _, _ in LINEARS:
+            M = base[(fmt, name)].M  # this rank's rows
             outs[(fmt, name)] = y_all[off:off + N * M].view(N, M)
             off += N * M
     keys = [(fmt, n) for fmt in FORMATS for n, _, _ in LINEARS]
@@ -503,46 +538,61 @@ def main():
     # finish).  The timed region replays K steps as K // G group graphs and
     # K % G single-step graphs.
     G = max(1, min(args.graph_steps, len(copies)))
-    graphs, ggraphs = [], []
-    launches_per_step = None
+    if world > 1:
+        # the step's outputs of every rank, rank-major (at batch 1 each
+        # linear's y is the concatenation of the ranks' row shards)
+        gather_buf = torch.empty(world * y_all.numel(), dtype=torch.float32, device=dev)
+        with torch.cuda.stream(stream):
+            dist.all_gather_into_tensor(gather_buf, y_all)  # communicator set-up before any capture
+        torch.cuda.synchronize()
+
+    def gstep(cp, gather):
+        step(cp)
+        if gather:
+            dist.all_gather_into_tensor(gather_buf, y_all)
+
+    # graphs of the step with the NCCL all-gather captured in them (at N GPUs)
+    # and without it (the kernel-only time; the same at one GPU)
+    def build(gather):
+        singles, groups = [], []
+        with torch.cuda.stream(stream):
+            for cp in copies:
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    gstep(cp, gather)
+                singles.append(gr)
+            for g0 in range(0, len(copies) - G + 1, G):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for cp in copies[g0:g0 + G]:
+                        gstep(cp, gather)
+                groups.append(gr)
+        torch.cuda.synchronize()
+        return singles, groups
+
+    n0 = kernel_launches()
     with torch.cuda.stream(stream):
-        for cp in copies:
-            gr = torch.cuda.CUDAGraph()
-            n0 = kernel_launches()
-            with torch.cuda.graph(gr, stream=stream):
-                step(cp)
-            # the library's own count of the kernels one step's graph holds
-            # (one x' preparation and one GEMV launch)
-            launches_per_step = kernel_launches() - n0
-            graphs.append(gr)
-        for g0 in range(0, len(copies) - G + 1, G):
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr, stream=stream):
-                for cp in copies[g0:g0 + G]:
-                    step(cp)
-            ggraphs.append(gr)
-    torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            step(copies[0])
+    # the library's own count of the kernels one step holds (one x'
+    # preparation and one GEMV launch)
+    launches_per_step = kernel_launches() - n0
+    del gr
+    graphs, ggraphs = build(world > 1)
+    kgraphs, kggraphs = build(False) if world > 1 else (graphs, ggraphs)
 
     def replay(k, gl):
         gl[k % len(gl)].replay()
-        if world > 1:
-            dist.all_gather_into_tensor(gather_buf, y_all)
 
     def replay_steps(n, gather=True):
-        """n steps: n // G group graphs, then n % G single-step graphs (each
-        step followed by the all-gather of its outputs at N GPUs)."""
+        """n steps: n // G group graphs, then n % G single-step graphs; with
+        `gather` (at N GPUs) the graphs that hold each step's all-gather."""
+        sg, gg = (graphs, ggraphs) if gather else (kgraphs, kggraphs)
         for i in range(n // G):
-            ggraphs[i % len(ggraphs)].replay()
-            if world > 1 and gather:
-                for _ in range(G):
-                    dist.all_gather_into_tensor(gather_buf, y_all)
+            gg[i % len(gg)].replay()
         for i in range(n % G):
-            graphs[i % len(graphs)].replay()
-            if world > 1 and gather:
-                dist.all_gather_into_tensor(gather_buf, y_all)
-
-    if world > 1:
-        gather_buf = torch.empty(world * y_all.numel(), dtype=torch.float32, device=dev)
+            sg[i % len(sg)].replay()
 
     with torch.cuda.stream(stream):
         for k in range(args.warmup):
@@ -575,9 +625,12 @@ def main():
             clk["window"] = "timed region + same-graph replays to 1.5 s"
 
         # kernel-only time per step: at one GPU the step holds nothing but the
-        # library's launches, so it is the timed region's; at N GPUs the same
-        # graphs are timed again without the all-gather
+        # library's launches, so it is the timed region's; at N GPUs graphs of
+        # the same steps without the all-gather are timed too
         if world > 1:
+            for k in range(args.warmup):
+                replay(k, kgraphs)
+            torch.cuda.synchronize()
             r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             r0.record(stream)
             replay_steps(args.steps, gather=False)
@@ -625,15 +678,15 @@ def main():
                 for grp in xs:
                     xs[grp].copy_(x_host[grp], non_blocking=True)
                 step(cp)
-                if world == 1:
+                if world > 1:
+                    dist.all_gather_into_tensor(gather_buf, y_all)
+                    y_host.copy_(gather_buf, non_blocking=True)
+                else:
                     y_host.copy_(y_all, non_blocking=True)
             e2e_graphs.append(gr)
 
         def e2e_step(k):
             e2e_graphs[k % len(e2e_graphs)].replay()
-            if world > 1:
-                dist.all_gather_into_tensor(gather_buf, y_all)
-                y_host.copy_(gather_buf, non_blocking=True)
 
         for k in range(5):
             e2e_step(k)
@@ -695,7 +748,7 @@ def main():
         pass
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:
         samples = []
         for fmt in FORMATS:
             for name, M, K in LINEARS:
@@ -703,18 +756,23 @@ def main():
                 grp = next(gp for gp in SHARED if name in gp)
                 samples.append((fmt, name, host_payload(qw), M, K, xs[grp].float().cpu().numpy()))
         gbs, secs, cores = cpu_reference_leg(None, samples)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port", "cpu_model": cpu_model(),
                "sample": f"one pass over the 14-linear set (decode + inverse RWHT + fp32 matvec), {secs:.1f} s"}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "batch": N, "copies": args.copies,
                        "packed_bytes_per_step": packed_bytes, "alg_bytes_per_step": step_bytes,
                        "l2": f"{args.copies} resident copies ({args.copies * packed_bytes / 1e9:.2f} GB) cycled; "
-                             "inputs > 126 MB L2", "parallelism": f"column-shard x{world}",
+                             "inputs > 126 MB L2",
+                       "parallelism": (f"column-shard x{world}: every linear's rows split over the ranks, "
+                                       "NCCL all-gather of the step's outputs in the CUDA graph"
+                                       if strong else f"x{world} ranks, each a full set of its own"
+                                       if world > 1 else "one GPU"),
                        "graph_steps": G},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
@@ -735,6 +793,7 @@ def main():
                             "launches_per_step": layer_launches,
                             "how": "the same weights as 8 calls per step, one per shared input (q|k|v, o, "
                                    "gate|up, down) and format, as a decoder layer issues them"},
+            "allgather_us_per_step": (round((ms_step - ms_run) * 1e3, 2) if world > 1 else None),
             "gpu_launches": launches_per_step * args.steps,
             "decode_tok_s": decode,
             "clocks": clk,
