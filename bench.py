@@ -570,15 +570,17 @@ def main():
         torch.cuda.synchronize()
         return singles, groups
 
-    n0 = kernel_launches()
-    with torch.cuda.stream(stream):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            step(copies[0])
-    # the library's own count of the kernels one step holds (one x'
-    # preparation and one GEMV launch)
-    launches_per_step = kernel_launches() - n0
-    del gr
+    def count_launches():
+        """The library's own count of the kernels one step holds (one x'
+        preparation and one GEMV launch), from a capture."""
+        n0 = kernel_launches()
+        with torch.cuda.stream(stream):
+            g1 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1, stream=stream):
+                step(copies[0])
+        return kernel_launches() - n0
+
+    launches_per_step = count_launches()
     graphs, ggraphs = build(world > 1)
     kgraphs, kggraphs = build(False) if world > 1 else (graphs, ggraphs)
 
@@ -662,7 +664,7 @@ def main():
         l1.record(stream)
         torch.cuda.synchronize()
         ms_layer = l0.elapsed_time(l1) / (n_lg * G)
-        del layer_graphs
+        del layer_graphs, gr
 
         # e2e through the public API with host buffers: pinned x in, y out,
         # copies inside the timed region (graph of H2D -> GEMVs -> D2H)
@@ -671,8 +673,7 @@ def main():
             x_host[grp].copy_(xs[grp].cpu())
         # at N GPUs the step's result is the all-gathered y of every rank's shard
         y_host = torch.empty(world * N * y_total, dtype=torch.float32, pin_memory=True)
-        e2e_graphs = []
-        for cp in copies[:4]:
+        def e2e_graph(cp):
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr, stream=stream):
                 for grp in xs:
@@ -683,7 +684,9 @@ def main():
                     y_host.copy_(gather_buf, non_blocking=True)
                 else:
                     y_host.copy_(y_all, non_blocking=True)
-            e2e_graphs.append(gr)
+            return gr
+
+        e2e_graphs = [e2e_graph(cp) for cp in copies[:4]]
 
         def e2e_step(k):
             e2e_graphs[k % len(e2e_graphs)].replay()
