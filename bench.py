@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--copies", type=int, default=32)
     ap.add_argument("--graph-steps", type=int, default=8, help="steps captured per CUDA graph (layers of a decode graph)")
+    ap.add_argument("--gather", default="nccl", choices=["peer", "nccl"],
+                    help="at N GPUs: peer = the GEMV stores its rows into every rank's buffer over NVLink "
+                         "(pf_qlinear_group_gather); nccl = an NCCL all-gather after the GEMV")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="at N GPUs: strong = one fixed set, each rank a row shard of every linear; "
                          "weak = each rank a full set of its own")
@@ -414,6 +417,20 @@ def run_reference(args, rank, world):
         t += tt
         b += gbs * tt * 1e9
     value = b / t / 1e9
+    # the reference engine's keep_cached=True steady state (cpu/engine.py:58-96):
+    # the fp32 weight decoded once, then one torch.matmul per call
+    tc, bc = 0.0, 0
+    for fmt, name, payload, M, K, x in samples[:len(LINEARS)]:
+        W = torch.from_numpy(oracle.dequantize(fmt, payload, M, K, {"hadamard_rotation": True,
+                                                                     "hadamard_block_size": 128}))
+        xt = torch.from_numpy(x)
+        torch.matmul(xt, W.t())
+        t0 = time.perf_counter()
+        for _ in range(3):
+            torch.matmul(xt, W.t())
+        tc += (time.perf_counter() - t0) / 3
+        bc += payload["words"].nbytes + payload["s"].nbytes + payload["m"].nbytes + x.size * 2 + M * 4
+        del W
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
@@ -422,7 +439,12 @@ def run_reference(args, rank, world):
         "config": {"workload": WORKLOAD, "batch": args.batch, "step": "one linear of the set, cycled"},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                          "cpu_model": cpu_model(),
-                         "sample": f"{args.steps} linears of the set (cycled), decode + inverse RWHT + fp32 matvec"},
+                         "sample": f"{args.steps} linears of the set (cycled), decode + inverse RWHT + fp32 matvec",
+                         "cached_steady": {"value": round(bc / tc / 1e9, 4), "unit": "GB/s",
+                                           "sample": "the reference engine's keep_cached=True steady state: "
+                                                     "fp32 weights decoded beforehand (4-byte weights held in "
+                                                     "host memory), one torch.matmul per linear, "
+                                                     f"{samples[0][0]} set"}},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -538,15 +560,37 @@ def main():
     # finish).  The timed region replays K steps as K // G group graphs and
     # K % G single-step graphs.
     G = max(1, min(args.graph_steps, len(copies)))
-    if world > 1:
+    fused = world > 1 and strong and args.gather == "peer"
+    peer = None
+    if fused:
+        # every rank's copy of every linear's whole y, written by all ranks'
+        # GEMVs (peer stores over NVLink) in place of an all-gather
+        from polarflash_b200.parallel import PeerBuffer, peers_wait, qlinear_group_gather
+
+        y_offs, off = [], PeerBuffer.HEADER
+        for k in keys:
+            y_offs.append(off)
+            off += (4 * N * world * base[k].M + 255) // 256 * 256
+        peer = PeerBuffer(off, device=dev)
+        gather_out = peer.local[PeerBuffer.HEADER:off]
+        set_ws = [copies[0][k] for k in keys]
+        with torch.cuda.stream(stream):  # set-up outside any capture
+            qlinear_group_gather(set_ws, set_xs, peer, y_offs, ws=ws, stream=stream)
+            peers_wait(peer, ws, stream=stream)
+        torch.cuda.synchronize()
+    elif world > 1:
         # the step's outputs of every rank, rank-major (at batch 1 each
         # linear's y is the concatenation of the ranks' row shards)
         gather_buf = torch.empty(world * y_all.numel(), dtype=torch.float32, device=dev)
+        gather_out = gather_buf
         with torch.cuda.stream(stream):
             dist.all_gather_into_tensor(gather_buf, y_all)  # communicator set-up before any capture
         torch.cuda.synchronize()
 
     def gstep(cp, gather):
+        if gather and fused:  # the GEMV's own last CTA waits for the other ranks' rows
+            qlinear_group_gather([cp[k] for k in keys], set_xs, peer, y_offs, ws=ws, stream=stream)
+            return
         step(cp)
         if gather:
             dist.all_gather_into_tensor(gather_buf, y_all)
@@ -671,19 +715,18 @@ def main():
         x_host = {grp: torch.empty(N, xs[grp].shape[1], dtype=torch.float16, pin_memory=True) for grp in xs}
         for grp in x_host:
             x_host[grp].copy_(xs[grp].cpu())
-        # at N GPUs the step's result is the all-gathered y of every rank's shard
-        y_host = torch.empty(world * N * y_total, dtype=torch.float32, pin_memory=True)
+        # at N GPUs the step's result is the gathered y of every rank's shard
+        y_src = gather_out if world > 1 else y_all
+        y_host = torch.empty(y_src.numel() // (4 if y_src.dtype == torch.uint8 else 1),
+                             dtype=torch.float32, pin_memory=True)
+
         def e2e_graph(cp):
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr, stream=stream):
                 for grp in xs:
                     xs[grp].copy_(x_host[grp], non_blocking=True)
-                step(cp)
-                if world > 1:
-                    dist.all_gather_into_tensor(gather_buf, y_all)
-                    y_host.copy_(gather_buf, non_blocking=True)
-                else:
-                    y_host.copy_(y_all, non_blocking=True)
+                gstep(cp, world > 1)
+                y_host.copy_(y_src.view(torch.float32) if y_src.dtype == torch.uint8 else y_src, non_blocking=True)
             return gr
 
         e2e_graphs = [e2e_graph(cp) for cp in copies[:4]]
@@ -789,7 +832,9 @@ def main():
             "e2e": {"value": round(world * step_bytes / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "how": "CUDA graph of public-API calls: pinned x H2D, one pf_qlinear_group call over the set"
-                           + (", NCCL all-gather of the column shards" if world > 1 else "") + ", y D2H"},
+                           + ((", the GEMV storing its rows into every rank's buffer (peer stores), peer wait"
+                               if fused else ", NCCL all-gather of the column shards") if world > 1 else "")
+                           + ", y D2H"},
             "layer_order": {"ms_per_step": round(ms_layer, 5),
                             "GB_s": round(world * step_bytes / (ms_layer / 1e3) / 1e9, 2),
                             "frac": round(step_bytes / (ms_layer / 1e3) / 1e9 / hbm_peak, 4),
@@ -797,6 +842,8 @@ def main():
                             "how": "the same weights as 8 calls per step, one per shared input (q|k|v, o, "
                                    "gate|up, down) and format, as a decoder layer issues them"},
             "allgather_us_per_step": (round((ms_step - ms_run) * 1e3, 2) if world > 1 else None),
+            "gather": (("peer stores from the GEMV over NVLink + flag wait (pf_qlinear_group_gather)" if fused
+                        else "NCCL all-gather captured in the graph") if world > 1 else None),
             "gpu_launches": launches_per_step * args.steps,
             "decode_tok_s": decode,
             "clocks": clk,
@@ -811,6 +858,9 @@ def main():
     gc.collect()
     if world > 1:
         dist.barrier()
+        if peer is not None:
+            peer.close()
+            dist.barrier()
         dist.destroy_process_group()
 
 

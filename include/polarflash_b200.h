@@ -71,7 +71,13 @@ typedef enum pf_status {
  *  PF_FMT_POLAR_RECURSIVE  encode_packed stream (polar_quant.py:381-487):
  *                    MSB-first blocks of params[1..d] bits, rows of K/d blocks;
  *                    params[0] = d (block size), params[1..d] = allocation;
- *                    tensor_scale = r_scale.
+ *                    tensor_scale = r_scale.  scales: NULL (uniform angle
+ *                    grid), or for a weight encoded with learned angle
+ *                    codebooks (fit_codebooks, polar_quant.py:274-300) fp32
+ *                    [d-1][64]: entry 64 j + c is the angle of code c in angle
+ *                    column j (level 0 columns first), i.e. the codebook of
+ *                    j's level at min(c, codebook length - 1)
+ *                    (decode_packed, polar_quant.py:552-554).
  *  PF_FMT_POLAR2D    2-D polar pairs (polar_quant.py:18-73): MSB-first
  *                    (r << theta_bits | theta); params[0] = r_bits,
  *                    params[1] = theta_bits; tensor_scale = r_scale.
@@ -186,6 +192,54 @@ PF_API int pf_qlinear_noalloc_status(int reset, int* status, int* busy_counters,
  * the timeout path for tests and deployment checks; no counterpart in the
  * reference. */
 PF_API int pf_wait_selftest(void* workspace, unsigned long long wait_ns, void* stream);
+
+/* ---- Column-parallel linears with the all-gather fused into the GEMV.
+ *
+ * Rank r of `world` holds rows [r M / world, (r + 1) M / world) of each
+ * weight.  Instead of an all-gather after the GEMV, every rank's kernel
+ * stores its output rows straight into every rank's peer buffer over NVLink
+ * (plain peer stores, no multicast), then raises its flag in every buffer
+ * and waits (bounded) for every rank's flag: when the call's kernels
+ * complete on a rank, all ranks' rows are in its buffer.  pf_peers_wait
+ * repeats that wait in a small kernel, for consumers on another stream.  The reference computes each
+ * linear on one device (polarflash_rt/cuda/engine.py:129-145); this sharding
+ * is the column-parallel form of that contract.
+ *
+ * A peer buffer is device memory of the same size on every rank (the caller
+ * allocates it, zero-filled); its first 256 bytes are the header the calls
+ * use (an epoch and one flag per rank), outputs live at byte offsets >= 256
+ * that are the same on every rank.  pf_peer_export / pf_peer_open exchange
+ * the buffers between the ranks' processes (CUDA IPC; the handle bytes are
+ * passed through the caller's own channel, e.g. torch.distributed). */
+typedef struct pf_peers {
+  int32_t world;              /* ranks, 1..8                                   */
+  int32_t rank;               /* this process's rank                           */
+  void* bases[8];             /* device: each rank's peer buffer, mapped here  */
+  size_t bytes;               /* size of every peer buffer                     */
+} pf_peers;
+/* 64-byte IPC handle of the allocation that holds `ptr`, and ptr's offset in it. */
+PF_API int pf_peer_export(const void* ptr, unsigned char handle[64], size_t* offset);
+/* Maps a peer's exported buffer into this process: *ptr = its base + offset.
+ * *mapping receives the mapping to pass to pf_peer_close. */
+PF_API int pf_peer_open(const unsigned char handle[64], size_t offset, void** ptr, void** mapping);
+PF_API int pf_peer_close(void* mapping);
+/* pf_qlinear_group on this rank's row shards ws[i] (M_i = m_full_i / world
+ * rows each, a multiple of 128), with y of linear i written as
+ * [N][m_full_i] fp32 at byte offset y_offsets[i] (16-byte aligned, >= 256)
+ * of every rank's peer buffer, this rank's rows from row rank * M_i.  Takes
+ * the streaming GEMV (group-128 INT formats, K % 512 == 0, N <= 16, x 16-byte
+ * aligned); else PF_ERR_UNSUPPORTED.  Every rank makes the same sequence of
+ * calls.  The workspace is pf_qlinear_group_workspace_size's. */
+PF_API int pf_qlinear_group_gather(int count, const pf_qweight* const* ws, const void* const* xs, int x_dtype,
+                                   int N, const float* const* biases, const size_t* y_offsets,
+                                   const int* m_full, const pf_peers* peers, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+/* Makes `stream` wait (one small kernel, each wait bounded to 2 s) until
+ * every rank's rows of this rank's latest pf_qlinear_group_gather call are
+ * in its peer buffer (the call's own kernel already waits for them; this is
+ * for consumers ordered after it on another stream).  A wait that gives up
+ * records PF_ERR_TIMEOUT in the workspace status word (pf_workspace_status). */
+PF_API int pf_peers_wait(const pf_peers* peers, void* workspace, void* stream);
 
 /* W_hat[M][K] (fp32) = decoded weight, followed by the inverse block RWHT
  * when `inverse_rwht` is non-zero and the weight is rotated.  Replaces

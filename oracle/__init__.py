@@ -45,6 +45,7 @@ def lib():
             "pfo_polar_alloc": [I, ctypes.c_double, P],
             "pfo_pack_bits_msb": [P, I64, I, P], "pfo_unpack_bits_msb": [P, I64, I, P],
             "pfo_polar_decode": [P, I64, I, P, ctypes.c_double, P],
+            "pfo_polar_decode_cb": [P, I64, I, P, ctypes.c_double, P, P, I, P],
             "pfo_polar2d_decode": [P, I64, I, I, ctypes.c_double, P],
             "pfo_matvec": [P, I64, I64, P, I64, P],
             "pfo_matvec_f32": [P, I64, I64, P, I64, P],
@@ -306,11 +307,19 @@ def unpack_bits_msb(packed, nblk, total_bits):
     return out
 
 
-def polar_decode(packed, nblk, d, alloc, r_scale):
+def polar_decode(packed, nblk, d, alloc, r_scale, codebooks=None):
+    """decode_packed (polar_quant.py:489-575); `codebooks` is the list of
+    learned per-level angle codebooks (fit_codebooks, polar_quant.py:274-300)
+    when the payload was encoded with them."""
     b = _c(np.frombuffer(bytes(packed), np.uint8), np.uint8)
     a = _c(alloc, np.int32)
     out = np.empty(nblk * d, np.float32)
-    lib().pfo_polar_decode(_p(b), nblk, d, _p(a), float(r_scale), _p(out))
+    if codebooks:
+        cb = _c(np.concatenate([np.asarray(c, np.float32).ravel() for c in codebooks]), np.float32)
+        ln = _c([len(np.asarray(c).ravel()) for c in codebooks], np.int32)
+        lib().pfo_polar_decode_cb(_p(b), nblk, d, _p(a), float(r_scale), _p(cb), _p(ln), len(codebooks), _p(out))
+    else:
+        lib().pfo_polar_decode(_p(b), nblk, d, _p(a), float(r_scale), _p(out))
     return out
 
 
@@ -363,8 +372,9 @@ def dequantize(fmt, payload, M, K, meta):
 
     fmt names: int4_g128 / int3_g128 / int2_g128 (payload = dict(words, s, m)),
     int4 / int3 / int2 (reference per-tensor streams), e8_rvq2_g128
-    (dict(idx, scales)), polar_recursive (bytes, meta alloc/r_scale/block_size),
-    polar (2-D pairs).
+    (dict(idx, scales)), polar_recursive (bytes, meta alloc/r_scale/block_size,
+    learned_codebooks when has_learned_codebooks), polar (2-D pairs), fp16 and
+    the e8 backends' fp16 reconstructions (e8_lattice, e8_rvq).
     """
     bits = {"int4": 4, "int3": 3, "int2": 2}
     if fmt.endswith("_g128") and fmt[:4] in bits:
@@ -386,7 +396,8 @@ def dequantize(fmt, payload, M, K, meta):
     elif fmt == "polar_recursive":
         d = int(meta.get("block_size", 8))
         nblk = int(meta["num_blocks"])
-        flat = polar_decode(payload, nblk, d, meta["alloc"], meta["r_scale"])
+        cbs = meta.get("learned_codebooks") if meta.get("has_learned_codebooks") else None
+        flat = polar_decode(payload, nblk, d, meta["alloc"], meta["r_scale"], cbs)
         pad = int(meta.get("pad_len", 0))
         if pad:
             flat = flat[:-pad]
@@ -396,7 +407,7 @@ def dequantize(fmt, payload, M, K, meta):
         flat = polar2d_decode(payload, npairs, int(meta.get("r_bits", 4)),
                               int(meta.get("theta_bits", 4)), meta.get("r_scale", 1.0))
         W = flat[: M * K].reshape(M, K)
-    elif fmt == "fp16":
+    elif fmt in ("fp16", "e8_lattice", "e8_rvq"):  # e8 backends store fp16 reconstructions (:304-306)
         W = np.frombuffer(bytes(payload), np.float16).astype(np.float32).reshape(M, K)
     else:
         raise ValueError(f"oracle: unknown format {fmt}")

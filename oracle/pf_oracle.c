@@ -528,9 +528,12 @@ PFO_API void pfo_unpack_bits_msb(const uint8_t* buf, int64_t nblk, int total_bit
 }
 
 /* decode_packed + inverse_recursive (polar_quant.py:489-575, 252-272), fp32.
- * Blocks start at bit b * total_bits of the stream. */
-PFO_API void pfo_polar_decode(const uint8_t* packed, int64_t nblk, int d, const int* alloc,
-                              double r_scale, float* out) {
+ * Blocks start at bit b * total_bits of the stream.  With learned angle
+ * codebooks (n_cb levels, level l holding cb_len[l] floats from cb +
+ * sum(cb_len[0..l-1]); polar_quant.py:552-554) an angle of level l < n_cb is
+ * cb[l][clamp(code, 0, cb_len[l] - 1)]; other levels use the uniform grid. */
+PFO_API void pfo_polar_decode_cb(const uint8_t* packed, int64_t nblk, int d, const int* alloc, double r_scale,
+                                 const float* cb, const int* cb_len, int n_cb, float* out) {
   int total_bits = 0;
   for (int i = 0; i < d; ++i) total_bits += alloc[i];
   float rs = (float)r_scale;
@@ -546,8 +549,15 @@ PFO_API void pfo_polar_decode(const uint8_t* packed, int64_t nblk, int d, const 
     float th[64];
     int col = 0, dd = d;
     for (int lvl = 0; dd > 1; ++lvl) {
+      int cb_off = 0;
+      for (int l = 0; l < lvl && l < n_cb; ++l) cb_off += cb_len[l];
       for (int j = 0; j < dd / 2; ++j) {
         int c = codes[1 + col + j];
+        if (lvl < n_cb) {
+          int cc = c < cb_len[lvl] - 1 ? c : cb_len[lvl] - 1;
+          th[col + j] = cb[cb_off + cc];
+          continue;
+        }
         float L = (float)(1 << alloc[1 + col + j]);
         float t = ((float)c + 0.5f) / L;
         th[col + j] = lvl == 0 ? t * PFO_2PI_F - PFO_PI_F : t * PFO_HALFPI_F;
@@ -572,6 +582,11 @@ PFO_API void pfo_polar_decode(const uint8_t* packed, int64_t nblk, int d, const 
     }
     for (int i = 0; i < d; ++i) out[b * d + i] = cur[i];
   }
+}
+
+PFO_API void pfo_polar_decode(const uint8_t* packed, int64_t nblk, int d, const int* alloc,
+                              double r_scale, float* out) {
+  pfo_polar_decode_cb(packed, nblk, d, alloc, r_scale, 0, 0, 0, out);
 }
 
 /* 2-D polar payload (polar_quant.py:18-73, unified_quantizer.py:288-312):

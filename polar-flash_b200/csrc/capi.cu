@@ -117,7 +117,12 @@ int check(const pf_qweight* w) {
     case PF_FMT_POLAR_RECURSIVE:
     case PF_FMT_POLAR2D: {
       PolarShape ps;
-      return polar_shape(w, &ps);
+      const int st = polar_shape(w, &ps);
+      if (st) return st;
+      // recursive polar: optional learned angle table (fp32 [d-1][64]); 2-D polar: none
+      if (w->scales && (w->format == PF_FMT_POLAR2D || !aligned(w->scales, 4)))
+        return w->format == PF_FMT_POLAR2D ? PF_ERR_INVALID_ARGUMENT : PF_ERR_ALIGNMENT;
+      return PF_OK;
     }
     default: return PF_ERR_INVALID_ARGUMENT;
   }
@@ -292,6 +297,7 @@ Polar8In polar8_in(const pf_qweight* w, const HadPlan& plan, const void* x, int 
   p.codes = w->codes;
   for (int i = 0; i < 8; ++i) p.alloc[i] = w->params[1 + i];
   p.r_scale = (float)w->tensor_scale;
+  p.angles = static_cast<const float*>(w->scales);
   p.x = x;
   p.x_dtype = x_dtype;
   p.signs = w->had_signs;
@@ -416,6 +422,7 @@ int do_run(const pf_qweight* w, int N, const float* bias, float* y, void* ws, cu
     memcpy(ca.alloc, ps.alloc, sizeof(ca.alloc));
     ca.r_scale = (float)w->tensor_scale;
     ca.zero_rule = w->format == PF_FMT_POLAR2D;
+    ca.angles = w->format == PF_FMT_POLAR_RECURSIVE ? static_cast<const float*>(w->scales) : nullptr;
   }
   return cuda_status(launch_gemv_cc(ca, s));
 }
@@ -480,7 +487,9 @@ constexpr int kStreamMaxMembers = 1024;
 // weights each.  Workspace: counters, then
 // x' records, then partial sums (at most tma_member_bytes per weight).
 static int stream_pass(int count, const pf_qweight* const* ws, const void* const* xs, int x_dtype, int np,
-                       const float* const* biases, float* const* ys, size_t t0, void* workspace, cudaStream_t s) {
+                       const float* const* biases, float* const* ys, size_t t0, void* workspace, cudaStream_t s,
+                       const pf_peers* peers = nullptr, const size_t* y_offsets = nullptr,
+                       const int* m_full = nullptr) {
   if (count < 1 || count > kStreamMaxMembers) return PF_ERR_INVALID_ARGUMENT;
   const size_t xsz = dtype_size(x_dtype);
   char* cursor = static_cast<char*>(workspace) + kCounterBytes;
@@ -541,18 +550,27 @@ static int stream_pass(int count, const pf_qweight* const* ws, const void* const
       if (done[i] || !joins(ws[i]->format, ws[i0]->format) || (ws[i]->scales != nullptr) != (ws[i0]->scales != nullptr))
         continue;
       const TmaWeight t = tma_weight(ws[i]);
-      if (n > 0 && (size_t)(tiles + tma_tiles(t)) > kWsStatusSlot) continue;
+      if (n > 0 && (size_t)(tiles + tma_tiles(t)) > kWsDoneSlot) continue;
       tw[n] = t;
       io[n].x = nullptr;
       io[n].bias = biases ? biases[i] : nullptr;
-      io[n].y = ys[i] + t0 * ws[i]->M;
+      io[n].y = ys ? ys[i] + t0 * ws[i]->M : nullptr;
       io[n].xq = xq_of[i];
+      if (peers) {  // tokens t0.. of linear i's gathered y, this rank's rows
+        io[n].yoff = y_offsets[i] + t0 * (size_t)m_full[i] * sizeof(float);
+        io[n].m_full = m_full[i];
+        io[n].row0 = peers->rank * ws[i]->M;
+      } else {
+        io[n].yoff = 0;
+        io[n].m_full = 0;
+        io[n].row0 = 0;
+      }
       tiles += tma_tiles(t);
       part += tma_partial_bytes(t, np);
       done[i] = true;
       ++n;
     }
-    int st = launch_gemv_tma(tw, io, n, np, workspace, part0, s, &e);
+    int st = launch_gemv_tma(tw, io, n, np, workspace, part0, peers, s, &e);
     if (st == PF_ERR_CUDA) return cuda_status(e);
     if (st) return st;
   }
@@ -717,7 +735,7 @@ static int group_lut_kind(int count, const pf_qweight* const* ws, int N) {
     const pf_qweight* w = ws[i];
     if (w->format != f || w->K != ws[0]->K || w->had_block != ws[0]->had_block || w->had_signs != ws[0]->had_signs)
       return 0;
-    if (pol && memcmp(w->params, ws[0]->params, 9 * sizeof(int32_t)) != 0) return 0;
+    if (pol && (memcmp(w->params, ws[0]->params, 9 * sizeof(int32_t)) != 0 || w->scales != ws[0]->scales)) return 0;
   }
   return e8 ? 1 : 2;
 }
@@ -815,6 +833,35 @@ int pf_qlinear_group(int count, const pf_qweight* const* ws, const void* const* 
   return PF_OK;
 }
 
+int pf_qlinear_group_gather(int count, const pf_qweight* const* ws, const void* const* xs, int x_dtype, int N,
+                            const float* const* biases, const size_t* y_offsets, const int* m_full,
+                            const pf_peers* peers, void* workspace, size_t ws_bytes, void* stream) {
+  if (count < 1 || !ws || !xs || !y_offsets || !m_full || !peers || N < 0) return PF_ERR_INVALID_ARGUMENT;
+  if (x_dtype < PF_DTYPE_F32 || x_dtype > PF_DTYPE_BF16) return PF_ERR_INVALID_ARGUMENT;
+  if (peers->world < 1 || peers->world > kMaxPeers || peers->rank < 0 || peers->rank >= peers->world)
+    return PF_ERR_INVALID_ARGUMENT;
+  for (int p = 0; p < peers->world; ++p)
+    if (!peers->bases[p] || !aligned(peers->bases[p], 256)) return PF_ERR_ALIGNMENT;
+  for (int i = 0; i < count; ++i) {
+    int st = check(ws[i]);
+    if (st) return st;
+    if (!xs[i]) return PF_ERR_INVALID_ARGUMENT;
+    const float* b = biases ? biases[i] : nullptr;
+    if ((b && !aligned(b, 4)) || !aligned(xs[i], dtype_size(x_dtype))) return PF_ERR_ALIGNMENT;
+    if ((long long)m_full[i] != (long long)peers->world * ws[i]->M) return PF_ERR_SHAPE;
+    if (y_offsets[i] < kPeerHeader || y_offsets[i] % 16) return PF_ERR_ALIGNMENT;
+    if (y_offsets[i] + (size_t)N * m_full[i] * sizeof(float) > peers->bytes) return PF_ERR_SHAPE;
+  }
+  if (N == 0) return PF_OK;
+  if (N > kMaxGemvTokens || !group_streams(count, ws)) return PF_ERR_UNSUPPORTED;
+  for (int i = 0; i < count; ++i)
+    if (!x_tma_aligned(xs[i], x_dtype)) return PF_ERR_UNSUPPORTED;
+  if (!workspace || ws_bytes < group_bytes(count, ws, N)) return PF_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return PF_ERR_ALIGNMENT;
+  return stream_pass(count, ws, xs, x_dtype, N, biases, nullptr, 0, workspace, static_cast<cudaStream_t>(stream),
+                     peers, y_offsets, m_full);
+}
+
 int pf_dequant(const pf_qweight* w, float* W_out, int inverse_rwht, void* stream) {
   int st = check(w);
   if (st) return st;
@@ -839,6 +886,7 @@ int pf_dequant(const pf_qweight* w, float* W_out, int inverse_rwht, void* stream
     memcpy(a.alloc, ps.alloc, sizeof(a.alloc));
     a.r_scale = (float)w->tensor_scale;
     a.zero_rule = w->format == PF_FMT_POLAR2D;
+    a.angles = w->format == PF_FMT_POLAR_RECURSIVE ? static_cast<const float*>(w->scales) : nullptr;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = cuda_status(launch_dequant(a, s));

@@ -48,10 +48,13 @@ __device__ __forceinline__ uint32_t read_bits_msb(const uint8_t* __restrict__ bu
 // Polar angle tables in shared memory: for angle column j (0..d-2, level 0
 // first), entry c holds (cos th, sin th) of the reference's uniform
 // reconstruction (polar_quant.py:540-559): level 0 th = ((c+.5)/2^b) 2pi - pi,
-// upper levels th = ((c+.5)/2^b) pi/2.
+// upper levels th = ((c+.5)/2^b) pi/2; or, for a weight encoded with learned
+// angle codebooks (polar_quant.py:552-554), th = angles[64 j + c] from the
+// weight's fp32 angle table.
 constexpr int kPolarTabPerCol = 64;  // angle codes up to 6 bits
 
-__device__ __forceinline__ void polar_fill_tables(float2* tab, int d, const int* alloc) {
+__device__ __forceinline__ void polar_fill_tables(float2* tab, int d, const int* alloc,
+                                                  const float* angles = nullptr) {
   const float kPi = 3.14159274101257324f, k2Pi = 6.28318548202514648f, kHalfPi = 1.57079637050628662f;
   for (int e = threadIdx.x; e < (d - 1) * kPolarTabPerCol; e += blockDim.x) {
     int j = e / kPolarTabPerCol, c = e % kPolarTabPerCol;
@@ -60,6 +63,7 @@ __device__ __forceinline__ void polar_fill_tables(float2* tab, int d, const int*
     float L = (float)(1 << bits);
     float t = ((float)c + 0.5f) / L;
     float th = (j < d / 2) ? t * k2Pi - kPi : t * kHalfPi;
+    if (angles) th = angles[e];
     tab[e] = make_float2(cosf(th), sinf(th));
   }
 }

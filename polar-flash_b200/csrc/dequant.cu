@@ -80,7 +80,7 @@ __global__ void dequant_polar_kernel(DequantArgs a) {
   __shared__ float2 tab[15 * kPolarTabPerCol];
   __shared__ int alloc_s[17];
   if (threadIdx.x < 17) alloc_s[threadIdx.x] = a.alloc[threadIdx.x];
-  polar_fill_tables(tab, a.d, a.alloc);
+  polar_fill_tables(tab, a.d, a.alloc, a.angles);
   __syncthreads();
   const int nblk = a.K / a.d;
   const long long total = (long long)a.M * a.row_bytes;

@@ -25,6 +25,8 @@ size_t min_workspace_bytes(const pf_qweight* w, int N);
 constexpr size_t kWsCounterSlots = 16384;
 constexpr size_t kWsCounterBytes = kWsCounterSlots * sizeof(unsigned);
 constexpr size_t kWsStatusSlot = kWsCounterSlots - 1;
+// CTAs of a gathering GEMV launch that have finished (zero, left zero)
+constexpr size_t kWsDoneSlot = kWsStatusSlot - 1;
 
 struct GemvIntArgs {
   const void* codes;
@@ -67,6 +69,7 @@ struct GemvCCArgs {
   int alloc[17];
   float r_scale;
   int zero_rule;   // 2-D polar: theta = 0 where r_hat <= 1e-12
+  const float* angles;  // recursive polar: learned angle table [d-1][64], or nullptr
 };
 
 cudaError_t launch_gemv_cc(const GemvCCArgs& a, cudaStream_t s);
@@ -90,12 +93,25 @@ struct TmaJob {  // device view of one weight of a launch
   int unit0;                  // first unit of the job
   int tile0;                  // first 16-row arrival counter of the job
   int fsel;                   // 0: the launch's first format, 1: its second
+  // gathering launches: y of the whole linear at byte offset yoff of every
+  // rank's peer buffer, [N][m_full], this rank's rows from row0
+  unsigned long long yoff;
+  int m_full, row0;
 };
+
+// Peer buffers of a gathering launch (pf_peers): world ranks' buffers, each
+// mapped in this process; the first kPeerHeader bytes hold the rank's epoch
+// (offset 0) and one flag per source rank (offset 16 + 4 q).
+constexpr int kMaxPeers = 8;
+constexpr size_t kPeerHeader = 256;
 
 struct TmaArgs {
   TmaJob job[kTmaMaxJobs];
   unsigned* counters;   // workspace head: 16-row arrival counters (zero, left zero)
   unsigned* status;     // workspace status word
+  unsigned* done;       // gathering launches: finished-CTA counter (zero, left zero)
+  unsigned char* peer[kMaxPeers];  // gathering launches: every rank's peer buffer
+  int world, rank;      // world 0: y goes to job.y (no gathering)
   int n_jobs, n_units, N;
   int NS, XS;           // ring stages of the CTA (XS unused)
   unsigned xstage;      // bytes of one stage of x' records (a multiple of 128)
@@ -114,6 +130,8 @@ struct TmaIO {
   const float* bias;
   float* y;
   const unsigned char* xq;  // the job's x' records (from launch_xprep_frag)
+  unsigned long long yoff;  // gathering launches: the job's y in the peer buffers
+  int m_full, row0;
 };
 
 // One input of launch_xprep_frag: x' records of x [N][K] for weights of
@@ -147,8 +165,10 @@ int launch_xprep_frag(XPrepJob* xj, int count, int N, int x_dtype, cudaStream_t 
 // tokens; split row blocks are reduced inside the launch.  `workspace` holds the counter/status head; every job's partial
 // sums follow one another from `partials` (tma_partial_bytes each, in job
 // order).  Returns a pf_status; *err receives a CUDA error.
+// `peers` (nullable): a gathering launch, each job's rows stored into every
+// rank's peer buffer, then the rank's flag raised in every buffer.
 int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void* workspace, char* partials,
-                    cudaStream_t s, cudaError_t* err);
+                    const pf_peers* peers, cudaStream_t s, cudaError_t* err);
 
 // ---- streaming lookup-table GEMVs at batch 1 (gemv_lut.cu): E8 RVQ2, and
 // recursive polar with block 8 and allocation [3 | 2 2 2 2 | 1 1 | 1]
@@ -177,6 +197,7 @@ struct Polar8In {
   const void* codes;     // rows of K/8 14-bit MSB-first block codes (K * 7 / 32 bytes per row)
   int alloc[8];          // the block allocation (must be 3 2 2 2 2 1 1 1)
   float r_scale;
+  const float* angles;   // learned angle table [7][64], or nullptr (uniform angles)
   const void* x;
   int x_dtype;
   const int8_t* signs;
@@ -228,6 +249,7 @@ struct DequantArgs {
   int d, tb, row_bytes, zero_rule;
   int alloc[17];
   float r_scale;
+  const float* angles;  // recursive polar: learned angle table [d-1][64], or nullptr
   float* W;        // [M][K] fp32, or nullptr
   uint8_t* codes_out;  // unpack mode
 };

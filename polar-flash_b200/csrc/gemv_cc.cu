@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(kWarpsCC * 32) gemv_polar_kernel(GemvCCArgs a)
   __shared__ float2 tab[15 * kPolarTabPerCol];
   __shared__ int alloc_s[17];
   if (threadIdx.x < 17) alloc_s[threadIdx.x] = a.alloc[threadIdx.x];
-  polar_fill_tables(tab, a.d, a.alloc);
+  polar_fill_tables(tab, a.d, a.alloc, a.angles);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kWarpsCC + warp;

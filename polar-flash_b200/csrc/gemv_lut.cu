@@ -73,6 +73,7 @@ struct LutArgs {
   LutJob job[kLutMaxJobs];
   const void* x;  // shared by the jobs
   const int8_t* signs;
+  const float* angles;  // polar: learned angle table shared by the jobs, or nullptr
   unsigned* status;
   float had_rscale;
   int n_jobs, had_block, x_dtype, K, G, n_rb, spb, n_units, NS, XS;
@@ -169,9 +170,9 @@ struct Polar8Pol {
   static constexpr int kTabFloats = (kCols / 8) * 128;
   static constexpr int kAuxFloat2 = 7 * kPolarTabPerCol;  // cos / sin of every angle column and code
   struct State {};
-  __device__ static void init(State&, float2* aux, const LutArgs&) {
+  __device__ static void init(State&, float2* aux, const LutArgs& a) {
     const int alloc[8] = {3, 2, 2, 2, 2, 1, 1, 1};
-    polar_fill_tables(aux, 8, alloc);
+    polar_fill_tables(aux, 8, alloc, a.angles);
   }
   // thread t: vector t / 8, half (t / 4) % 2, entries 16 (t % 4) .. + 16
   __device__ static void build(const State&, const LutArgs& a, const float* xs, float* tab, const float2* cs) {
@@ -719,7 +720,8 @@ int launch_polar8_lut(const Polar8In* in, int count, void* workspace, cudaStream
   const void* codes[kLutMaxJobs];
   for (int k = 0; k < count; ++k) {
     if (!polar8_lut_eligible(in[k]) || in[k].x != in[0].x || in[k].K != in[0].K ||
-        in[k].had_block != in[0].had_block || in[k].signs != in[0].signs || in[k].x_dtype != in[0].x_dtype)
+        in[k].had_block != in[0].had_block || in[k].signs != in[0].signs || in[k].x_dtype != in[0].x_dtype ||
+        in[k].angles != in[0].angles)
       return PF_ERR_UNSUPPORTED;
     LutJob& jb = a.job[k];
     jb.bias = in[k].bias;
@@ -729,6 +731,7 @@ int launch_polar8_lut(const Polar8In* in, int count, void* workspace, cudaStream
     codes[k] = in[k].codes;
   }
   a.n_jobs = count;
+  a.angles = in[0].angles;
   return launch_lut<Polar8Pol>(a, codes, workspace, s, err);
 }
 

@@ -604,7 +604,48 @@ __global__ void __launch_bounds__(kThreadsT, 2)
   if (threadIdx.x < kMaxStages) scnt[threadIdx.x] = 0u;
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   __syncthreads();
-  if (nunits <= 0) return;
+  // Gathering launches: once every CTA's rows are stored (in every rank's
+  // buffer), the last CTA to finish raises this rank's flag in every buffer
+  // to the rank's next epoch (system-scope release), then waits (bounded)
+  // until every rank's flag in the local buffer has reached that epoch
+  // (acquire): when the launch completes, all ranks' rows are here.  Every
+  // rank raises its flag before it waits, and each rank runs on its own GPU.
+  auto signal_done = [&]() {
+    if (a.world <= 0) return;
+    __syncthreads();  // the block's peer stores come before thread 0's fence (cumulative)
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    if (atomicAdd(a.done, 1u) == gridDim.x - 1) {
+      atomicExch(a.done, 0u);
+      __threadfence_system();
+      volatile unsigned* ep = reinterpret_cast<volatile unsigned*>(a.peer[a.rank]);
+      const unsigned e = *ep + 1u;
+      *ep = e;
+      for (int pr = 0; pr < a.world; ++pr) {
+        unsigned* flag = reinterpret_cast<unsigned*>(a.peer[pr] + 16 + 4 * a.rank);
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(e) : "memory");
+      }
+      const unsigned long long t0 = now_ns();
+      for (int q = 0; q < a.world; ++q) {
+        const unsigned* flag = reinterpret_cast<const unsigned*>(a.peer[a.rank] + 16 + 4 * q);
+        for (;;) {
+          unsigned f;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flag) : "memory");
+          if ((int)(f - e) >= 0) break;
+          if (now_ns() - t0 > kWaitNs) {
+            atomicExch(a.status, (unsigned)PF_ERR_TIMEOUT);
+            q = a.world;
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+    }
+  };
+  if (nunits <= 0) {
+    signal_done();
+    return;
+  }
   const int N = a.N;
   const int c = lane & 3, rq = lane >> 2;
   uint64_t policy;
@@ -760,11 +801,24 @@ __global__ void __launch_bounds__(kThreadsT, 2)
       const int grow = rb * kRowsBlk + warp * kWarpRows + rl[hh];
       if (grow >= jM) continue;
       const float bv = jb.bias ? jb.bias[grow] : 0.f;
+      if (a.world > 0) {
+        // the row goes straight into every rank's copy of the whole y (peer stores over NVLink)
+        const size_t base = (size_t)jb.row0 + grow;
+        for (int pr = 0; pr < a.world; ++pr) {
+          float* yp = reinterpret_cast<float*>(a.peer[pr] + jb.yoff);
 #pragma unroll
-      for (int i = 0; i < NT; ++i)
+          for (int i = 0; i < NT; ++i)
 #pragma unroll
-        for (int u = 0; u < YT; ++u)
-          if (holds(tok(i, u))) jb.y[(size_t)tok(i, u) * jM + grow] = y[i][hh][u] + bv;
+            for (int u = 0; u < YT; ++u)
+              if (holds(tok(i, u))) yp[(size_t)tok(i, u) * jb.m_full + base] = y[i][hh][u] + bv;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < NT; ++i)
+#pragma unroll
+          for (int u = 0; u < YT; ++u)
+            if (holds(tok(i, u))) jb.y[(size_t)tok(i, u) * jM + grow] = y[i][hh][u] + bv;
+      }
     }
   };
 
@@ -832,6 +886,8 @@ __global__ void __launch_bounds__(kThreadsT, 2)
     volatile int keep_waiting = 0;
     for (int k = max(flast - NS + 1, 0); k <= flast; ++k) mbar_wait(full0 + 8 * (k % NS), (k / NS) & 1, &keep_waiting);
   }
+  // (after a timeout too: the epochs of the ranks stay in step; the status word records it)
+  signal_done();
 }
 
 // ------------------------------------------------------------------ host side
@@ -1080,7 +1136,7 @@ int launch_xprep_frag(XPrepJob* xj, int count, int N, int x_dtype, cudaStream_t 
 }
 
 int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void* workspace, char* partials,
-                    cudaStream_t s, cudaError_t* err) {
+                    const pf_peers* peers, cudaStream_t s, cudaError_t* err) {
   *err = cudaSuccess;
   if (count < 1 || count > kTmaMaxJobs || N < 1 || N > kMaxGemvTokens) return PF_ERR_INVALID_ARGUMENT;
   // one format, or the group-128 INT3 and INT2 pair (same stage width)
@@ -1117,6 +1173,9 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void
     jb.tile0 = tile0;
     // INT3 is always the launch's first format when mixed
     jb.fsel = mixed ? (w.format == PF_FMT_INT2_G128 ? 1 : 0) : 0;
+    jb.yoff = io[k].yoff;
+    jb.m_full = io[k].m_full;
+    jb.row0 = io[k].row0;
     jb.partials = reinterpret_cast<float*>(part);
     part += tma_partial_bytes(w, N);
     unit0 += jb.n_rb * jb.spb;
@@ -1126,12 +1185,19 @@ int launch_gemv_tma(const TmaWeight* ws, const TmaIO* io, int count, int N, void
   }
   if ((unsigned long long)unit0 * (unsigned long long)(sm_count() * ctas_per_sm() + 1) >= (1ull << 32))
     return PF_ERR_SHAPE;
-  if ((size_t)tile0 > kWsStatusSlot) return PF_ERR_SHAPE;
+  if ((size_t)tile0 > kWsDoneSlot) return PF_ERR_SHAPE;
   a.n_jobs = count;
   a.n_units = unit0;
   a.N = N;
   a.counters = counters;
   a.status = counters + kWsStatusSlot;
+  a.done = counters + kWsDoneSlot;
+  if (peers) {
+    if (peers->world < 1 || peers->world > kMaxPeers) return PF_ERR_INVALID_ARGUMENT;
+    a.world = peers->world;
+    a.rank = peers->rank;
+    for (int p = 0; p < peers->world; ++p) a.peer[p] = static_cast<unsigned char*>(peers->bases[p]);
+  }
   cudaError_t e;
   if (mixed) {
     e = launch_fmt<PF_FMT_INT3_G128, PF_FMT_INT2_G128>(a, kScaleGroup, codes, rw, s);

@@ -45,6 +45,7 @@ EXPORTS = (
     "pf_add_rmsnorm", "pf_rope_kv", "pf_decode_attention_workspace_size", "pf_decode_attention", "pf_silu_mul",
     "pf_kv_row_bytes", "pf_kv_quantize", "pf_kv_dequantize", "pf_rope_kv_compressed",
     "pf_decode_attention_compressed", "pf_workspace_status", "pf_qlinear_noalloc_status", "pf_wait_selftest",
+    "pf_peer_export", "pf_peer_open", "pf_peer_close", "pf_qlinear_group_gather", "pf_peers_wait",
 )
 
 
@@ -62,6 +63,17 @@ class PFQWeight(ctypes.Structure):
         ("had_signs", ctypes.c_void_p),
         ("tensor_scale", ctypes.c_double),
         ("params", ctypes.c_int32 * 20),
+    ]
+
+
+class PFPeers(ctypes.Structure):
+    """Mirror of ``struct pf_peers``."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("bases", ctypes.c_void_p * 8),
+        ("bytes", ctypes.c_size_t),
     ]
 
 
@@ -145,6 +157,18 @@ def load():
     L.pf_qlinear_noalloc_status.argtypes = [I, IP, IP, P]
     L.pf_wait_selftest.restype = I
     L.pf_wait_selftest.argtypes = [P, ctypes.c_ulonglong, P]
+    U8P = ctypes.POINTER(ctypes.c_ubyte)
+    L.pf_peer_export.restype = I
+    L.pf_peer_export.argtypes = [P, U8P, ctypes.POINTER(SZ)]
+    L.pf_peer_open.restype = I
+    L.pf_peer_open.argtypes = [U8P, SZ, ctypes.POINTER(P), ctypes.POINTER(P)]
+    L.pf_peer_close.restype = I
+    L.pf_peer_close.argtypes = [P]
+    PEERS = ctypes.POINTER(PFPeers)
+    L.pf_qlinear_group_gather.restype = I
+    L.pf_qlinear_group_gather.argtypes = [I, QWP, PP, I, I, PP, ctypes.POINTER(SZ), ctypes.POINTER(I), PEERS, P, SZ, P]
+    L.pf_peers_wait.restype = I
+    L.pf_peers_wait.argtypes = [PEERS, P, P]
     _lib = L
     return L
 

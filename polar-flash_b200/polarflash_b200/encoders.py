@@ -218,6 +218,96 @@ def e8_decode(idx: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     return (a + b).reshape(M, -1)
 
 
+# ---------------------------------------------------------------- E8 lattice (fp16 reconstructions)
+def _d8_nearest(x: torch.Tensor) -> torch.Tensor:
+    """Nearest point of D8 = {z in Z^8 : sum z even} to each 8-vector: round
+    every coordinate; when the rounded sum is odd, move the coordinate with
+    the largest rounding error one step toward x (the first such coordinate on
+    a tie; an error of exactly 0 steps up).  quantize_d8, e8_lattice.py:53-84."""
+    f = torch.round(x)
+    err = x - f
+    odd = torch.remainder(torch.sum(f, dim=-1, keepdim=True).long(), 2) != 0
+    worst = torch.argmax(torch.abs(err), dim=-1, keepdim=True)
+    step = torch.where(err >= 0, torch.ones_like(err), -torch.ones_like(err))
+    fix = torch.zeros_like(x, dtype=torch.bool).scatter_(-1, worst, True) & odd
+    return torch.where(fix, f + step, f)
+
+
+def e8_nearest(x: torch.Tensor) -> torch.Tensor:
+    """Nearest point of the E8 lattice, E8 = D8 u (D8 + 1/2), to each
+    8-vector of x [..., 8] (Conway & Sloane, "Fast quantizing and decoding
+    algorithms for lattice quantizers and codes", IEEE Trans. IT 28 (1982)):
+    the nearer of the two cosets' nearest points, D8's on a tie (quantize_e8,
+    e8_lattice.py:87-105)."""
+    a = _d8_nearest(x)
+    b = _d8_nearest(x - 0.5) + 0.5
+    da = torch.sum((x - a) ** 2, dim=-1, keepdim=True)
+    db = torch.sum((x - b) ** 2, dim=-1, keepdim=True)
+    return torch.where(da <= db, a, b)
+
+
+def _e8_best_scale(blocks: torch.Tensor, steps: int, eps: float = 1e-12) -> float:
+    """Grid search of s in [0.2 rms, 2.5 rms] (`steps` points) minimising
+    mean |x - s Q_E8(x / s)|^2, the first minimum kept (optimize_scale,
+    e8_lattice.py:118-145)."""
+    rms = float(torch.sqrt(torch.mean(blocks ** 2)).item())
+    if rms <= eps:
+        return 1.0
+    best, best_loss = rms, float("inf")
+    for s in torch.linspace(0.2 * rms, 2.5 * rms, steps=steps, device=blocks.device).tolist():
+        if s <= eps:
+            continue
+        loss = float(torch.mean((blocks - e8_nearest(blocks / s) * s) ** 2).item())
+        if loss < best_loss:
+            best, best_loss = s, loss
+    return best
+
+
+def e8_lattice_quantize(x: torch.Tensor, search_steps: int = 16, scale: float = None,
+                        eps: float = 1e-12) -> Tuple[torch.Tensor, Dict]:
+    """x_hat = s Q_E8(x / s) over consecutive 8-element blocks of x (flattened,
+    zero-padded to a multiple of 8), s from _e8_best_scale unless given.
+    Returns x_hat (fp32, x's shape) and the reference's metadata keys
+    (E8LatticeQuantizer.quantize, e8_lattice.py:147-190)."""
+    flat = x.reshape(-1)
+    pad = (-flat.numel()) % 8
+    if pad:
+        flat = torch.cat([flat, torch.zeros(pad, device=x.device, dtype=x.dtype)])
+    blocks = flat.view(-1, 8).float()
+    if scale is None:
+        scale = _e8_best_scale(blocks, search_steps, eps)
+    xh = (e8_nearest(blocks / max(scale, eps)) * scale).view(-1)
+    if pad:
+        xh = xh[:-pad]
+    xh = xh.reshape(x.shape)
+    mse = float(torch.mean((x - xh) ** 2).item())
+    var = float(torch.var(x).item())
+    return xh, {"optimal_scale": scale, "mse_distortion": mse,
+                "snr_db": 10.0 * math.log10(max(var, 1e-15) / max(mse, 1e-15)), "dimension": 8,
+                "sphere_packing_density_e8": math.pi ** 4 / 384.0, "padding_added": pad}
+
+
+def e8_rvq_quantize(x: torch.Tensor, num_stages: int = 2, search_steps: int = 12) -> Tuple[torch.Tensor, Dict]:
+    """Residual E8 lattice VQ: stage t quantizes x - (sum of earlier stages)
+    with its own searched scale; x_hat is the sum of the stages
+    (E8ResidualVectorQuantizer.quantize, e8_lattice.py:193-232)."""
+    stages = max(1, num_stages)
+    residual = x.clone()
+    rec = torch.zeros_like(x)
+    scales, mses = [], []
+    for _ in range(stages):
+        q, m = e8_lattice_quantize(residual, search_steps)
+        rec += q
+        residual = x - rec
+        scales.append(m["optimal_scale"])
+        mses.append(float(torch.mean(residual ** 2).item()))
+    total = float(torch.mean((x - rec) ** 2).item())
+    var = float(torch.var(x).item())
+    return rec.reshape(x.shape), {"num_stages": stages, "stage_scales": scales, "stage_mses": mses,
+                                  "total_mse": total,
+                                  "snr_db": 10.0 * math.log10(max(var, 1e-15) / max(total, 1e-15))}
+
+
 # ---------------------------------------------------------------- recursive polar
 def polar_alloc(block_size: int, target_bpw: float) -> List[int]:
     """compute_adaptive_bit_allocation (polar_quant.py:352-379)."""
@@ -281,11 +371,68 @@ def pack_bits_msb(words: torch.Tensor, total_bits: int) -> torch.Tensor:
     return out
 
 
+def fit_polar_codebooks(sample: torch.Tensor, block_size: int, angle_bits: int = 4,
+                        iters: int = 15) -> List[torch.Tensor]:
+    """Per-level angle codebooks of 2^angle_bits entries by 1-D Lloyd-Max
+    iterations (fit_codebooks, polar_quant.py:274-300): the sample's blocks
+    are taken to polar form; each level's centroids start evenly spaced over
+    the level's range ([-pi, pi] at level 0, [0, pi/2] above, 1e-3 in from
+    each end), then `iters` times every angle is assigned to its nearest
+    centroid (the lowest index on a tie) and each centroid that received
+    angles moves to their mean; the result is sorted."""
+    L = 1 << angle_bits
+    _, levels = _forward_recursive(sample.detach().cpu().reshape(-1, block_size))
+    books = []
+    for lvl, angles in enumerate(levels):
+        a = angles.flatten()
+        c = (torch.linspace(-math.pi + 1e-3, math.pi - 1e-3, L) if lvl == 0
+             else torch.linspace(1e-3, 0.5 * math.pi - 1e-3, L))
+        for _ in range(iters):
+            near = torch.argmin(torch.abs(a.unsqueeze(1) - c.unsqueeze(0)), dim=1)
+            for k in range(L):
+                members = a[near == k]
+                if members.numel() > 0:
+                    c[k] = members.mean()
+        books.append(torch.sort(c)[0])
+    return books
+
+
+def polar_angle_table(block_size: int, alloc: List[int], codebooks, device="cpu") -> torch.Tensor:
+    """The device decoders' learned angle table, fp32 [d-1][64]: entry 64 j + c
+    is the angle of code c in angle column j (level 0 columns first), i.e.
+    codebook[level(j)][min(c, len - 1)] (decode_packed, polar_quant.py:552-554);
+    columns of levels without a codebook keep the uniform grid (:555-558)."""
+    d = block_size
+    tab = torch.zeros(d - 1, 64, dtype=torch.float32)
+    col, width, lvl = 0, d // 2, 0
+    while width >= 1:
+        for j in range(width):
+            levels = 1 << alloc[1 + col + j]
+            c = torch.arange(levels)
+            if lvl < len(codebooks):
+                cb = torch.as_tensor(codebooks[lvl], dtype=torch.float32).flatten()
+                tab[col + j, :levels] = cb[torch.clamp(c, 0, cb.numel() - 1)]
+            elif lvl == 0:
+                tab[col + j, :levels] = ((c.float() + 0.5) / float(levels)) * (2.0 * math.pi) - math.pi
+            else:
+                tab[col + j, :levels] = ((c.float() + 0.5) / float(levels)) * (0.5 * math.pi)
+        col += width
+        width //= 2
+        lvl += 1
+    return tab.flatten().to(device)
+
+
 def polar_encode(w: torch.Tensor, block_size: int = 8, target_bpw: float = 1.75,
-                 blocks_per_chunk: int = 1 << 22) -> Tuple[torch.Tensor, Dict]:
-    """RecursivePolarQuant.encode_packed (polar_quant.py:381-487) with uniform
-    angle codes; returns (payload uint8, meta) with the reference's meta keys.
-    The global max radius fixes r_scale, then blocks are coded chunk by chunk."""
+                 blocks_per_chunk: int = 1 << 22, codebooks=None) -> Tuple[torch.Tensor, Dict]:
+    """RecursivePolarQuant.encode_packed (polar_quant.py:381-487); returns
+    (payload uint8, meta) with the reference's meta keys.  The global max
+    radius fixes r_scale, then blocks are coded chunk by chunk.  Angles are
+    coded on the uniform grid, or, at the levels `codebooks` covers, as the
+    index of the nearest codebook entry (lowest on a tie).  As in the
+    reference, a codebook index wider than its column's bit field is OR-ed
+    in unmasked (polar_quant.py:440-444), so its high bits land in the
+    fields above; meta then also carries the codebooks (learned_codebooks),
+    which the reference keeps on the quantizer object."""
     d = block_size
     flat = w.float().flatten()
     pad = (-flat.numel()) % d
@@ -318,6 +465,11 @@ def polar_encode(w: torch.Tensor, block_size: int = 8, target_bpw: float = 1.75,
             for j in range(fa.shape[1]):
                 th = fa[:, j]
                 levels = 1 << alloc[col]
+                if codebooks and lvl < len(codebooks):
+                    cb = torch.as_tensor(codebooks[lvl], dtype=torch.float32, device=th.device)
+                    codes.append(torch.argmin(torch.abs(th.unsqueeze(1) - cb.unsqueeze(0)), dim=1).long())
+                    col += 1
+                    continue
                 nt = (th + math.pi) / (2.0 * math.pi) if lvl == 0 else th / (0.5 * math.pi)
                 nt = torch.clamp(nt, 0.0, 1.0 - 1e-7)
                 codes.append(torch.clamp(torch.floor(nt * levels), 0, levels - 1).long())
@@ -332,6 +484,8 @@ def polar_encode(w: torch.Tensor, block_size: int = 8, target_bpw: float = 1.75,
     meta = {
         "block_size": d, "orig_shape": list(w.shape), "pad_len": pad, "num_blocks": nblk,
         "alloc": alloc, "r_scale": r_scale,
-        "exact_bpw": payload.numel() * 8.0 / float(w.numel()), "has_learned_codebooks": False,
+        "exact_bpw": payload.numel() * 8.0 / float(w.numel()), "has_learned_codebooks": bool(codebooks),
     }
+    if codebooks:
+        meta["learned_codebooks"] = [[float(v) for v in torch.as_tensor(cb).flatten().tolist()] for cb in codebooks]
     return payload, meta

@@ -9,10 +9,13 @@ concatenation is the full [N, M] after one transpose of a tiny buffer.
 """
 from typing import List, Optional
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from .qweight import QWeight, qlinear
+from . import _lib
+from .qweight import QWeight, _desc_array, _X_DTYPES, group_workspace_bytes, qlinear, workspace
 
 
 def shard_bounds(M: int, world: int, rank: int):
@@ -58,3 +61,100 @@ def gather_rows(y_local: torch.Tensor, world: int, group=None) -> torch.Tensor:
     out: List[torch.Tensor] = [torch.empty_like(y_local) for _ in range(world)]
     dist.all_gather(out, y_local.contiguous(), group=group)
     return torch.cat(out, dim=1)
+
+
+class PeerBuffer:
+    """A device buffer of the same size on every rank of `group`, each rank's
+    mapped into every other rank's process (CUDA IPC; the handles travel
+    through torch.distributed), for column-parallel linears that store their
+    rows straight into every rank's copy of y (pf_qlinear_group_gather).
+
+    The first 256 bytes are the header of the fused calls (an epoch and one
+    flag per rank); `view(offset, shape)` gives fp32 views of the local buffer
+    at byte offsets >= 256.  Every rank must create its PeerBuffers in the
+    same order and make the same sequence of gathering calls."""
+
+    HEADER = 256
+
+    def __init__(self, nbytes: int, group: Optional[dist.ProcessGroup] = None, device=None):
+        L = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.nbytes = (nbytes + 255) // 256 * 256
+        # its own allocation (the IPC handle covers the whole allocation)
+        self.local = torch.zeros(self.nbytes, dtype=torch.uint8, device=dev)
+        handle = (ctypes.c_ubyte * 64)()
+        off = ctypes.c_size_t(0)
+        _lib.check(L.pf_peer_export(ctypes.c_void_p(self.local.data_ptr()), handle, ctypes.byref(off)),
+                   "pf_peer_export")
+        mine = (bytes(handle), int(off.value))
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=group)
+        self._mappings = []
+        self.peers = _lib.PFPeers()
+        self.peers.world, self.peers.rank, self.peers.bytes = self.world, self.rank, self.nbytes
+        for r, (h, o) in enumerate(allh):
+            if r == self.rank:
+                self.peers.bases[r] = self.local.data_ptr()
+                continue
+            ptr, mp = ctypes.c_void_p(0), ctypes.c_void_p(0)
+            hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+            _lib.check(L.pf_peer_open(hb, o, ctypes.byref(ptr), ctypes.byref(mp)), "pf_peer_open")
+            self.peers.bases[r] = ptr.value
+            self._mappings.append(mp.value)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    def view(self, offset: int, shape) -> torch.Tensor:
+        n = 1
+        for d in shape:
+            n *= d
+        if offset < self.HEADER or offset % 16 or offset + 4 * n > self.nbytes:
+            raise ValueError("view outside the buffer's output area")
+        return self.local[offset:offset + 4 * n].view(torch.float32).view(*shape)
+
+    def close(self):
+        """Unmaps the peers' buffers (after all work that uses them)."""
+        L = _lib.load()
+        for mp in self._mappings:
+            _lib.check(L.pf_peer_close(ctypes.c_void_p(mp)), "pf_peer_close")
+        self._mappings = []
+
+
+def qlinear_group_gather(shards, xs, peer: PeerBuffer, y_offsets, biases=None, ws: Optional[torch.Tensor] = None,
+                         stream=None):
+    """Row shards `shards` (this rank's rows of each linear) times xs, each
+    linear's whole y [N, world * M_i] written into every rank's peer buffer at
+    y_offsets[i] (pf_qlinear_group_gather).  Call peers_wait before reading
+    the outputs on this rank."""
+    L = _lib.load()
+    n = len(shards)
+    N = xs[0].shape[0]
+    dt = xs[0].dtype
+    dev = xs[0].device
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    need = group_workspace_bytes(shards, N)
+    ws = ws if ws is not None else workspace(dev, need, s)
+    VP = ctypes.c_void_p * n
+    xa = VP(*[x.data_ptr() for x in xs])
+    ba = VP(*[b.data_ptr() if b is not None else None for b in (biases or [None] * n)])
+    offs = (ctypes.c_size_t * n)(*y_offsets)
+    mfull = (ctypes.c_int * n)(*[peer.world * q.M for q in shards])
+    _lib.check(L.pf_qlinear_group_gather(n, _desc_array(shards), xa, _X_DTYPES[dt], N, ba, offs, mfull,
+                                         ctypes.byref(peer.peers), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+                                         ctypes.c_void_p(s.cuda_stream)), "pf_qlinear_group_gather")
+
+
+def peers_wait(peer: PeerBuffer, ws: torch.Tensor, stream=None):
+    """Makes `stream` wait until every rank's rows of its latest gathering
+    call are in this rank's buffer (bounded; a wait that gives up is recorded
+    in the workspace status word)."""
+    L = _lib.load()
+    s = stream if stream is not None else torch.cuda.current_stream(ws.device)
+    _lib.check(L.pf_peers_wait(ctypes.byref(peer.peers), ctypes.c_void_p(ws.data_ptr()),
+                               ctypes.c_void_p(s.cuda_stream)), "pf_peers_wait")
+

@@ -6,12 +6,11 @@ lives (a CPU weight follows the reference's CPU arithmetic step for step, so
 reference backends give byte-identical payloads; a CUDA weight is rotated by
 pf_rwht and encoded with torch CUDA ops).  ``dequantize`` decodes on the GPU.
 
-Backends: the reference's fp16, bf16, int8, int4, int3, int2 and (2-D) polar,
-plus the packed formats of this library: int4_g128, int3_g128, int2_g128
-(group-128 asymmetric), e8_rvq2_g128 (E8 root residual VQ indices) and
-polar_recursive (RecursivePolarQuant block codes).  The reference's "e8"
-backend stores an fp16 reconstruction; such payloads decode here (dense path)
-but are not produced.
+Backends: the reference's fp16, bf16, int8, int4, int3, int2, e8 (E8
+lattice / residual E8 lattice VQ, stored as an fp16 reconstruction) and (2-D)
+polar, plus the packed formats of this library: int4_g128, int3_g128,
+int2_g128 (group-128 asymmetric), e8_rvq2_g128 (E8 root residual VQ indices)
+and polar_recursive (RecursivePolarQuant block codes).
 """
 import math
 from typing import Any, Dict, List, Tuple
@@ -80,7 +79,7 @@ def _bytes(t: torch.Tensor) -> bytes:
 class UnifiedQuantizer:
     """Mirror of the reference UnifiedQuantizer (unified_quantizer.py:83-324)."""
 
-    SUPPORTED_BACKENDS = ["fp16", "bf16", "int8", "int4", "int3", "int2", "polar",
+    SUPPORTED_BACKENDS = ["fp16", "bf16", "int8", "int4", "int3", "int2", "e8", "polar",
                           "int4_g128", "int3_g128", "int2_g128", "e8_rvq2_g128", "polar_recursive"]
 
     def __init__(self, backend: str = "polar", hadamard_block_size: int = 512, apply_hadamard: bool = True,
@@ -116,7 +115,19 @@ class UnifiedQuantizer:
             rotated = True
         be = self.backend
         meta: Dict[str, Any]
-        if be in ("fp16", "bf16", "int8", "int4", "int3", "int2", "polar"):
+        w_rec = None  # the e8 backend's fp32 reconstruction (the reference's w_hat before the cast)
+        if be == "e8":
+            # unified_quantizer.py:180-192: one lattice stage (8-point scale grid) or
+            # e8_stages residual stages (12-point grids); the payload is fp16
+            wc = w.cpu()
+            if self.e8_stages > 1:
+                w_rec, em = encoders.e8_rvq_quantize(wc, self.e8_stages)
+                meta = {"dtype": "e8_rvq", "stages": self.e8_stages, "bpw": 8.0 / 8.0 + 1.0, **em}
+            else:
+                w_rec, em = encoders.e8_lattice_quantize(wc, search_steps=8)
+                meta = {"dtype": "e8_lattice", "bpw": 2.0, **em}
+            payload = _bytes(w_rec.half())
+        elif be in ("fp16", "bf16", "int8", "int4", "int3", "int2", "polar"):
             wc = w.cpu()
             if be == "fp16":
                 payload = _bytes(wc.half())
@@ -160,7 +171,10 @@ class UnifiedQuantizer:
                      "effective_bpw": round(len(payload) * 8.0 / max(n, 1), 3)})
         w_hat = None
         if return_w_hat:
-            w_hat = UnifiedQuantizer.dequantize(payload, orig_shape, meta["dtype"], meta).cpu()
+            if w_rec is not None:  # the reference reports the fp32 reconstruction, not the fp16 payload
+                w_hat = (rotate(w_rec, self.hadamard_block_size, inverse=True) if rotated else w_rec).view(*orig_shape)
+            else:
+                w_hat = UnifiedQuantizer.dequantize(payload, orig_shape, meta["dtype"], meta).cpu()
             ref = weight.detach().float().cpu()
             mse = float(torch.mean((ref - w_hat) ** 2).item())
             var = float(torch.var(ref).item()) if ref.numel() > 1 else 0.0

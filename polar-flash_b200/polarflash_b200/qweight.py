@@ -12,7 +12,7 @@ from typing import Dict, List, Optional
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, encoders
 from .hadamard import column_signs, effective_block
 
 # quant_meta "dtype" -> pf_format for the packed formats
@@ -111,8 +111,8 @@ class QWeight:
             codes = self.codes.view(self.M, rb)[r0:r1].contiguous()
         else:
             codes = self.codes.view(self.M, -1)[r0:r1].contiguous()
-        sc = self.scales
-        if sc is not None and sc.dim() > 0 and sc.shape[0] == self.M:
+        sc = self.scales  # recursive polar: the learned angle table, shared by every row
+        if sc is not None and sc.dim() > 0 and sc.shape[0] == self.M and self.format != _lib.FMT_POLAR_RECURSIVE:
             sc = sc[r0:r1].contiguous()
         mins = self.mins[r0:r1].contiguous() if self.mins is not None else None
         return QWeight(self.format, r1 - r0, self.K, codes, sc, mins, self.had_block, self.had_signs,
@@ -141,7 +141,10 @@ def qweight_from_payload(dtype: str, quant_meta: Dict, payload, M: int, K: int, 
         d = int(quant_meta.get("block_size", 8))
         alloc = [int(a) for a in quant_meta["alloc"]]
         codes = _as_u8(payload, device)
-        return QWeight(fmt, M, K, codes, None, None, hb, signs, float(quant_meta["r_scale"]), [d] + alloc)
+        angles = None
+        if quant_meta.get("has_learned_codebooks") and quant_meta.get("learned_codebooks"):
+            angles = encoders.polar_angle_table(d, alloc, quant_meta["learned_codebooks"], device)
+        return QWeight(fmt, M, K, codes, angles, None, hb, signs, float(quant_meta["r_scale"]), [d] + alloc)
     if fmt == _lib.FMT_POLAR2D:
         codes = _as_u8(payload, device)
         return QWeight(fmt, M, K, codes, None, None, hb, signs, float(quant_meta.get("r_scale", 1.0)),

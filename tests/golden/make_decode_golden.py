@@ -1,14 +1,14 @@
 """Golden logits for the decode-step integration test, from the reference's
 own PFlashModelForCausalLM (polarflash_core/model_integration.py:203-254).
 
-    python tests/golden/make_decode_golden.py
+    POLARFLASH_REF=/path/to/POLAR-FLASH python tests/golden/make_decode_golden.py
 
 The tiny model of tests/decode_model.py (seeded weights, oracle INT4 g128
 payloads decoded back to dense W_hat) is loaded into the reference model;
 it runs the prompt (prefill, causal mask) and then three single-token steps
 with its KV caches.  Writes decode_step.npz: prompt, decode tokens, prefill
-and step logits.  Needs the reference sources at $POLARFLASH_REF (default
-/root/reference); the GPU machines only read the .npz.
+and step logits.  Needs the reference sources at $POLARFLASH_REF (required);
+the GPU machines only read the .npz.
 """
 import os
 import sys
@@ -18,7 +18,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("POLARFLASH_REF", "/root/reference")
+REF = os.environ.get("POLARFLASH_REF")
+if not REF or not os.path.isdir(REF):
+    sys.exit("set POLARFLASH_REF to a checkout of the reference POLAR-FLASH sources")
 sys.path[:0] = [os.path.dirname(HERE), ROOT, os.path.join(ROOT, "polar-flash_b200"), REF]
 
 import decode_model as dm  # noqa: E402

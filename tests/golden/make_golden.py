@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder by running the reference itself.
 
 Run in a checkout that has the reference POLAR-FLASH sources (read-only) at
-``$POLARFLASH_REF`` (default ``/root/reference``):
+``$POLARFLASH_REF`` (required):
 
-    python tests/golden/make_golden.py
+    POLARFLASH_REF=/path/to/POLAR-FLASH python tests/golden/make_golden.py
 
 Every array written here comes out of the reference's own Python functions on
 seeded inputs; the tests compare the CPU oracle (and, on a GPU, the CUDA
@@ -16,7 +16,9 @@ import sys
 import numpy as np
 import torch
 
-REF = os.environ.get("POLARFLASH_REF", "/root/reference")
+REF = os.environ.get("POLARFLASH_REF")
+if not REF or not os.path.isdir(REF):
+    sys.exit("set POLARFLASH_REF to a checkout of the reference POLAR-FLASH sources")
 OUT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REF)
 

@@ -1,7 +1,7 @@
 """Golden vectors for the compressed KV cache, from the reference's own
 CompressedKVCache (polarflash_rt/kv_cache/compressed_kv.py).
 
-    python tests/golden/make_kv_golden.py
+    POLARFLASH_REF=/path/to/POLAR-FLASH python tests/golden/make_kv_golden.py
 
 For modes int8, 2bit and 2bit_asym: seeded randn keys/values [1, 4, 16, 64]
 (the shape of the reference's own test) appended in two update() calls
@@ -10,7 +10,7 @@ hand-made rows that land on rounding ties, exact floor boundaries, a
 constant row and an all-zero row (the 1e-8 scale clamp).  Stores the
 reference's codes, scales, zeros and returned (dequantized) K/V, plus one
 sliding-window call (window 12, 4 sinks).  Needs the reference sources at
-$POLARFLASH_REF (default /root/reference); the GPU machines only read the
+$POLARFLASH_REF (required); the GPU machines only read the
 .npz.
 """
 import os
@@ -20,7 +20,9 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("POLARFLASH_REF", "/root/reference")
+REF = os.environ.get("POLARFLASH_REF")
+if not REF or not os.path.isdir(REF):
+    sys.exit("set POLARFLASH_REF to a checkout of the reference POLAR-FLASH sources")
 sys.path.insert(0, REF)
 
 from polarflash_rt.kv_cache.compressed_kv import CompressedKVCache  # noqa: E402

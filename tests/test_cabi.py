@@ -149,3 +149,29 @@ def test_status_entry_points_validate_on_the_host():
     assert L.pf_wait_selftest(0x10000, 3_000_000_000, None) == _lib.ERR_INVALID_ARGUMENT  # above the 2 s limit
     assert L.pf_wait_selftest(0x10010, 1000, None) == _lib.ERR_ALIGNMENT
     assert L.pf_qlinear_noalloc_status(0, None, None, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_gather_entry_points_validate_on_the_host():
+    """pf_qlinear_group_gather and pf_peers_wait refuse bad peer sets before
+    touching the device."""
+    L = _lib.load()
+    peers = _lib.PFPeers()
+    peers.world, peers.rank, peers.bytes = 2, 0, 1 << 20
+    peers.bases[0], peers.bases[1] = 0x100000, 0x200000
+    d = _desc(fmt=_lib.FMT_INT3_G128, M=128, K=512)
+    arr = (ctypes.POINTER(_lib.PFQWeight) * 1)(ctypes.pointer(d))
+    xs = (ctypes.c_void_p * 1)(0x300000)
+    offs = (ctypes.c_size_t * 1)(256)
+    mfull = (ctypes.c_int * 1)(256)
+    call = lambda p, o=offs, m=mfull: L.pf_qlinear_group_gather(1, arr, xs, 1, 1, None, o, m, ctypes.byref(p),  # noqa: E731
+                                                                  0x400000, 1 << 20, None)
+    assert call(peers, m=(ctypes.c_int * 1)(200)) == _lib.ERR_SHAPE          # m_full != world * M
+    assert call(peers, o=(ctypes.c_size_t * 1)(64)) == _lib.ERR_ALIGNMENT    # inside the header
+    assert call(peers, o=(ctypes.c_size_t * 1)(1 << 20)) == _lib.ERR_SHAPE   # past the buffer
+    bad = _lib.PFPeers()
+    bad.world, bad.rank, bad.bytes = 9, 0, 1 << 20
+    assert call(bad) == _lib.ERR_INVALID_ARGUMENT
+    bad.world, bad.rank = 2, 2
+    assert call(bad) == _lib.ERR_INVALID_ARGUMENT
+    assert L.pf_peers_wait(ctypes.byref(bad), 0x400000, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.pf_peers_wait(ctypes.byref(peers), None, None) == _lib.ERR_INVALID_ARGUMENT
