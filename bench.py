@@ -350,10 +350,11 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_reference_leg(fmt_sets, samples, threads=None):
+def cpu_reference_leg(fmt_sets, samples, threads=None, outputs=None):
     """The reference's CPU path (decode -> inverse block RWHT -> fp32 matvec,
     polarflash_rt/cpu/engine.py:58-96 via unified_quantizer.py:242-324) as the
-    oracle's C port, all host threads.  Returns (GB/s, seconds, cores, desc)."""
+    oracle's C port, all host threads.  Returns (GB/s, seconds, cores); the
+    y of every sample is appended to `outputs` when given."""
     import oracle
 
     if threads:
@@ -363,10 +364,35 @@ def cpu_reference_leg(fmt_sets, samples, threads=None):
     for (fmt, name, payload, M, K, x) in samples:
         t0 = time.perf_counter()
         W = oracle.dequantize(fmt, payload, M, K, {"hadamard_rotation": True, "hadamard_block_size": 128})
-        oracle.matvec_f32(W, x)
+        y = oracle.matvec_f32(W, x)
         t_total += time.perf_counter() - t0
         b_total += payload["words"].nbytes + payload["s"].nbytes + payload["m"].nbytes + x.size * 2 + M * 4
+        if outputs is not None:
+            outputs.append(y)
     return b_total / t_total / 1e9, t_total, cores
+
+
+def parity_stats(pairs):
+    """Device y against the CPU reference y over (y, y_ref) pairs: the bound
+    the tests apply is normwise per linear, max|y - y_ref| <= 1e-3 max|y_ref|;
+    the elementwise relative error |y_i - y_ref_i| / |y_ref_i| is reported
+    beside it (its max over elements with |y_ref_i| >= 1 % of max|y_ref|, and
+    its 99th percentile over all elements)."""
+    norm, emax, ep99 = 0.0, 0.0, []
+    for y, r in pairs:
+        y = np.asarray(y, np.float64).ravel()
+        r = np.asarray(r, np.float64).ravel()
+        d = np.abs(y - r)
+        scale = np.abs(r).max()
+        norm = max(norm, d.max() / scale)
+        big = np.abs(r) >= 0.01 * scale
+        emax = max(emax, float((d[big] / np.abs(r[big])).max()))
+        nz = np.abs(r) > 0
+        ep99.append(d[nz] / np.abs(r[nz]))
+    return {"bound": "normwise per linear: max|y - y_ref| <= 1e-3 * max|y_ref| (the 1e-3 of the tests)",
+            "normwise_max": float(f"{norm:.3e}"), "elementwise_max_rel_above_1pct": float(f"{emax:.3e}"),
+            "elementwise_p99_rel": float(f"{np.percentile(np.concatenate(ep99), 99):.3e}"),
+            "reference": "the oracle's fp32 decode + inverse RWHT + matvec (the CPU baseline leg's outputs)"}
 
 
 def cpu_model():
@@ -470,7 +496,7 @@ def main():
 
     from polarflash_b200 import encoders
     from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
-    from polarflash_b200.qweight import QWeight, group_workspace_bytes, qlinear_group, qlinear_multi, workspace
+    from polarflash_b200.qweight import QWeight, group_workspace_bytes, qlinear, qlinear_group, qlinear_multi, workspace
     from polarflash_b200._lib import kernel_launches
 
     N = args.batch
@@ -801,9 +827,15 @@ def main():
                 qw = base[(fmt, name)]
                 grp = next(gp for gp in SHARED if name in gp)
                 samples.append((fmt, name, host_payload(qw), M, K, xs[grp].float().cpu().numpy()))
-        gbs, secs, cores = cpu_reference_leg(None, samples)
+        y_ref = []
+        gbs, secs, cores = cpu_reference_leg(None, samples, outputs=y_ref)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port", "cpu_model": cpu_model(),
                "sample": f"one pass over the 14-linear set (decode + inverse RWHT + fp32 matvec), {secs:.1f} s"}
+        pairs = []
+        for (fmt, name, _, _, _, _), yr in zip(samples, y_ref):
+            grp = next(gp for gp in SHARED if name in gp)
+            pairs.append((qlinear(base[(fmt, name)], xs[grp]).cpu().numpy(), yr))
+        cpu["parity"] = parity_stats(pairs)
 
     if rank == 0:
         line = {

@@ -229,12 +229,19 @@ size_t pass_bytes(const pf_qweight* w, int np) {
 // the tensor-core dequant-GEMM, kGemmChunk tokens per launch; its workspace
 // holds fp32 x' and the per-token-scaled fp16 copy the GEMM reads.
 constexpr int kGemmChunk = 512;
+// Recursive polar with block 8 and allocation [3 | 2 2 2 2 | 1 1 | 1] (1.75 bpw).
+bool is_polar8_175(const pf_qweight* w) {
+  static const int32_t k[9] = {8, 3, 2, 2, 2, 2, 1, 1, 1};
+  return w->format == PF_FMT_POLAR_RECURSIVE && memcmp(w->params, k, sizeof(k)) == 0;
+}
 bool use_gemm(const pf_qweight* w, int N) {
   static int mode = -1;
   if (mode < 0) {
     const char* e = getenv("PF_GEMM");
     mode = (e && strcmp(e, "0") == 0) ? 0 : 1;
   }
+  if (w->format == PF_FMT_POLAR_RECURSIVE)  // above batch 1 (the table GEMV's), on the persistent kernel
+    return mode && N >= 2 && is_polar8_175(w) && gemm_eligible(w->format, w->K) && aligned(w->codes, 16);
   // E8 decodes through a shared-memory root table: the tensor-core kernel
   // serves it at every batch size; the INT formats use it above 16 tokens
   const int min_tokens = w->format == PF_FMT_E8_RVQ2_G128 ? 1 : kMaxGemvTokens + 1;
@@ -326,12 +333,17 @@ size_t workspace_bytes(const pf_qweight* w, int N, bool full = true) {
     const size_t other = use_gemm(w, N) ? gemm_bytes(w, N, full) : pass_bytes(w, 1);
     return lut > other ? lut : other;
   }
-  if (use_gemm(w, N)) return gemm_bytes(w, N, full);
   size_t b = pass_bytes(w, tokens_per_pass(N));
   int tail = N % kMaxGemvTokens;
   if (N > kMaxGemvTokens && tail) {
     size_t t = pass_bytes(w, tail);
     if (t > b) b = t;
+  }
+  if (use_gemm(w, N)) {
+    const size_t g = gemm_bytes(w, N, full);
+    if (w->format != PF_FMT_POLAR_RECURSIVE) return g;
+    // polar takes the GEMM only with room for its partial tiles, else the CUDA-core passes
+    return full ? (g > b ? g : b) : b;
   }
   return b;
 }
@@ -606,6 +618,7 @@ static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x,
       with_partials ? reinterpret_cast<float*>(reinterpret_cast<char*>(x16) + gemm_x16_bytes(cmax, K)) : nullptr;
   // rotation blocks that tile K: x' straight from x in the GEMM's own prep
   const bool direct = plan.ncasc == 0 && (plan.block == 0 || plan.rot_end == K) && K <= kGemmPrepMaxK;
+  const bool pol = w->format == PF_FMT_POLAR_RECURSIVE;
   for (int t0 = 0; t0 < N; t0 += kGemmChunk) {
     const int nc = N - t0 < kGemmChunk ? N - t0 : kGemmChunk;
     if (direct) {
@@ -613,8 +626,10 @@ static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x,
       memset(&g, 0, sizeof(g));
       g.fmt = w->format;
       g.codes = w->codes;
-      g.scales = static_cast<const __half*>(w->scales);
+      g.scales = pol ? nullptr : static_cast<const __half*>(w->scales);
       g.mins = static_cast<const __half*>(w->mins);
+      g.r_scale = (float)w->tensor_scale;
+      g.angles = pol ? static_cast<const float*>(w->scales) : nullptr;
       g.M = w->M;
       g.K = K;
       g.Kp = Kp;
@@ -657,8 +672,10 @@ static int qlinear_gemm(const pf_qweight* w, const HadPlan& plan, const void* x,
     memset(&g, 0, sizeof(g));
     g.fmt = w->format;
     g.codes = w->codes;
-    g.scales = static_cast<const __half*>(w->scales);
+    g.scales = pol ? nullptr : static_cast<const __half*>(w->scales);
     g.mins = static_cast<const __half*>(w->mins);
+    g.r_scale = (float)w->tensor_scale;
+    g.angles = pol ? static_cast<const float*>(w->scales) : nullptr;
     g.M = w->M;
     g.K = K;
     g.Kp = Kp;
@@ -701,8 +718,11 @@ int pf_qlinear(const pf_qweight* w, const void* x, int x_dtype, int N, const flo
     st = launch_polar8_lut(&in, 1, workspace, s, &e);
     return st == PF_ERR_CUDA ? cuda_status(e) : st;
   }
-  if (use_gemm(w, N))
-    return qlinear_gemm(w, plan, x, x_dtype, N, bias, y, workspace, ws_bytes >= workspace_bytes(w, N), s);
+  if (use_gemm(w, N)) {
+    const bool full = ws_bytes >= workspace_bytes(w, N);
+    if (full || w->format != PF_FMT_POLAR_RECURSIVE)
+      return qlinear_gemm(w, plan, x, x_dtype, N, bias, y, workspace, full, s);
+  }
   const size_t xs = dtype_size(x_dtype);
   for (int t0 = 0; t0 < N; t0 += kMaxGemvTokens) {
     int np = N - t0 < kMaxGemvTokens ? N - t0 : kMaxGemvTokens;

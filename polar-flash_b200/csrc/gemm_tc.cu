@@ -1,7 +1,8 @@
 // Dequant-GEMM on the 5th-generation tensor cores (tcgen05 + TMEM) for
 // batches of more than 16 tokens: Y[N][M] = X'[N][K] * W_hat^T, W_hat decoded
 // from the packed payload inside the kernel (INT4 / INT3 / INT2 group-128
-// asymmetric and E8 RVQ2), X' = the forward block RWHT of X in fp16 with a
+// asymmetric, E8 RVQ2, and, in the persistent kernel only, recursive polar
+// with block 8 at 1.75 bpw), X' = the forward block RWHT of X in fp16 with a
 // power-of-two scale per token (the same fusion identity as the GEMV).
 //
 // CTA = 128 weight rows x 128 tokens, one CTA per SM, ten warps:
@@ -65,6 +66,10 @@ struct GemmArgs {
   long long units;
   unsigned* counters;
   float* partials;
+  // recursive polar: the radius scale (applied with the token scale) and the
+  // learned angle table [7][64], or nullptr for the uniform angle grid
+  float r_scale;
+  const float* angles;
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -433,6 +438,10 @@ template <>
 struct TcBox<PF_FMT_E8_RVQ2_G128> {
   static constexpr int GB = 32, CB = 4, SB = 4, SW = 4;  // scales: (s1, s2) fp16 per group
 };
+template <>
+struct TcBox<PF_FMT_POLAR_RECURSIVE> {  // block 8, 14-bit blocks: 16 blocks = 28 bytes per group, no scales
+  static constexpr int GB = 28, CB = 4, SB = 8, SW = 2;
+};
 // 128 weight rows x 256 tokens per CTA (one N = 256 MMA per k-step, 256 TMEM
 // columns), so every decoded weight feeds twice the MACs of a 128-token tile;
 // stages of 64 columns (half a scale group, the dequant groups take
@@ -460,8 +469,49 @@ __device__ __forceinline__ void tma2d_plain(uint32_t dst, const CUtensorMap* map
 // half-stage A tile at `at` (one 64-column swizzle atom).
 template <int FMT, int H>
 __device__ __forceinline__ void sk_decode(const unsigned char* cp, uint32_t sc, int r, int lane, unsigned char* at,
-                                           const uint4* roots16) {
+                                           const uint4* roots16, const float2* ptab) {
   using B = TcBox<FMT>;
+  if constexpr (FMT == PF_FMT_POLAR_RECURSIVE) {
+    // Recursive polar, block 8, allocation [3 | 2 2 2 2 | 1 1 | 1]: block c of
+    // the group is the 14 bits at bit 14 c of its 28 bytes (MSB first); code
+    // fields from the LSB: psi 0, phi1 1, phi0 2, th3 3-4, th2 5-6, th1 7-8,
+    // th0 9-10, radius 11-13.  inverse_recursive (polar_quant.py:252-272):
+    // (a, b) = R (cos psi, sin psi); (A0, A1, A2, A3) = (a cos phi0,
+    // a sin phi0, b cos phi1, b sin phi1); w(2i, 2i + 1) = A_i (cos th_i,
+    // sin th_i), with R the radius code (r_scale joins the token scale) and
+    // the cos / sin pairs from the angle tables (ptab: column j, code c at
+    // 64 j + c).  The block's 8 weights are the 8 columns of A-tile chunk c.
+    (void)sc;
+    (void)lane;
+    (void)roots16;
+    uint32_t be[8];
+#pragma unroll
+    for (int q = 0; q < 7; ++q) be[q] = __byte_perm(*reinterpret_cast<const uint32_t*>(cp + 4 * q), 0u, 0x0123);
+    be[7] = 0u;
+#pragma unroll
+    for (int c = 8 * H; c < 8 * H + 8; ++c) {
+      constexpr int kBits = 14;
+      const int o = kBits * c, i = o >> 5, sh = o & 31;
+      const unsigned long long v = ((unsigned long long)be[i] << 32) | be[i + 1];
+      const uint32_t w = (uint32_t)(v >> (64 - sh - kBits)) & 0x3FFFu;
+      const float R = (float)(w >> 11);
+      const float2 ps = ptab[6 * kPolarTabPerCol + (w & 1u)];
+      const float2 f0 = ptab[4 * kPolarTabPerCol + ((w >> 2) & 1u)];
+      const float2 f1 = ptab[5 * kPolarTabPerCol + ((w >> 1) & 1u)];
+      const float ra = R * ps.x, rb = R * ps.y;
+      const float A[4] = {ra * f0.x, ra * f0.y, rb * f1.x, rb * f1.y};
+      uint4 o4;
+      uint32_t* ov = reinterpret_cast<uint32_t*>(&o4);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 t = ptab[e * kPolarTabPerCol + ((w >> (9 - 2 * e)) & 3u)];
+        const __half2 h = __floats2half2_rn(A[e] * t.x, A[e] * t.y);
+        ov[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) = o4;  // rows past M: zero codes (TMA fill)
+    }
+    return;
+  }
   uint32_t cw[16];
   if constexpr (FMT == PF_FMT_INT3_G128) {
 #pragma unroll
@@ -674,6 +724,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                    const __grid_constant__ GemmArgs a) {
   using B = TcBox<FMT>;
   constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
+  constexpr bool kPolar = FMT == PF_FMT_POLAR_RECURSIVE;  // no scale boxes
   constexpr int kSt = kPair ? kStagesPair : kStages2;    // A/B ring slots
   constexpr int kXRows = kPair ? kBN2 / 2 : kBN2;       // token rows of this CTA's x' box
   constexpr uint32_t kSB = kATile2 + kXRows * kBK2 * 2;  // bytes per stage
@@ -688,6 +739,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   __shared__ int abort_flag;
   __shared__ unsigned arrival;
   __shared__ uint4 roots16[kE8 ? 256 * 4 : 1];
+  __shared__ float2 ptab[kPolar ? 7 * kPolarTabPerCol : 1];  // polar cos / sin by angle column and code
   __shared__ float etscale[kBN2];  // token scales of the epilogue's current segment
 
   unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
@@ -723,8 +775,12 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&cmap)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&smap)) : "memory");
-    if (!kE8) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mmap)) : "memory");
+    if (!kPolar) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&smap)) : "memory");
+    if (!kE8 && !kPolar) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&mmap)) : "memory");
+  }
+  if constexpr (kPolar) {
+    const int alloc[8] = {3, 2, 2, 2, 2, 1, 1, 1};
+    polar_fill_tables(ptab, 8, alloc, a.angles);
   }
   if constexpr (kE8) {
     for (int k = threadIdx.x; k < 256; k += blockDim.x) {
@@ -829,7 +885,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             tma2d_plain(su32(codes + cs * kCodeSlot), &cmap, (s - s % B::CB) * (B::GB / 4), m0, cfull0 + 8 * cs);
             ++kc;
           }
-          if (s == g0 || s % B::SB == 0) {
+          if (!kPolar && (s == g0 || s % B::SB == 0)) {
             const uint32_t ss = ks & 1;
             if (ks >= 2 && !bar_wait(sfree0 + 8 * ss, ((ks >> 1) - 1) & 1, &abort_flag)) {
               ok = false;
@@ -934,7 +990,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           ++kc;
           if (live && !bar_wait(cfull0 + 8 * cs, cpar, &abort_flag)) fail();
         }
-        if (s == g0 || s % B::SB == 0) {
+        if (!kPolar && (s == g0 || s % B::SB == 0)) {
           ss = ks & 1;
           spar = (ks >> 1) & 1;
           ++ks;
@@ -943,7 +999,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const uint32_t q = 2 * gs + grp, slot = q % kSt;
         // this row's scale (and zero point) of group s
         uint32_t sc = 0u;
-        if (live) {
+        if (live && !kPolar) {
           const unsigned char* sp = scl + ss * kScaleSlot + r * 16 + (s % B::SB) * B::SW;
           if constexpr (kE8) {
             sc = *reinterpret_cast<const uint32_t*>(sp);
@@ -958,14 +1014,14 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         if (live) {
           unsigned char* at = base + slot * kSB;
           if (grp == 0)
-            sk_decode<FMT, 0>(cp, sc, r, lane, at, roots16);
+            sk_decode<FMT, 0>(cp, sc, r, lane, at, roots16, ptab);
           else
-            sk_decode<FMT, 1>(cp, sc, r, lane, at, roots16);
+            sk_decode<FMT, 1>(cp, sc, r, lane, at, roots16, ptab);
         }
         // hand the code / scale boxes back after this thread's last group in them
         if (s + 1 == g1 || (s + 1) % B::CB == 0)
           asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(cfree0 + 8 * cs) : "memory");
-        if (s + 1 == g1 || (s + 1) % B::SB == 0)
+        if (!kPolar && (s + 1 == g1 || (s + 1) % B::SB == 0))
           asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sfree0 + 8 * ss) : "memory");
         // every lane's A-tile stores visible to the tensor core, then one arrival per warp
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -999,7 +1055,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       // this segment's token scales in shared memory: the y stores below then
       // need no global load between them
       asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");
-      for (int i = r; i < kBN2; i += kBM) etscale[i] = n0 + i < a.N ? a.tok_scale[n0 + i] : 0.f;
+      for (int i = r; i < kBN2; i += kBM)
+        etscale[i] = n0 + i < a.N ? a.tok_scale[n0 + i] * (kPolar ? a.r_scale : 1.f) : 0.f;
       asm volatile("bar.sync 1, %0;" ::"r"(kBM) : "memory");
       bool ok = bar_wait(accf0 + 8 * buf, (j >> 1) & 1, &abort_flag);
       ok = __all_sync(0xffffffffu, ok);
@@ -1345,15 +1402,18 @@ template <int FMT, bool kPair>
 cudaError_t launch_gemm_sk_impl(GemmArgs a, const __half* x16, cudaStream_t s, bool* taken) {
   using B = TcBox<FMT>;
   constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
+  constexpr bool kPolar = FMT == PF_FMT_POLAR_RECURSIVE;
   constexpr int kSt = kPair ? kStagesPair : kStages2;
   constexpr int kXRows = kPair ? kBN2 / 2 : kBN2;
   constexpr size_t kSB = kATile2 + (size_t)kXRows * kBK2 * 2;
   constexpr int kRowsT = kPair ? 2 * kBM : kBM;
   *taken = false;
   const size_t row_bytes = (size_t)a.G * B::GB, srow = (size_t)a.G * B::SW;
-  if (!gemm_tma_enabled() || row_bytes % 16 || srow % 16 || reinterpret_cast<uintptr_t>(a.codes) % 16 ||
-      reinterpret_cast<uintptr_t>(a.scales) % 16 || (!kE8 && reinterpret_cast<uintptr_t>(a.mins) % 16) ||
-      !a.counters || !a.partials)
+  if (!gemm_tma_enabled() || row_bytes % 16 || reinterpret_cast<uintptr_t>(a.codes) % 16 || !a.counters ||
+      !a.partials)
+    return cudaSuccess;
+  if (!kPolar && (srow % 16 || reinterpret_cast<uintptr_t>(a.scales) % 16 ||
+                  (!kE8 && reinterpret_cast<uintptr_t>(a.mins) % 16)))
     return cudaSuccess;
   const int n_mb = (a.M + kRowsT - 1) / kRowsT, n_nb = (a.N + kBN2 - 1) / kBN2;
   const long long tiles = (long long)n_mb * n_nb;
@@ -1384,7 +1444,7 @@ cudaError_t launch_gemm_sk_impl(GemmArgs a, const __half* x16, cudaStream_t s, b
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaSuccess;
   }
-  for (int k = 0; k < (kE8 ? 1 : 2); ++k) {
+  for (int k = 0; k < (kPolar ? 0 : kE8 ? 1 : 2); ++k) {
     // scale (and zero-point) rows: SB groups of SW bytes per box row (16 bytes)
     cuuint64_t dims[2] = {(cuuint64_t)(srow / 2), (cuuint64_t)a.M};
     cuuint64_t strides[1] = {(cuuint64_t)srow};
@@ -1396,8 +1456,10 @@ cudaError_t launch_gemm_sk_impl(GemmArgs a, const __half* x16, cudaStream_t s, b
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaSuccess;
   }
-  if (kE8) mmap = smap;
-  const size_t smem = 1024 + (size_t)kSt * kSB + 2 * (size_t)kBM * B::CB * B::GB + (kE8 ? 2 : 4) * (size_t)kBM * 16;
+  if (kPolar) smap = cmap;  // never read: polar has no scale boxes
+  if (kE8 || kPolar) mmap = smap;
+  const size_t smem = 1024 + (size_t)kSt * kSB + 2 * (size_t)kBM * B::CB * B::GB +
+                      (kPolar ? 0 : kE8 ? 2 : 4) * (size_t)kBM * 16;
   auto kern = gemm_sk_kernel<FMT, kPair>;
   // programmatic dependent launch: barrier setup, TMEM allocation, the code and
   // scale loads and the first decodes overlap the x' preparation's tail
@@ -1459,6 +1521,16 @@ cudaError_t launch_gemm_sk(const GemmArgs& a, const __half* x16, cudaStream_t s,
   return launch_gemm_sk_impl<FMT, false>(a, x16, s, taken);
 }
 
+// Recursive polar runs on the persistent kernel only (the plain kernel has
+// no polar decoder); the caller checks gemm_eligible and passes a workspace
+// with the partial tiles.
+cudaError_t launch_gemm_polar(const GemmArgs& a, const __half* x16, cudaStream_t s) {
+  bool taken = false;
+  const cudaError_t e = launch_gemm_sk<PF_FMT_POLAR_RECURSIVE>(a, x16, s, &taken);
+  if (e != cudaSuccess) return e;
+  return taken ? cudaSuccess : cudaErrorNotSupported;
+}
+
 template <int FMT>
 cudaError_t launch_gemm_fmt(const GemmArgs& a, const __half* x16, cudaStream_t s) {
   auto fn = encode_fn_gemm();
@@ -1501,6 +1573,8 @@ cudaError_t launch_gemm_fmt(const GemmArgs& a, const __half* x16, cudaStream_t s
 }  // namespace
 
 bool gemm_eligible(int fmt, int K) {
+  if (fmt == PF_FMT_POLAR_RECURSIVE)  // block 8 at 1.75 bpw (the caller checks the allocation): 16-byte code rows
+    return K % 512 == 0 && gemm_tma_enabled() && encode_fn_gemm() != nullptr;
   if (!(fmt == PF_FMT_INT4_G128 || fmt == PF_FMT_INT3_G128 || fmt == PF_FMT_INT2_G128 ||
         fmt == PF_FMT_E8_RVQ2_G128))
     return false;
@@ -1571,11 +1645,14 @@ cudaError_t launch_gemm(const GemmIn& in, cudaStream_t s) {
   a.status = in.status;
   a.counters = in.counters;
   a.partials = in.partials;
+  a.r_scale = in.r_scale;
+  a.angles = in.angles;
   switch (in.fmt) {
     case PF_FMT_INT4_G128: return launch_gemm_fmt<PF_FMT_INT4_G128>(a, in.x16, s);
     case PF_FMT_INT3_G128: return launch_gemm_fmt<PF_FMT_INT3_G128>(a, in.x16, s);
     case PF_FMT_INT2_G128: return launch_gemm_fmt<PF_FMT_INT2_G128>(a, in.x16, s);
     case PF_FMT_E8_RVQ2_G128: return launch_gemm_fmt<PF_FMT_E8_RVQ2_G128>(a, in.x16, s);
+    case PF_FMT_POLAR_RECURSIVE: return launch_gemm_polar(a, in.x16, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -230,6 +230,8 @@ struct GemmIn {
   unsigned* status;
   unsigned* counters;  // workspace arrival counters (zero; left zero)
   float* partials;     // gemm_partial_bytes() of split-tile partial sums
+  float r_scale;        // recursive polar: radius scale
+  const float* angles;  // recursive polar: learned angle table [7][64], or nullptr
 };
 constexpr int kGemmPrepMaxK = 49152;  // K of the one-kernel x' preparation (K floats of smem)
 constexpr int kGemmCounterSlots = (int)kWsStatusSlot;  // tiles one GEMM launch may split

@@ -70,11 +70,18 @@ class PFlashDecoder:
     (polarflash_rt/kv_cache/compressed_kv.py:68-150): each (token, KV head)
     row as codes plus an fp32 scale (and zero), written by the RoPE kernel and
     dequantized inside the attention kernel; the eager forward attends over
-    the dequantized rows.
+    the dequantized rows.  ``faithful_prefill`` runs the packed linears of a
+    multi-token forward in slices of at most 16 tokens, so they take the
+    streaming GEMV (fp32 group scales, x' as an fp16 hi + lo pair: fp32-level
+    products) instead of the tensor-core GEMM (fp16 weights and x'); it costs
+    one weight pass per 16 tokens.
     """
 
+    GEMV_TOKENS = 16  # the largest batch the streaming GEMV takes in one pass
+
     def __init__(self, config: Dict, layers: List[DecoderLayer], embed: torch.Tensor, final_norm: torch.Tensor,
-                 lm_head: torch.Tensor, max_seq: int, kv_dtype: torch.dtype = torch.float32, kv_mode: str = "fp32"):
+                 lm_head: torch.Tensor, max_seq: int, kv_dtype: torch.dtype = torch.float32, kv_mode: str = "fp32",
+                 faithful_prefill: bool = False):
         self.hidden = int(config["hidden_size"])
         self.nh = int(config["num_attention_heads"])
         self.nkv = int(config["num_key_value_heads"])
@@ -82,6 +89,7 @@ class PFlashDecoder:
         self.theta = float(config.get("rope_theta", 1000000.0))
         self.eps = float(config.get("rms_norm_eps", 1e-6))
         self.layers = layers
+        self.faithful_prefill = bool(faithful_prefill)
         self.embed = embed
         self.final_norm = final_norm
         self.lm_head = lm_head
@@ -138,19 +146,30 @@ class PFlashDecoder:
         x1, x2 = x[..., :half], x[..., half:]
         return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
 
+    def _sliced(self, fn, x: torch.Tensor):
+        """fn(x), or, under faithful_prefill, fn over 16-token slices of x
+        with the outputs concatenated (fn returns a tensor or a list)."""
+        n = self.GEMV_TOKENS
+        if not self.faithful_prefill or x.shape[0] <= n:
+            return fn(x)
+        parts = [fn(x[i:i + n]) for i in range(0, x.shape[0], n)]
+        if isinstance(parts[0], torch.Tensor):
+            return torch.cat(parts)
+        return [torch.cat([p[j] for p in parts]) for j in range(len(parts[0]))]
+
     def _layer(self, li: int, h: torch.Tensor, cs, attend, ws) -> torch.Tensor:
         ly = self.layers[li]
         S = h.shape[0]
         n = self._rmsnorm(h, ly.input_norm)
-        q, k, v = qlinear_multi([ly.q, ly.k, ly.v], n, ly.qkv_bias, workspace=ws)
+        q, k, v = self._sliced(lambda t: qlinear_multi([ly.q, ly.k, ly.v], t, ly.qkv_bias, workspace=ws), n)
         q = self._rope(q.view(S, self.nh, self.hd), cs)
         k = self._rope(k.view(S, self.nkv, self.hd), cs)
         v = v.view(S, self.nkv, self.hd)
         attn = attend(li, q, k, v)  # [S, hidden]
-        h = h + qlinear(ly.o, attn, workspace=ws)
+        h = h + self._sliced(lambda t: qlinear(ly.o, t, workspace=ws), attn)
         n2 = self._rmsnorm(h, ly.post_norm)
-        g, u = qlinear_multi([ly.gate, ly.up], n2, workspace=ws)
-        return h + qlinear(ly.down, F.silu(g) * u, workspace=ws)
+        g, u = self._sliced(lambda t: qlinear_multi([ly.gate, ly.up], t, workspace=ws), n2)
+        return h + self._sliced(lambda t: qlinear(ly.down, t, workspace=ws), F.silu(g) * u)
 
     # ---- eager forward (prefill, or any number of new tokens) --------------
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:

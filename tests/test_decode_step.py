@@ -5,9 +5,12 @@ PFlashModelForCausalLM (tests/golden/make_decode_golden.py): a 20-token
 prefill (tensor-core GEMM for the linears, causal mask) and three cached
 single-token steps (streaming GEMV, CUDA-graph replays).
 
-Tolerances: the fp32 restatement reproduces the reference's logits within
-1e-5 (normwise); the GPU decoder within 1e-2 (its linears compute with fp16
-x', 1e-3 per linear, compounded over two layers)."""
+Tolerances (normwise, max|a - b| / max|b|): the fp32 restatement reproduces
+the reference's logits within 1e-5; the GPU decoder within 1e-3, both with
+the default tensor-core prefill GEMM (fp16 weights and x' products; measured
+on a B200: 4.9e-5 at the prefill, <= 1e-5 at the steps) and with
+faithful_prefill (every packed linear on the streaming GEMV: fp32 group
+scales, x' as an fp16 hi + lo pair; 2.3e-5 and <= 5e-7)."""
 import os
 
 import numpy as np
@@ -35,7 +38,7 @@ def test_restatement_matches_reference_logits():
         assert _rel(lg, g["step_logits"][i]) < 1e-5
 
 
-def _decoder(w, max_seq=32, kv_mode="fp32"):
+def _decoder(w, max_seq=32, kv_mode="fp32", faithful_prefill=False):
     from polarflash_b200.decode import DecoderLayer, PFlashDecoder
     from polarflash_b200.hadamard import column_signs, effective_block
     from polarflash_b200.qweight import QWeight
@@ -53,21 +56,24 @@ def _decoder(w, max_seq=32, kv_mode="fp32"):
         layers.append(DecoderLayer(qw["q"], qw["k"], qw["v"], qw["o"], qw["gate"], qw["up"], qw["down"],
                                    t(ly["in_norm"]), t(ly["post_norm"])))
     return PFlashDecoder(dm.CFG, layers, t(w["embed"]), t(w["final_norm"]), t(w["lm_head"]), max_seq,
-                         kv_mode=kv_mode)
+                         kv_mode=kv_mode, faithful_prefill=faithful_prefill)
 
 
 @pytest.mark.gpu
-def test_prefill_and_graph_steps_match_reference():
+@pytest.mark.parametrize("faithful,tol", [(True, 1e-3), (False, 1e-3)])
+def test_prefill_and_graph_steps_match_reference(faithful, tol):
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     g = np.load(GOLD)
-    dec = _decoder(dm.build())
+    dec = _decoder(dm.build(), faithful_prefill=faithful)
     pre = dec.forward(torch.tensor(g["prompt"], device="cuda")).cpu().numpy()
-    assert _rel(pre, g["prefill_logits"]) < 1e-2
+    errs = [_rel(pre, g["prefill_logits"])]
     dec.capture()
     for i, tok in enumerate(g["decode"].tolist()):
-        lg = dec.step(tok)[0].cpu().numpy()
-        assert _rel(lg, g["step_logits"][i]) < 1e-2, f"step {i}"
+        errs.append(_rel(dec.step(tok)[0].cpu().numpy(), g["step_logits"][i]))
+    print(f"faithful_prefill={faithful}: normwise logits error prefill {errs[0]:.2e}, steps "
+          + ", ".join(f"{e:.2e}" for e in errs[1:]))
+    assert max(errs) < tol, errs
     assert dec.length == len(g["prompt"]) + len(g["decode"])
 
 

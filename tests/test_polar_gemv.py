@@ -1,10 +1,17 @@
-"""GPU parity of the recursive-polar lookup-table GEMV (batch 1, block 8,
-1.75 bpw: allocation 3 | 2 2 2 2 | 1 1 | 1).  The kernel folds the radius
-scale and the psi / phi / theta cos-sin tree into two 64-entry tables per
-x'-vector, so these tests cover rotation blocks from none to 512 columns, the
-three activation dtypes, ragged row blocks, a full Llama-3-8B layer shape
-against the CUDA-core kernel, and the inputs and allocations the kernel does
-not take (which stay on the CUDA-core kernel).
+"""GPU parity of recursive polar (block 8, 1.75 bpw: allocation
+3 | 2 2 2 2 | 1 1 | 1) on its two fast paths.
+
+* The lookup-table GEMV (batch 1): the kernel folds the radius scale and the
+  psi / phi / theta cos-sin tree into two 64-entry tables per x'-vector, so
+  these tests cover rotation blocks from none to 512 columns, the three
+  activation dtypes, ragged row blocks, a full Llama-3-8B layer shape against
+  the CUDA-core kernel, and the inputs and allocations the kernel does not
+  take.
+* The tcgen05 stream-K GEMM (batches of 2 and more, K a multiple of 512):
+  every block decoded into the fp16 A tile from the same cos / sin tables,
+  against the reference's own payload and decode_packed output
+  (tests/golden/polar_recursive.npz, 128 x 1024) at N = 2 ... 2048, and a
+  ragged 1000 x 4096 weight with and without learned angle codebooks.
 
 Tolerance as in test_gpu_parity: y within 1e-3 normwise of the oracle's fp32
 decode + double-accumulated matvec.
@@ -89,9 +96,10 @@ def test_repeated_calls_bit_identical():
         assert torch.equal(qlinear(qw, x), y0)
 
 
-def test_other_inputs_take_the_cuda_core_kernel():
-    """A 2-byte aligned fp16 x, batch 3, and the 2.0 bpw allocation
-    (3 | 2 2 2 2 | 2 2 | 1) are served by the CUDA-core kernel, and agree."""
+def test_other_inputs_take_other_kernels():
+    """A 2-byte aligned fp16 x and the 2.0 bpw allocation (3 | 2 2 2 2 | 2 2 |
+    1) are served by the CUDA-core kernel, batch 3 by the tensor-core GEMM;
+    all agree."""
     from polarflash_b200 import qlinear
 
     M, K = 256, 1024
@@ -172,3 +180,54 @@ def test_group_launch_bit_identical_to_single():
     for i, qw in enumerate(qws):
         assert torch.equal(ys[i], qlinear(qw, x)), f"weight {i}"
         assert_rel(ys[i].cpu().numpy(), _ref(pays[i], qw.M, K, metas[i], x.float().cpu().numpy()))
+
+
+def _golden_polar(key):
+    import json
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    g = np.load(os.path.join(here, "golden", "polar_recursive.npz"))
+    with open(os.path.join(here, "golden", "polar_recursive_meta.json")) as f:
+        meta = dict(json.load(f)[key])
+    meta.update(hadamard_rotation=True, hadamard_block_size=128)
+    return g, meta
+
+
+@pytest.mark.parametrize("N", [2, 17, 64, 300, 2048])
+def test_tensor_core_gemm_reference_payload(N):
+    """The reference's own 1.75 bpw payload (128 x 1024, RWHT-128): y on the
+    tcgen05 GEMM against the reference's decode_packed output, rotated back
+    (the oracle's inverse RWHT), times x."""
+    from polarflash_b200 import dequantize, qlinear, qweight_from_payload
+    from test_gpu_parity import _x
+
+    key = "d8_b1.75_128x1024"
+    g, meta = _golden_polar(key)
+    M, K = 128, 1024
+    qw = qweight_from_payload("polar_recursive", meta, g[f"packed_{key}"].tobytes(), M, K, "cuda")
+    x = _x(N, K, 40 + N)
+    y = qlinear(qw, x.cuda()).cpu().numpy()
+    signs, block = oracle.hadamard_signs(K, 128)
+    W = oracle.rwht(np.ascontiguousarray(g[f"dec_{key}"], np.float32), block, signs, inverse=True)
+    assert_rel(y, oracle.matvec(W, x.float().numpy()))
+    np.testing.assert_allclose(dequantize(qw, inverse_rwht=False).cpu().numpy(), g[f"dec_{key}"], atol=1e-6)
+
+
+@pytest.mark.parametrize("codebooks", [False, True])
+@pytest.mark.parametrize("N", [5, 64, 512])
+def test_tensor_core_gemm_ragged(N, codebooks):
+    """1000 x 4096 (a ragged last row tile), RWHT-128, device-encoded, with
+    the uniform angle grid or learned codebooks (fitted on the weight)."""
+    from polarflash_b200 import encoders, qlinear
+    from polarflash_b200.quantizer import rwht_cpu
+    from polarflash_b200.qweight import qweight_from_payload
+
+    M, K = 1000, 4096
+    Wr = rwht_cpu(_w(M, K, 77), 128)
+    books = encoders.fit_polar_codebooks(Wr[:64], 8, 4, 8) if codebooks else None
+    payload, meta = encoders.polar_encode(Wr.cuda(), 8, 1.75, codebooks=books)
+    meta.update(hadamard_rotation=True, hadamard_block_size=128)
+    qw = qweight_from_payload("polar_recursive", meta, payload, M, K, "cuda")
+    x = _x(N, K, 78)
+    y = qlinear(qw, x.cuda()).cpu().numpy()
+    assert_rel(y, _ref(payload.cpu().numpy().tobytes(), M, K, meta, x.float().numpy()))
