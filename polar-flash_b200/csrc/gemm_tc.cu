@@ -80,16 +80,16 @@ __device__ __forceinline__ unsigned long long gtime() {
   return t;
 }
 
-// The waiting thread may be suspended in try_wait until the phase completes
-// (or 100 us pass) instead of spinning.
+// Bounded wait on an mbarrier phase: try_wait with the hardware's own
+// time limit per attempt, then the abort flag and the 2 s bound.
 __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, const volatile int* abort_flag) {
   unsigned long long t0 = 0;
   for (;;) {
     uint32_t done;
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
         : "=r"(done)
-        : "r"(bar), "r"(parity), "r"(100000u)
+        : "r"(bar), "r"(parity)
         : "memory");
     if (done) return true;
     if (*abort_flag) return false;
@@ -426,6 +426,11 @@ template <>
 struct TcBox<PF_FMT_INT4_G128> {
   static constexpr int GB = 64, CB = 2, SB = 8, SW = 2;  // group bytes, code / scale box groups, scale bytes
 };
+// Code boxes whose rows are exactly 128 bytes (INT4, INT2, E8) are loaded
+// 128B-swizzled (16-byte chunk j of row r at chunk j ^ (r & 7)), so the 32
+// rows a warp reads at one offset fall in eight different bank groups.
+template <class B>
+__host__ __device__ constexpr bool code_swizzled() { return B::CB * B::GB == 128; }
 template <>
 struct TcBox<PF_FMT_INT3_G128> {
   static constexpr int GB = 52, CB = 4, SB = 8, SW = 2;
@@ -449,6 +454,14 @@ struct TcBox<PF_FMT_POLAR_RECURSIVE> {  // block 8, 14-bit blocks: 16 blocks = 2
 constexpr int kBN2 = 256;
 constexpr int kBK2 = 64;
 constexpr int kStages2 = 3;
+// Batches of at most kSmallN tokens: the x' box is at most 32 rows (4 KB per
+// half-stage instead of 32 KB), so the ring holds seven slots and more
+// half-stages are in flight while slots wait on their x' fetch and commit.
+constexpr int kSmallN = 32;
+constexpr int kStagesSmall = 5;
+// Code and scale box slots: two for 256-token tiles; four for small batches,
+// whose decode outruns the DRAM latency of two boxes in flight.
+__host__ __device__ constexpr int sk_box_slots(int xr) { return xr == kBN2 ? 2 : 4; }
 constexpr int kTmemCols2 = 256;
 constexpr uint32_t kATile2 = kBM * kBK2 * 2;  // one 64-column swizzle atom
 
@@ -467,10 +480,25 @@ __device__ __forceinline__ void tma2d_plain(uint32_t dst, const CUtensorMap* map
 // Decodes half H of a row's scale group (A-tile slots 64 H .. 64 H + 63, the
 // 16-byte chunks 8 H .. 8 H + 7) from its packed words at cp into the
 // half-stage A tile at `at` (one 64-column swizzle atom).
-template <int FMT, int H>
-__device__ __forceinline__ void sk_decode(const unsigned char* cp, uint32_t sc, int r, int lane, unsigned char* at,
-                                           const uint4* roots16, const float2* ptab) {
+__device__ __forceinline__ __half2 u32_h2(uint32_t v) {
+  __half2 h;
+  memcpy(&h, &v, 4);
+  return h;
+}
+__device__ __forceinline__ uint32_t h2_u32(__half2 h) {
+  uint32_t v;
+  memcpy(&v, &h, 4);
+  return v;
+}
+
+// crow: this row's bytes in the code slot; gb: the group's byte offset in the
+// row (logical, before the swizzle).  RC: copies of each root in roots16
+// (entry RC k + c), read by lane group c = lane % RC.
+template <int FMT, int H, int RC>
+__device__ __forceinline__ void sk_decode(const unsigned char* crow, int gb, uint32_t sc, int r, int lane,
+                                           unsigned char* at, const uint4* roots16, const float2* ptab) {
   using B = TcBox<FMT>;
+  const unsigned char* cp = crow + gb;
   if constexpr (FMT == PF_FMT_POLAR_RECURSIVE) {
     // Recursive polar, block 8, allocation [3 | 2 2 2 2 | 1 1 | 1]: block c of
     // the group is the 14 bits at bit 14 c of its 28 bytes (MSB first); code
@@ -499,15 +527,13 @@ __device__ __forceinline__ void sk_decode(const unsigned char* cp, uint32_t sc, 
       const float2 f0 = ptab[4 * kPolarTabPerCol + ((w >> 2) & 1u)];
       const float2 f1 = ptab[5 * kPolarTabPerCol + ((w >> 1) & 1u)];
       const float ra = R * ps.x, rb = R * ps.y;
-      const float A[4] = {ra * f0.x, ra * f0.y, rb * f1.x, rb * f1.y};
-      uint4 o4;
-      uint32_t* ov = reinterpret_cast<uint32_t*>(&o4);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 t = ptab[e * kPolarTabPerCol + ((w >> (9 - 2 * e)) & 3u)];
-        const __half2 h = __floats2half2_rn(A[e] * t.x, A[e] * t.y);
-        ov[e] = *reinterpret_cast<const uint32_t*>(&h);
-      }
+      const float2 t0 = ptab[0 * kPolarTabPerCol + ((w >> 9) & 3u)], t1 = ptab[1 * kPolarTabPerCol + ((w >> 7) & 3u)];
+      const float2 t2 = ptab[2 * kPolarTabPerCol + ((w >> 5) & 3u)], t3 = ptab[3 * kPolarTabPerCol + ((w >> 3) & 3u)];
+      const float a0 = ra * f0.x, a1 = ra * f0.y, a2 = rb * f1.x, a3 = rb * f1.y;
+      const uint4 o4 = make_uint4(h2_u32(__floats2half2_rn(a0 * t0.x, a0 * t0.y)),
+                                  h2_u32(__floats2half2_rn(a1 * t1.x, a1 * t1.y)),
+                                  h2_u32(__floats2half2_rn(a2 * t2.x, a2 * t2.y)),
+                                  h2_u32(__floats2half2_rn(a3 * t3.x, a3 * t3.y)));
       *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) = o4;  // rows past M: zero codes (TMA fill)
     }
     return;
@@ -520,7 +546,8 @@ __device__ __forceinline__ void sk_decode(const unsigned char* cp, uint32_t sc, 
   } else {
 #pragma unroll
     for (int q = 0; q < B::GB / 16; ++q) {
-      const uint4 v = *reinterpret_cast<const uint4*>(cp + 16 * q);
+      const int off = code_swizzled<B>() ? ((((gb >> 4) + q) ^ (r & 7)) << 4) : gb + 16 * q;
+      const uint4 v = *reinterpret_cast<const uint4*>(crow + off);
       cw[4 * q] = v.x; cw[4 * q + 1] = v.y; cw[4 * q + 2] = v.z; cw[4 * q + 3] = v.w;
     }
 #pragma unroll
@@ -534,17 +561,11 @@ __device__ __forceinline__ void sk_decode(const unsigned char* cp, uint32_t sc, 
     for (int c = 8 * H; c < 8 * H + 8; ++c) {
       const uint32_t wv = cw[c >> 1] >> (16 * (c & 1));
       const uint32_t i1 = wv & 0xFFu, i2 = (wv >> 8) & 0xFFu;
-      const uint4 ra = roots16[4 * i1 + (lane & 3)], rb = roots16[4 * i2 + (lane & 3)];
-      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&ra);
-      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&rb);
-      uint4 o;
-      uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const __half2 h = __hfma2(s2, *reinterpret_cast<const __half2*>(&pb[e]),
-                                  __hmul2(s1, *reinterpret_cast<const __half2*>(&pa[e])));
-        ov[e] = *reinterpret_cast<const uint32_t*>(&h);
-      }
+      const uint4 ra = roots16[RC * i1 + (lane % RC)], rb = roots16[RC * i2 + (lane % RC)];
+      const uint4 o = make_uint4(h2_u32(__hfma2(s2, u32_h2(rb.x), __hmul2(s1, u32_h2(ra.x)))),
+                                 h2_u32(__hfma2(s2, u32_h2(rb.y), __hmul2(s1, u32_h2(ra.y)))),
+                                 h2_u32(__hfma2(s2, u32_h2(rb.z), __hmul2(s1, u32_h2(ra.z)))),
+                                 h2_u32(__hfma2(s2, u32_h2(rb.w), __hmul2(s1, u32_h2(ra.w)))));
       *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) = o;  // rows past M: zero codes (TMA fill)
     }
   } else {
@@ -559,8 +580,7 @@ __device__ __forceinline__ void sk_decode(const unsigned char* cp, uint32_t sc, 
     }
 #pragma unroll
     for (int c = 8 * H; c < 8 * H + 8; ++c) {
-      uint4 o;
-      uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+      uint32_t ov[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         uint32_t mk;
@@ -572,10 +592,10 @@ __device__ __forceinline__ void sk_decode(const unsigned char* cp, uint32_t sc, 
           const int p = 4 * c + e;
           mk = p < 60 ? (g3[p / 5] >> (3 * (p % 5))) & 0x00070007u : (g3[12] >> (3 * (p - 60))) & 0x00070007u;
         }
-        const __half2 h = __hfma2(pair_fp16(mk), sx, mx);
-        ov[e] = *reinterpret_cast<const uint32_t*>(&h);
+        ov[e] = h2_u32(__hfma2(pair_fp16(mk), sx, mx));
       }
-      *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) = o;  // rows past M: zero codes (TMA fill)
+      *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) =
+          make_uint4(ov[0], ov[1], ov[2], ov[3]);  // rows past M: zero codes (TMA fill)
     }
   }
 }
@@ -717,7 +737,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* f) {
 // loads half of the x' tile (128 tokens), the first CTA of the pair issues
 // the MMAs (reading both CTAs' shared memory) and each CTA's TMEM holds its
 // rows' accumulators.  Half the x' bytes per CTA leave room for five stages.
-template <int FMT, bool kPair>
+template <int FMT, bool kPair, int kXR>
 __global__ void __launch_bounds__(kSkThreads, 1)
     gemm_sk_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
                    const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap mmap,
@@ -725,32 +745,35 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   using B = TcBox<FMT>;
   constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
   constexpr bool kPolar = FMT == PF_FMT_POLAR_RECURSIVE;  // no scale boxes
-  constexpr int kSt = kPair ? kStagesPair : kStages2;    // A/B ring slots
-  constexpr int kXRows = kPair ? kBN2 / 2 : kBN2;       // token rows of this CTA's x' box
+  static_assert(!kPair || kXR == kBN2, "pairs run 256-token tiles");
+  constexpr int kSt = kPair ? kStagesPair : (kXR == kBN2 ? kStages2 : kStagesSmall);  // A/B ring slots
+  constexpr int kXRows = kPair ? kBN2 / 2 : kXR;        // token rows of this CTA's x' box (at most)
   constexpr uint32_t kSB = kATile2 + kXRows * kBK2 * 2;  // bytes per stage
   constexpr int kRowsT = kPair ? 2 * kBM : kBM;          // weight rows per tile
   constexpr uint32_t kCodeSlot = kBM * B::CB * B::GB;  // 128 rows x CB groups
   constexpr uint32_t kScaleSlot = kBM * 16;            // 128 rows x SB groups x SW bytes (16)
+  constexpr int kCS = kPair ? 2 : sk_box_slots(kXR);     // code (and scale) box slots
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // A/B ring full / free, then code full / free and scale full / free (two
+  // A/B ring full / free, then code full / free and scale full / free (kCS
   // slots each), then accumulator full and TMEM-buffer empty (two each)
-  __shared__ uint64_t bars[2 * kSt + 8 + 4];
+  __shared__ uint64_t bars[2 * kSt + 4 * kCS + 4];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
   __shared__ unsigned arrival;
-  __shared__ uint4 roots16[kE8 ? 256 * 4 : 1];
+  constexpr int kRC = kPair ? 4 : 8;  // copies of each root (the pair kernel has less shared memory to spare)
+  __shared__ uint4 roots16[kE8 ? 256 * kRC : 1];
   __shared__ float2 ptab[kPolar ? 7 * kPolarTabPerCol : 1];  // polar cos / sin by angle column and code
   __shared__ float etscale[kBN2];  // token scales of the epilogue's current segment
 
   unsigned char* const base = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
-  unsigned char* const codes = base + kSt * kSB;  // [2][kCodeSlot]
-  unsigned char* const scl = codes + 2 * kCodeSlot;             // [2][kScaleSlot] (+ [2][kScaleSlot] mins)
+  unsigned char* const codes = base + kSt * kSB;  // [kCS][kCodeSlot]
+  unsigned char* const scl = codes + kCS * kCodeSlot;           // [kCS][kScaleSlot] (+ [kCS][kScaleSlot] mins)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // full0: one barrier per ring slot for the decoded A stage and the x' bytes
   const uint32_t full0 = su32(&bars[0]), free0 = su32(&bars[kSt]);
-  const uint32_t cfull0 = su32(&bars[2 * kSt]), cfree0 = cfull0 + 16;
-  const uint32_t sfull0 = cfull0 + 32, sfree0 = cfull0 + 48;
-  const uint32_t accf0 = cfull0 + 64, tempty0 = cfull0 + 80;
+  const uint32_t cfull0 = su32(&bars[2 * kSt]), cfree0 = cfull0 + 8 * kCS;
+  const uint32_t sfull0 = cfree0 + 8 * kCS, sfree0 = sfull0 + 8 * kCS;
+  const uint32_t accf0 = sfree0 + 8 * kCS, tempty0 = accf0 + 16;
   const uint32_t rank = kPair ? cta_rank() : 0u;
   // barriers of the pair's first CTA as cluster addresses (own ones without kPair)
   const uint32_t full_l = kPair ? map_rank0(full0) : full0;
@@ -764,11 +787,13 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                    "r"((kPair ? kDqWarps : kDqWarps / 2) + 1));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(free0 + 8 * s));
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kCS; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(cfull0 + 8 * s));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(cfree0 + 8 * s), "r"(2 * kBM));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sfull0 + 8 * s));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sfree0 + 8 * s), "r"(2 * kBM));
+    }
+    for (int s = 0; s < 2; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(accf0 + 8 * s));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tempty0 + 8 * s), "r"(kPair ? 8 : 4));
     }
@@ -798,7 +823,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         h[q] = *reinterpret_cast<const uint32_t*>(&v);
       }
 #pragma unroll
-      for (int c = 0; c < 4; ++c) roots16[4 * k + c] = make_uint4(h[0], h[1], h[2], h[3]);
+      for (int c = 0; c < kRC; ++c) roots16[kRC * k + c] = make_uint4(h[0], h[1], h[2], h[3]);
     }
   }
   if (warp == kMmaWarp) {
@@ -874,8 +899,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const int m0 = (t % a.n_mb) * kRowsT + (int)rank * kBM;
         for (int s = g0; s < g1 && ok; ++s) {
           if (s == g0 || s % B::CB == 0) {
-            const uint32_t cs = kc & 1;
-            if (kc >= 2 && !bar_wait(cfree0 + 8 * cs, ((kc >> 1) - 1) & 1, &abort_flag)) {
+            const uint32_t cs = kc % kCS;
+            if (kc >= kCS && !bar_wait(cfree0 + 8 * cs, ((kc / kCS) - 1) & 1, &abort_flag)) {
               ok = false;
               break;
             }
@@ -886,8 +911,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             ++kc;
           }
           if (!kPolar && (s == g0 || s % B::SB == 0)) {
-            const uint32_t ss = ks & 1;
-            if (ks >= 2 && !bar_wait(sfree0 + 8 * ss, ((ks >> 1) - 1) & 1, &abort_flag)) {
+            const uint32_t ss = ks % kCS;
+            if (ks >= kCS && !bar_wait(sfree0 + 8 * ss, ((ks / kCS) - 1) & 1, &abort_flag)) {
               ok = false;
               break;
             }
@@ -897,7 +922,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             // x in fp16 elements: E8 keeps two scales per group
             const int sx = s - s % B::SB;
             tma2d_plain(su32(scl + ss * kScaleSlot), &smap, kE8 ? 2 * sx : sx, m0, sfull0 + 8 * ss);
-            if (!kE8) tma2d_plain(su32(scl + (2 + ss) * kScaleSlot), &mmap, sx, m0, sfull0 + 8 * ss);
+            if (!kE8) tma2d_plain(su32(scl + (kCS + ss) * kScaleSlot), &mmap, sx, m0, sfull0 + 8 * ss);
             ++ks;
           }
         }
@@ -985,14 +1010,14 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         // a code / scale box stays put until this thread's last group in it:
         // wait for it once, on entering it
         if (s == g0 || s % B::CB == 0) {
-          cs = kc & 1;
-          cpar = (kc >> 1) & 1;
+          cs = kc % kCS;
+          cpar = (kc / kCS) & 1;
           ++kc;
           if (live && !bar_wait(cfull0 + 8 * cs, cpar, &abort_flag)) fail();
         }
         if (!kPolar && (s == g0 || s % B::SB == 0)) {
-          ss = ks & 1;
-          spar = (ks >> 1) & 1;
+          ss = ks % kCS;
+          spar = (ks / kCS) & 1;
           ++ks;
           if (live && !bar_wait(sfull0 + 8 * ss, spar, &abort_flag)) fail();
         }
@@ -1005,18 +1030,18 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             sc = *reinterpret_cast<const uint32_t*>(sp);
           } else {
             const uint32_t lo = *reinterpret_cast<const uint16_t*>(sp);
-            const uint32_t hi = *reinterpret_cast<const uint16_t*>(sp + 2 * kScaleSlot);
+            const uint32_t hi = *reinterpret_cast<const uint16_t*>(sp + kCS * kScaleSlot);
             sc = lo | (hi << 16);
           }
         }
-        const unsigned char* cp = codes + cs * kCodeSlot + r * (B::CB * B::GB) + (s % B::CB) * B::GB;
+        const unsigned char* crow = codes + cs * kCodeSlot + r * (B::CB * B::GB);
         if (live && q >= kSt && !bar_wait(free0 + 8 * slot, ((q / kSt) - 1) & 1, &abort_flag)) fail();
         if (live) {
           unsigned char* at = base + slot * kSB;
           if (grp == 0)
-            sk_decode<FMT, 0>(cp, sc, r, lane, at, roots16, ptab);
+            sk_decode<FMT, 0, kRC>(crow, (s % B::CB) * B::GB, sc, r, lane, at, roots16, ptab);
           else
-            sk_decode<FMT, 1>(cp, sc, r, lane, at, roots16, ptab);
+            sk_decode<FMT, 1, kRC>(crow, (s % B::CB) * B::GB, sc, r, lane, at, roots16, ptab);
         }
         // hand the code / scale boxes back after this thread's last group in them
         if (s + 1 == g1 || (s + 1) % B::CB == 0)
@@ -1398,13 +1423,13 @@ bool gemm_pair_enabled() {
 // the scale rows need 16-byte aligned bases and row strides, and the tile
 // count must fit the workspace's arrival counters.  kPair: two-CTA clusters,
 // as many as can be resident at once.
-template <int FMT, bool kPair>
+template <int FMT, bool kPair, int kXR = kBN2>
 cudaError_t launch_gemm_sk_impl(GemmArgs a, const __half* x16, cudaStream_t s, bool* taken) {
   using B = TcBox<FMT>;
   constexpr bool kE8 = FMT == PF_FMT_E8_RVQ2_G128;
   constexpr bool kPolar = FMT == PF_FMT_POLAR_RECURSIVE;
-  constexpr int kSt = kPair ? kStagesPair : kStages2;
-  constexpr int kXRows = kPair ? kBN2 / 2 : kBN2;
+  constexpr int kSt = kPair ? kStagesPair : (kXR == kBN2 ? kStages2 : kStagesSmall);
+  constexpr int kXRows = kPair ? kBN2 / 2 : kXR;
   constexpr size_t kSB = kATile2 + (size_t)kXRows * kBK2 * 2;
   constexpr int kRowsT = kPair ? 2 * kBM : kBM;
   *taken = false;
@@ -1440,8 +1465,8 @@ cudaError_t launch_gemm_sk_impl(GemmArgs a, const __half* x16, cudaStream_t s, b
     cuuint32_t box[2] = {(cuuint32_t)(B::CB * B::GB / 4), (cuuint32_t)kBM};
     cuuint32_t estr[2] = {1, 1};
     if (fn(&cmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(a.codes), dims, strides, box, estr,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+           CU_TENSOR_MAP_INTERLEAVE_NONE, code_swizzled<B>() ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaSuccess;
   }
   for (int k = 0; k < (kPolar ? 0 : kE8 ? 1 : 2); ++k) {
@@ -1458,9 +1483,10 @@ cudaError_t launch_gemm_sk_impl(GemmArgs a, const __half* x16, cudaStream_t s, b
   }
   if (kPolar) smap = cmap;  // never read: polar has no scale boxes
   if (kE8 || kPolar) mmap = smap;
-  const size_t smem = 1024 + (size_t)kSt * kSB + 2 * (size_t)kBM * B::CB * B::GB +
-                      (kPolar ? 0 : kE8 ? 2 : 4) * (size_t)kBM * 16;
-  auto kern = gemm_sk_kernel<FMT, kPair>;
+  constexpr int kCS = kPair ? 2 : sk_box_slots(kXR);
+  const size_t smem = 1024 + (size_t)kSt * kSB + (size_t)kCS * kBM * B::CB * B::GB +
+                      (size_t)kCS * (kPolar ? 0 : kE8 ? 1 : 2) * kBM * 16;
+  auto kern = gemm_sk_kernel<FMT, kPair, kXR>;
   // programmatic dependent launch: barrier setup, TMEM allocation, the code and
   // scale loads and the first decodes overlap the x' preparation's tail
   cudaLaunchAttribute attr[2];
@@ -1518,6 +1544,7 @@ cudaError_t launch_gemm_sk(const GemmArgs& a, const __half* x16, cudaStream_t s,
     const cudaError_t e = launch_gemm_sk_impl<FMT, true>(a, x16, s, taken);
     if (*taken || e != cudaSuccess) return e;
   }
+  if (a.N <= kSmallN) return launch_gemm_sk_impl<FMT, false, kSmallN>(a, x16, s, taken);
   return launch_gemm_sk_impl<FMT, false>(a, x16, s, taken);
 }
 

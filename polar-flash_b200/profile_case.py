@@ -36,6 +36,8 @@ def main():
     ap.add_argument("--N", type=int, default=1)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="report device time per call (CUDA events)")
+    ap.add_argument("--graph", action="store_true", help="with --time: replay the calls as one CUDA graph "
+                                                         "(no host launch overhead between calls)")
     ap.add_argument("--copies", type=int, default=1,
                     help="resident copies of the weight cycled by the timed calls (more than L2 holds: 126 MB)")
     ap.add_argument("--attention", default=None, help="comma-separated KV cache modes: run decode attention")
@@ -69,10 +71,26 @@ def main():
             qlinear(qws[i], x, out=out)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = max(5, a.iters)
-        e0.record()
-        for i in range(reps):
-            qlinear(qws[i % len(qws)], x, out=out)
-        e1.record()
+        if a.graph:
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(st):
+                qlinear(qws[0], x, out=out)  # the workspace exists before the capture
+                st.synchronize()
+                with torch.cuda.graph(g, stream=st):
+                    for i in range(reps):
+                        qlinear(qws[i % len(qws)], x, out=out)
+            g.replay()
+            torch.cuda.synchronize()
+            e0.record()
+            g.replay()
+            e1.record()
+        else:
+            e0.record()
+            for i in range(reps):
+                qlinear(qws[i % len(qws)], x, out=out)
+            e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / reps
         flops = 2.0 * a.M * a.K * a.N
