@@ -148,19 +148,25 @@ def decode_rates(copies, xs, outs, ws, stream, dev, layers, tokens=20):
     nb = sum(q.nbytes() + q.K * 2 + q.M * 4 for q in base.values()) * layers
     res["polar_recursive_1.75"] = {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
                                    "GB_s": round(nb / ms / 1e6, 1)}
-    del graphs, pc, base
-    res.update(decode_full_step(copies, stream, dev, layers, tokens=tokens))
+    del graphs
+    # the whole step of the recursive-polar stack at a 2048-token context
+    res.update(decode_full_step(pc, stream, dev, 2048, tokens, "llama3_8b_polar1.75_full_step_ctx2048", nb))
+    del pc, base
+    int3 = [{n: copies[li % len(copies)][("int3_g128", n)] for n, _, _ in LINEARS} for li in range(layers)]
+    nb3 = sum(alg_bytes(copies[0][("int3_g128", n)], 1) for n, _, _ in LINEARS) * layers
+    res.update(decode_full_step(int3, stream, dev, 512, tokens, "llama3_8b_int3_full_step_ctx512", nb3))
     res.update(decode_rates_70b_e8(stream, dev, tokens))
     res.update(kv_attention_rates(stream, dev, tokens=tokens))
     return res
 
 
-def decode_full_step(copies, stream, dev, layers=32, ctx=512, tokens=20):
+def decode_full_step(layer_ws, stream, dev, ctx, tokens, name, lin_bytes):
     """Tokens/s of a whole batch-1 decode step of the Llama-3-8B shape
     (polarflash_b200.decode.PFlashDecoder, one CUDA graph per token): the
-    INT3 g128 linears of `layers` layers (the bench's weights), RMSNorms,
-    RoPE, the fp32 KV cache at `ctx` previous tokens, the library's attention
-    kernels and a dense fp16 embedding and lm_head (128256 x 4096, 1.05 GB)."""
+    packed linears of every layer (`layer_ws`: one dict q..down -> QWeight
+    per layer, `lin_bytes` their algorithmic bytes), RMSNorms, RoPE, the fp32
+    KV cache at `ctx` previous tokens, the library's attention kernels and a
+    dense fp16 embedding and lm_head (128256 x 4096, 1.05 GB)."""
     from polarflash_b200.decode import DecoderLayer, PFlashDecoder
 
     H, V = 4096, 128256
@@ -168,11 +174,8 @@ def decode_full_step(copies, stream, dev, layers=32, ctx=512, tokens=20):
                rope_theta=500000.0, rms_norm_eps=1e-5)
     g = torch.Generator(device=dev).manual_seed(5)
     ones = torch.ones(H, device=dev)
-    lys = []
-    for li in range(layers):
-        cp = copies[li % len(copies)]
-        w = {n: cp[("int3_g128", n)] for n, _, _ in LINEARS}
-        lys.append(DecoderLayer(w["q"], w["k"], w["v"], w["o"], w["gate"], w["up"], w["down"], ones, ones))
+    layers = len(layer_ws)
+    lys = [DecoderLayer(w["q"], w["k"], w["v"], w["o"], w["gate"], w["up"], w["down"], ones, ones) for w in layer_ws]
     embed = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
     head = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
     dec = PFlashDecoder(cfg, lys, embed, ones, head, max_seq=ctx + 1)
@@ -191,11 +194,9 @@ def decode_full_step(copies, stream, dev, layers=32, ctx=512, tokens=20):
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / tokens
-    nb = sum(alg_bytes(copies[0][("int3_g128", n)], 1) for n, _, _ in LINEARS) * layers + V * H * 2 + \
-        layers * 2 * (ctx + 1) * 8 * 128 * 4
-    del dec, embed, head
-    return {"llama3_8b_int3_full_step_ctx512": {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4),
-                                                "GB_s": round(nb / ms / 1e6, 1)}}
+    nb = lin_bytes + V * H * 2 + layers * 2 * (ctx + 1) * 8 * 128 * 4
+    del dec, embed, head, lys
+    return {name: {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4), "GB_s": round(nb / ms / 1e6, 1)}}
 
 
 def kv_attention_rates(stream, dev, layers=32, ctx=16384, tokens=20):
@@ -785,9 +786,10 @@ def main():
         decode["what"] = ("linears of one decode step: Llama-3-8B shape (32 layers x q|k|v, o, gate|up, down) at "
                           "batch 1 for INT3 / INT2 / polar 1.75, Llama-3-70B shape (80 layers, E8 RVQ2) at batch 1 "
                           "and 32; one resident weight copy per layer, CUDA-graph replays; attention, norms and "
-                          "lm_head not included, except llama3_8b_int3_full_step_ctx512: the whole batch-1 step "
+                          "lm_head not included, except llama3_8b_int3_full_step_ctx512 and "
+                          "llama3_8b_polar1.75_full_step_ctx2048: the whole batch-1 step "
                           "through polarflash_b200.decode (the library's RMSNorm, RoPE + cache write, attention "
-                          "and SiLU kernels, fp32 KV cache at 512 tokens, fp16 embedding and lm_head), one CUDA "
+                          "and SiLU kernels, fp32 KV cache at 512 / 2048 tokens, fp16 embedding and lm_head), one CUDA "
                           "graph per token; kv_attention_llama3_8b_ctx16k: the attention alone over 32 layers' "
                           "caches at 16384 tokens, fp32 and compressed (int8, 2bit, 2bit_asym) caches")
 
