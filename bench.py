@@ -299,6 +299,27 @@ def decode_rates_70b_e8(stream, dev, tokens, layers=80):
         res[f"e8_rvq2_70b_batch{B}"] = {"tok_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
                                         "GB_s": round(layer_bytes * layers / ms / 1e6, 1)}
         del graphs
+    # config 5's prefill: 2048 tokens through the linears of `pl` layers (each
+    # layer's own copy), the tensor-core GEMM in 512-token chunks
+    B, pl = 2048, 4
+    g = torch.Generator().manual_seed(B)
+    xs = {grp: torch.randn(B, kdim[grp[0]], generator=g).half().to(dev) for grp in SHARED}
+    outs = {n: torch.empty(B, M, device=dev) for n, M, _ in LINEARS_70B}
+    need = max(group_workspace_bytes([base[n] for n in grp], B) for grp in SHARED)
+    ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+    graphs = []
+    with torch.cuda.stream(stream):
+        for cp in pc[:pl]:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for grp in SHARED:
+                    qlinear_multi([cp[n] for n in grp], xs[grp], workspace=ws, outs=[outs[n] for n in grp])
+            graphs.append(gr)
+    ms = time_tokens(graphs, stream, 2) / pl  # ms per layer
+    flops = 2.0 * B * sum(M * K for _, M, K in LINEARS_70B)
+    res["e8_rvq2_70b_prefill_2048"] = {"ms_per_layer": round(ms, 4), "TFLOP_s": round(flops / ms / 1e9, 1),
+                                       "tok_s": round(B * 1e3 / (ms * layers), 1)}
+    del graphs, xs, outs, ws
     del pc, base
     return res
 
@@ -785,7 +806,9 @@ def main():
             decode = {"error": f"{type(e).__name__}: {e}"[:300]}
         decode["what"] = ("linears of one decode step: Llama-3-8B shape (32 layers x q|k|v, o, gate|up, down) at "
                           "batch 1 for INT3 / INT2 / polar 1.75, Llama-3-70B shape (80 layers, E8 RVQ2) at batch 1 "
-                          "and 32; one resident weight copy per layer, CUDA-graph replays; attention, norms and "
+                          "and 32 and its 2048-token prefill (e8_rvq2_70b_prefill_2048: the linears of one layer "
+                          "per graph, tensor-core GEMM; tok_s scales the layer time to 80 layers); "
+                          "one resident weight copy per layer, CUDA-graph replays; attention, norms and "
                           "lm_head not included, except llama3_8b_int3_full_step_ctx512 and "
                           "llama3_8b_polar1.75_full_step_ctx2048: the whole batch-1 step "
                           "through polarflash_b200.decode (the library's RMSNorm, RoPE + cache write, attention "

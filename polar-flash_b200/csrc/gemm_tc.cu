@@ -499,6 +499,14 @@ __device__ __forceinline__ void sk_decode(const unsigned char* crow, int gb, uin
                                            unsigned char* at, const uint4* roots16, const float2* ptab) {
   using B = TcBox<FMT>;
   const unsigned char* cp = crow + gb;
+  // the eight decoded chunks are kept in registers and stored together at the
+  // end, so no A-tile store sits between two of the decode's shared loads
+  uint4 ob[8];
+  auto store_all = [&]() {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)  // rows past M: zero codes (TMA fill)
+      *reinterpret_cast<uint4*>(at + a_chunk(r, 8 * H + k) - H * (kBM * 128)) = ob[k];
+  };
   if constexpr (FMT == PF_FMT_POLAR_RECURSIVE) {
     // Recursive polar, block 8, allocation [3 | 2 2 2 2 | 1 1 | 1]: block c of
     // the group is the 14 bits at bit 14 c of its 28 bytes (MSB first); code
@@ -534,8 +542,9 @@ __device__ __forceinline__ void sk_decode(const unsigned char* crow, int gb, uin
                                   h2_u32(__floats2half2_rn(a1 * t1.x, a1 * t1.y)),
                                   h2_u32(__floats2half2_rn(a2 * t2.x, a2 * t2.y)),
                                   h2_u32(__floats2half2_rn(a3 * t3.x, a3 * t3.y)));
-      *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) = o4;  // rows past M: zero codes (TMA fill)
+      ob[c - 8 * H] = o4;
     }
+    store_all();
     return;
   }
   uint32_t cw[16];
@@ -566,8 +575,9 @@ __device__ __forceinline__ void sk_decode(const unsigned char* crow, int gb, uin
                                  h2_u32(__hfma2(s2, u32_h2(rb.y), __hmul2(s1, u32_h2(ra.y)))),
                                  h2_u32(__hfma2(s2, u32_h2(rb.z), __hmul2(s1, u32_h2(ra.z)))),
                                  h2_u32(__hfma2(s2, u32_h2(rb.w), __hmul2(s1, u32_h2(ra.w)))));
-      *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) = o;  // rows past M: zero codes (TMA fill)
+      ob[c - 8 * H] = o;
     }
+    store_all();
   } else {
     // w = q s + m as one fp16 FMA of the exact code (the stored fp16 s and m)
     const __half2 sx = __half2half2(__ushort_as_half((unsigned short)(sc & 0xFFFFu)));
@@ -594,9 +604,9 @@ __device__ __forceinline__ void sk_decode(const unsigned char* crow, int gb, uin
         }
         ov[e] = h2_u32(__hfma2(pair_fp16(mk), sx, mx));
       }
-      *reinterpret_cast<uint4*>(at + a_chunk(r, c) - H * (kBM * 128)) =
-          make_uint4(ov[0], ov[1], ov[2], ov[3]);  // rows past M: zero codes (TMA fill)
+      ob[c - 8 * H] = make_uint4(ov[0], ov[1], ov[2], ov[3]);
     }
+    store_all();
   }
 }
 
