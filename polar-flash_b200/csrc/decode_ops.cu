@@ -56,6 +56,60 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
   for (int i = threadIdx.x; i < H; i += blockDim.x) out[(size_t)blockIdx.x * H + i] = hr[i] * r * w[i];
 }
 
+// The same for rows of H % 4 == 0 floats (16-byte aligned): each thread
+// issues all its float4 loads of h, delta and w (at most V of each) before
+// any arithmetic, so a row costs one memory latency instead of one per
+// strided iteration.
+template <int V>
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_vec_kernel(float* __restrict__ h,
+                                                                       const float* __restrict__ delta,
+                                                                       const float* __restrict__ w,
+                                                                       float* __restrict__ out, int H, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  pdl_enter();
+  const int n4 = H >> 2;
+  float4* hr = reinterpret_cast<float4*>(h + (size_t)blockIdx.x * H);
+  const float4* dr = delta ? reinterpret_cast<const float4*>(delta + (size_t)blockIdx.x * H) : nullptr;
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  float4 hv[V], dv[V], wv[V];
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    if (i < n4) {
+      hv[k] = hr[i];
+      dv[k] = dr ? dr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      wv[k] = wr[i];
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    if (i < n4) {
+      if (dr) {
+        hv[k].x += dv[k].x;
+        hv[k].y += dv[k].y;
+        hv[k].z += dv[k].z;
+        hv[k].w += dv[k].w;
+        hr[i] = hv[k];
+      }
+      ss += hv[k].x * hv[k].x;
+      ss += hv[k].y * hv[k].y;
+      ss += hv[k].z * hv[k].z;
+      ss += hv[k].w * hv[k].w;
+    }
+  }
+  const float r = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  float4* orow = reinterpret_cast<float4*>(out + (size_t)blockIdx.x * H);
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    if (i < n4)
+      orow[i] = make_float4(hv[k].x * r * wv[k].x, hv[k].y * r * wv[k].y, hv[k].z * r * wv[k].z,
+                            hv[k].w * r * wv[k].w);
+  }
+}
+
 // The pair (x1, x2) rotated by the angle with cosine c and sine s, each
 // product and sum rounded on its own (as the reference's separate tensor
 // ops round them; no fma contraction, so every kernel rotates alike).
@@ -571,6 +625,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, int threads, cudaStrea
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 bool al4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 }  // namespace pfb
@@ -581,8 +636,14 @@ int pf_add_rmsnorm(float* h, const float* delta, const float* w, float* out, int
   if (!h || !w || !out || rows < 0 || H <= 0 || !(eps >= 0.f)) return PF_ERR_INVALID_ARGUMENT;
   if (!al4(h) || !al4(w) || !al4(out) || (delta && !al4(delta))) return PF_ERR_ALIGNMENT;
   if (rows == 0) return PF_OK;
-  return status_of(launch_pdl(add_rmsnorm_kernel, dim3(rows), kNormThreads, static_cast<cudaStream_t>(stream), h, delta,
-                              w, out, H, eps));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool vec = H % 4 == 0 && al16(h) && al16(w) && al16(out) && (!delta || al16(delta));
+  const int per = (H / 4 + kNormThreads - 1) / kNormThreads;  // float4 per thread
+  if (vec && per <= 1) return status_of(launch_pdl(add_rmsnorm_vec_kernel<1>, dim3(rows), kNormThreads, st, h, delta, w, out, H, eps));
+  if (vec && per <= 2) return status_of(launch_pdl(add_rmsnorm_vec_kernel<2>, dim3(rows), kNormThreads, st, h, delta, w, out, H, eps));
+  if (vec && per <= 4) return status_of(launch_pdl(add_rmsnorm_vec_kernel<4>, dim3(rows), kNormThreads, st, h, delta, w, out, H, eps));
+  if (vec && per <= 8) return status_of(launch_pdl(add_rmsnorm_vec_kernel<8>, dim3(rows), kNormThreads, st, h, delta, w, out, H, eps));
+  return status_of(launch_pdl(add_rmsnorm_kernel, dim3(rows), kNormThreads, st, h, delta, w, out, H, eps));
 }
 
 int pf_rope_kv(float* q, const float* k, const float* v, float* k_cache, float* v_cache, const long long* pos,

@@ -16,6 +16,13 @@ random rows, for each listed cache mode (fp32 through pf_decode_attention,
 int8 / 2bit / 2bit_asym through pf_decode_attention_compressed):
 
     python polar-flash_b200/profile_case.py --attention fp32,int8,2bit --ctx 16384 --iters 1
+
+With --decode-step, a whole batch-1 decode step of a Llama-3-8B-shaped stack
+(PFlashDecoder, --layers layers, recursive polar 1.75 bpw or INT3 g128 linears
+via --fmt, fp32 KV cache at --ctx positions, fp16 embedding and lm_head),
+captured once as a CUDA graph and replayed --iters times:
+
+    python polar-flash_b200/profile_case.py --decode-step --fmt polar_recursive --layers 32 --ctx 2048 --iters 3
 """
 import argparse
 import os
@@ -44,11 +51,15 @@ def main():
     ap.add_argument("--ctx", type=int, default=16384, help="cached positions (--attention)")
     ap.add_argument("--set", action="store_true", help="the Llama-3-8B linear set at INT3 + INT2 in one call")
     ap.add_argument("--layer-order", action="store_true", help="with --set: one call per shared input")
+    ap.add_argument("--decode-step", action="store_true", help="a whole batch-1 decode step (PFlashDecoder)")
+    ap.add_argument("--layers", type=int, default=32, help="layers of the --decode-step stack")
     a = ap.parse_args()
     if a.attention:
         return attention_case(a)
     if a.set:
         return set_case(a)
+    if a.decode_step:
+        return decode_step_case(a)
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
     W = torch.randn(a.M, a.K, generator=g, device=dev) * 0.02
@@ -203,6 +214,50 @@ def attention_case(a):
             us = e0.elapsed_time(e1) * 1e3 / reps
             nb = 2 * ms * nkv * (rb + (0 if mode == "fp32" else 4) + (4 if mode == "2bit_asym" else 0))
             print(f"time {us:.1f} us  {nb / us / 1e3:.1f} GB/s of cache rows")
+
+
+def decode_step_case(a):
+    from polarflash_b200.decode import DecoderLayer, PFlashDecoder
+
+    dev = torch.device("cuda")
+    H, V, FF = 4096, 128256, 14336
+    shapes = {"q": (4096, H), "k": (1024, H), "v": (1024, H), "o": (H, 4096), "gate": (FF, H), "up": (FF, H),
+              "down": (H, FF)}
+    g = torch.Generator(device=dev).manual_seed(0)
+    base = {}
+    for n, (M, K) in shapes.items():
+        W = torch.randn(M, K, generator=g, device=dev) * 0.02
+        base[n], _ = UnifiedQuantizer(backend=a.fmt, hadamard_block_size=128).quantize_to_qweight(W)
+        del W
+    from polarflash_b200.qweight import QWeight
+
+    def copy(q):
+        return QWeight(q.format, q.M, q.K, q.codes.clone(), q.scales.clone() if q.scales is not None else None,
+                       q.mins.clone() if q.mins is not None else None, q.had_block, q.had_signs, q.tensor_scale,
+                       list(q.params))
+    ones = torch.ones(H, device=dev)
+    layers = []
+    for li in range(a.layers):
+        w = base if li == 0 else {n: copy(q) for n, q in base.items()}
+        layers.append(DecoderLayer(w["q"], w["k"], w["v"], w["o"], w["gate"], w["up"], w["down"], ones, ones))
+    cfg = dict(hidden_size=H, num_attention_heads=32, num_key_value_heads=8, intermediate_size=FF, vocab_size=V,
+               rope_theta=500000.0, rms_norm_eps=1e-5)
+    embed = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
+    head = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
+    dec = PFlashDecoder(cfg, layers, embed, ones, head, max_seq=a.ctx + 1)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        dec.forward(torch.tensor([1], device=dev))
+        dec.length = a.ctx
+        dec.capture(st)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dec._graph.replay()
+        e0.record(st)
+        for _ in range(a.iters):
+            dec._graph.replay()
+        e1.record(st)
+    torch.cuda.synchronize()
+    print(f"decode step {a.fmt}, {a.layers} layers, ctx {a.ctx}: {e0.elapsed_time(e1) / a.iters:.3f} ms per token")
 
 
 if __name__ == "__main__":
