@@ -66,6 +66,8 @@ def parse():
                          "weak = each rank a full set of its own")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode tokens/s figures")
+    ap.add_argument("--tp-decode", action="store_true",
+                    help="at N GPUs: also time the column-parallel config-4 decode step (4 all-gathers per layer)")
     return ap.parse_args()
 
 
@@ -197,6 +199,69 @@ def decode_full_step(layer_ws, stream, dev, ctx, tokens, name, lin_bytes):
     nb = lin_bytes + V * H * 2 + layers * 2 * (ctx + 1) * 8 * 128 * 4
     del dec, embed, head, lys
     return {name: {"tok_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4), "GB_s": round(nb / ms / 1e6, 1)}}
+
+
+def decode_tp_step(stream, dev, world, layers=32, ctx=2048, tokens=20):
+    """Config 4 column-parallel: the whole batch-1 decode step of the
+    recursive-polar 1.75 bpw Llama-3-8B stack at a `ctx`-token context with
+    every projection row-sharded over the `world` ranks
+    (PFlashDecoder(tp=GroupGather()): one NCCL all-gather per projection
+    group, four per layer, inside the step's CUDA graph); norms, RoPE,
+    attention, the KV cache and the lm_head replicated.  Returns ms per token,
+    max over ranks."""
+    import torch.distributed as dist
+
+    from polarflash_b200 import encoders
+    from polarflash_b200.decode import DecoderLayer, PFlashDecoder
+    from polarflash_b200.hadamard import BlockHadamardTransform, column_signs, effective_block
+    from polarflash_b200.parallel import GroupGather, shard_bounds
+    from polarflash_b200.qweight import QWeight
+
+    rank = dist.get_rank()
+    shards = {}
+    for i, (name, M, K) in enumerate(LINEARS):
+        W = synth_weight(M, K, 2000 + i, dev)
+        payload, meta = encoders.polar_encode(BlockHadamardTransform(K, 128, device=dev).forward(W), 8, 1.75)
+        full = QWeight(8, M, K, payload, None, None, effective_block(128, K), column_signs(K, 128, dev),
+                       meta["r_scale"], [8] + meta["alloc"])
+        shards[name] = full.shard_rows(*shard_bounds(M, world, rank))
+        del W, full, payload
+    H, V = 4096, 128256
+    ones = torch.ones(H, device=dev)
+    lys = []
+    for li in range(layers):
+        w = shards if li == 0 else {n: QWeight(q.format, q.M, q.K, q.codes.clone(), None, None, q.had_block,
+                                               q.had_signs, q.tensor_scale, list(q.params))
+                                    for n, q in shards.items()}
+        lys.append(DecoderLayer(w["q"], w["k"], w["v"], w["o"], w["gate"], w["up"], w["down"], ones, ones))
+    g = torch.Generator(device=dev).manual_seed(5)
+    embed = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
+    head = (torch.randn(V, H, generator=g, device=dev) * 0.02).half()
+    cfg = dict(hidden_size=H, num_attention_heads=32, num_key_value_heads=8, intermediate_size=14336,
+               vocab_size=V, rope_theta=500000.0, rms_norm_eps=1e-5)
+    dec = PFlashDecoder(cfg, lys, embed, ones, head, max_seq=ctx + 1, tp=GroupGather())
+    with torch.cuda.stream(stream):
+        dec.forward(torch.tensor([1], device=dev))
+        dec.length = ctx
+        dec.capture(stream)
+        for _ in range(2):
+            dec._graph.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(tokens):
+            dec._graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / tokens], device=dev, dtype=torch.float64)
+    dec._graph = None  # holds NCCL calls: released before the process group
+    del dec, lys, shards, embed, head
+    import gc
+
+    gc.collect()
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return float(ms.item())
 
 
 def kv_attention_rates(stream, dev, layers=32, ctx=16384, tokens=20):
@@ -816,6 +881,15 @@ def main():
                           "graph per token; kv_attention_llama3_8b_ctx16k: the attention alone over 32 layers' "
                           "caches at 16384 tokens, fp32 and compressed (int8, 2bit, 2bit_asym) caches")
 
+    tp_step = None
+    if world > 1 and args.tp_decode:
+        ms_tok = decode_tp_step(stream, dev, world)
+        tp_step = {"llama3_8b_polar1.75_full_step_ctx2048": {"tok_s": round(1e3 / ms_tok, 1),
+                                                             "ms_per_token": round(ms_tok, 4)},
+                   "what": f"config 4 column-parallel over {world} GPUs: every projection row-sharded, one NCCL "
+                           "all-gather per projection group (4 per layer) in the step's CUDA graph, the rest "
+                           "replicated; max over ranks"}
+
     # max over ranks
     t = torch.tensor([ms, ms_run, ms_e2e, ms_layer], device=dev, dtype=torch.float64)
     if world > 1:
@@ -903,6 +977,7 @@ def main():
                         else "NCCL all-gather captured in the graph") if world > 1 else None),
             "gpu_launches": launches_per_step * args.steps,
             "decode_tok_s": decode,
+            "decode_tp": tp_step,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

@@ -75,13 +75,20 @@ class PFlashDecoder:
     streaming GEMV (fp32 group scales, x' as an fp16 hi + lo pair: fp32-level
     products) instead of the tensor-core GEMM (fp16 weights and x'); it costs
     one weight pass per 16 tokens.
+
+    ``tp`` runs the stack column-parallel (one process per GPU): every layer
+    holds this rank's row shards of its seven projections (QWeight.shard_rows:
+    rows [r M / P, (r + 1) M / P), q|k|v biases sliced alike), and after each
+    projection group (q|k|v, o, gate|up, down) ``tp.gather`` assembles the full
+    outputs (parallel.GroupGather: one all-gather per group); norms, RoPE,
+    attention, the cache and the lm_head are replicated on every rank.
     """
 
     GEMV_TOKENS = 16  # the largest batch the streaming GEMV takes in one pass
 
     def __init__(self, config: Dict, layers: List[DecoderLayer], embed: torch.Tensor, final_norm: torch.Tensor,
                  lm_head: torch.Tensor, max_seq: int, kv_dtype: torch.dtype = torch.float32, kv_mode: str = "fp32",
-                 faithful_prefill: bool = False):
+                 faithful_prefill: bool = False, tp=None):
         self.hidden = int(config["hidden_size"])
         self.nh = int(config["num_attention_heads"])
         self.nkv = int(config["num_key_value_heads"])
@@ -90,6 +97,7 @@ class PFlashDecoder:
         self.eps = float(config.get("rms_norm_eps", 1e-6))
         self.layers = layers
         self.faithful_prefill = bool(faithful_prefill)
+        self.tp = tp
         self.embed = embed
         self.final_norm = final_norm
         self.lm_head = lm_head
@@ -157,19 +165,25 @@ class PFlashDecoder:
             return torch.cat(parts)
         return [torch.cat([p[j] for p in parts]) for j in range(len(parts[0]))]
 
+    def _lin(self, ws: List[QWeight], x: torch.Tensor, biases=None, workspace=None) -> List[torch.Tensor]:
+        """One projection group over input x (full outputs under tp)."""
+        ys = qlinear_multi(ws, x, biases, workspace=workspace) if len(ws) > 1 else \
+            [qlinear(ws[0], x, biases[0] if biases else None, workspace=workspace)]
+        return self.tp.gather(ys) if self.tp is not None else ys
+
     def _layer(self, li: int, h: torch.Tensor, cs, attend, ws) -> torch.Tensor:
         ly = self.layers[li]
         S = h.shape[0]
         n = self._rmsnorm(h, ly.input_norm)
-        q, k, v = self._sliced(lambda t: qlinear_multi([ly.q, ly.k, ly.v], t, ly.qkv_bias, workspace=ws), n)
+        q, k, v = self._sliced(lambda t: self._lin([ly.q, ly.k, ly.v], t, ly.qkv_bias, workspace=ws), n)
         q = self._rope(q.view(S, self.nh, self.hd), cs)
         k = self._rope(k.view(S, self.nkv, self.hd), cs)
         v = v.view(S, self.nkv, self.hd)
         attn = attend(li, q, k, v)  # [S, hidden]
-        h = h + self._sliced(lambda t: qlinear(ly.o, t, workspace=ws), attn)
+        h = h + self._sliced(lambda t: self._lin([ly.o], t, workspace=ws)[0], attn)
         n2 = self._rmsnorm(h, ly.post_norm)
-        g, u = self._sliced(lambda t: qlinear_multi([ly.gate, ly.up], t, workspace=ws), n2)
-        return h + self._sliced(lambda t: qlinear(ly.down, t, workspace=ws), F.silu(g) * u)
+        g, u = self._sliced(lambda t: self._lin([ly.gate, ly.up], t, workspace=ws), n2)
+        return h + self._sliced(lambda t: self._lin([ly.down], t, workspace=ws)[0], F.silu(g) * u)
 
     # ---- eager forward (prefill, or any number of new tokens) --------------
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
@@ -246,7 +260,7 @@ class PFlashDecoder:
         for li, ly in enumerate(self.layers):
             _lib.check(L.pf_add_rmsnorm(_p(h), _p(delta), _p(ly.input_norm), _p(n), 1, H, self.eps, st),
                        "pf_add_rmsnorm")
-            q, k, v = qlinear_multi([ly.q, ly.k, ly.v], n, ly.qkv_bias, workspace=self.ws1)
+            q, k, v = self._lin([ly.q, ly.k, ly.v], n, ly.qkv_bias, workspace=self.ws1)
             attn = torch.empty(1, H, dtype=torch.float32, device=self.device)
             if self.kv_mode == "fp32":
                 _lib.check(L.pf_rope_kv(_p(q), _p(k), _p(v), _p(self.k_cache[li]), _p(self.v_cache[li]),
@@ -265,14 +279,14 @@ class PFlashDecoder:
                                                             _p(self._pos), _p(attn), nh, nkv, hd, ms, m, scale,
                                                             _p(self.attn_ws), self.attn_ws.numel(), st),
                            "pf_decode_attention_compressed")
-            o = qlinear(ly.o, attn, workspace=self.ws1)
+            o = self._lin([ly.o], attn, workspace=self.ws1)[0]
             n2 = torch.empty_like(h)
             _lib.check(L.pf_add_rmsnorm(_p(h), _p(o), _p(ly.post_norm), _p(n2), 1, H, self.eps, st),
                        "pf_add_rmsnorm")
-            g, u = qlinear_multi([ly.gate, ly.up], n2, workspace=self.ws1)
+            g, u = self._lin([ly.gate, ly.up], n2, workspace=self.ws1)
             a = torch.empty_like(g)
             _lib.check(L.pf_silu_mul(_p(g), _p(u), _p(a), g.numel(), st), "pf_silu_mul")
-            delta = qlinear(ly.down, a, workspace=self.ws1)
+            delta = self._lin([ly.down], a, workspace=self.ws1)[0]
         hn = torch.empty_like(h)
         _lib.check(L.pf_add_rmsnorm(_p(h), _p(delta), _p(self.final_norm), _p(hn), 1, H, self.eps, st),
                    "pf_add_rmsnorm")

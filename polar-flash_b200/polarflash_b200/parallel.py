@@ -55,6 +55,35 @@ class ColumnParallelQLinear:
     __call__ = forward
 
 
+class GroupGather:
+    """Assembles the full outputs of one group of row-sharded linears that
+    read one input (q|k|v, gate|up, or a single linear) with ONE all-gather:
+    the group's shard outputs [S, M_i / P] are packed side by side, gathered
+    rank-major into [P, S, sum M_i / P] and each output taken back out as the
+    full [S, M_i] (rank r's rows at [r M_i / P, (r + 1) M_i / P)).  Used by
+    PFlashDecoder(tp=...) for a column-parallel decode step; capturable in a
+    CUDA graph."""
+
+    def __init__(self, group: Optional[dist.ProcessGroup] = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def gather(self, ys: List[torch.Tensor]) -> List[torch.Tensor]:
+        if self.world == 1:
+            return ys
+        S = ys[0].shape[0]
+        packed = torch.cat([y.reshape(S, -1) for y in ys], dim=1).contiguous()
+        out = torch.empty(self.world, S, packed.shape[1], dtype=packed.dtype, device=packed.device)
+        dist.all_gather_into_tensor(out.view(-1), packed.view(-1), group=self.group)
+        full, off = [], 0
+        for y in ys:
+            m = y.shape[-1]
+            full.append(out[:, :, off:off + m].permute(1, 0, 2).reshape(S, self.world * m))
+            off += m
+        return full
+
+
 def gather_rows(y_local: torch.Tensor, world: int, group=None) -> torch.Tensor:
     """All-gather of [N, M/P] shards into [N, M] (host-side helper for tests)."""
     N, m = y_local.shape

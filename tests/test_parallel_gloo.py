@@ -86,3 +86,42 @@ def test_shard_bounds_rejects_uneven():
     assert shard_bounds(1024, 8, 7) == (896, 1024)
     with pytest.raises(ValueError):
         shard_bounds(1001, 8, 0)
+
+
+def _group_worker(rank, world, port, out_q):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "polar-flash_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from polarflash_b200.parallel import GroupGather
+
+        g = torch.Generator().manual_seed(1)
+        S, Ms = 3, (96, 24, 24)  # q|k|v-like group, full widths
+        full = [torch.randn(S, M, generator=g) for M in Ms]
+        shards = [f[:, rank * (M // world):(rank + 1) * (M // world)].contiguous() for f, M in zip(full, Ms)]
+        out = GroupGather().gather(shards)
+        if rank == 0:
+            out_q.put(([o.numpy() for o in out], [f.numpy() for f in full]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_group_gather_one_collective_world2():
+    """GroupGather packs a projection group's row-shard outputs, gathers them
+    in one collective and hands back each full output (the tensor-parallel
+    decode step's gather)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_group_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out, full = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for o, f in zip(out, full):
+        np.testing.assert_array_equal(o, f)
