@@ -234,6 +234,19 @@ PF_API int pf_qlinear_group_gather(int count, const pf_qweight* const* ws, const
                                    int N, const float* const* biases, const size_t* y_offsets,
                                    const int* m_full, const pf_peers* peers, void* workspace,
                                    size_t workspace_bytes, void* stream);
+/* All-gather of row shards that are already computed, over the same peer
+ * buffers (replaces an ncclAllGather after a column-parallel linear whose
+ * shard came from elsewhere; polarflash_rt/cuda/engine.py:129-145 computes
+ * the whole y on one device).  This rank's `bytes` at `src` (device,
+ * 16-byte aligned, a multiple of 16) land at byte dst_offset + rank * bytes
+ * of every rank's buffer (rank-major, as ncclAllGather orders them;
+ * dst_offset >= 256 and 16-byte aligned, world * bytes must fit).  One
+ * kernel: plain peer stores, then the launch's last block raises this rank's
+ * flag in every buffer and waits (bounded) for every rank's flag, so when the
+ * kernel completes the gathered rows are in the local buffer.  Every rank
+ * makes the same sequence of gathering calls. */
+PF_API int pf_allgather_rows(const pf_peers* peers, const void* src, size_t bytes, size_t dst_offset,
+                             void* workspace, void* stream);
 /* Makes `stream` wait (one small kernel, each wait bounded to 2 s) until
  * every rank's rows of this rank's latest pf_qlinear_group_gather call are
  * in its peer buffer (the call's own kernel already waits for them; this is

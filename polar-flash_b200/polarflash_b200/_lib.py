@@ -46,6 +46,7 @@ EXPORTS = (
     "pf_kv_row_bytes", "pf_kv_quantize", "pf_kv_dequantize", "pf_rope_kv_compressed",
     "pf_decode_attention_compressed", "pf_workspace_status", "pf_qlinear_noalloc_status", "pf_wait_selftest",
     "pf_peer_export", "pf_peer_open", "pf_peer_close", "pf_qlinear_group_gather", "pf_peers_wait",
+    "pf_allgather_rows",
 )
 
 
@@ -169,6 +170,8 @@ def load():
     L.pf_qlinear_group_gather.argtypes = [I, QWP, PP, I, I, PP, ctypes.POINTER(SZ), ctypes.POINTER(I), PEERS, P, SZ, P]
     L.pf_peers_wait.restype = I
     L.pf_peers_wait.argtypes = [PEERS, P, P]
+    L.pf_allgather_rows.restype = I
+    L.pf_allgather_rows.argtypes = [PEERS, P, ctypes.c_size_t, ctypes.c_size_t, P, P]
     _lib = L
     return L
 

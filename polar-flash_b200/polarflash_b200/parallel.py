@@ -187,3 +187,17 @@ def peers_wait(peer: PeerBuffer, ws: torch.Tensor, stream=None):
     _lib.check(L.pf_peers_wait(ctypes.byref(peer.peers), ctypes.c_void_p(ws.data_ptr()),
                                ctypes.c_void_p(s.cuda_stream)), "pf_peers_wait")
 
+
+def allgather_rows(peer: PeerBuffer, src: torch.Tensor, dst_offset: int, ws: torch.Tensor, stream=None):
+    """pf_allgather_rows: this rank's contiguous `src` lands at byte
+    dst_offset + rank * src.nbytes of every rank's peer buffer (rank-major);
+    when the launch completes on this rank, every rank's part is in its
+    buffer.  Returns the local gathered view [world, *src.shape]."""
+    L = _lib.load()
+    s = stream if stream is not None else torch.cuda.current_stream(src.device)
+    nb = src.numel() * src.element_size()
+    _lib.check(L.pf_allgather_rows(ctypes.byref(peer.peers), ctypes.c_void_p(src.data_ptr()), nb, dst_offset,
+                                   ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(s.cuda_stream)),
+               "pf_allgather_rows")
+    return peer.local[dst_offset:dst_offset + peer.world * nb].view(src.dtype).view(peer.world, *src.shape)
+

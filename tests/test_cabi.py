@@ -152,8 +152,8 @@ def test_status_entry_points_validate_on_the_host():
 
 
 def test_gather_entry_points_validate_on_the_host():
-    """pf_qlinear_group_gather and pf_peers_wait refuse bad peer sets before
-    touching the device."""
+    """pf_qlinear_group_gather, pf_peers_wait and pf_allgather_rows refuse bad
+    peer sets, sizes and alignments before touching the device."""
     L = _lib.load()
     peers = _lib.PFPeers()
     peers.world, peers.rank, peers.bytes = 2, 0, 1 << 20
@@ -175,3 +175,13 @@ def test_gather_entry_points_validate_on_the_host():
     assert call(bad) == _lib.ERR_INVALID_ARGUMENT
     assert L.pf_peers_wait(ctypes.byref(bad), 0x400000, None) == _lib.ERR_INVALID_ARGUMENT
     assert L.pf_peers_wait(ctypes.byref(peers), None, None) == _lib.ERR_INVALID_ARGUMENT
+    # pf_allgather_rows: the same peer-set checks, then sizes and alignments
+    ag = lambda p, src=0x500000, nb=4096, off=256: L.pf_allgather_rows(ctypes.byref(p), src, nb, off,  # noqa: E731
+                                                                       0x400000, None)
+    assert ag(bad) == _lib.ERR_INVALID_ARGUMENT
+    assert ag(peers, off=64) == _lib.ERR_SHAPE            # inside the header
+    assert ag(peers, nb=1 << 20) == _lib.ERR_SHAPE        # world x bytes past the buffer
+    assert ag(peers, nb=0) == _lib.ERR_SHAPE
+    assert ag(peers, nb=4100) == _lib.ERR_ALIGNMENT       # not whole 16-byte words
+    assert ag(peers, src=0x500004) == _lib.ERR_ALIGNMENT
+    assert L.pf_allgather_rows(ctypes.byref(peers), None, 4096, 256, 0x400000, None) == _lib.ERR_INVALID_ARGUMENT

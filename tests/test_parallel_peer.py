@@ -7,11 +7,14 @@ Checked: the gathered y on every rank equals the one-GPU product of the
 whole weight within 1e-5 normwise (the shard's launch sums the same stage
 partials in a different CTA grouping) and the oracle within 1e-3, over three
 calls in a row (the epochs advance) and over replays of a CUDA graph of the
-call.  Needs two CUDA devices; the process group has a short timeout.
+call; and pf_allgather_rows of already computed shards, interleaved with the
+fused calls, puts each rank's shard rank-major in both buffers, bit for bit.
+Needs two CUDA devices; the process group has a short timeout.
 """
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 import torch.multiprocessing as mp
@@ -43,7 +46,8 @@ def _worker(rank, world, port, out_q):
     try:
         from test_gpu_parity import _g128_qweight, _w, _x
 
-        from polarflash_b200.parallel import PeerBuffer, peers_wait, qlinear_group_gather, shard_bounds
+        from polarflash_b200.parallel import (PeerBuffer, allgather_rows, peers_wait, qlinear_group_gather,
+                                              shard_bounds)
         from polarflash_b200.qweight import qlinear, workspace, workspace_status
 
         # a q|k|v-like group (INT3) and an o-like weight (INT2) on different inputs
@@ -59,7 +63,8 @@ def _worker(rank, world, port, out_q):
         for M, _, _ in shapes:
             offs.append(off)
             off += ((4 * M + 255) // 256) * 256
-        peer = PeerBuffer(off, device=dev)
+        gather_off = off  # pf_allgather_rows of a 3 x 1000 fp32 shard per rank
+        peer = PeerBuffer(off + world * 3 * 1000 * 4, device=dev)
         ws = workspace(dev, 1)
         res = {"calls": [], "graph": None}
         for call in range(3):
@@ -94,6 +99,15 @@ def _worker(rank, world, port, out_q):
         refs = [qlinear(q, x) for q, x in zip(full, xs)]
         torch.cuda.synchronize()
         res["graph"] = [(y.cpu().numpy(), r.cpu().numpy(), x.float().cpu().numpy()) for y, r, x in zip(ys, refs, xs)]
+        # standalone all-gather of already computed shards, interleaved with the fused calls
+        got = []
+        for rep in range(2):
+            shard = torch.randn(3, 1000, generator=torch.Generator().manual_seed(10 * rep + rank)).to(dev)
+            out = allgather_rows(peer, shard, gather_off, ws).clone()
+            got.append(out.cpu().numpy())
+            qlinear_group_gather(shards, xs, peer, offs)
+        torch.cuda.synchronize()
+        res["allgather"] = got
         res["status"] = workspace_status(ws, counters=True)
         del g
         dist.barrier()
@@ -128,6 +142,10 @@ def test_gathering_linears_world2():
     meta = {"hadamard_rotation": True, "hadamard_block_size": 128}
     for rank, res, pays, shapes in outs:
         assert res["status"] == (0, 0)
+        for rep, got in enumerate(res["allgather"]):
+            for r in range(2):  # rank-major: rank r's shard at [r]
+                want = torch.randn(3, 1000, generator=torch.Generator().manual_seed(10 * rep + r)).numpy()
+                np.testing.assert_array_equal(got[r], want)
         for triples in res["calls"] + [res["graph"]]:
             for (y, ref, x), pay, (M, K, bits) in zip(triples, pays, shapes):
                 assert_rel(y, ref, rel=1e-5)
