@@ -57,7 +57,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--copies", type=int, default=32)
-    ap.add_argument("--graph-steps", type=int, default=8, help="steps captured per CUDA graph (layers of a decode graph)")
+    ap.add_argument("--graph-steps", type=int, default=32,
+                    help="steps captured per CUDA graph (the 32 layers of an 8B decode graph)")
     ap.add_argument("--gather", default="nccl", choices=["peer", "nccl"],
                     help="at N GPUs: peer = the GEMV stores its rows into every rank's buffer over NVLink "
                          "(pf_qlinear_group_gather); nccl = an NCCL all-gather after the GEMV")
