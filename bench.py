@@ -96,8 +96,10 @@ def upload_graphs(gl, stream):
     cu.cuGraphUpload.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
     cu.cuGraphUpload.restype = ctypes.c_int
     for g in gl:
-        if cu.cuGraphUpload(ctypes.c_void_p(g.raw_cuda_graph_exec()), ctypes.c_void_p(stream.cuda_stream)) != 0:
-            raise RuntimeError("cuGraphUpload failed")
+        ex = g.raw_cuda_graph_exec()
+        if not ex or cu.cuGraphUpload(ctypes.c_void_p(ex), ctypes.c_void_p(stream.cuda_stream)) != 0:
+            print("bench: a CUDA graph was not uploaded ahead of its first replay", file=sys.stderr)
+            return
 
 
 def time_tokens(graphs, stream, tokens):
