@@ -54,7 +54,6 @@ constexpr int kThreadsT = kWarps * 32;
 constexpr int kWarpRows = 16;              // rows per warp and unit (one MMA row tile)
 constexpr int kRowsBlk = kWarpRows * kWarps;  // rows per unit
 constexpr int kMaxStages = 8;
-constexpr int kMaxXSlots = 8;
 
 // Dynamic shared memory per CTA: two CTAs share an SM's 228 KB.
 int smem_budget(int ctas_per_sm) { return ctas_per_sm >= 2 ? 110 * 1024 : 200 * 1024; }
